@@ -1,0 +1,469 @@
+"""Benchmark of the OomLlama GQA attention step on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--no-secondary]
+
+Headline workload (the causal-prefill configuration of the metric): one
+Qwen2.5-7B-shaped layer, 28 q / 4 kv heads, head_dim 128, 4096 new tokens,
+bf16 Q/K/V ~N(0,1), interleaved RoPE theta=1e6, causal.  One step = K-A
+(RoPE of Q and K + append of K/V into the paged bf16 cache) + K-C (tcgen05
+causal prefill) for one sequence per GPU (weak scaling: N GPUs process N
+independent sequences).  Metric: algorithmic causal FLOPs
+4*d*Hq*S(S+1)/2 per sequence / step time (TFLOP/s).
+
+Secondary lines in the same JSON object ("decode"): split-KV decode HBM GB/s
+and tokens/s for the Llama-3-8B long-context shape (32q/8kv, batch 8, 32768
+context, bf16, sharded by kv-head group across GPUs) and the batched
+Qwen2.5-7B decode (batch 64, context U[1024, 8192], shuffled 16-token pages;
+with more GPUs than kv heads the context is split and the partial (O, lse)
+are all-gathered over NCCL and merged).
+
+--impl reference times the oracle's restatement of the reference's scalar
+f32 CPU attention (src/oom_inference.rs:240-272) on the host's cores over a
+bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+S_PREFILL, HQ, HKV, D = 4096, 28, 4, 128
+PREFILL_FLOPS = 4 * D * HQ * S_PREFILL * (S_PREFILL + 1) // 2   # 120,288,444,416 per sequence
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+# dram__bytes_read.sum + dram__bytes_write.sum per launch from ncu captures of
+# this workload (summaries in profiles/); None until captured.
+NCU_TRAFFIC_BYTES = {"prefill_bf16_kernel": None, "decode_bf16_kernel": None}
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--no-secondary", action="store_true")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    return p.parse_args()
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            pk = json.load(f)
+        return {k: float(pk[k]) for k in FALLBACK_PEAKS}, "measured"
+    except Exception:
+        return dict(FALLBACK_PEAKS), "fallback"
+
+
+# ---------------------------------------------------------------- distributed
+class Dist:
+    def __init__(self, gpus):
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        self.pg = False
+        if self.world > 1:
+            import datetime
+
+            import torch
+            import torch.distributed as dist
+            torch.cuda.set_device(self.local)
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
+                                    device_id=torch.device(f"cuda:{self.local}"))
+            self.pg = True
+
+    def barrier(self):
+        if self.pg:
+            import torch
+            import torch.distributed as dist
+            dist.barrier(device_ids=[self.local])
+            torch.cuda.synchronize()
+
+    def max(self, x: float) -> float:
+        if not self.pg:
+            return x
+        import torch
+        import torch.distributed as dist
+        t = torch.tensor([x], dtype=torch.float64, device=f"cuda:{self.local}")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def close(self):
+        if self.pg:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+# ---------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.idx), f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except Exception:
+                self.proc.kill()
+                out = ""
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+        return False
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() in ("active", "1", "yes"):
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------- prefill (headline)
+def bench_prefill(args, dist_, torch):
+    from oomllama_b200 import TurboConfig, TurboEngine
+    dev = torch.cuda.current_device()
+    cfg = TurboConfig(n_layers=1, hidden_size=HQ * D, n_heads=HQ, n_kv_heads=HKV, max_seq_len=S_PREFILL,
+                      max_seqs=1, kv_dtype="bf16", rope_variant="interleaved", rope_theta=1e6)
+    eng = TurboEngine(cfg, device=dev)
+    n_sets = 4  # 4 x 37.7 MB of Q/K/V inputs > 126 MB L2, rotated between steps
+    g = torch.Generator(device="cuda").manual_seed(1 + dist_.rank)
+    sets = []
+    for _ in range(n_sets):
+        q = torch.randn(S_PREFILL, HQ * D, generator=g, device="cuda").to(torch.bfloat16)
+        k = torch.randn(S_PREFILL, HKV * D, generator=g, device="cuda").to(torch.bfloat16)
+        v = torch.randn(S_PREFILL, HKV * D, generator=g, device="cuda").to(torch.bfloat16)
+        sets.append((q, k, v))
+    q_rot = torch.empty(S_PREFILL, HQ, D, dtype=torch.bfloat16, device="cuda")
+    out = torch.empty(S_PREFILL, HQ, D, dtype=torch.float32, device="cuda")
+
+    def step(i, ev=None):
+        q, k, v = sets[i % n_sets]
+        eng.reset()
+        qr = eng.rope_append(0, [0], q, k, v, q_out_dtype=torch.bfloat16)
+        if ev is not None:
+            ev[0].record()
+        eng.prefill(0, 0, qr, out=out)
+        if ev is not None:
+            ev[1].record()
+
+    for i in range(args.warmup):
+        step(i)
+    eng.sync()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    dist_.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(dev) as clk:
+        t0.record()
+        for i in range(args.steps):
+            step(i, evs[i])
+        t1.record()
+        torch.cuda.synchronize()
+    dist_.barrier()
+    eng.sync()
+    ms = t0.elapsed_time(t1) / args.steps
+    kern_ms = sum(a.elapsed_time(b) for a, b in evs) / args.steps
+    ms_max = dist_.max(ms)
+    kern_max = dist_.max(kern_ms)
+
+    # e2e through the public API with pinned host buffers: H2D of Q/K/V, the
+    # step, D2H of the attention output, every step
+    hq = [tuple(t.cpu().pin_memory() for t in s) for s in sets[:2]]
+    ho = torch.empty(S_PREFILL, HQ, D, dtype=torch.float32).pin_memory()
+    dq = [torch.empty_like(t) for t in sets[0]]
+
+    def e2e_step(i):
+        for d_, h_ in zip(dq, hq[i % 2]):
+            d_.copy_(h_, non_blocking=True)
+        eng.reset()
+        qr = eng.rope_append(0, [0], dq[0], dq[1], dq[2], q_out_dtype=torch.bfloat16)
+        eng.prefill(0, 0, qr, out=out)
+        ho.copy_(out, non_blocking=True)
+
+    for i in range(2):
+        e2e_step(i)
+    torch.cuda.synchronize()
+    e_steps = max(3, args.steps // 2)
+    dist_.barrier()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for i in range(e_steps):
+        e2e_step(i)
+    b.record()
+    torch.cuda.synchronize()
+    dist_.barrier()
+    e2e_ms = dist_.max(a.elapsed_time(b) / e_steps)
+    h2d = sum(t.numel() * t.element_size() for t in hq[0])
+    d2h = ho.numel() * ho.element_size()
+    eng.close()
+    return {
+        "ms": ms_max, "kernel_ms": kern_max, "clocks": clk.summary(), "e2e_ms": e2e_ms, "h2d": h2d, "d2h": d2h,
+        "launches_per_step": 2,
+    }
+
+
+# ---------------------------------------------------------------- decode (secondary)
+def bench_decode(args, dist_, torch, name):
+    """Split-KV decode.  llama: 32q/8kv, batch 8, 32768 context, split-half
+    theta=5e5, sharded by kv-head group.  qwen-batched: 28q/4kv, batch 64,
+    context U[1024,8192], shuffled pages; beyond 4 GPUs the context is split
+    in world/4 slices and partials are merged after an NCCL all-gather."""
+    from oomllama_b200 import TurboConfig, TurboEngine
+    dev = torch.cuda.current_device()
+    W, r = dist_.world, dist_.rank
+    if name == "llama-32k":
+        hq, hkv, B, variant, theta = 32, 8, 8, "split_half", 5e5
+        lens = [32768] * B
+    else:
+        hq, hkv, B, variant, theta = 28, 4, 64, "interleaved", 1e6
+        lens = np.random.default_rng(2).integers(1024, 8193, size=B).tolist()
+        lens = [L + 1 for L in lens]  # cached tokens + the new one
+    groups = min(W, hkv)              # kv-head groups
+    ctx_split = W // groups           # context slices when GPUs > kv heads
+    grp, cs = r // ctx_split, r % ctx_split
+    l_hkv, l_hq = hkv // groups, hq // groups
+    # this rank's slice of every sequence: whole pages [c0, c1)
+    slices = []
+    for L in lens:
+        pages = -(-L // 16)
+        p0, p1 = pages * cs // ctx_split, pages * (cs + 1) // ctx_split
+        slices.append((p0 * 16, min(L, p1 * 16)))
+    local = [b - a for a, b in slices]
+    n_pages = sum(-(-x // 16) for x in local)
+    cfg = TurboConfig(n_layers=1, hidden_size=0, n_heads=l_hq, n_kv_heads=l_hkv, max_seq_len=max(lens) + 16,
+                      max_seqs=B, n_pages=max(1, n_pages), kv_dtype="bf16", rope_variant=variant, rope_theta=theta)
+    eng = TurboEngine(cfg, device=dev, assign_pages=False)
+    perm = np.random.default_rng(3 + r).permutation(max(1, n_pages))
+    o = 0
+    for s in range(B):
+        np_s = -(-local[s] // 16)
+        eng.set_block_table(s, perm[o:o + np_s].tolist())
+        o += np_s
+        eng.set_seq_len(0, s, local[s])
+    kp, vp = eng.kv_pool()
+    g = torch.Generator(device="cuda").manual_seed(11 + r)
+    kp.normal_(generator=g)
+    vp.normal_(generator=g)
+    kp[:, -1].zero_()
+    vp[:, -1].zero_()  # the null page stays zero
+    q = torch.randn(B, l_hq, D, generator=g, device="cuda")
+    outb = torch.empty(B, l_hq, D, device="cuda")
+    lse = torch.empty(B, l_hq, device="cuda")
+    merge = ctx_split > 1
+    if merge:
+        import torch.distributed as tdist
+        gparts = torch.empty(W, B * l_hq * D, device="cuda")
+        glses = torch.empty(W, B * l_hq, device="cuda")
+        sub = None  # ranks of this kv-head group gather each other's partials
+        groups_pg = [tdist.new_group(list(range(g_ * ctx_split, (g_ + 1) * ctx_split))) for g_ in range(groups)]
+        sub = groups_pg[grp]
+        gparts = torch.empty(ctx_split, B * l_hq * D, device="cuda")
+        glses = torch.empty(ctx_split, B * l_hq, device="cuda")
+
+    def step(ev=None):
+        if ev is not None:
+            ev[0].record()
+        eng.decode(0, list(range(B)), q, with_lse=merge, out=outb, lse=lse)
+        if ev is not None:
+            ev[1].record()
+        if merge:
+            import torch.distributed as tdist
+            tdist.all_gather_into_tensor(gparts, outb.view(-1), group=sub)
+            tdist.all_gather_into_tensor(glses, lse.view(-1), group=sub)
+            eng.merge_partials(gparts.view(ctx_split, B * l_hq, D), glses)
+
+    steps = max(5, args.steps)
+    for _ in range(args.warmup):
+        step()
+    eng.sync()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    dist_.barrier()
+    t0.record()
+    for i in range(steps):
+        step(evs[i])
+    t1.record()
+    torch.cuda.synchronize()
+    dist_.barrier()
+    eng.sync()
+    ms = dist_.max(t0.elapsed_time(t1) / steps)
+    kern_ms = sum(a.elapsed_time(b) for a, b in evs) / steps
+    kern_max = dist_.max(kern_ms)
+    local_bytes = sum(local) * l_hkv * D * 2 * 2
+    total_bytes = sum(lens) * hkv * D * 2 * 2
+    eng.close()
+    return {"ms": ms, "kernel_ms": kern_max, "local_bytes": local_bytes, "total_bytes": total_bytes, "batch": B,
+            "merge": merge, "lens_sum": sum(lens), "kern_local_ms": kern_ms}
+
+
+# ---------------------------------------------------------------- CPU baseline (oracle port)
+def cpu_prefill_sample(seconds_budget=8.0, threads=None):
+    """Time the oracle's scalar causal attention (oom_inference.rs:240-272 per
+    (query row, head)) on a sample of (row, head) pairs of the 4096-token
+    prefill; returns (TFLOP/s, threads, description)."""
+    from oracle import oracle as O
+    O.build()
+    rng = np.random.default_rng(0)
+    q = rng.standard_normal((S_PREFILL, HQ, D), dtype=np.float32)
+    k = rng.standard_normal((HKV, S_PREFILL, D), dtype=np.float32)
+    v = rng.standard_normal((HKV, S_PREFILL, D), dtype=np.float32)
+    nt = O.omp_max_threads() if threads is None else threads
+    n_pairs = 64 * nt
+    while True:
+        rows = rng.integers(0, S_PREFILL, n_pairs).astype(np.int32)
+        heads = rng.integers(0, HQ, n_pairs).astype(np.int32)
+        t = time.perf_counter()
+        O.gqa_attention_rows(q, k, v, rows, heads, causal=True)
+        dt = time.perf_counter() - t
+        flops = float(np.sum(4.0 * D * (rows.astype(np.float64) + 1)))
+        if dt > 1.0 or n_pairs > 4096 * nt:
+            break
+        n_pairs = int(n_pairs * min(8.0, max(2.0, seconds_budget / 4 / max(dt, 1e-3))))
+    return flops / dt / 1e12, nt, f"{n_pairs} random (query row, head) pairs of the 4096-token causal prefill"
+
+
+def reference_arm(args):
+    """--impl reference: the oracle port of the reference's CPU attention, all host threads."""
+    dist_ = Dist(args.gpus)
+    if dist_.rank != 0:
+        dist_.close()
+        return
+    from oracle import oracle as O
+    O.build()
+    nt = O.omp_max_threads()
+    rng = np.random.default_rng(0)
+    q = rng.standard_normal((S_PREFILL, HQ, D), dtype=np.float32)
+    k = rng.standard_normal((HKV, S_PREFILL, D), dtype=np.float32)
+    v = rng.standard_normal((HKV, S_PREFILL, D), dtype=np.float32)
+    n_pairs = 48 * nt
+    vals = []
+    for i in range(args.warmup + args.steps):
+        rows = rng.integers(0, S_PREFILL, n_pairs).astype(np.int32)
+        heads = rng.integers(0, HQ, n_pairs).astype(np.int32)
+        t = time.perf_counter()
+        O.gqa_attention_rows(q, k, v, rows, heads, causal=True)
+        dt = time.perf_counter() - t
+        if i >= args.warmup:
+            vals.append((float(np.sum(4.0 * D * (rows + 1.0))), dt))
+    flops = sum(f for f, _ in vals)
+    secs = sum(t for _, t in vals)
+    value = flops / secs / 1e12
+    ms_step = secs / len(vals) * 1e3
+    line = {
+        "impl": "reference", "metric": "prefill-attn TFLOPS (causal GQA 28q/4kv d128, S=4096)",
+        "value": value, "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic ~N(0,1), seeded", "config": workload_config(args.gpus),
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": nt, "kind": "port",
+                         "sample": f"{n_pairs} random (query row, head) pairs per step of the 4096-token causal "
+                                   f"prefill (oracle/attn_ref.c restating src/oom_inference.rs:240-272)"},
+        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line))
+    dist_.close()
+
+
+def workload_config(n):
+    return {"workload": "causal prefill, Qwen2.5-7B GQA 28q/4kv d128, 4096 tokens/seq, bf16 Q/K/V ~N(0,1), "
+                        "interleaved RoPE theta=1e6, paged bf16 KV cache (16-token pages)",
+            "sequences": n, "seq_len": S_PREFILL, "parallelism": f"sequence-sharded x{n} (one sequence per GPU)",
+            "l2": "inputs rotated over 4 sets of 37.7 MB (> 126 MB L2)"}
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        reference_arm(args)
+        return
+    import torch
+    dist_ = Dist(args.gpus)
+    torch.cuda.set_device(dist_.local)
+    from oomllama_b200 import _lib
+    _lib.load()  # fail loudly when the library is missing
+    peaks, peak_src = load_peaks()
+    pf = bench_prefill(args, dist_, torch)
+    W = dist_.world
+    value = W * PREFILL_FLOPS / (pf["ms"] * 1e-3) / 1e12
+    achieved = PREFILL_FLOPS / (pf["kernel_ms"] * 1e-3) / 1e12
+    timed_s = pf["ms"] * args.steps * 1e-3
+    peak_key = "bf16_tflops_sustained" if timed_s > 1.0 else "bf16_tflops"
+    line = {
+        "metric": "prefill-attn TFLOPS (causal GQA 28q/4kv d128, S=4096)", "value": value, "unit": "TFLOP/s",
+        "n_gpus": W, "steps": args.steps, "warmup": args.warmup, "ms_per_step": pf["ms"], "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic ~N(0,1), seeded",
+        "config": workload_config(W),
+        "roofline": {"bound": "tensor", "kernel": "prefill_bf16_kernel", "achieved": achieved,
+                     "peak": peaks[peak_key], "unit": "TFLOP/s", "frac": achieved / peaks[peak_key],
+                     "peak_source": f"{peak_src} {peak_key}",
+                     "traffic": NCU_TRAFFIC_BYTES["prefill_bf16_kernel"],
+                     "algorithmic_flops_per_launch": PREFILL_FLOPS},
+        "e2e": {"value": W * PREFILL_FLOPS / (pf["e2e_ms"] * 1e-3) / 1e12, "unit": "TFLOP/s",
+                "h2d_bytes_per_step": pf["h2d"], "d2h_bytes_per_step": pf["d2h"],
+                "api": "TurboEngine.rope_append + TurboEngine.prefill (C ABI) from pinned host buffers"},
+        "gpu_launches": pf["launches_per_step"] * args.steps,
+        "clocks": pf["clocks"],
+    }
+    if not args.no_secondary:
+        dec = {}
+        for name in ("llama-32k", "qwen-batched"):
+            r = bench_decode(args, dist_, torch, name)
+            gbs = r["total_bytes"] / (r["ms"] * 1e-3) / 1e9
+            kern_gbs = r["local_bytes"] / (r["kernel_ms"] * 1e-3) / 1e9
+            dec[name] = {
+                "hbm_gbs": gbs, "tok_s": r["batch"] / (r["ms"] * 1e-3), "ms_per_step": r["ms"],
+                "bytes_per_step": r["total_bytes"], "split_context_merge": r["merge"],
+                "roofline": {"bound": "hbm", "kernel": "decode_bf16_kernel", "achieved": kern_gbs,
+                             "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": kern_gbs / peaks["hbm_gbs"],
+                             "traffic": NCU_TRAFFIC_BYTES["decode_bf16_kernel"]},
+            }
+        line["decode"] = dec
+    if dist_.rank == 0 and W == 1 and not args.no_cpu_baseline:
+        v, nt, desc = cpu_prefill_sample()
+        line["cpu_baseline"] = {"value": v, "unit": "TFLOP/s", "cores": nt, "kind": "port", "sample": desc}
+    if dist_.rank == 0:
+        print(json.dumps(line))
+    dist_.close()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,214 @@
+/*
+ * oomattn -- B200 (sm_100a) grouped-query attention step for OomLlama, behind
+ * a plain C ABI.
+ *
+ * What it replaces (paths relative to the jaspertvdm/oomllama project root):
+ *   TurboEngine::new / reset / seq_len            src/oomllama_turbo.rs:528-538, 726-733
+ *   TurboEngine::attention_forward_with_bias       src/oomllama_turbo.rs:618-723
+ *   LayerKVCache / ModelKVCache (append, get, ...) src/oomllama_turbo.rs:26-104
+ *   TurboEngine::apply_rope, apply_rope,
+ *   apply_rope_llama, compute_rope_freqs           src/oomllama_turbo.rs:376-467, 737-786
+ *   flash_attention_forward                        src/oomllama_turbo.rs:304-369
+ *   attention_head / softmax (CPU scalar path)     src/oom_inference.rs:152-164, 240-272
+ *
+ * Conventions
+ *  - Every function returns an oomattn_status (0 = OK).  Nothing aborts or
+ *    throws across the ABI; oomattn_last_error() holds the message of the last
+ *    failure on a context.  Invalid shapes, indices and positions are rejected
+ *    on the host before any GPU work is queued.
+ *  - Device pointers are raw CUDA device addresses owned by the caller;
+ *    host pointers are marked "host".  All GPU work is queued on the context's
+ *    stream (oomattn_set_stream); nothing synchronises the host except
+ *    oomattn_sync and oomattn_kv_read.
+ *  - A context owns the paged K/V pools of all layers, the block tables, the
+ *    RoPE table and the split-KV scratch.  One context per device per host
+ *    thread; calls on one context are not thread-safe (the reference engine
+ *    sits behind a Mutex / RwLock, src/python.rs:38, src/main.rs:617).
+ *  - head_dim is 128 and a page holds 16 tokens.  Tensor layouts are
+ *    row-major: tokens [T][heads][128]; weights [out][in] (HF/GGUF layout,
+ *    src/oomllama_turbo.rs:637).
+ */
+#ifndef OOMATTN_H
+#define OOMATTN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define OOMATTN_ABI_VERSION 1
+
+typedef enum oomattn_status {
+  OOMATTN_OK = 0,
+  OOMATTN_ERR_INVALID_ARG = 1,  /* null pointer, negative size, unknown enum value */
+  OOMATTN_ERR_BAD_CONFIG = 2,   /* unsupported head_dim / page size, heads not divisible */
+  OOMATTN_ERR_OUT_OF_RANGE = 3, /* layer, sequence, page or position outside its range */
+  OOMATTN_ERR_CUDA = 4,         /* a CUDA runtime / driver call failed */
+  OOMATTN_ERR_NCCL = 5,         /* reserved for communicator failures */
+  OOMATTN_ERR_TIMEOUT = 6,      /* a bounded device-side wait gave up */
+  OOMATTN_ERR_NO_MEMORY = 7,    /* device allocation failed */
+  OOMATTN_ERR_UNSUPPORTED = 8,  /* valid request this build does not implement */
+  OOMATTN_ERR_DEVICE_CHECK = 9  /* a kernel's own index check failed */
+} oomattn_status;
+
+enum { OOMATTN_DTYPE_F32 = 0, OOMATTN_DTYPE_BF16 = 1 };
+/* RoPE pairing: split-half pairs (x[i], x[i+64]) -- apply_rope_llama,
+ * src/oomllama_turbo.rs:443-467, and TurboEngine::apply_rope :737-786;
+ * interleaved pairs (x[2i], x[2i+1]) -- apply_rope, :402-438. */
+enum { OOMATTN_ROPE_SPLIT_HALF = 0, OOMATTN_ROPE_INTERLEAVED = 1 };
+
+/* TurboConfig (src/oomllama_turbo.rs:474-497) plus the fields the reference
+ * hard-codes (theta, :746) or leaves implicit (paging, cache dtype). */
+typedef struct oomattn_config {
+  int32_t n_layers;     /* TurboConfig::n_layers */
+  int32_t hidden_size;  /* TurboConfig::hidden_size (projection input width) */
+  int32_t n_heads;      /* TurboConfig::n_heads (q heads held by this context) */
+  int32_t n_kv_heads;   /* TurboConfig::n_kv_heads; n_heads / n_kv_heads <= 8 */
+  int32_t head_dim;     /* must be 128 */
+  int32_t max_seq_len;  /* TurboConfig::max_seq_len: RoPE positions are < this */
+  int32_t max_seqs;     /* sequence slots (batch rows) */
+  int32_t page_size;    /* must be 16 */
+  int32_t n_pages;      /* pages per layer pool shared by all sequences */
+  int32_t kv_dtype;     /* OOMATTN_DTYPE_F32 or OOMATTN_DTYPE_BF16 */
+  int32_t rope_variant; /* OOMATTN_ROPE_* */
+  float rope_theta;     /* 1e6 for Qwen2.5, 5e5 for Llama-3 */
+  float softmax_scale;  /* <= 0 selects 1/sqrt(head_dim) (src/oomllama_turbo.rs:688) */
+} oomattn_config;
+
+typedef struct oomattn_ctx oomattn_ctx;
+
+/* ---------------------------------------------------------------- lifecycle */
+
+/* Version string of the library build. */
+const char* oomattn_version(void);
+
+/* TurboEngine::new (src/oomllama_turbo.rs:528-538).  Allocates the pools
+ * (zeroed), the RoPE table (host-computed in f32 as :753-761) and scratch on
+ * `device`; `stream` is a cudaStream_t (NULL = legacy default stream). */
+int oomattn_create(const oomattn_config* cfg, int device, void* stream, oomattn_ctx** out);
+int oomattn_destroy(oomattn_ctx* ctx);
+const char* oomattn_last_error(const oomattn_ctx* ctx);
+int oomattn_set_stream(oomattn_ctx* ctx, void* stream);
+/* Waits for the context's stream and reports device-side check failures
+ * (OOMATTN_ERR_TIMEOUT / OOMATTN_ERR_DEVICE_CHECK), clearing them. */
+int oomattn_sync(oomattn_ctx* ctx);
+
+/* TurboEngine::reset / ModelKVCache::clear (src/oomllama_turbo.rs:95-99,
+ * 726-728): every layer's length of every sequence becomes 0.  Page
+ * assignments are kept. */
+int oomattn_reset(oomattn_ctx* ctx);
+
+/* TurboEngine::seq_len / LayerKVCache::seq_len (src/oomllama_turbo.rs:32,
+ * 731-733), per layer and sequence (the reference reads layer 0 only). */
+int oomattn_seq_len(const oomattn_ctx* ctx, int32_t layer, int32_t seq, int32_t* out_len /* host */);
+
+/* ------------------------------------------------------------ cache layout */
+
+/* Assigns pool pages to a sequence: logical page i of `seq` (tokens
+ * 16i..16i+15) lives in pool page pages[i] in every layer.  Unassigned logical
+ * pages point at a zero null page.  pages: host array of n ids in
+ * [0, n_pages). */
+int oomattn_set_block_table(oomattn_ctx* ctx, int32_t seq, const int32_t* pages /* host */, int32_t n);
+
+/* Absolute RoPE position of the sequence's cache slot 0 (default 0).  A
+ * context that holds a later slice of a split context sets it to the slice
+ * start, so appended tokens rotate at their global position. */
+int oomattn_set_position_offset(oomattn_ctx* ctx, int32_t seq, int32_t offset);
+
+/* Sets a sequence's cached length in one layer without writing data (the
+ * pool contents written by other means, e.g. oomattn_kv_pool, are taken as
+ * already rotated). */
+int oomattn_set_seq_len(oomattn_ctx* ctx, int32_t layer, int32_t seq, int32_t len);
+
+/* Device addresses of the K and V pools: element (layer, page, kv, slot, d)
+ * at (((layer*(n_pages+1) + page)*n_kv + kv)*16 + slot)*128 + d, in kv_dtype.
+ * Page n_pages is the null page. */
+int oomattn_kv_pool(const oomattn_ctx* ctx, void** k_pool, void** v_pool);
+
+/* LayerKVCache::append (src/oomllama_turbo.rs:41-55) of already-rotated rows:
+ * k, v: device [n][n_kv][128] in src_dtype appended after the current length. */
+int oomattn_kv_write(oomattn_ctx* ctx, int32_t layer, int32_t seq, const void* k, const void* v, int32_t n,
+                     int32_t src_dtype);
+
+/* LayerKVCache::get (src/oomllama_turbo.rs:57-63): copies the layer's cache of
+ * `seq` to host k_out, v_out [n_kv][len][128] in kv_dtype (synchronises). */
+int oomattn_kv_read(oomattn_ctx* ctx, int32_t layer, int32_t seq, void* k_out /* host */, void* v_out /* host */);
+
+/* Host copy of the f32 RoPE table rows [pos0, pos0+n) as cos, sin
+ * [n][64] (compute_rope_freqs, src/oomllama_turbo.rs:376-396). */
+int oomattn_rope_table(const oomattn_ctx* ctx, int32_t pos0, int32_t n, float* cos_out /* host */,
+                       float* sin_out /* host */);
+
+/* compute_rope_freqs (src/oomllama_turbo.rs:376-396) without a context: the
+ * same host f32 table, rows [pos0, pos0+n), head_dim 128. */
+int oomattn_compute_rope_table(float theta, int32_t head_dim, int32_t pos0, int32_t n, float* cos_out /* host */,
+                               float* sin_out /* host */);
+
+/* ---------------------------------------------------------------- K-A */
+
+/* Bias + RoPE + paged append for already-projected rows (epilogue of
+ * src/oomllama_turbo.rs:647-681).  Rows are n_seqs x n_new tokens, token t of
+ * sequence seq_ids[t / n_new] at position offset + len + t % n_new.
+ *   q: [T][n_heads][128]  k, v: [T][n_kv][128]  in in_dtype (device)
+ *   bq, bk, bv: f32 biases or NULL   q_out: [T][n_heads][128] in q_out_dtype
+ * Every sequence's length grows by n_new in `layer`. */
+int oomattn_rope_append(oomattn_ctx* ctx, int32_t layer, int32_t n_seqs, const int32_t* seq_ids /* host */,
+                        int32_t n_new, const void* q, const void* k, const void* v, int32_t in_dtype,
+                        const float* bq, const float* bk, const float* bv, void* q_out, int32_t q_out_dtype);
+
+/* Fused QKV projection + bias + RoPE + append (src/oomllama_turbo.rs:638-681).
+ *   x: f32 [T][hidden]; wq [n_heads*128][hidden], wk/wv [n_kv*128][hidden] in
+ *   w_dtype; bq/bk/bv f32 or NULL; q_out as in oomattn_rope_append.
+ * T <= 8 runs one fused GEMV kernel (weights read once); larger T runs a
+ * cuBLAS GEMM followed by the K-A epilogue kernel. */
+int oomattn_qkv_rope_append(oomattn_ctx* ctx, int32_t layer, int32_t n_seqs, const int32_t* seq_ids /* host */,
+                            int32_t n_new, const float* x, const void* wq, const void* wk, const void* wv,
+                            int32_t w_dtype, const float* bq, const float* bk, const float* bv, void* q_out,
+                            int32_t q_out_dtype);
+
+/* ---------------------------------------------------------------- K-B */
+
+/* One-query-per-row GQA attention over the paged cache (split-KV flash
+ * decode with an in-kernel LSE merge).  Row z attends to the first lens[z]
+ * slots of sequence seq_ids[z] (lens NULL: the whole current length).
+ *   q: f32 [n_rows][n_heads][128] rotated; out: f32 [n_rows][n_heads][128];
+ *   lse: f32 [n_rows][n_heads] natural-log LSE of the scaled scores, or NULL. */
+int oomattn_decode(oomattn_ctx* ctx, int32_t layer, int32_t n_rows, const int32_t* seq_ids /* host */,
+                   const int32_t* lens /* host, may be NULL */, const float* q, float* out, float* lse);
+
+/* K-B2 / K-D merge: combine n_parts split-context results of n_rows rows:
+ * parts [n_parts][n_rows][128] (each normalised), lses [n_parts][n_rows]
+ * (natural log); out [n_rows][128], lse_out [n_rows] or NULL. */
+int oomattn_merge_partials(oomattn_ctx* ctx, int32_t n_parts, int32_t n_rows, const float* parts, const float* lses,
+                           float* out, float* lse_out);
+
+/* ---------------------------------------------------------------- K-C */
+
+/* Causal prefill of the n_new newest tokens of `seq` (bf16 cache only):
+ * query i (absolute slot len-n_new+i) attends to slots 0..len-n_new+i.
+ *   q: bf16 [n_new][n_heads][128] rotated; out: [n_new][n_heads][128] in
+ *   out_dtype; lse: f32 [n_new][n_heads] or NULL. */
+int oomattn_prefill(oomattn_ctx* ctx, int32_t layer, int32_t seq, int32_t n_new, const void* q, void* out,
+                    int32_t out_dtype, float* lse);
+
+/* ------------------------------------------------------- the layer step */
+
+/* TurboEngine::attention_forward_with_bias (src/oomllama_turbo.rs:618-723) for
+ * batch rows 0..batch-1 (sequence slot b = batch row b), seq_len new tokens
+ * each: QKV + bias -> RoPE at each sequence's own length -> append ->
+ * causal GQA attention -> o_proj.  f32 activations and weights:
+ *   x [batch][seq_len][hidden]; wq [n_heads*128][hidden]; wk, wv
+ *   [n_kv*128][hidden]; wo [o_out][n_heads*128]; bq/bk/bv or NULL;
+ *   out [batch][seq_len][o_out]. */
+int oomattn_attention_forward_with_bias(oomattn_ctx* ctx, int32_t layer, int32_t batch, int32_t seq_len,
+                                        const float* x, const float* wq, const float* wk, const float* wv,
+                                        const float* wo, int32_t o_out, const float* bq, const float* bk,
+                                        const float* bv, float* out);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* OOMATTN_H */

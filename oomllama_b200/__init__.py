@@ -1,0 +1,8 @@
+"""B200-native (sm_100a) grouped-query attention step for OomLlama.
+
+The compute path is liboomattn.so (C ABI in include/oomattn.h); this package is
+its host-side mirror of the reference's TurboEngine interface.
+"""
+from .turbo import TurboConfig, TurboEngine, compute_rope_freqs  # noqa: F401
+
+__all__ = ["TurboConfig", "TurboEngine", "compute_rope_freqs"]

@@ -1,0 +1,404 @@
+// K-B / K-B2: split-KV GQA flash-decode over the paged cache, with the
+// log-sum-exp merge of the splits done by the last CTA of each (row, kv head).
+//
+// Work unit: one CTA per (split, kv head g, row z).  The CTA streams pages
+// [split*pps, (split+1)*pps) of row z's block table and serves all `group`
+// q heads that read kv head g (q head h -> kv head h / group, the
+// repeat_interleave grouping of oomllama_turbo.rs:313-316), so each KV byte is
+// read from HBM once per step instead of `group` times.
+//
+// bf16 cache (decode_bf16_kernel): a producer warp moves each (page, kv head)
+// chunk -- 16 tokens x 128 dims, two 2 KB TMA boxes with the 128-byte swizzle --
+// into a 3-stage shared-memory ring (mbarrier complete_tx); four consumer
+// warps each take one page per stage.  Per page a warp computes
+//   S^T[16 tok x 8 heads] = K[16 x 128] . Q^T        (m16n8k16, Q split hi+lo)
+// then an online softmax per head column (exp2 of log2e-prescaled scores), and
+//   O^T[128 x 8] += V^T[128 x 16] . P^T[16 x 8]       (P split hi+lo)
+// with P^T moved into the B-operand layout by movmatrix.  The hi/lo splits
+// make the bf16 tensor-core products carry ~16 significant bits of the f32
+// query and probabilities; the cached K/V are bf16 by contract.
+//
+// f32 cache (decode_f32_kernel): plain 128-bit loads and f32 FMAs (the f32
+// path's 1e-4 tolerance rules out bf16/tf32 products); same split/merge.
+#pragma once
+#include "common.cuh"
+#include "params.cuh"
+
+namespace oomattn {
+
+constexpr int kDecWarps = 4;                       // consumer warps per CTA
+constexpr int kDecStages = 3;
+constexpr int kChunkBytes = kPageSize * kHeadDim * 2;           // one (page, kv head) bf16 chunk: 4 KB
+constexpr int kDecStageBytes = 2 * kDecWarps * kChunkBytes;     // K and V of 4 pages: 32 KB
+constexpr int kDecSmemBytes = kDecStages * kDecStageBytes + 1024 + 2 * kDecStages * 8 + 64;
+
+constexpr int kMergeStride = kHeadDim + 4;  // padded row of the per-warp O staging area
+struct MergeSmem {
+  float m[kDecWarps][kMaxGroup];
+  float l[kDecWarps][kMaxGroup];
+  float o[kDecWarps][kMaxGroup][kMergeStride];
+};
+
+__device__ __forceinline__ void consumer_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+// Combine the four warps' (m, l, O) of this CTA, then either write the final
+// row (single split) or this split's normalised partial; the last CTA of the
+// (row, kv head) to finish merges all partials:
+//   M = max lse_s ; O = sum 2^(lse_s - M) O_s / sum 2^(lse_s - M) ;
+//   lse = M + log2(sum 2^(lse_s - M))   (base 2; stored as natural log).
+// Runs on the 128 consumer threads (tid 0..127).
+__device__ __forceinline__ void combine_and_store(const MergeSmem& ms, const DecodeArgs& a, int z, int g, int split,
+                                                  int nsplit, int n_kv, int tid, int* s_last) {
+  const int j = tid >> 4;           // q head within the group
+  const int d0 = (tid & 15) * 8;    // 8 output dims per thread
+  const bool active = j < a.group;
+  const int h = g * a.group + j;
+  float acc[8];
+  float lse2 = -INFINITY;
+  if (active) {
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kDecWarps; ++w) M = fmaxf(M, ms.m[w][j]);
+    float lsum = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+#pragma unroll
+    for (int w = 0; w < kDecWarps; ++w) {
+      const float mw = ms.m[w][j];
+      const float wt = (mw == -INFINITY) ? 0.f : exp2f(mw - M);
+      lsum += wt * ms.l[w][j];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] += wt * ms.o[w][j][d0 + i];
+    }
+    const float inv = 1.f / lsum;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] *= inv;
+    lse2 = M + log2f(lsum);
+    if (nsplit == 1) {
+      float4* op = reinterpret_cast<float4*>(a.out + ((size_t)z * a.n_heads + h) * kHeadDim + d0);
+      op[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+      op[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+      if (a.lse && (tid & 15) == 0) a.lse[(size_t)z * a.n_heads + h] = lse2 * 0.69314718055994531f;
+    } else {
+      const size_t prow = ((size_t)z * a.n_heads + h) * a.max_splits + split;
+      float4* pp = reinterpret_cast<float4*>(a.part_o + prow * kHeadDim + d0);
+      pp[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+      pp[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+      if ((tid & 15) == 0) a.part_lse[prow] = lse2;
+    }
+  }
+  if (nsplit == 1) return;
+  __threadfence();
+  consumer_bar();
+  if (tid == 0) {
+    const unsigned prev = atomicAdd(&a.counters[(size_t)z * n_kv + g], 1u);
+    *s_last = (prev == (unsigned)(nsplit - 1));
+  }
+  consumer_bar();
+  if (!*s_last) return;
+  __threadfence();
+  if (active) {
+    const size_t prow0 = ((size_t)z * a.n_heads + h) * a.max_splits;
+    float M = -INFINITY;
+    for (int s = 0; s < nsplit; ++s) M = fmaxf(M, __ldcg(a.part_lse + prow0 + s));
+    float wsum = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+    for (int s = 0; s < nsplit; ++s) {
+      const float ls = __ldcg(a.part_lse + prow0 + s);
+      const float wt = (ls == -INFINITY) ? 0.f : exp2f(ls - M);
+      wsum += wt;
+      const float4* pp = reinterpret_cast<const float4*>(a.part_o + (prow0 + s) * kHeadDim + d0);
+      const float4 u = __ldcg(pp), v = __ldcg(pp + 1);
+      acc[0] += wt * u.x; acc[1] += wt * u.y; acc[2] += wt * u.z; acc[3] += wt * u.w;
+      acc[4] += wt * v.x; acc[5] += wt * v.y; acc[6] += wt * v.z; acc[7] += wt * v.w;
+    }
+    const float inv = 1.f / wsum;
+    float4* op = reinterpret_cast<float4*>(a.out + ((size_t)z * a.n_heads + h) * kHeadDim + d0);
+    op[0] = make_float4(acc[0] * inv, acc[1] * inv, acc[2] * inv, acc[3] * inv);
+    op[1] = make_float4(acc[4] * inv, acc[5] * inv, acc[6] * inv, acc[7] * inv);
+    if (a.lse && (tid & 15) == 0) a.lse[(size_t)z * a.n_heads + h] = (M + log2f(wsum)) * 0.69314718055994531f;
+  }
+  if (tid == 0) a.counters[(size_t)z * n_kv + g] = 0u;
+}
+
+// A row with no visible keys gets O = 0 and lse = -inf (written by split 0).
+__device__ __forceinline__ void write_empty_row(const DecodeArgs& a, int z, int g) {
+  for (int i = threadIdx.x; i < a.group * kHeadDim; i += blockDim.x) {
+    const int h = g * a.group + i / kHeadDim;
+    a.out[((size_t)z * a.n_heads + h) * kHeadDim + (i % kHeadDim)] = 0.f;
+    if (a.lse && (i % kHeadDim) == 0) a.lse[(size_t)z * a.n_heads + h] = -INFINITY;
+  }
+}
+
+__global__ void __launch_bounds__((kDecWarps + 1) * 32, 2)
+    decode_bf16_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
+                       const KVPool pool, const DecodeArgs a, const __grid_constant__ SeqBatch sb) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kDecStages * kDecStageBytes);
+  uint64_t* empty = full + kDecStages;
+  int* s_last = reinterpret_cast<int*>(empty + kDecStages);
+
+  const int split = blockIdx.x, g = blockIdx.y, z = blockIdx.z;
+  const int seq = sb.seq[z];
+  const int L = sb.len[z];
+  const int n_pages = (L + kPageSize - 1) / kPageSize;
+  const int pb = split * a.pages_per_split;
+  const int pe = min(pb + a.pages_per_split, n_pages);
+  if (pb >= pe) {
+    if (L <= 0 && split == 0) write_empty_row(a, z, g);
+    return;
+  }
+  const int nsplit = (n_pages + a.pages_per_split - 1) / a.pages_per_split;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_iter = (pe - pb + kDecWarps - 1) / kDecWarps;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kDecStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kDecWarps);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  if (warp == kDecWarps) {
+    // ---------------- producer: one elected lane issues the TMA loads
+    if (lane == 0) {
+      prefetch_tensormap(&kmap);
+      prefetch_tensormap(&vmap);
+      const int* bt = pool.block_table + (size_t)seq * pool.max_pages_per_seq;
+      for (int it = 0; it < n_iter; ++it) {
+        const int s = it % kDecStages;
+        if (it >= kDecStages) {
+          if (!mbar_wait(&empty[s], ((it / kDecStages) - 1) & 1, a.status, a.timeout_ns)) break;
+        }
+        const int p0 = pb + it * kDecWarps;
+        const int np = min(kDecWarps, pe - p0);
+        mbar_arrive_expect_tx(&full[s], (uint32_t)(np * 2 * kChunkBytes));
+        uint8_t* kst = smem + s * kDecStageBytes;
+        uint8_t* vst = kst + kDecWarps * kChunkBytes;
+        for (int j = 0; j < np; ++j) {
+          int page = __ldg(bt + p0 + j);
+          if ((unsigned)page >= (unsigned)pool.n_pool_pages) {
+            report_error(a.status, kDevErrBounds);
+            page = pool.n_pool_pages - 1;
+          }
+          const int row = ((a.layer * pool.n_pool_pages + page) * pool.n_kv + g) * kPageSize;
+          tma_load_2d(kst + j * kChunkBytes, &kmap, &full[s], 0, row);
+          tma_load_2d(kst + j * kChunkBytes + kChunkBytes / 2, &kmap, &full[s], 64, row);
+          tma_load_2d(vst + j * kChunkBytes, &vmap, &full[s], 0, row);
+          tma_load_2d(vst + j * kChunkBytes + kChunkBytes / 2, &vmap, &full[s], 64, row);
+        }
+      }
+    }
+    return;
+  }
+
+  // ---------------- consumers
+  // Q^T as the B operand of S^T = K Q^T: lane holds head lane/4, dims
+  // kk*16 + 2*(lane%4) + {0,1} and +8, prescaled by scale*log2(e), split hi/lo.
+  uint32_t qh[8][2], ql[8][2];
+  {
+    const int hq = lane >> 2;
+    const bool valid = hq < a.group;
+    const float* qp = a.q + ((size_t)z * a.n_heads + g * a.group + (valid ? hq : 0)) * kHeadDim;
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk) {
+      const int d0 = kk * 16 + 2 * (lane & 3);
+      const float2 x01 = valid ? *reinterpret_cast<const float2*>(qp + d0) : make_float2(0.f, 0.f);
+      const float2 x89 = valid ? *reinterpret_cast<const float2*>(qp + d0 + 8) : make_float2(0.f, 0.f);
+      split_bf16x2(x01.x * a.qscale, x01.y * a.qscale, qh[kk][0], ql[kk][0]);
+      split_bf16x2(x89.x * a.qscale, x89.y * a.qscale, qh[kk][1], ql[kk][1]);
+    }
+  }
+  float o[8][4];
+#pragma unroll
+  for (int mt = 0; mt < 8; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+  const int lrow = lane & 7, lmat = lane >> 3;
+
+  for (int it = 0; it < n_iter; ++it) {
+    const int s = it % kDecStages;
+    if (!mbar_wait(&full[s], (it / kDecStages) & 1, a.status, a.timeout_ns)) break;
+    const int pi = pb + it * kDecWarps + warp;
+    if (pi < pe) {
+      const uint32_t kbase = smem_u32(smem + s * kDecStageBytes + warp * kChunkBytes);
+      const uint32_t vbase = kbase + kDecWarps * kChunkBytes;
+      float sc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {
+        uint32_t a0, a1, a2, a3;
+        ldsm_x4(kbase + sw128_off(lrow + (lmat & 1) * 8, kk * 16 + (lmat >> 1) * 8), a0, a1, a2, a3);
+        mma_bf16_16816(sc, a0, a1, a2, a3, qh[kk][0], qh[kk][1]);
+        mma_bf16_16816(sc, a0, a1, a2, a3, ql[kk][0], ql[kk][1]);
+      }
+      const int t0 = pi * kPageSize + (lane >> 2);
+      if (t0 >= L) sc[0] = sc[1] = -INFINITY;
+      if (t0 + 8 >= L) sc[2] = sc[3] = -INFINITY;
+      float mt0 = fmaxf(sc[0], sc[2]), mt1 = fmaxf(sc[1], sc[3]);
+#pragma unroll
+      for (int off = 4; off < 32; off <<= 1) {
+        mt0 = fmaxf(mt0, __shfl_xor_sync(0xffffffffu, mt0, off));
+        mt1 = fmaxf(mt1, __shfl_xor_sync(0xffffffffu, mt1, off));
+      }
+      const float mn0 = fmaxf(m0, mt0), mn1 = fmaxf(m1, mt1);
+      const float al0 = exp2f(m0 - mn0), al1 = exp2f(m1 - mn1);
+      m0 = mn0;
+      m1 = mn1;
+      const float p0 = exp2f(sc[0] - mn0), p1 = exp2f(sc[1] - mn1);
+      const float p2 = exp2f(sc[2] - mn0), p3 = exp2f(sc[3] - mn1);
+      l0 = l0 * al0 + (p0 + p2);
+      l1 = l1 * al1 + (p1 + p3);
+      uint32_t xh, xl, yh, yl;
+      split_bf16x2(p0, p1, xh, xl);
+      split_bf16x2(p2, p3, yh, yl);
+      const uint32_t bxh = movmatrix_trans(xh), bxl = movmatrix_trans(xl);
+      const uint32_t byh = movmatrix_trans(yh), byl = movmatrix_trans(yl);
+#pragma unroll
+      for (int mt = 0; mt < 8; ++mt) {
+        o[mt][0] *= al0;
+        o[mt][1] *= al1;
+        o[mt][2] *= al0;
+        o[mt][3] *= al1;
+        uint32_t a0, a1, a2, a3;
+        ldsm_x4_trans(vbase + sw128_off(lrow + (lmat >> 1) * 8, mt * 16 + (lmat & 1) * 8), a0, a1, a2, a3);
+        mma_bf16_16816(o[mt], a0, a1, a2, a3, bxh, byh);
+        mma_bf16_16816(o[mt], a0, a1, a2, a3, bxl, byl);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+  }
+
+  // per-warp l: sum the partial sums of the 8 lanes sharing a head column
+#pragma unroll
+  for (int off = 4; off < 32; off <<= 1) {
+    l0 += __shfl_xor_sync(0xffffffffu, l0, off);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, off);
+  }
+  consumer_bar();  // every consumer is done with the stage buffers
+  MergeSmem& ms = *reinterpret_cast<MergeSmem*>(smem);
+  const int h0 = 2 * (lane & 3);
+  if (lane < 4) {
+    ms.m[warp][h0] = m0;
+    ms.m[warp][h0 + 1] = m1;
+    ms.l[warp][h0] = l0;
+    ms.l[warp][h0 + 1] = l1;
+  }
+#pragma unroll
+  for (int mt = 0; mt < 8; ++mt) {
+    const int d = mt * 16 + (lane >> 2);
+    ms.o[warp][h0][d] = o[mt][0];
+    ms.o[warp][h0 + 1][d] = o[mt][1];
+    ms.o[warp][h0][d + 8] = o[mt][2];
+    ms.o[warp][h0 + 1][d + 8] = o[mt][3];
+  }
+  consumer_bar();
+  combine_and_store(ms, a, z, g, split, nsplit, pool.n_kv, threadIdx.x, s_last);
+}
+
+__global__ void __launch_bounds__(kDecWarps * 32)
+    decode_f32_kernel(const KVPool pool, const DecodeArgs a, const __grid_constant__ SeqBatch sb) {
+  __shared__ MergeSmem ms;
+  __shared__ int s_last;
+  const int split = blockIdx.x, g = blockIdx.y, z = blockIdx.z;
+  const int seq = sb.seq[z];
+  const int L = sb.len[z];
+  const int n_pages = (L + kPageSize - 1) / kPageSize;
+  const int pb = split * a.pages_per_split;
+  const int pe = min(pb + a.pages_per_split, n_pages);
+  if (pb >= pe) {
+    if (L <= 0 && split == 0) write_empty_row(a, z, g);
+    return;
+  }
+  const int nsplit = (n_pages + a.pages_per_split - 1) / a.pages_per_split;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const float* kp = reinterpret_cast<const float*>(pool.k);
+  const float* vp = reinterpret_cast<const float*>(pool.v);
+  const int* bt = pool.block_table + (size_t)seq * pool.max_pages_per_seq;
+
+  float4 q[kMaxGroup], o[kMaxGroup];
+  float m[kMaxGroup], l[kMaxGroup];
+#pragma unroll
+  for (int j = 0; j < kMaxGroup; ++j) {
+    if (j < a.group) {
+      const float4 t = *reinterpret_cast<const float4*>(
+          a.q + ((size_t)z * a.n_heads + g * a.group + j) * kHeadDim + lane * 4);
+      q[j] = make_float4(t.x * a.qscale, t.y * a.qscale, t.z * a.qscale, t.w * a.qscale);
+    } else {
+      q[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    o[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+    m[j] = -INFINITY;
+    l[j] = 0.f;
+  }
+  for (int pi = pb + warp; pi < pe; pi += kDecWarps) {
+    int page = __ldg(bt + pi);
+    if ((unsigned)page >= (unsigned)pool.n_pool_pages) {
+      if (lane == 0) report_error(a.status, kDevErrBounds);
+      page = pool.n_pool_pages - 1;
+    }
+    const size_t base = ((size_t)(a.layer * pool.n_pool_pages + page) * pool.n_kv + g) * kPageSize * kHeadDim;
+    const int nt = min(kPageSize, L - pi * kPageSize);
+    for (int t = 0; t < nt; ++t) {
+      const float4 kv = __ldg(reinterpret_cast<const float4*>(kp + base + t * kHeadDim) + lane);
+      const float4 vv = __ldg(reinterpret_cast<const float4*>(vp + base + t * kHeadDim) + lane);
+#pragma unroll
+      for (int j = 0; j < kMaxGroup; ++j) {
+        if (j < a.group) {
+          float s = q[j].x * kv.x + q[j].y * kv.y + q[j].z * kv.z + q[j].w * kv.w;
+#pragma unroll
+          for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+          const float mn = fmaxf(m[j], s);
+          const float al = exp2f(m[j] - mn);
+          const float p = exp2f(s - mn);
+          m[j] = mn;
+          l[j] = l[j] * al + p;
+          o[j].x = o[j].x * al + p * vv.x;
+          o[j].y = o[j].y * al + p * vv.y;
+          o[j].z = o[j].z * al + p * vv.z;
+          o[j].w = o[j].w * al + p * vv.w;
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < kMaxGroup; ++j) {
+    if (lane == 0) {
+      ms.m[warp][j] = m[j];
+      ms.l[warp][j] = l[j];
+    }
+    *reinterpret_cast<float4*>(&ms.o[warp][j][lane * 4]) = o[j];
+  }
+  __syncthreads();
+  combine_and_store(ms, a, z, g, split, nsplit, pool.n_kv, threadIdx.x, &s_last);
+}
+
+// K-B2 standalone: merge P split-context partials (from P GPUs or P launches)
+// given as normalised O_p [P][rows][128] and natural-log lse_p [P][rows].
+__global__ void merge_partials_kernel(const float* __restrict__ parts, const float* __restrict__ lses, int n_parts,
+                                      int n_rows, float* __restrict__ out, float* __restrict__ lse_out) {
+  const int r = blockIdx.x;
+  const int d = threadIdx.x;  // 128 threads
+  if (r >= n_rows) return;
+  float M = -INFINITY;
+  for (int p = 0; p < n_parts; ++p) M = fmaxf(M, lses[(size_t)p * n_rows + r]);
+  if (M == -INFINITY) {
+    out[(size_t)r * kHeadDim + d] = 0.f;
+    if (lse_out && d == 0) lse_out[r] = -INFINITY;
+    return;
+  }
+  float acc = 0.f, wsum = 0.f;
+  for (int p = 0; p < n_parts; ++p) {
+    const float lp = lses[(size_t)p * n_rows + r];
+    const float wt = (lp == -INFINITY) ? 0.f : expf(lp - M);
+    wsum += wt;
+    acc += wt * parts[((size_t)p * n_rows + r) * kHeadDim + d];
+  }
+  out[(size_t)r * kHeadDim + d] = acc / wsum;
+  if (lse_out && d == 0) lse_out[r] = M + logf(wsum);
+}
+
+}  // namespace oomattn

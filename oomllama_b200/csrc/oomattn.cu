@@ -1,0 +1,856 @@
+// Host side of the oomattn C ABI (include/oomattn.h): context lifetime, host
+// validation, the paged-cache bookkeeping that mirrors LayerKVCache /
+// ModelKVCache (src/oomllama_turbo.rs:26-104), tensor maps, split planning and
+// kernel launches.  Everything here is plain host C++ over the CUDA runtime;
+// the only library calls are cuBLAS GEMMs for projections of more than 8
+// tokens and for o_proj.
+#include <cublas_v2.h>
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <math.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <algorithm>
+#include <string>
+#include <vector>
+
+#include "../../include/oomattn.h"
+#include "common.cuh"
+#include "decode.cuh"
+#include "params.cuh"
+#include "prefill.cuh"
+#include "rope_append.cuh"
+
+using namespace oomattn;
+
+namespace {
+
+constexpr int kMaxSplits = 32;                        // split-KV partials per (row, q head)
+constexpr unsigned long long kDefaultTimeoutNs = 2000000000ull;  // bounded device waits: 2 s
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn get_encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+}  // namespace
+
+struct oomattn_ctx {
+  oomattn_config cfg;
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  std::string err;
+  int num_sms = 148;
+  int group = 1;
+  int max_pages_per_seq = 0;
+  int n_pool_pages = 0;  // cfg.n_pages + null page
+  size_t esize = 4;
+  float scale = 0.f;
+  unsigned long long timeout_ns = kDefaultTimeoutNs;
+  // device state
+  void* kpool = nullptr;
+  void* vpool = nullptr;
+  int* d_block_table = nullptr;
+  float* d_cos = nullptr;
+  float* d_sin = nullptr;
+  float* d_part_o = nullptr;
+  float* d_part_lse = nullptr;
+  unsigned* d_counters = nullptr;
+  int* d_status = nullptr;
+  CUtensorMap kmap{}, vmap{};
+  bool have_maps = false;
+  // host mirrors (authoritative for lengths; updated at enqueue time)
+  std::vector<int> h_block_table;  // [max_seqs][max_pages_per_seq]
+  std::vector<int> h_len;          // [n_layers][max_seqs]
+  std::vector<int> h_pos_off;      // [max_seqs]
+  std::vector<float> h_cos, h_sin; // [max_seq_len][64]
+  // lazily grown scratch for the layer step
+  cublasHandle_t cublas = nullptr;
+  float* d_scratch = nullptr;
+  size_t scratch_bytes = 0;
+};
+
+namespace {
+
+int fail(oomattn_ctx* ctx, int code, const char* fmt, ...) {
+  if (ctx) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    ctx->err = buf;
+  }
+  return code;
+}
+
+#define CK(call)                                                                                     \
+  do {                                                                                               \
+    cudaError_t e_ = (call);                                                                         \
+    if (e_ != cudaSuccess) return fail(ctx, OOMATTN_ERR_CUDA, "%s: %s", #call, cudaGetErrorString(e_)); \
+  } while (0)
+
+#define CKLAUNCH()                                                                                          \
+  do {                                                                                                      \
+    cudaError_t e_ = cudaGetLastError();                                                                    \
+    if (e_ != cudaSuccess) return fail(ctx, OOMATTN_ERR_CUDA, "kernel launch: %s", cudaGetErrorString(e_)); \
+  } while (0)
+
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev) {
+    cudaGetDevice(&prev);
+    if (prev != dev) cudaSetDevice(dev);
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+// f32 RoPE table exactly as the reference builds it on the host
+// (src/oomllama_turbo.rs:753-761): inv_freq = 1 / theta^(2i/d) with f32 powf,
+// angle = (f32)pos * inv_freq, cos/sin in f32.
+void build_rope_table(float theta, int n_pos, std::vector<float>& c, std::vector<float>& s) {
+  const int half = kHeadDim / 2;
+  std::vector<float> inv(half);
+  for (int i = 0; i < half; ++i) {
+    volatile float e = (2.0f * (float)i) / (float)kHeadDim;
+    inv[i] = 1.0f / powf(theta, e);
+  }
+  c.resize((size_t)n_pos * half);
+  s.resize((size_t)n_pos * half);
+  for (int p = 0; p < n_pos; ++p) {
+    const float pos = (float)p;
+    for (int i = 0; i < half; ++i) {
+      volatile float a = pos * inv[i];
+      c[(size_t)p * half + i] = cosf(a);
+      s[(size_t)p * half + i] = sinf(a);
+    }
+  }
+}
+
+int encode_pool_map(oomattn_ctx* ctx, void* base, CUtensorMap* map) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) return fail(ctx, OOMATTN_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  const uint64_t rows = (uint64_t)ctx->cfg.n_layers * ctx->n_pool_pages * ctx->cfg.n_kv_heads * kPageSize;
+  cuuint64_t dims[2] = {(cuuint64_t)kHeadDim, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)kHeadDim * 2};
+  cuuint32_t box[2] = {64, (cuuint32_t)kPageSize};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(ctx, OOMATTN_ERR_CUDA, "cuTensorMapEncodeTiled(pool) failed: %d", (int)r);
+  return OOMATTN_OK;
+}
+
+int encode_q_map(oomattn_ctx* ctx, const void* q, int n_new, CUtensorMap* map) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) return fail(ctx, OOMATTN_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  cuuint64_t dims[3] = {(cuuint64_t)kHeadDim, (cuuint64_t)ctx->cfg.n_heads, (cuuint64_t)n_new};
+  cuuint64_t strides[2] = {(cuuint64_t)kHeadDim * 2, (cuuint64_t)ctx->cfg.n_heads * kHeadDim * 2};
+  cuuint32_t box[3] = {64, 1, 128};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(q), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(ctx, OOMATTN_ERR_CUDA, "cuTensorMapEncodeTiled(q) failed: %d", (int)r);
+  return OOMATTN_OK;
+}
+
+KVPool make_pool(const oomattn_ctx* ctx) {
+  KVPool p;
+  p.k = ctx->kpool;
+  p.v = ctx->vpool;
+  p.block_table = ctx->d_block_table;
+  p.max_pages_per_seq = ctx->max_pages_per_seq;
+  p.n_pool_pages = ctx->n_pool_pages;
+  p.n_kv = ctx->cfg.n_kv_heads;
+  p.kv_bf16 = ctx->cfg.kv_dtype == OOMATTN_DTYPE_BF16;
+  return p;
+}
+
+int check_layer(oomattn_ctx* ctx, int layer) {
+  if (layer < 0 || layer >= ctx->cfg.n_layers)
+    return fail(ctx, OOMATTN_ERR_OUT_OF_RANGE, "layer %d outside [0, %d)", layer, ctx->cfg.n_layers);
+  return OOMATTN_OK;
+}
+
+int check_seq(oomattn_ctx* ctx, int seq) {
+  if (seq < 0 || seq >= ctx->cfg.max_seqs)
+    return fail(ctx, OOMATTN_ERR_OUT_OF_RANGE, "sequence %d outside [0, %d)", seq, ctx->cfg.max_seqs);
+  return OOMATTN_OK;
+}
+
+// Slots [from, to) of `seq` must sit in assigned pages.
+int check_slots(oomattn_ctx* ctx, int seq, int from, int to) {
+  if (to > ctx->max_pages_per_seq * kPageSize)
+    return fail(ctx, OOMATTN_ERR_OUT_OF_RANGE, "sequence %d: %d slots exceed max_seq_len capacity %d", seq, to,
+                ctx->max_pages_per_seq * kPageSize);
+  const int null_page = ctx->n_pool_pages - 1;
+  for (int lp = from / kPageSize; lp * kPageSize < to; ++lp)
+    if (ctx->h_block_table[(size_t)seq * ctx->max_pages_per_seq + lp] == null_page)
+      return fail(ctx, OOMATTN_ERR_OUT_OF_RANGE, "sequence %d: logical page %d (slot %d) has no pool page", seq, lp,
+                  std::max(from, lp * kPageSize));
+  return OOMATTN_OK;
+}
+
+int validate_dtype(oomattn_ctx* ctx, int dt, const char* what) {
+  if (dt != OOMATTN_DTYPE_F32 && dt != OOMATTN_DTYPE_BF16)
+    return fail(ctx, OOMATTN_ERR_INVALID_ARG, "%s: unknown dtype %d", what, dt);
+  return OOMATTN_OK;
+}
+
+int ensure_scratch(oomattn_ctx* ctx, size_t bytes) {
+  if (bytes <= ctx->scratch_bytes) return OOMATTN_OK;
+  if (ctx->d_scratch) {
+    cudaStreamSynchronize(ctx->stream);
+    cudaFree(ctx->d_scratch);
+    ctx->d_scratch = nullptr;
+    ctx->scratch_bytes = 0;
+  }
+  if (cudaMalloc(&ctx->d_scratch, bytes) != cudaSuccess)
+    return fail(ctx, OOMATTN_ERR_NO_MEMORY, "scratch allocation of %zu bytes failed", bytes);
+  ctx->scratch_bytes = bytes;
+  return OOMATTN_OK;
+}
+
+int ensure_cublas(oomattn_ctx* ctx) {
+  if (!ctx->cublas) {
+    if (cublasCreate(&ctx->cublas) != CUBLAS_STATUS_SUCCESS)
+      return fail(ctx, OOMATTN_ERR_CUDA, "cublasCreate failed");
+    cublasSetMathMode(ctx->cublas, CUBLAS_PEDANTIC_MATH);  // true f32, no TF32
+  }
+  cublasSetStream(ctx->cublas, ctx->stream);
+  return OOMATTN_OK;
+}
+
+// C[T][N] = A[T][K] . W[N][K]^T in f32 (row-major); with a bf16 W the
+// activations arrive already converted to bf16 (A16) and the GEMM accumulates
+// in f32.
+int gemm_xwT(oomattn_ctx* ctx, const float* A, const void* W, int w_bf16, float* C, int T, int N, int K,
+             const void* A16 = nullptr) {
+  int rc = ensure_cublas(ctx);
+  if (rc) return rc;
+  const float one = 1.f, zero = 0.f;
+  cublasStatus_t st;
+  if (!w_bf16) {
+    st = cublasSgemm(ctx->cublas, CUBLAS_OP_T, CUBLAS_OP_N, N, T, K, &one, (const float*)W, K, A, K, &zero, C, N);
+  } else {
+    st = cublasGemmEx(ctx->cublas, CUBLAS_OP_T, CUBLAS_OP_N, N, T, K, &one, W, CUDA_R_16BF, K, A16, CUDA_R_16BF, K,
+                      &zero, C, CUDA_R_32F, N, CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
+  }
+  if (st != CUBLAS_STATUS_SUCCESS) return fail(ctx, OOMATTN_ERR_CUDA, "cuBLAS GEMM failed: %d", (int)st);
+  return OOMATTN_OK;
+}
+
+// Fills the SeqBatch of an append over rows [r0, r0+n) and advances the host lengths.
+int plan_append(oomattn_ctx* ctx, int layer, int n, const int32_t* seq_ids, int n_new, SeqBatch& sb) {
+  sb.n = n;
+  for (int z = 0; z < n; ++z) {
+    const int seq = seq_ids[z];
+    int rc = check_seq(ctx, seq);
+    if (rc) return rc;
+    for (int w = 0; w < z; ++w)
+      if (sb.seq[w] == seq) return fail(ctx, OOMATTN_ERR_INVALID_ARG, "sequence %d appears twice in one append", seq);
+    const int len = ctx->h_len[(size_t)layer * ctx->cfg.max_seqs + seq];
+    const int pos = ctx->h_pos_off[seq] + len;
+    if (pos + n_new > ctx->cfg.max_seq_len)
+      return fail(ctx, OOMATTN_ERR_OUT_OF_RANGE, "sequence %d: positions up to %d exceed max_seq_len %d", seq,
+                  pos + n_new - 1, ctx->cfg.max_seq_len);
+    rc = check_slots(ctx, seq, len, len + n_new);
+    if (rc) return rc;
+    sb.seq[z] = seq;
+    sb.len[z] = len;
+    sb.pos[z] = pos;
+  }
+  return OOMATTN_OK;
+}
+
+void commit_append(oomattn_ctx* ctx, int layer, const SeqBatch& sb, int n_new) {
+  for (int z = 0; z < sb.n; ++z) ctx->h_len[(size_t)layer * ctx->cfg.max_seqs + sb.seq[z]] += n_new;
+}
+
+AppendArgs base_append_args(oomattn_ctx* ctx, int layer, int n_new) {
+  AppendArgs ap;
+  memset(&ap, 0, sizeof(ap));
+  ap.cos_t = ctx->d_cos;
+  ap.sin_t = ctx->d_sin;
+  ap.max_pos = ctx->cfg.max_seq_len;
+  ap.n_heads = ctx->cfg.n_heads;
+  ap.n_new = n_new;
+  ap.layer = layer;
+  ap.variant = ctx->cfg.rope_variant;
+  ap.rope_k = 1;
+  ap.status = ctx->d_status;
+  return ap;
+}
+
+int launch_decode_rows(oomattn_ctx* ctx, int layer, const SeqBatch& sb, const float* q, float* out, float* lse) {
+  const int n_kv = ctx->cfg.n_kv_heads;
+  long long unit_pages = 0;
+  int max_pages = 0;
+  for (int z = 0; z < sb.n; ++z) {
+    const int pages = (sb.len[z] + kPageSize - 1) / kPageSize;
+    unit_pages += (long long)pages * n_kv;
+    max_pages = std::max(max_pages, pages);
+  }
+  // Split size: ~8 CTAs per SM in total, at least 8 pages (one per consumer
+  // warp per two stages) and few enough splits to fit the partial scratch.
+  long long target = (unit_pages + (long long)ctx->num_sms * 8 - 1) / ((long long)ctx->num_sms * 8);
+  int pps = (int)std::max<long long>(8, (target + 3) / 4 * 4);
+  pps = std::max(pps, (max_pages + kMaxSplits - 1) / kMaxSplits);
+  const int nsplit = std::max(1, (max_pages + pps - 1) / pps);
+  DecodeArgs a;
+  a.q = q;
+  a.out = out;
+  a.lse = lse;
+  a.layer = layer;
+  a.n_heads = ctx->cfg.n_heads;
+  a.group = ctx->group;
+  a.pages_per_split = pps;
+  a.max_splits = kMaxSplits;
+  a.qscale = ctx->scale * 1.4426950408889634f;
+  a.part_o = ctx->d_part_o;
+  a.part_lse = ctx->d_part_lse;
+  a.counters = ctx->d_counters;
+  a.status = ctx->d_status;
+  a.timeout_ns = ctx->timeout_ns;
+  KVPool pool = make_pool(ctx);
+  dim3 grid(nsplit, n_kv, sb.n);
+  if (ctx->cfg.kv_dtype == OOMATTN_DTYPE_BF16) {
+    decode_bf16_kernel<<<grid, (kDecWarps + 1) * 32, kDecSmemBytes, ctx->stream>>>(ctx->kmap, ctx->vmap, pool, a, sb);
+  } else {
+    decode_f32_kernel<<<grid, kDecWarps * 32, 0, ctx->stream>>>(pool, a, sb);
+  }
+  CKLAUNCH();
+  return OOMATTN_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* oomattn_version(void) { return "oomattn 0.1 (sm_100a)"; }
+
+const char* oomattn_last_error(const oomattn_ctx* ctx) { return ctx ? ctx->err.c_str() : "null context"; }
+
+int oomattn_create(const oomattn_config* cfg, int device, void* stream, oomattn_ctx** out) {
+  if (!cfg || !out) return OOMATTN_ERR_INVALID_ARG;
+  *out = nullptr;
+  const oomattn_config& c = *cfg;
+  if (c.head_dim != kHeadDim || c.page_size != kPageSize || c.n_heads <= 0 || c.n_kv_heads <= 0 ||
+      c.n_heads % c.n_kv_heads != 0 || c.n_heads / c.n_kv_heads > kMaxGroup || c.n_layers <= 0 ||
+      c.max_seq_len <= 0 || c.max_seqs <= 0 || c.n_pages <= 0 || c.hidden_size < 0 || !(c.rope_theta > 0.f) ||
+      (c.kv_dtype != OOMATTN_DTYPE_F32 && c.kv_dtype != OOMATTN_DTYPE_BF16) ||
+      (c.rope_variant != OOMATTN_ROPE_SPLIT_HALF && c.rope_variant != OOMATTN_ROPE_INTERLEAVED))
+    return OOMATTN_ERR_BAD_CONFIG;
+  const long long rows = (long long)c.n_layers * (c.n_pages + 1) * c.n_kv_heads * kPageSize;
+  if (rows >= (1ll << 31)) return OOMATTN_ERR_BAD_CONFIG;
+
+  oomattn_ctx* ctx = new oomattn_ctx();
+  ctx->cfg = c;
+  ctx->device = device;
+  ctx->stream = reinterpret_cast<cudaStream_t>(stream);
+  ctx->group = c.n_heads / c.n_kv_heads;
+  ctx->max_pages_per_seq = (c.max_seq_len + kPageSize - 1) / kPageSize;
+  ctx->n_pool_pages = c.n_pages + 1;
+  ctx->esize = c.kv_dtype == OOMATTN_DTYPE_BF16 ? 2 : 4;
+  ctx->scale = c.softmax_scale > 0.f ? c.softmax_scale : 1.0f / sqrtf((float)kHeadDim);
+  DeviceGuard dg(device);
+  auto bail = [&](int code) {
+    oomattn_destroy(ctx);
+    return code;
+  };
+  if (cudaSetDevice(device) != cudaSuccess) return bail(OOMATTN_ERR_CUDA);
+  cudaDeviceGetAttribute(&ctx->num_sms, cudaDevAttrMultiProcessorCount, device);
+  const size_t pool_bytes = (size_t)rows * kHeadDim * ctx->esize;
+  if (cudaMalloc(&ctx->kpool, pool_bytes) != cudaSuccess || cudaMalloc(&ctx->vpool, pool_bytes) != cudaSuccess)
+    return bail(OOMATTN_ERR_NO_MEMORY);
+  if (cudaMemset(ctx->kpool, 0, pool_bytes) != cudaSuccess || cudaMemset(ctx->vpool, 0, pool_bytes) != cudaSuccess)
+    return bail(OOMATTN_ERR_CUDA);
+  const size_t bt_n = (size_t)c.max_seqs * ctx->max_pages_per_seq;
+  ctx->h_block_table.assign(bt_n, ctx->n_pool_pages - 1);
+  ctx->h_len.assign((size_t)c.n_layers * c.max_seqs, 0);
+  ctx->h_pos_off.assign(c.max_seqs, 0);
+  if (cudaMalloc(&ctx->d_block_table, bt_n * sizeof(int)) != cudaSuccess) return bail(OOMATTN_ERR_NO_MEMORY);
+  if (cudaMemcpy(ctx->d_block_table, ctx->h_block_table.data(), bt_n * sizeof(int), cudaMemcpyHostToDevice) !=
+      cudaSuccess)
+    return bail(OOMATTN_ERR_CUDA);
+  build_rope_table(c.rope_theta, c.max_seq_len, ctx->h_cos, ctx->h_sin);
+  const size_t tab = ctx->h_cos.size() * sizeof(float);
+  if (cudaMalloc(&ctx->d_cos, tab) != cudaSuccess || cudaMalloc(&ctx->d_sin, tab) != cudaSuccess)
+    return bail(OOMATTN_ERR_NO_MEMORY);
+  if (cudaMemcpy(ctx->d_cos, ctx->h_cos.data(), tab, cudaMemcpyHostToDevice) != cudaSuccess ||
+      cudaMemcpy(ctx->d_sin, ctx->h_sin.data(), tab, cudaMemcpyHostToDevice) != cudaSuccess)
+    return bail(OOMATTN_ERR_CUDA);
+  const size_t parts = (size_t)kMaxBatch * c.n_heads * kMaxSplits;
+  if (cudaMalloc(&ctx->d_part_o, parts * kHeadDim * sizeof(float)) != cudaSuccess ||
+      cudaMalloc(&ctx->d_part_lse, parts * sizeof(float)) != cudaSuccess ||
+      cudaMalloc(&ctx->d_counters, (size_t)kMaxBatch * c.n_kv_heads * sizeof(unsigned)) != cudaSuccess ||
+      cudaMalloc(&ctx->d_status, sizeof(int)) != cudaSuccess)
+    return bail(OOMATTN_ERR_NO_MEMORY);
+  if (cudaMemset(ctx->d_counters, 0, (size_t)kMaxBatch * c.n_kv_heads * sizeof(unsigned)) != cudaSuccess ||
+      cudaMemset(ctx->d_status, 0, sizeof(int)) != cudaSuccess)
+    return bail(OOMATTN_ERR_CUDA);
+  if (c.kv_dtype == OOMATTN_DTYPE_BF16) {
+    if (encode_pool_map(ctx, ctx->kpool, &ctx->kmap) || encode_pool_map(ctx, ctx->vpool, &ctx->vmap))
+      return bail(OOMATTN_ERR_CUDA);
+    ctx->have_maps = true;
+  }
+  if (cudaFuncSetAttribute(decode_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kDecSmemBytes) !=
+          cudaSuccess ||
+      cudaFuncSetAttribute(prefill_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kPfSmemBytes) !=
+          cudaSuccess)
+    return bail(OOMATTN_ERR_CUDA);
+  if (cudaDeviceSynchronize() != cudaSuccess) return bail(OOMATTN_ERR_CUDA);
+  *out = ctx;
+  return OOMATTN_OK;
+}
+
+int oomattn_destroy(oomattn_ctx* ctx) {
+  if (!ctx) return OOMATTN_ERR_INVALID_ARG;
+  DeviceGuard dg(ctx->device);
+  if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+  if (ctx->cublas) cublasDestroy(ctx->cublas);
+  void* ptrs[] = {ctx->kpool,     ctx->vpool,      ctx->d_block_table, ctx->d_cos,    ctx->d_sin,
+                  ctx->d_part_o,  ctx->d_part_lse, ctx->d_counters,    ctx->d_status, ctx->d_scratch};
+  for (void* p : ptrs)
+    if (p) cudaFree(p);
+  delete ctx;
+  return OOMATTN_OK;
+}
+
+int oomattn_set_stream(oomattn_ctx* ctx, void* stream) {
+  if (!ctx) return OOMATTN_ERR_INVALID_ARG;
+  ctx->stream = reinterpret_cast<cudaStream_t>(stream);
+  return OOMATTN_OK;
+}
+
+int oomattn_sync(oomattn_ctx* ctx) {
+  if (!ctx) return OOMATTN_ERR_INVALID_ARG;
+  DeviceGuard dg(ctx->device);
+  CK(cudaStreamSynchronize(ctx->stream));
+  int st = 0;
+  CK(cudaMemcpy(&st, ctx->d_status, sizeof(int), cudaMemcpyDeviceToHost));
+  if (st) {
+    CK(cudaMemset(ctx->d_status, 0, sizeof(int)));
+    if (st & kDevErrTimeout) return fail(ctx, OOMATTN_ERR_TIMEOUT, "a device-side wait timed out (status %d)", st);
+    return fail(ctx, OOMATTN_ERR_DEVICE_CHECK, "a device-side index check failed (status %d)", st);
+  }
+  return OOMATTN_OK;
+}
+
+int oomattn_reset(oomattn_ctx* ctx) {
+  if (!ctx) return OOMATTN_ERR_INVALID_ARG;
+  std::fill(ctx->h_len.begin(), ctx->h_len.end(), 0);
+  return OOMATTN_OK;
+}
+
+int oomattn_seq_len(const oomattn_ctx* ctx, int32_t layer, int32_t seq, int32_t* out_len) {
+  if (!ctx || !out_len) return OOMATTN_ERR_INVALID_ARG;
+  if (layer < 0 || layer >= ctx->cfg.n_layers || seq < 0 || seq >= ctx->cfg.max_seqs) return OOMATTN_ERR_OUT_OF_RANGE;
+  *out_len = ctx->h_len[(size_t)layer * ctx->cfg.max_seqs + seq];
+  return OOMATTN_OK;
+}
+
+int oomattn_set_block_table(oomattn_ctx* ctx, int32_t seq, const int32_t* pages, int32_t n) {
+  if (!ctx || (n > 0 && !pages) || n < 0) return fail(ctx, OOMATTN_ERR_INVALID_ARG, "bad block-table arguments");
+  int rc = check_seq(ctx, seq);
+  if (rc) return rc;
+  if (n > ctx->max_pages_per_seq)
+    return fail(ctx, OOMATTN_ERR_OUT_OF_RANGE, "%d pages exceed max_seq_len / 16 = %d", n, ctx->max_pages_per_seq);
+  for (int i = 0; i < n; ++i)
+    if (pages[i] < 0 || pages[i] >= ctx->cfg.n_pages)
+      return fail(ctx, OOMATTN_ERR_OUT_OF_RANGE, "page id %d outside [0, %d)", pages[i], ctx->cfg.n_pages);
+  int* row = ctx->h_block_table.data() + (size_t)seq * ctx->max_pages_per_seq;
+  for (int i = 0; i < ctx->max_pages_per_seq; ++i) row[i] = i < n ? pages[i] : ctx->n_pool_pages - 1;
+  DeviceGuard dg(ctx->device);
+  CK(cudaMemcpyAsync(ctx->d_block_table + (size_t)seq * ctx->max_pages_per_seq, row,
+                     ctx->max_pages_per_seq * sizeof(int), cudaMemcpyHostToDevice, ctx->stream));
+  CK(cudaStreamSynchronize(ctx->stream));  // the host row may change again before the copy would run
+  return OOMATTN_OK;
+}
+
+int oomattn_set_position_offset(oomattn_ctx* ctx, int32_t seq, int32_t offset) {
+  if (!ctx || offset < 0) return fail(ctx, OOMATTN_ERR_INVALID_ARG, "bad position offset");
+  int rc = check_seq(ctx, seq);
+  if (rc) return rc;
+  ctx->h_pos_off[seq] = offset;
+  return OOMATTN_OK;
+}
+
+int oomattn_set_seq_len(oomattn_ctx* ctx, int32_t layer, int32_t seq, int32_t len) {
+  if (!ctx || len < 0) return fail(ctx, OOMATTN_ERR_INVALID_ARG, "bad length");
+  int rc = check_layer(ctx, layer);
+  if (!rc) rc = check_seq(ctx, seq);
+  if (!rc) rc = check_slots(ctx, seq, 0, len);
+  if (rc) return rc;
+  ctx->h_len[(size_t)layer * ctx->cfg.max_seqs + seq] = len;
+  return OOMATTN_OK;
+}
+
+int oomattn_kv_pool(const oomattn_ctx* ctx, void** k_pool, void** v_pool) {
+  if (!ctx || !k_pool || !v_pool) return OOMATTN_ERR_INVALID_ARG;
+  *k_pool = ctx->kpool;
+  *v_pool = ctx->vpool;
+  return OOMATTN_OK;
+}
+
+int oomattn_kv_write(oomattn_ctx* ctx, int32_t layer, int32_t seq, const void* k, const void* v, int32_t n,
+                     int32_t src_dtype) {
+  if (!ctx || !k || !v || n < 0) return fail(ctx, OOMATTN_ERR_INVALID_ARG, "bad kv_write arguments");
+  int rc = check_layer(ctx, layer);
+  if (!rc) rc = validate_dtype(ctx, src_dtype, "kv_write");
+  if (rc) return rc;
+  if (n == 0) return OOMATTN_OK;
+  SeqBatch sb;
+  int32_t sid = seq;
+  rc = plan_append(ctx, layer, 1, &sid, n, sb);
+  if (rc) return rc;
+  AppendArgs ap = base_append_args(ctx, layer, n);
+  ap.q = nullptr;
+  ap.k = k;
+  ap.v = v;
+  ap.in_bf16 = src_dtype == OOMATTN_DTYPE_BF16;
+  ap.rope_k = 0;  // K is stored as given: no rotation
+  DeviceGuard dg(ctx->device);
+  rope_append_kernel<<<n, 256, 0, ctx->stream>>>(ap, make_pool(ctx), sb);
+  CKLAUNCH();
+  commit_append(ctx, layer, sb, n);
+  return OOMATTN_OK;
+}
+
+int oomattn_kv_read(oomattn_ctx* ctx, int32_t layer, int32_t seq, void* k_out, void* v_out) {
+  if (!ctx || !k_out || !v_out) return fail(ctx, OOMATTN_ERR_INVALID_ARG, "bad kv_read arguments");
+  int rc = check_layer(ctx, layer);
+  if (!rc) rc = check_seq(ctx, seq);
+  if (rc) return rc;
+  DeviceGuard dg(ctx->device);
+  CK(cudaStreamSynchronize(ctx->stream));
+  const int L = ctx->h_len[(size_t)layer * ctx->cfg.max_seqs + seq];
+  const int n_kv = ctx->cfg.n_kv_heads;
+  const size_t es = ctx->esize;
+  std::vector<uint8_t> page(kPageSize * kHeadDim * es);
+  for (int lp = 0; lp * kPageSize < L; ++lp) {
+    const int pg = ctx->h_block_table[(size_t)seq * ctx->max_pages_per_seq + lp];
+    const int nt = std::min(kPageSize, L - lp * kPageSize);
+    for (int g = 0; g < n_kv; ++g) {
+      const size_t off = (((size_t)layer * ctx->n_pool_pages + pg) * n_kv + g) * kPageSize * kHeadDim * es;
+      for (int which = 0; which < 2; ++which) {
+        const uint8_t* src = (const uint8_t*)(which ? ctx->vpool : ctx->kpool) + off;
+        CK(cudaMemcpy(page.data(), src, page.size(), cudaMemcpyDeviceToHost));
+        uint8_t* dst = (uint8_t*)(which ? v_out : k_out) + ((size_t)g * L + (size_t)lp * kPageSize) * kHeadDim * es;
+        memcpy(dst, page.data(), (size_t)nt * kHeadDim * es);
+      }
+    }
+  }
+  return OOMATTN_OK;
+}
+
+int oomattn_rope_table(const oomattn_ctx* ctx, int32_t pos0, int32_t n, float* cos_out, float* sin_out) {
+  if (!ctx || !cos_out || !sin_out || n < 0 || pos0 < 0) return OOMATTN_ERR_INVALID_ARG;
+  if (pos0 + n > ctx->cfg.max_seq_len) return OOMATTN_ERR_OUT_OF_RANGE;
+  memcpy(cos_out, ctx->h_cos.data() + (size_t)pos0 * 64, (size_t)n * 64 * sizeof(float));
+  memcpy(sin_out, ctx->h_sin.data() + (size_t)pos0 * 64, (size_t)n * 64 * sizeof(float));
+  return OOMATTN_OK;
+}
+
+int oomattn_compute_rope_table(float theta, int32_t head_dim, int32_t pos0, int32_t n, float* cos_out,
+                               float* sin_out) {
+  if (!cos_out || !sin_out || n < 0 || pos0 < 0 || !(theta > 0.f)) return OOMATTN_ERR_INVALID_ARG;
+  if (head_dim != kHeadDim) return OOMATTN_ERR_BAD_CONFIG;
+  std::vector<float> c, s;
+  build_rope_table(theta, pos0 + n, c, s);
+  memcpy(cos_out, c.data() + (size_t)pos0 * 64, (size_t)n * 64 * sizeof(float));
+  memcpy(sin_out, s.data() + (size_t)pos0 * 64, (size_t)n * 64 * sizeof(float));
+  return OOMATTN_OK;
+}
+
+int oomattn_rope_append(oomattn_ctx* ctx, int32_t layer, int32_t n_seqs, const int32_t* seq_ids, int32_t n_new,
+                        const void* q, const void* k, const void* v, int32_t in_dtype, const float* bq,
+                        const float* bk, const float* bv, void* q_out, int32_t q_out_dtype) {
+  if (!ctx) return OOMATTN_ERR_INVALID_ARG;
+  if (!seq_ids || !q || !k || !v || !q_out || n_seqs <= 0 || n_new <= 0)
+    return fail(ctx, OOMATTN_ERR_INVALID_ARG, "bad rope_append arguments");
+  int rc = check_layer(ctx, layer);
+  if (!rc) rc = validate_dtype(ctx, in_dtype, "rope_append input");
+  if (!rc) rc = validate_dtype(ctx, q_out_dtype, "rope_append q_out");
+  if (rc) return rc;
+  DeviceGuard dg(ctx->device);
+  const int in_es = in_dtype == OOMATTN_DTYPE_BF16 ? 2 : 4, out_es = q_out_dtype == OOMATTN_DTYPE_BF16 ? 2 : 4;
+  for (int r0 = 0; r0 < n_seqs; r0 += kMaxBatch) {
+    const int n = std::min(kMaxBatch, n_seqs - r0);
+    SeqBatch sb;
+    rc = plan_append(ctx, layer, n, seq_ids + r0, n_new, sb);
+    if (rc) return rc;
+    const size_t t0 = (size_t)r0 * n_new;
+    AppendArgs ap = base_append_args(ctx, layer, n_new);
+    ap.q = (const uint8_t*)q + t0 * ctx->cfg.n_heads * kHeadDim * in_es;
+    ap.k = (const uint8_t*)k + t0 * ctx->cfg.n_kv_heads * kHeadDim * in_es;
+    ap.v = (const uint8_t*)v + t0 * ctx->cfg.n_kv_heads * kHeadDim * in_es;
+    ap.in_bf16 = in_dtype == OOMATTN_DTYPE_BF16;
+    ap.q_out = (uint8_t*)q_out + t0 * ctx->cfg.n_heads * kHeadDim * out_es;
+    ap.q_out_bf16 = q_out_dtype == OOMATTN_DTYPE_BF16;
+    ap.bq = bq;
+    ap.bk = bk;
+    ap.bv = bv;
+    rope_append_kernel<<<n * n_new, 256, 0, ctx->stream>>>(ap, make_pool(ctx), sb);
+    CKLAUNCH();
+    commit_append(ctx, layer, sb, n_new);
+  }
+  return OOMATTN_OK;
+}
+
+int oomattn_qkv_rope_append(oomattn_ctx* ctx, int32_t layer, int32_t n_seqs, const int32_t* seq_ids, int32_t n_new,
+                            const float* x, const void* wq, const void* wk, const void* wv, int32_t w_dtype,
+                            const float* bq, const float* bk, const float* bv, void* q_out, int32_t q_out_dtype) {
+  if (!ctx) return OOMATTN_ERR_INVALID_ARG;
+  if (!seq_ids || !x || !wq || !wk || !wv || !q_out || n_seqs <= 0 || n_new <= 0)
+    return fail(ctx, OOMATTN_ERR_INVALID_ARG, "bad qkv_rope_append arguments");
+  int rc = check_layer(ctx, layer);
+  if (!rc) rc = validate_dtype(ctx, w_dtype, "weights");
+  if (!rc) rc = validate_dtype(ctx, q_out_dtype, "q_out");
+  if (rc) return rc;
+  const int H = ctx->cfg.hidden_size;
+  if (H <= 0 || H % 8 != 0) return fail(ctx, OOMATTN_ERR_BAD_CONFIG, "hidden_size %d must be a positive multiple of 8", H);
+  DeviceGuard dg(ctx->device);
+  const long long T = (long long)n_seqs * n_new;
+  const int nq = ctx->cfg.n_heads * kHeadDim, nk = ctx->cfg.n_kv_heads * kHeadDim;
+  if (T <= kGemvMaxT) {
+    SeqBatch sb;
+    rc = plan_append(ctx, layer, n_seqs, seq_ids, n_new, sb);
+    if (rc) return rc;
+    GemvArgs ga;
+    ga.x = x;
+    ga.wq = wq;
+    ga.wk = wk;
+    ga.wv = wv;
+    ga.w_bf16 = w_dtype == OOMATTN_DTYPE_BF16;
+    ga.hidden = H;
+    ga.T = (int)T;
+    ga.ap = base_append_args(ctx, layer, n_new);
+    ga.ap.q_out = q_out;
+    ga.ap.q_out_bf16 = q_out_dtype == OOMATTN_DTYPE_BF16;
+    ga.ap.bq = bq;
+    ga.ap.bk = bk;
+    ga.ap.bv = bv;
+    const int grid = (ctx->cfg.n_heads + 2 * ctx->cfg.n_kv_heads) * 8;
+    KVPool pool = make_pool(ctx);
+#define OOMATTN_GEMV_CASE(TT)                                                                          \
+  case TT:                                                                                             \
+    if (ga.w_bf16)                                                                                     \
+      qkv_gemv_rope_append_kernel<TT, true><<<grid, 256, 0, ctx->stream>>>(ga, pool, sb);              \
+    else                                                                                               \
+      qkv_gemv_rope_append_kernel<TT, false><<<grid, 256, 0, ctx->stream>>>(ga, pool, sb);             \
+    break;
+    switch ((int)T) {
+      OOMATTN_GEMV_CASE(1)
+      OOMATTN_GEMV_CASE(2)
+      OOMATTN_GEMV_CASE(3)
+      OOMATTN_GEMV_CASE(4)
+      OOMATTN_GEMV_CASE(5)
+      OOMATTN_GEMV_CASE(6)
+      OOMATTN_GEMV_CASE(7)
+      OOMATTN_GEMV_CASE(8)
+      OOMATTN_GEMV_CASE(9)
+      OOMATTN_GEMV_CASE(10)
+      OOMATTN_GEMV_CASE(11)
+      OOMATTN_GEMV_CASE(12)
+      OOMATTN_GEMV_CASE(13)
+      OOMATTN_GEMV_CASE(14)
+      OOMATTN_GEMV_CASE(15)
+      OOMATTN_GEMV_CASE(16)
+    }
+#undef OOMATTN_GEMV_CASE
+    CKLAUNCH();
+    commit_append(ctx, layer, sb, n_new);
+    return OOMATTN_OK;
+  }
+  // Larger T: cuBLAS projections into scratch, then the K-A epilogue kernel.
+  const int wb = w_dtype == OOMATTN_DTYPE_BF16;
+  const size_t proj_bytes = (size_t)T * (nq + 2 * nk) * sizeof(float);
+  rc = ensure_scratch(ctx, proj_bytes + (wb ? (size_t)T * H * 2 : 0));
+  if (rc) return rc;
+  float* sq = ctx->d_scratch;
+  float* sk = sq + (size_t)T * nq;
+  float* sv = sk + (size_t)T * nk;
+  void* x16 = nullptr;
+  if (wb) {
+    x16 = (uint8_t*)ctx->d_scratch + proj_bytes;
+    f32_to_bf16_kernel<<<std::min<long long>(4096, (T * H + 255) / 256), 256, 0, ctx->stream>>>(
+        x, (uint16_t*)x16, (size_t)T * H);
+    CKLAUNCH();
+  }
+  if ((rc = gemm_xwT(ctx, x, wq, wb, sq, (int)T, nq, H, x16)) ||
+      (rc = gemm_xwT(ctx, x, wk, wb, sk, (int)T, nk, H, x16)) || (rc = gemm_xwT(ctx, x, wv, wb, sv, (int)T, nk, H, x16)))
+    return rc;
+  return oomattn_rope_append(ctx, layer, n_seqs, seq_ids, n_new, sq, sk, sv, OOMATTN_DTYPE_F32, bq, bk, bv, q_out,
+                             q_out_dtype);
+}
+
+int oomattn_decode(oomattn_ctx* ctx, int32_t layer, int32_t n_rows, const int32_t* seq_ids, const int32_t* lens,
+                   const float* q, float* out, float* lse) {
+  if (!ctx) return OOMATTN_ERR_INVALID_ARG;
+  if (!seq_ids || !q || !out || n_rows <= 0) return fail(ctx, OOMATTN_ERR_INVALID_ARG, "bad decode arguments");
+  int rc = check_layer(ctx, layer);
+  if (rc) return rc;
+  DeviceGuard dg(ctx->device);
+  const int hq = ctx->cfg.n_heads;
+  for (int r0 = 0; r0 < n_rows; r0 += kMaxBatch) {
+    const int n = std::min(kMaxBatch, n_rows - r0);
+    SeqBatch sb;
+    sb.n = n;
+    for (int z = 0; z < n; ++z) {
+      const int seq = seq_ids[r0 + z];
+      rc = check_seq(ctx, seq);
+      if (rc) return rc;
+      const int cur = ctx->h_len[(size_t)layer * ctx->cfg.max_seqs + seq];
+      const int len = lens ? lens[r0 + z] : cur;
+      if (len < 0 || len > cur)
+        return fail(ctx, OOMATTN_ERR_OUT_OF_RANGE, "row %d: length %d outside [0, %d]", r0 + z, len, cur);
+      sb.seq[z] = seq;
+      sb.len[z] = len;
+      sb.pos[z] = 0;
+    }
+    rc = launch_decode_rows(ctx, layer, sb, q + (size_t)r0 * hq * kHeadDim, out + (size_t)r0 * hq * kHeadDim,
+                            lse ? lse + (size_t)r0 * hq : nullptr);
+    if (rc) return rc;
+  }
+  return OOMATTN_OK;
+}
+
+int oomattn_merge_partials(oomattn_ctx* ctx, int32_t n_parts, int32_t n_rows, const float* parts, const float* lses,
+                           float* out, float* lse_out) {
+  if (!ctx) return OOMATTN_ERR_INVALID_ARG;
+  if (!parts || !lses || !out || n_parts <= 0 || n_rows < 0)
+    return fail(ctx, OOMATTN_ERR_INVALID_ARG, "bad merge arguments");
+  if (n_rows == 0) return OOMATTN_OK;
+  DeviceGuard dg(ctx->device);
+  merge_partials_kernel<<<n_rows, kHeadDim, 0, ctx->stream>>>(parts, lses, n_parts, n_rows, out, lse_out);
+  CKLAUNCH();
+  return OOMATTN_OK;
+}
+
+int oomattn_prefill(oomattn_ctx* ctx, int32_t layer, int32_t seq, int32_t n_new, const void* q, void* out,
+                    int32_t out_dtype, float* lse) {
+  if (!ctx) return OOMATTN_ERR_INVALID_ARG;
+  if (!q || !out || n_new <= 0) return fail(ctx, OOMATTN_ERR_INVALID_ARG, "bad prefill arguments");
+  int rc = check_layer(ctx, layer);
+  if (!rc) rc = check_seq(ctx, seq);
+  if (!rc) rc = validate_dtype(ctx, out_dtype, "prefill out");
+  if (rc) return rc;
+  if (ctx->cfg.kv_dtype != OOMATTN_DTYPE_BF16)
+    return fail(ctx, OOMATTN_ERR_UNSUPPORTED, "the tensor-core prefill needs a bf16 cache");
+  if (reinterpret_cast<uintptr_t>(q) % 16 != 0) return fail(ctx, OOMATTN_ERR_INVALID_ARG, "q must be 16-byte aligned");
+  const int L = ctx->h_len[(size_t)layer * ctx->cfg.max_seqs + seq];
+  if (n_new > L) return fail(ctx, OOMATTN_ERR_OUT_OF_RANGE, "n_new %d exceeds the cached length %d", n_new, L);
+  DeviceGuard dg(ctx->device);
+  CUtensorMap qmap;
+  rc = encode_q_map(ctx, q, n_new, &qmap);
+  if (rc) return rc;
+  PrefillArgs a;
+  a.out = out;
+  a.out_bf16 = out_dtype == OOMATTN_DTYPE_BF16;
+  a.lse = lse;
+  a.n_new = n_new;
+  a.prefix = L - n_new;
+  a.seq = seq;
+  a.layer = layer;
+  a.n_heads = ctx->cfg.n_heads;
+  a.group = ctx->group;
+  a.n_pairs = (n_new + 255) / 256;
+  a.qscale = ctx->scale * 1.4426950408889634f;
+  a.status = ctx->d_status;
+  a.timeout_ns = ctx->timeout_ns;
+  prefill_bf16_kernel<<<a.n_pairs * a.n_heads, kPfThreads, kPfSmemBytes, ctx->stream>>>(qmap, ctx->kmap, ctx->vmap,
+                                                                                        make_pool(ctx), a);
+  CKLAUNCH();
+  return OOMATTN_OK;
+}
+
+int oomattn_attention_forward_with_bias(oomattn_ctx* ctx, int32_t layer, int32_t batch, int32_t seq_len,
+                                        const float* x, const float* wq, const float* wk, const float* wv,
+                                        const float* wo, int32_t o_out, const float* bq, const float* bk,
+                                        const float* bv, float* out) {
+  if (!ctx) return OOMATTN_ERR_INVALID_ARG;
+  if (!x || !wq || !wk || !wv || !wo || !out || batch <= 0 || seq_len <= 0 || o_out <= 0)
+    return fail(ctx, OOMATTN_ERR_INVALID_ARG, "bad attention_forward_with_bias arguments");
+  if (batch > ctx->cfg.max_seqs)
+    return fail(ctx, OOMATTN_ERR_OUT_OF_RANGE, "batch %d exceeds max_seqs %d", batch, ctx->cfg.max_seqs);
+  int rc = check_layer(ctx, layer);
+  if (rc) return rc;
+  DeviceGuard dg(ctx->device);
+  const long long T = (long long)batch * seq_len;
+  const int hq = ctx->cfg.n_heads, qo = hq * kHeadDim;
+  const bool use_prefill = ctx->cfg.kv_dtype == OOMATTN_DTYPE_BF16 && seq_len > 16;
+  // scratch: q (f32) | attention out (f32) | q bf16 for the prefill path
+  const size_t q_bytes = (size_t)T * qo * sizeof(float);
+  const size_t need = 2 * q_bytes + (use_prefill ? (size_t)T * qo * 2 : 0);
+  // projection scratch is separate from the q/attention buffers; allocate both in one block
+  const size_t proj = T > kGemvMaxT ? (size_t)T * (qo + 2 * ctx->cfg.n_kv_heads * kHeadDim) * sizeof(float) : 0;
+  rc = ensure_scratch(ctx, need + proj + 256);
+  if (rc) return rc;
+  float* qbuf = (float*)((uint8_t*)ctx->d_scratch + proj);
+  float* abuf = (float*)((uint8_t*)qbuf + q_bytes);
+  void* qb16 = (uint8_t*)abuf + q_bytes;
+  std::vector<int32_t> seqs(batch);
+  for (int b = 0; b < batch; ++b) seqs[b] = b;
+  std::vector<int> plen(batch);
+  for (int b = 0; b < batch; ++b) plen[b] = ctx->h_len[(size_t)layer * ctx->cfg.max_seqs + b];
+  // K-A (the cuBLAS branch writes its projections at the start of the scratch block)
+  if (T <= kGemvMaxT) {
+    rc = oomattn_qkv_rope_append(ctx, layer, batch, seqs.data(), seq_len, x, wq, wk, wv, OOMATTN_DTYPE_F32, bq, bk,
+                                 bv, use_prefill ? qb16 : (void*)qbuf,
+                                 use_prefill ? OOMATTN_DTYPE_BF16 : OOMATTN_DTYPE_F32);
+  } else {
+    float* sq = ctx->d_scratch;
+    float* sk = sq + (size_t)T * qo;
+    float* sv = sk + (size_t)T * ctx->cfg.n_kv_heads * kHeadDim;
+    const int nk = ctx->cfg.n_kv_heads * kHeadDim;
+    const int H = ctx->cfg.hidden_size;
+    if ((rc = gemm_xwT(ctx, x, wq, 0, sq, (int)T, qo, H)) || (rc = gemm_xwT(ctx, x, wk, 0, sk, (int)T, nk, H)) ||
+        (rc = gemm_xwT(ctx, x, wv, 0, sv, (int)T, nk, H)))
+      return rc;
+    rc = oomattn_rope_append(ctx, layer, batch, seqs.data(), seq_len, sq, sk, sv, OOMATTN_DTYPE_F32, bq, bk, bv,
+                             use_prefill ? qb16 : (void*)qbuf, use_prefill ? OOMATTN_DTYPE_BF16 : OOMATTN_DTYPE_F32);
+  }
+  if (rc) return rc;
+  // attention
+  if (use_prefill) {
+    for (int b = 0; b < batch; ++b) {
+      rc = oomattn_prefill(ctx, layer, b, seq_len, (uint8_t*)qb16 + (size_t)b * seq_len * qo * 2,
+                           abuf + (size_t)b * seq_len * qo, OOMATTN_DTYPE_F32, nullptr);
+      if (rc) return rc;
+    }
+  } else {
+    // one decode row per new token: token s of sequence b sees slots 0..P_b+s
+    std::vector<int32_t> rs(T), rl(T);
+    for (int b = 0; b < batch; ++b)
+      for (int s = 0; s < seq_len; ++s) {
+        rs[(size_t)b * seq_len + s] = b;
+        rl[(size_t)b * seq_len + s] = plen[b] + s + 1;
+      }
+    rc = oomattn_decode(ctx, layer, (int)T, rs.data(), rl.data(), qbuf, abuf, nullptr);
+    if (rc) return rc;
+  }
+  // o_proj: out = attn . Wo^T   (src/oomllama_turbo.rs:715-720)
+  return gemm_xwT(ctx, abuf, wo, 0, out, (int)T, o_out, qo);
+}
+
+}  // extern "C"

@@ -1,0 +1,88 @@
+// Kernel-side argument structures shared by the host launcher and the kernels.
+#pragma once
+#include <stdint.h>
+
+namespace oomattn {
+
+constexpr int kHeadDim = 128;   // head_dim this library is built for (Qwen2.5 / Llama-3: 128)
+constexpr int kPageSize = 16;   // tokens per KV page
+constexpr int kMaxBatch = 128;  // sequence rows carried in one launch's parameters
+constexpr int kMaxGroup = 8;    // q heads per kv head handled by one decode CTA
+
+// Per-launch sequence rows, passed by value so a launch needs no host->device
+// metadata copy (and can be captured in a CUDA graph).
+//   seq[i]: context sequence slot (selects the block-table row)
+//   len[i]: cache slots visible to row i (decode) or the cache length before
+//           the append (append kernels)
+//   pos[i]: absolute RoPE position of the row's first new token (append)
+struct SeqBatch {
+  int n;
+  int seq[kMaxBatch];
+  int len[kMaxBatch];
+  int pos[kMaxBatch];
+};
+
+// Paged KV pool of all layers: element (layer, page, kv, slot, d) lives at
+// (((layer * n_pool_pages + page) * n_kv + kv) * kPageSize + slot) * kHeadDim + d.
+// Page n_pool_pages - 1 is the null page: zero, never written, and the
+// block-table entry of every unassigned logical page.
+struct KVPool {
+  void* k;
+  void* v;
+  const int* block_table;  // [max_seqs][max_pages_per_seq]
+  int max_pages_per_seq;
+  int n_pool_pages;        // including the null page
+  int n_kv;
+  int kv_bf16;
+};
+
+struct DecodeArgs {
+  const float* q;       // [rows][n_heads][128], rotated
+  float* out;           // [rows][n_heads][128]
+  float* lse;           // [rows][n_heads], natural log; may be null
+  int layer;
+  int n_heads;
+  int group;            // n_heads / n_kv
+  int pages_per_split;
+  int max_splits;
+  float qscale;         // softmax scale * log2(e)
+  float* part_o;        // [rows][n_heads][max_splits][128]
+  float* part_lse;      // [rows][n_heads][max_splits], base 2
+  unsigned* counters;   // [rows][n_kv], zero between launches
+  int* status;
+  unsigned long long timeout_ns;
+};
+
+struct AppendArgs {
+  const void* q;        // [T][n_heads][128]
+  const void* k;        // [T][n_kv][128]
+  const void* v;        // [T][n_kv][128]
+  int in_bf16;
+  void* q_out;          // [T][n_heads][128]
+  int q_out_bf16;
+  const float* bq;      // optional biases, added before RoPE
+  const float* bk;
+  const float* bv;
+  const float* cos_t;   // [max_pos][64]
+  const float* sin_t;
+  int max_pos;
+  int n_heads;
+  int n_new;            // tokens per row; token t belongs to row t / n_new
+  int layer;
+  int variant;          // 0 split-half, 1 interleaved
+  int rope_k;           // 0: store K as given (already rotated rows)
+  int* status;
+};
+
+struct GemvArgs {
+  const float* x;       // [T][hidden] f32
+  const void* wq;       // [n_heads*128][hidden]
+  const void* wk;       // [n_kv*128][hidden]
+  const void* wv;
+  int w_bf16;
+  int hidden;
+  int T;
+  AppendArgs ap;        // epilogue (q/k/v pointers unused)
+};
+
+}  // namespace oomattn

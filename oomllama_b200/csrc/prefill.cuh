@@ -1,0 +1,443 @@
+// K-C: causal GQA prefill on the 5th-generation tensor cores (tcgen05 + TMEM).
+//
+// Semantics: flash_attention_forward with causal=true (oomllama_turbo.rs:304-369)
+// for the n_new newest tokens of one sequence: query i (cache slot
+// P + i, P = cache length before the chunk) sees key slots 0..P+i, scale
+// 1/sqrt(128), GQA grouping h -> h / group.  Scores and softmax statistics are
+// f32; Q, K, V and P enter the tensor cores as bf16 (f32 accumulate).
+//
+// CTA work unit: one q head and 256 query rows held as two 128-row tiles
+// (Q0, Q1).  Warp roles (384 threads):
+//   warp 0      TMA producer: Q0/Q1 once, then K_j and V_j (128 keys each,
+//               gathered page by page from the paged pool) into a 2-stage ring
+//   warp 1      MMA issuer (one lane): S_i = Q_i K_j^T and O_i += P_i V_j
+//   warps 4-7   softmax of tile Q0, warps 8-11 softmax of tile Q1: one query
+//               row per thread, read from TMEM, online softmax with a lazily
+//               rescaled O (only when the running max grows by > 2^8), P
+//               written back into TMEM over the S columns as a bf16 hi/lo pair
+//               (P = P_hi + P_lo; two MMAs keep P's rounding ~2^-17), then the
+//               final O / l epilogue
+// The two softmax groups ping-pong: while one computes exponentials the tensor
+// core runs the other tile's MMAs.
+// TMEM (512 columns): S0 [0,128) S1 [128,256) O0 [256,384) O1 [384,512);
+// P_hi of tile i aliases columns [0,64) of S_i and P_lo columns [64,128)
+// (two bf16 per column).
+// Shared memory: Q0, Q1 (2 x 32 KB) + 2 stages x (K 32 KB + V 32 KB), all
+// 128-byte swizzled; each operand is two 64-column halves of [128 rows][128 B].
+#pragma once
+#include "common.cuh"
+#include "params.cuh"
+
+namespace oomattn {
+
+constexpr int kPfThreads = 384;
+constexpr int kPfStages = 2;
+constexpr int kTileBytes = 128 * kHeadDim * 2;    // 32 KB: one 128 x 128 bf16 operand tile
+constexpr int kHalfTileBytes = kTileBytes / 2;    // one 64-column half
+constexpr int kPfSmemBytes = 2 * kTileBytes + kPfStages * 2 * kTileBytes + 1024 + 256;
+constexpr float kRescaleThreshold = 8.0f;         // log2 units: rescale O only when the max grows by > 256x
+
+struct PrefillArgs {
+  void* out;           // [n_new][n_heads][128]
+  int out_bf16;
+  float* lse;          // [n_new][n_heads] natural log, or null
+  int n_new;
+  int prefix;          // P: cache slots before the chunk
+  int seq;
+  int layer;
+  int n_heads;
+  int group;
+  int n_pairs;         // ceil(n_new / 256)
+  float qscale;        // softmax scale * log2(e)
+  int* status;
+  unsigned long long timeout_ns;
+};
+
+// ------------------------------------------------------------ tcgen05 PTX
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+// D[tmem] (+)= A[smem desc] * B[smem desc]
+__device__ __forceinline__ void mma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                       uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// D[tmem] (+)= A[tmem] * B[smem desc]
+__device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                       uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+#define OOMATTN_TMEM_LD32(taddr, r)                                                                               \
+  asm volatile(                                                                                                   \
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18," \
+      "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"                                              \
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),            \
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),      \
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),    \
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])     \
+      : "r"(taddr))
+
+#define OOMATTN_TMEM_ST32(taddr, r)                                                                                \
+  asm volatile(                                                                                                    \
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17," \
+      "%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),                                \
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),           \
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]),   \
+      "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]),  \
+      "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])                                                   \
+      : "memory")
+
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// Shared-memory matrix descriptor (sm_100 format): start address, leading /
+// stride byte offsets (16-byte units), version 1, layout type 2 = 128B swizzle.
+__device__ __forceinline__ uint64_t make_sdesc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1 << 46;   // descriptor version for sm_100
+  d |= (uint64_t)2 << 61;   // SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor, kind::f16: f32 accumulate, bf16 A and B, M = 128,
+// N = 128; b_mn_major selects an N-contiguous B operand (V in P.V).
+__host__ __device__ constexpr uint32_t make_idesc_bf16(bool b_mn_major) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((b_mn_major ? 1u : 0u) << 16) | ((128u >> 3) << 17) |
+         ((128u >> 4) << 24);
+}
+
+// ------------------------------------------------------------ the kernel
+__global__ void __launch_bounds__(kPfThreads, 1)
+    prefill_bf16_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
+                        const __grid_constant__ CUtensorMap vmap, const KVPool pool, const PrefillArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;                                // [2 tiles][2 halves][128][128 B]
+  uint8_t* sK = smem + 2 * kTileBytes;               // [stage][2 halves][128][128 B]
+  uint8_t* sV = sK + kPfStages * kTileBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + kPfStages * kTileBytes);
+  uint64_t* q_full = bars + 0;
+  uint64_t* k_full = bars + 1;                       // [kPfStages]
+  uint64_t* v_full = k_full + kPfStages;             // [kPfStages]
+  uint64_t* kv_empty = v_full + kPfStages;           // [kPfStages]
+  uint64_t* s_full = kv_empty + kPfStages;           // [2]
+  uint64_t* p_full = s_full + 2;                     // [2]
+  uint64_t* o_full = p_full + 2;                     // [2]
+  uint64_t* mma_done = o_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // heaviest work first: block b -> pair (n_pairs - 1 - b / n_heads), head b % n_heads
+  const int h = blockIdx.x % a.n_heads;
+  const int pair = a.n_pairs - 1 - (int)(blockIdx.x / a.n_heads);
+  const int g = h / a.group;
+  const int q0 = pair * 256;
+  int rows_valid[2], ntile[2];
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    rows_valid[i] = max(0, min(128, a.n_new - (q0 + 128 * i)));
+    // KV tiles needed by the last valid row (slot P + q0 + 128 i + rows - 1)
+    ntile[i] = rows_valid[i] > 0 ? (a.prefix + q0 + 128 * i + rows_valid[i] + 127) / 128 : 0;
+  }
+  const int n_kv_tiles = max(ntile[0], ntile[1]);
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < kPfStages; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&v_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 128);
+      mbar_init(&o_full[i], 1);
+    }
+    mbar_init(mma_done, 1);
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------ TMA producer
+    if (lane == 0) {
+      prefetch_tensormap(&qmap);
+      prefetch_tensormap(&kmap);
+      prefetch_tensormap(&vmap);
+      mbar_arrive_expect_tx(q_full, 2 * kTileBytes);
+      for (int i = 0; i < 2; ++i)
+        for (int c = 0; c < 2; ++c)
+          tma_load_3d(sQ + i * kTileBytes + c * kHalfTileBytes, &qmap, q_full, c * 64, h, q0 + 128 * i);
+      const int* bt = pool.block_table + (size_t)a.seq * pool.max_pages_per_seq;
+      const int null_page = pool.n_pool_pages - 1;
+      bool ok = true;
+      for (int j = 0; j < n_kv_tiles && ok; ++j) {
+        const int s = j % kPfStages;
+        if (j >= kPfStages) ok = mbar_wait(&kv_empty[s], ((j / kPfStages) - 1) & 1, a.status, a.timeout_ns);
+        if (!ok) break;
+        mbar_arrive_expect_tx(&k_full[s], kTileBytes);
+        mbar_arrive_expect_tx(&v_full[s], kTileBytes);
+        for (int p = 0; p < 8; ++p) {
+          const int lp = j * 8 + p;
+          int page = lp < pool.max_pages_per_seq ? __ldg(bt + lp) : null_page;
+          if ((unsigned)page >= (unsigned)pool.n_pool_pages) {
+            report_error(a.status, kDevErrBounds);
+            page = null_page;
+          }
+          const int row = ((a.layer * pool.n_pool_pages + page) * pool.n_kv + g) * kPageSize;
+          uint8_t* kd = sK + s * kTileBytes + p * 2048;
+          uint8_t* vd = sV + s * kTileBytes + p * 2048;
+          tma_load_2d(kd, &kmap, &k_full[s], 0, row);
+          tma_load_2d(kd + kHalfTileBytes, &kmap, &k_full[s], 64, row);
+          tma_load_2d(vd, &vmap, &v_full[s], 0, row);
+          tma_load_2d(vd + kHalfTileBytes, &vmap, &v_full[s], 64, row);
+        }
+      }
+      // drain: the last loads this lane issued land before the CTA can exit
+      for (int j = max(0, n_kv_tiles - kPfStages); j < n_kv_tiles; ++j) {
+        const int s = j % kPfStages;
+        mbar_wait(&k_full[s], (j / kPfStages) & 1, a.status, a.timeout_ns);
+        mbar_wait(&v_full[s], (j / kPfStages) & 1, a.status, a.timeout_ns);
+      }
+      mbar_wait(q_full, 0, a.status, a.timeout_ns);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc_qk = make_idesc_bf16(false);
+      constexpr uint32_t idesc_pv = make_idesc_bf16(true);
+      bool ok = mbar_wait(q_full, 0, a.status, a.timeout_ns);
+      tc_fence_after();
+      const uint32_t q_addr = smem_u32(sQ), k_addr = smem_u32(sK), v_addr = smem_u32(sV);
+      // S_i(j) = Q_i K_j^T : 8 k-steps of 16 dims; halves at +16 KB, steps +32 B inside a half
+      auto issue_s = [&](int i, int j) {
+        const int s = j % kPfStages;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t off = (kk >> 2) * kHalfTileBytes + (kk & 3) * 32;
+          const uint64_t ad = make_sdesc(q_addr + i * kTileBytes + off, 16, 1024);
+          const uint64_t bd = make_sdesc(k_addr + s * kTileBytes + off, 16, 1024);
+          mma_ss((tmem + i * 128), ad, bd, idesc_qk, kk > 0 ? 1u : 0u);
+        }
+      };
+      // O_i (+)= (P_hi + P_lo)_i V_j : 8 k-steps of 16 keys; P_hi / P_lo from TMEM
+      // (8 columns per step, P_lo 64 columns after P_hi); V N-major: LBO = 16 KB
+      // between 64-dim halves, SBO = 1 KB between 8-key groups
+      auto issue_pv = [&](int i, int j) {
+        const int s = j % kPfStages;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint64_t bd = make_sdesc(v_addr + s * kTileBytes + kk * 2048, kHalfTileBytes, 1024);
+          mma_ts((tmem + 256 + i * 128), (tmem + i * 128) + kk * 8, bd, idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
+          mma_ts((tmem + 256 + i * 128), (tmem + i * 128) + 64 + kk * 8, bd, idesc_pv, 1u);
+        }
+      };
+      int k_waited = -1, v_waited = -1;
+      auto wait_k = [&](int j) {
+        if (ok && j > k_waited) {
+          ok = mbar_wait(&k_full[j % kPfStages], (j / kPfStages) & 1, a.status, a.timeout_ns);
+          tc_fence_after();
+          k_waited = j;
+        }
+      };
+      auto wait_v = [&](int j) {
+        if (ok && j > v_waited) {
+          ok = mbar_wait(&v_full[j % kPfStages], (j / kPfStages) & 1, a.status, a.timeout_ns);
+          tc_fence_after();
+          v_waited = j;
+        }
+      };
+      if (ok && n_kv_tiles > 0) {
+        wait_k(0);
+        for (int i = 0; i < 2 && ok; ++i)
+          if ((i ? ntile[1] : ntile[0]) > 0) {
+            issue_s(i, 0);
+            tc_commit(&s_full[i]);
+          }
+      }
+      for (int j = 0; j < n_kv_tiles && ok; ++j) {
+        for (int i = 0; i < 2 && ok; ++i) {
+          if (j >= (i ? ntile[1] : ntile[0])) continue;
+          ok = mbar_wait(&p_full[i], j & 1, a.status, a.timeout_ns);
+          if (!ok) break;
+          tc_fence_after();
+          wait_v(j);
+          if (!ok) break;
+          issue_pv(i, j);
+          if (j + 1 < (i ? ntile[1] : ntile[0])) {
+            wait_k(j + 1);
+            if (!ok) break;
+            issue_s(i, j + 1);
+            tc_commit(&s_full[i]);
+          } else {
+            tc_commit(&o_full[i]);
+          }
+        }
+        tc_commit(&kv_empty[j % kPfStages]);
+      }
+      // every MMA this lane issued has completed before TMEM can be released
+      tc_commit(mma_done);
+      mbar_wait(mma_done, 0, a.status, a.timeout_ns);
+    }
+  } else if (warp >= 4) {
+    // ------------------------------------------------ softmax / epilogue
+    const int i = (warp - 4) >> 2;           // q tile
+    const int quarter = warp & 3;            // TMEM lane quarter of this warp
+    const int r = quarter * 32 + lane;       // row within the tile
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const int row_in_chunk = q0 + 128 * i + r;
+    const int qslot = a.prefix + row_in_chunk;  // absolute cache slot of this query
+    float m_used = -INFINITY, l = 0.f;
+    bool ok = true;
+    const float cl = a.qscale;
+    for (int j = 0; j < (i ? ntile[1] : ntile[0]) && ok; ++j) {
+      ok = mbar_wait(&s_full[i], j & 1, a.status, a.timeout_ns);
+      if (!ok) break;
+      tc_fence_after();
+      uint32_t sr[128];
+      OOMATTN_TMEM_LD32((tmem + i * 128) + lane_off + 0, (sr + 0));
+      OOMATTN_TMEM_LD32((tmem + i * 128) + lane_off + 32, (sr + 32));
+      OOMATTN_TMEM_LD32((tmem + i * 128) + lane_off + 64, (sr + 64));
+      OOMATTN_TMEM_LD32((tmem + i * 128) + lane_off + 96, (sr + 96));
+      tmem_wait_ld();
+      const int lim = qslot - j * 128;  // columns c <= lim are visible
+      if (__any_sync(0xffffffffu, lim < 127)) {
+#pragma unroll
+        for (int c = 0; c < 128; ++c)
+          if (c > lim) sr[c] = __float_as_uint(-INFINITY);
+      }
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 128; ++c) mx = fmaxf(mx, __uint_as_float(sr[c]));
+      const float mxs = mx * cl;
+      bool need = false;
+      float alpha = 1.f;
+      if (j == 0) {
+        m_used = mxs;
+      } else if (mxs > m_used + kRescaleThreshold) {
+        need = true;
+        alpha = exp2f(m_used - mxs);
+        m_used = mxs;
+        l *= alpha;
+      }
+      // P = P_hi + P_lo, both bf16: P_hi into S columns [0,64), P_lo into [64,128)
+      // (the scores there are already in registers).  Two bf16 MMAs then carry P
+      // to ~16 significant bits, so P's rounding stays far below the bf16-KV
+      // tolerance.  P_hi is packed in place (step c reads sr[2c], sr[2c+1],
+      // writes sr[c], c <= 2c); P_lo goes to its own array, so the live set
+      // stays near 130 registers.
+      float lsum = 0.f;
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        uint32_t plo[32];
+#pragma unroll
+        for (int cc = 0; cc < 32; ++cc) {
+          const int c = half * 32 + cc;
+          const float p0 = exp2f(fmaf(__uint_as_float(sr[2 * c]), cl, -m_used));
+          const float p1 = exp2f(fmaf(__uint_as_float(sr[2 * c + 1]), cl, -m_used));
+          uint32_t hi, lo;
+          split_bf16x2(p0, p1, hi, lo);
+          lsum += p0 + p1;
+          sr[c] = hi;
+          plo[cc] = lo;
+        }
+        OOMATTN_TMEM_ST32((tmem + i * 128) + lane_off + half * 32, (sr + half * 32));
+        OOMATTN_TMEM_ST32((tmem + i * 128) + lane_off + 64 + half * 32, plo);
+      }
+      l += lsum;
+      if (__any_sync(0xffffffffu, need)) {
+#pragma unroll
+        for (int ch = 0; ch < 4; ++ch) {
+          uint32_t orr[32];
+          OOMATTN_TMEM_LD32((tmem + 256 + i * 128) + lane_off + ch * 32, orr);
+          tmem_wait_ld();
+#pragma unroll
+          for (int c = 0; c < 32; ++c) orr[c] = __float_as_uint(__uint_as_float(orr[c]) * alpha);
+          OOMATTN_TMEM_ST32((tmem + 256 + i * 128) + lane_off + ch * 32, orr);
+        }
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(&p_full[i]);
+    }
+    if (ok && (i ? ntile[1] : ntile[0]) > 0) {
+      ok = mbar_wait(&o_full[i], 0, a.status, a.timeout_ns);
+      tc_fence_after();
+      if (ok) {
+        const bool valid = r < (i ? rows_valid[1] : rows_valid[0]);
+        const float inv = 1.f / l;
+        const size_t orow = ((size_t)row_in_chunk * a.n_heads + h) * kHeadDim;
+#pragma unroll
+        for (int ch = 0; ch < 4; ++ch) {
+          uint32_t orr[32];
+          OOMATTN_TMEM_LD32((tmem + 256 + i * 128) + lane_off + ch * 32, orr);
+          tmem_wait_ld();
+          if (valid) {
+            if (a.out_bf16) {
+              uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(a.out) + orow + ch * 32);
+#pragma unroll
+              for (int v = 0; v < 4; ++v) {
+                uint4 w;
+                w.x = pack_bf16(__uint_as_float(orr[8 * v + 0]) * inv, __uint_as_float(orr[8 * v + 1]) * inv);
+                w.y = pack_bf16(__uint_as_float(orr[8 * v + 2]) * inv, __uint_as_float(orr[8 * v + 3]) * inv);
+                w.z = pack_bf16(__uint_as_float(orr[8 * v + 4]) * inv, __uint_as_float(orr[8 * v + 5]) * inv);
+                w.w = pack_bf16(__uint_as_float(orr[8 * v + 6]) * inv, __uint_as_float(orr[8 * v + 7]) * inv);
+                dst[v] = w;
+              }
+            } else {
+              float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(a.out) + orow + ch * 32);
+#pragma unroll
+              for (int v = 0; v < 8; ++v)
+                dst[v] = make_float4(__uint_as_float(orr[4 * v + 0]) * inv, __uint_as_float(orr[4 * v + 1]) * inv,
+                                     __uint_as_float(orr[4 * v + 2]) * inv, __uint_as_float(orr[4 * v + 3]) * inv);
+            }
+          }
+        }
+        if (valid && a.lse) a.lse[(size_t)row_in_chunk * a.n_heads + h] = (m_used + log2f(l)) * 0.69314718055994531f;
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+}  // namespace oomattn

@@ -1,0 +1,206 @@
+// K-A: bias + RoPE + paged KV append, standalone (epilogue-only, for
+// projections computed elsewhere) and fused behind a QKV GEMV for decode-sized
+// token counts.
+//
+// Reference semantics (oomllama_turbo.rs:638-681): q = x Wq^T + bq, k = x Wk^T
+// + bk, v = x Wv^T + bv (bias added after the product, :648-656), then RoPE on
+// q and k at position pos(token) and LayerKVCache::append of k, v (:41-55).
+// RoPE pairs (x0, x1) are (x[i], x[i+64]) for the split-half variant
+// (apply_rope_llama :443-467 and TurboEngine::apply_rope :773-783) or
+// (x[2i], x[2i+1]) for the interleaved one (apply_rope :402-438):
+//   x0' = x0*cos - x1*sin ; x1' = x0*sin + x1*cos
+// with every product and sum separately rounded (__fmul_rn/__fadd_rn keep
+// nvcc from contracting them into FMAs), using the host-built f32 cos/sin
+// table, so rotated values are bit-identical to the f32 reference arithmetic.
+// K/V stored in a bf16 cache and q written as bf16 are rounded to nearest even.
+#pragma once
+#include "common.cuh"
+#include "params.cuh"
+
+namespace oomattn {
+
+__device__ __forceinline__ void rope_pair(float x0, float x1, float c, float s, float& y0, float& y1) {
+  const float a = __fmul_rn(x0, c), b = __fmul_rn(x1, s);
+  const float e = __fmul_rn(x0, s), f = __fmul_rn(x1, c);
+  y0 = __fsub_rn(a, b);
+  y1 = __fadd_rn(e, f);
+}
+
+__device__ __forceinline__ float load_elem(const void* p, size_t i, int bf16) {
+  return bf16 ? bf16_bits_to_f32(reinterpret_cast<const uint16_t*>(p)[i]) : reinterpret_cast<const float*>(p)[i];
+}
+
+__device__ __forceinline__ void store_elem(void* p, size_t i, float x, int bf16) {
+  if (bf16)
+    reinterpret_cast<uint16_t*>(p)[i] = f32_to_bf16_bits(x);
+  else
+    reinterpret_cast<float*>(p)[i] = x;
+}
+
+// Element offset of (layer, slot, kv head g, dim 0) in the pool, resolving the
+// slot through the block table.  Returns false when the page is out of range.
+__device__ __forceinline__ bool cache_offset(const KVPool& pool, int layer, int seq, int slot, int g, size_t& off) {
+  const int lp = slot / kPageSize;
+  if ((unsigned)lp >= (unsigned)pool.max_pages_per_seq) return false;
+  const int page = pool.block_table[(size_t)seq * pool.max_pages_per_seq + lp];
+  if ((unsigned)page >= (unsigned)(pool.n_pool_pages - 1)) return false;  // the null page is never written
+  off = (((size_t)(layer * pool.n_pool_pages + page) * pool.n_kv + g) * kPageSize + (slot % kPageSize)) * kHeadDim;
+  return true;
+}
+
+// Rotate / store one (q or k) pair or copy one v pair of token t.
+// item < n_heads*64: q pairs; < (n_heads+n_kv)*64: k pairs; else v pairs.
+// vals: the un-rotated (biased) pair values.
+__device__ __forceinline__ void emit_pair(const AppendArgs& ap, const KVPool& pool, const SeqBatch& sb, int t,
+                                          int item, float x0, float x1) {
+  const int nq = ap.n_heads * 64, nk = pool.n_kv * 64;
+  const int row = t / ap.n_new, s = t % ap.n_new;
+  const int pos = sb.pos[row] + s;
+  const int sec = item < nq ? 0 : (item < nq + nk ? 1 : 2);
+  const int local = sec == 0 ? item : (sec == 1 ? item - nq : item - nq - nk);
+  const int head = local / 64, i = local % 64;
+  const int i0 = (ap.variant == 1 || sec == 2) ? 2 * i : i;
+  const int i1 = (ap.variant == 1 || sec == 2) ? 2 * i + 1 : i + 64;
+  float y0 = x0, y1 = x1;
+  if (sec == 0 || (sec == 1 && ap.rope_k)) {
+    if ((unsigned)pos >= (unsigned)ap.max_pos) {
+      report_error(ap.status, kDevErrBounds);
+      return;
+    }
+    rope_pair(x0, x1, ap.cos_t[(size_t)pos * 64 + i], ap.sin_t[(size_t)pos * 64 + i], y0, y1);
+  }
+  if (sec == 0) {
+    const size_t o = ((size_t)t * ap.n_heads + head) * kHeadDim;
+    store_elem(ap.q_out, o + i0, y0, ap.q_out_bf16);
+    store_elem(ap.q_out, o + i1, y1, ap.q_out_bf16);
+  } else {
+    size_t off;
+    if (!cache_offset(pool, ap.layer, sb.seq[row], sb.len[row] + s, head, off)) {
+      report_error(ap.status, kDevErrBounds);
+      return;
+    }
+    void* dst = sec == 1 ? pool.k : pool.v;
+    store_elem(dst, off + i0, y0, pool.kv_bf16);
+    store_elem(dst, off + i1, y1, pool.kv_bf16);
+  }
+}
+
+// Epilogue-only K-A.  grid.x = T tokens, block = 256 threads.
+__global__ void __launch_bounds__(256)
+    rope_append_kernel(const AppendArgs ap, const KVPool pool, const __grid_constant__ SeqBatch sb) {
+  const int t = blockIdx.x;
+  const int nq = ap.n_heads * 64, nk = pool.n_kv * 64;
+  const int total = nq + 2 * nk;
+  const int first = ap.q ? 0 : nq;  // no q: K/V rows only
+  for (int item = first + threadIdx.x; item < total; item += blockDim.x) {
+    const int sec = item < nq ? 0 : (item < nq + nk ? 1 : 2);
+    const int local = sec == 0 ? item : (sec == 1 ? item - nq : item - nq - nk);
+    const int head = local / 64, i = local % 64;
+    const int i0 = (ap.variant == 1 || sec == 2) ? 2 * i : i;
+    const int i1 = (ap.variant == 1 || sec == 2) ? 2 * i + 1 : i + 64;
+    const void* src = sec == 0 ? ap.q : (sec == 1 ? ap.k : ap.v);
+    const int nh = sec == 0 ? ap.n_heads : pool.n_kv;
+    const size_t base = ((size_t)t * nh + head) * kHeadDim;
+    float x0 = load_elem(src, base + i0, ap.in_bf16);
+    float x1 = load_elem(src, base + i1, ap.in_bf16);
+    const float* b = sec == 0 ? ap.bq : (sec == 1 ? ap.bk : ap.bv);
+    if (b) {
+      x0 = __fadd_rn(x0, b[head * kHeadDim + i0]);
+      x1 = __fadd_rn(x1, b[head * kHeadDim + i1]);
+    }
+    emit_pair(ap, pool, sb, t, item, x0, x1);
+  }
+}
+
+// Fused QKV GEMV + bias + RoPE + append for T <= kGemvMaxT tokens.
+// One CTA owns 16 output rows that are closed under the RoPE pairing (for the
+// split-half variant rows c*8..c*8+7 and 64+c*8.. of one head; otherwise 16
+// adjacent rows), so the rotation completes inside the CTA.  8 warps x 2 rows;
+// each warp streams its weight rows with 128-bit loads (HBM-bound on W).
+constexpr int kGemvMaxT = 16;
+
+// x (f32) -> bf16 (RNE) for the cuBLAS projection of bf16 weights, whose
+// GEMM takes both operands in one type.
+__global__ void f32_to_bf16_kernel(const float* __restrict__ x, uint16_t* __restrict__ y, size_t n) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+    y[i] = f32_to_bf16_bits(x[i]);
+}
+
+template <int T, bool WBF16>
+__global__ void __launch_bounds__(256)
+    qkv_gemv_rope_append_kernel(const GemvArgs ga, const KVPool pool, const __grid_constant__ SeqBatch sb) {
+  __shared__ float y[16][T];
+  const AppendArgs& ap = ga.ap;
+  const int grp = blockIdx.x;
+  const int nq_grp = ap.n_heads * 8, nk_grp = pool.n_kv * 8;
+  const int sec = grp < nq_grp ? 0 : (grp < nq_grp + nk_grp ? 1 : 2);
+  const int lg = sec == 0 ? grp : (sec == 1 ? grp - nq_grp : grp - nq_grp - nk_grp);
+  const int head = lg / 8, c = lg % 8;
+  const bool split_half = (ap.variant == 0) && sec < 2;
+  const void* W = sec == 0 ? ga.wq : (sec == 1 ? ga.wk : ga.wv);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int H = ga.hidden;
+
+  for (int rr = 0; rr < 2; ++rr) {
+    const int r = warp * 2 + rr;  // 0..15
+    const int drow = split_half ? (r < 8 ? c * 8 + r : 64 + c * 8 + (r - 8)) : c * 16 + r;
+    const size_t wrow = (size_t)(head * kHeadDim + drow) * H;
+    float acc[T];
+#pragma unroll
+    for (int t = 0; t < T; ++t) acc[t] = 0.f;
+    if (WBF16) {
+      const uint16_t* wp = reinterpret_cast<const uint16_t*>(W) + wrow;
+      for (int j = lane * 8; j < H; j += 256) {
+        const uint4 wv = __ldcs(reinterpret_cast<const uint4*>(wp + j));
+        const float w[8] = {bf16_lo_f32(wv.x), bf16_hi_f32(wv.x), bf16_lo_f32(wv.y), bf16_hi_f32(wv.y),
+                            bf16_lo_f32(wv.z), bf16_hi_f32(wv.z), bf16_lo_f32(wv.w), bf16_hi_f32(wv.w)};
+#pragma unroll
+        for (int t = 0; t < T; ++t) {
+          const float4 x0 = __ldg(reinterpret_cast<const float4*>(ga.x + (size_t)t * H + j));
+          const float4 x1 = __ldg(reinterpret_cast<const float4*>(ga.x + (size_t)t * H + j + 4));
+          acc[t] += x0.x * w[0] + x0.y * w[1] + x0.z * w[2] + x0.w * w[3] + x1.x * w[4] + x1.y * w[5] +
+                    x1.z * w[6] + x1.w * w[7];
+        }
+      }
+    } else {
+      const float* wp = reinterpret_cast<const float*>(W) + wrow;
+#pragma unroll 4
+      for (int j = lane * 4; j < H; j += 128) {
+        const float4 w = __ldcs(reinterpret_cast<const float4*>(wp + j));
+#pragma unroll
+        for (int t = 0; t < T; ++t) {
+          const float4 x = __ldg(reinterpret_cast<const float4*>(ga.x + (size_t)t * H + j));
+          acc[t] += x.x * w.x + x.y * w.y + x.z * w.z + x.w * w.w;
+        }
+      }
+    }
+#pragma unroll
+    for (int t = 0; t < T; ++t) {
+      float v = acc[t];
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+      if (lane == 0) y[r][t] = v;
+    }
+  }
+  __syncthreads();
+  // epilogue: 8 pairs x T tokens
+  for (int idx = threadIdx.x; idx < 8 * ga.T; idx += blockDim.x) {
+    const int pr = idx % 8, t = idx / 8;
+    // pair pr = rows (pr, pr+8) for split-half; (2pr, 2pr+1) otherwise
+    const int r0 = split_half ? pr : 2 * pr, r1 = split_half ? pr + 8 : 2 * pr + 1;
+    const int d0 = split_half ? c * 8 + pr : c * 16 + 2 * pr;
+    const int d1 = split_half ? 64 + c * 8 + pr : d0 + 1;
+    float x0 = y[r0][t], x1 = y[r1][t];
+    const float* b = sec == 0 ? ap.bq : (sec == 1 ? ap.bk : ap.bv);
+    if (b) {
+      x0 = __fadd_rn(x0, b[head * kHeadDim + d0]);
+      x1 = __fadd_rn(x1, b[head * kHeadDim + d1]);
+    }
+    // pair index in emit_pair's numbering: split-half pair i = d0; interleaved i = d0 / 2
+    const int i = split_half ? d0 : d0 / 2;
+    const int item = (sec == 0 ? 0 : (sec == 1 ? ap.n_heads * 64 : (ap.n_heads + pool.n_kv) * 64)) + head * 64 + i;
+    emit_pair(ap, pool, sb, t, item, x0, x1);
+  }
+}
+
+}  // namespace oomattn

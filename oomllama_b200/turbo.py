@@ -1,0 +1,334 @@
+"""TurboEngine-compatible host interface over the oomattn C ABI.
+
+Mirrors the reference's public turbo API (src/oomllama_turbo.rs, re-exported
+at src/lib.rs:99): ``TurboConfig`` (:474-516), ``TurboEngine.new`` (:528),
+``attention_forward_with_bias`` (:618-723), ``reset`` (:726), ``seq_len``
+(:731) and the per-layer cache view of ``LayerKVCache`` / ``ModelKVCache``
+(:26-104).  Tensors are torch CUDA tensors used only as device buffers; every
+computation runs in liboomattn.so on the caller's current CUDA stream.
+
+Differences from the reference, all deliberate and matching its intended
+semantics:
+  * RoPE positions come from each layer's own cache length (the reference
+    reads layer 0's, :671 with :101-103), and positions are checked against
+    max_seq_len (the reference never enforces it, :74-85);
+  * GQA uses the KV length (the reference reshapes with q's length, :324);
+  * the causal mask is aligned to the end of the cache, so chunked prefill on
+    a non-empty cache works (the reference's mask assumes q_len == kv_len);
+  * the RoPE variant and theta are configuration, not hard-coded (:746).
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass, field
+
+import torch
+
+from . import _lib
+from ._lib import DTYPE_BF16, DTYPE_F32, ROPE_INTERLEAVED, ROPE_SPLIT_HALF, check, int_array
+
+PAGE_SIZE = 16
+HEAD_DIM = 128
+
+_DT = {torch.float32: DTYPE_F32, torch.bfloat16: DTYPE_BF16}
+
+
+def _dtype_code(t: torch.Tensor) -> int:
+    if t.dtype not in _DT:
+        raise TypeError(f"unsupported dtype {t.dtype}; expected float32 or bfloat16")
+    return _DT[t.dtype]
+
+
+def _ptr(t):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _dev(t: torch.Tensor, name: str, device: int, dtype=None, numel=None):
+    if not isinstance(t, torch.Tensor) or not t.is_cuda:
+        raise TypeError(f"{name} must be a CUDA tensor")
+    if t.device.index != device:
+        raise ValueError(f"{name} is on cuda:{t.device.index}, the engine on cuda:{device}")
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+    if dtype is not None and t.dtype != dtype:
+        raise TypeError(f"{name} must be {dtype}, got {t.dtype}")
+    if numel is not None and t.numel() != numel:
+        raise ValueError(f"{name} has {t.numel()} elements, expected {numel}")
+    return t
+
+
+@dataclass
+class TurboConfig:
+    """TurboConfig (src/oomllama_turbo.rs:474-497) plus the settings the
+    reference hard-codes (theta at :746) or does not have (paging, cache
+    dtype, RoPE variant).  The layer-pinning / prefetch fields are kept for
+    signature parity; weights are the caller's device tensors here."""
+
+    n_layers: int
+    hidden_size: int
+    n_heads: int
+    n_kv_heads: int
+    head_dim: int = HEAD_DIM
+    max_seq_len: int = 8192
+    vram_budget_gb: float = 0.0
+    pin_strategy: object = None
+    prefetch_lookahead: int = 0
+    use_flash_attention: bool = True
+    use_fp16: bool = False
+    # new settings
+    max_seqs: int = 1
+    n_pages: int | None = None          # default: every sequence can reach max_seq_len
+    kv_dtype: str = "f32"               # "f32" or "bf16"
+    rope_variant: str = "interleaved"   # "interleaved" (apply_rope) or "split_half" (apply_rope_llama)
+    rope_theta: float = 1e6
+    softmax_scale: float | None = None  # None: 1/sqrt(head_dim)
+
+    @staticmethod
+    def qwen32b_dual3060() -> "TurboConfig":
+        """The reference's preset (src/oomllama_turbo.rs:500-515)."""
+        return TurboConfig(n_layers=64, hidden_size=5120, n_heads=40, n_kv_heads=8, head_dim=128,
+                           max_seq_len=8192, vram_budget_gb=20.0, prefetch_lookahead=2, use_fp16=True)
+
+    def pages_per_seq(self) -> int:
+        return -(-self.max_seq_len // PAGE_SIZE)
+
+    def to_c(self) -> _lib.Config:
+        n_pages = self.n_pages if self.n_pages is not None else self.max_seqs * self.pages_per_seq()
+        kv = {"f32": DTYPE_F32, "bf16": DTYPE_BF16}[self.kv_dtype]
+        rv = {"split_half": ROPE_SPLIT_HALF, "interleaved": ROPE_INTERLEAVED}[self.rope_variant]
+        return _lib.Config(self.n_layers, self.hidden_size, self.n_heads, self.n_kv_heads, self.head_dim,
+                           self.max_seq_len, self.max_seqs, PAGE_SIZE, n_pages, kv, rv, float(self.rope_theta),
+                           float(self.softmax_scale or 0.0))
+
+
+def compute_rope_freqs(head_dim: int, max_seq_len: int, rope_theta: float):
+    """compute_rope_freqs (src/oomllama_turbo.rs:376-396): (sin, cos) f32 CPU
+    tensors [max_seq_len, head_dim/2], computed by the library's host code."""
+    if head_dim != HEAD_DIM:
+        raise ValueError("head_dim must be 128")
+    L = _lib.load()
+    cos = torch.empty(max_seq_len, head_dim // 2, dtype=torch.float32)
+    sin = torch.empty_like(cos)
+    check(None, L.oomattn_compute_rope_table(ctypes.c_float(rope_theta), head_dim, 0, max_seq_len,
+                                             _ptr(cos), _ptr(sin)))
+    return sin, cos
+
+
+class TurboEngine:
+    """TurboEngine (src/oomllama_turbo.rs:519-787) on one GPU."""
+
+    def __init__(self, config: TurboConfig, device: int = 0, assign_pages: bool = True):
+        self.config = config
+        self.device = int(device)
+        self._L = _lib.load()
+        cfg = config.to_c()
+        self._n_pages = cfg.n_pages
+        ctx = ctypes.c_void_p()
+        with torch.cuda.device(self.device):
+            stream = torch.cuda.current_stream().cuda_stream
+            code = self._L.oomattn_create(ctypes.byref(cfg), self.device, ctypes.c_void_p(stream), ctypes.byref(ctx))
+        if code != 0:
+            raise _lib.OomAttnError(code, "oomattn_create rejected the configuration or failed to allocate")
+        self._ctx = ctx
+        if assign_pages:
+            pps = config.pages_per_seq()
+            if self._n_pages >= config.max_seqs * pps:
+                for s in range(config.max_seqs):
+                    self.set_block_table(s, range(s * pps, (s + 1) * pps))
+
+    # ------------------------------------------------------------ lifecycle
+    def close(self):
+        if getattr(self, "_ctx", None):
+            self._L.oomattn_destroy(self._ctx)
+            self._ctx = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def _bind_stream(self):
+        s = torch.cuda.current_stream(self.device).cuda_stream
+        self._L.oomattn_set_stream(self._ctx, ctypes.c_void_p(s))
+
+    def sync(self):
+        """Wait for queued work; raises on a device-side timeout or index-check failure."""
+        self._bind_stream()
+        check(self._ctx, self._L.oomattn_sync(self._ctx))
+
+    def reset(self):
+        """TurboEngine::reset (src/oomllama_turbo.rs:726-728)."""
+        check(self._ctx, self._L.oomattn_reset(self._ctx))
+
+    def seq_len(self, layer: int = 0, seq: int = 0) -> int:
+        """TurboEngine::seq_len (src/oomllama_turbo.rs:731-733), per layer and sequence."""
+        out = ctypes.c_int32()
+        check(self._ctx, self._L.oomattn_seq_len(self._ctx, layer, seq, ctypes.byref(out)))
+        return out.value
+
+    # ------------------------------------------------------------ cache
+    def set_block_table(self, seq: int, pages):
+        pages = list(pages)
+        check(self._ctx, self._L.oomattn_set_block_table(self._ctx, seq, int_array(pages), len(pages)))
+
+    def set_position_offset(self, seq: int, offset: int):
+        check(self._ctx, self._L.oomattn_set_position_offset(self._ctx, seq, offset))
+
+    def set_seq_len(self, layer: int, seq: int, length: int):
+        check(self._ctx, self._L.oomattn_set_seq_len(self._ctx, layer, seq, length))
+
+    def kv_pool(self):
+        """(k_pool, v_pool) device tensors [n_layers, n_pages+1, n_kv, 16, 128] aliasing the pools."""
+        kp, vp = ctypes.c_void_p(), ctypes.c_void_p()
+        check(self._ctx, self._L.oomattn_kv_pool(self._ctx, ctypes.byref(kp), ctypes.byref(vp)))
+        c = self.config
+        shape = (c.n_layers, self._n_pages + 1, c.n_kv_heads, PAGE_SIZE, HEAD_DIM)
+        dt = torch.bfloat16 if c.kv_dtype == "bf16" else torch.float32
+        return _alias(kp.value, shape, dt, self.device), _alias(vp.value, shape, dt, self.device)
+
+    def kv_write(self, layer: int, seq: int, k: torch.Tensor, v: torch.Tensor):
+        """Append already-rotated rows k, v [n, n_kv, 128] (LayerKVCache::append, :41-55)."""
+        n = k.shape[0]
+        nk = self.config.n_kv_heads * HEAD_DIM
+        _dev(k, "k", self.device, numel=n * nk)
+        _dev(v, "v", self.device, dtype=k.dtype, numel=n * nk)
+        self._bind_stream()
+        check(self._ctx, self._L.oomattn_kv_write(self._ctx, layer, seq, _ptr(k), _ptr(v), n, _dtype_code(k)))
+
+    def kv_read(self, layer: int, seq: int):
+        """LayerKVCache::get (src/oomllama_turbo.rs:57-63): host tensors [n_kv, L, 128]."""
+        L_ = self.seq_len(layer, seq)
+        dt = torch.bfloat16 if self.config.kv_dtype == "bf16" else torch.float32
+        k = torch.empty(self.config.n_kv_heads, L_, HEAD_DIM, dtype=dt)
+        v = torch.empty_like(k)
+        self._bind_stream()
+        check(self._ctx, self._L.oomattn_kv_read(self._ctx, layer, seq, _ptr(k), _ptr(v)))
+        return k, v
+
+    # ------------------------------------------------------------ K-A
+    def rope_append(self, layer: int, seq_ids, q, k, v, bq=None, bk=None, bv=None, q_out_dtype=torch.float32):
+        """Bias + RoPE + append for projected rows; q [T, Hq*128], k/v [T, Hkv*128]
+        with T = len(seq_ids) * n_new.  Returns the rotated q [T, Hq, 128]."""
+        seq_ids = list(seq_ids)
+        T = q.shape[0]
+        if T % len(seq_ids):
+            raise ValueError("token count is not a multiple of the number of sequences")
+        n_new = T // len(seq_ids)
+        c = self.config
+        _dev(q, "q", self.device, numel=T * c.n_heads * HEAD_DIM)
+        _dev(k, "k", self.device, dtype=q.dtype, numel=T * c.n_kv_heads * HEAD_DIM)
+        _dev(v, "v", self.device, dtype=q.dtype, numel=T * c.n_kv_heads * HEAD_DIM)
+        for b, n in ((bq, c.n_heads), (bk, c.n_kv_heads), (bv, c.n_kv_heads)):
+            if b is not None:
+                _dev(b, "bias", self.device, dtype=torch.float32, numel=n * HEAD_DIM)
+        q_out = torch.empty(T, c.n_heads, HEAD_DIM, dtype=q_out_dtype, device=q.device)
+        self._bind_stream()
+        check(self._ctx, self._L.oomattn_rope_append(
+            self._ctx, layer, len(seq_ids), int_array(seq_ids), n_new, _ptr(q), _ptr(k), _ptr(v), _dtype_code(q),
+            _ptr(bq), _ptr(bk), _ptr(bv), _ptr(q_out), _DT[q_out_dtype]))
+        return q_out
+
+    def qkv_rope_append(self, layer: int, seq_ids, x, wq, wk, wv, bq=None, bk=None, bv=None,
+                        q_out_dtype=torch.float32):
+        """QKV projection + bias + RoPE + append (src/oomllama_turbo.rs:638-681).
+        x [T, hidden] f32; weights [out, hidden] f32 or bf16."""
+        seq_ids = list(seq_ids)
+        c = self.config
+        T = x.shape[0]
+        n_new = T // len(seq_ids)
+        H = c.hidden_size
+        _dev(x, "x", self.device, dtype=torch.float32, numel=T * H)
+        _dev(wq, "wq", self.device, numel=c.n_heads * HEAD_DIM * H)
+        _dev(wk, "wk", self.device, dtype=wq.dtype, numel=c.n_kv_heads * HEAD_DIM * H)
+        _dev(wv, "wv", self.device, dtype=wq.dtype, numel=c.n_kv_heads * HEAD_DIM * H)
+        q_out = torch.empty(T, c.n_heads, HEAD_DIM, dtype=q_out_dtype, device=x.device)
+        self._bind_stream()
+        check(self._ctx, self._L.oomattn_qkv_rope_append(
+            self._ctx, layer, len(seq_ids), int_array(seq_ids), n_new, _ptr(x), _ptr(wq), _ptr(wk), _ptr(wv),
+            _dtype_code(wq), _ptr(bq), _ptr(bk), _ptr(bv), _ptr(q_out), _DT[q_out_dtype]))
+        return q_out
+
+    # ------------------------------------------------------------ K-B / K-C
+    def decode(self, layer: int, seq_ids, q, lens=None, with_lse: bool = False, out=None, lse=None):
+        """One query row per entry of seq_ids over the paged cache.
+        q [rows, Hq, 128] f32 (rotated) -> out [rows, Hq, 128] f32 (, lse [rows, Hq])."""
+        seq_ids = list(seq_ids)
+        c = self.config
+        rows = len(seq_ids)
+        _dev(q, "q", self.device, dtype=torch.float32, numel=rows * c.n_heads * HEAD_DIM)
+        if out is None:
+            out = torch.empty(rows, c.n_heads, HEAD_DIM, dtype=torch.float32, device=q.device)
+        if with_lse and lse is None:
+            lse = torch.empty(rows, c.n_heads, dtype=torch.float32, device=q.device)
+        self._bind_stream()
+        check(self._ctx, self._L.oomattn_decode(
+            self._ctx, layer, rows, int_array(seq_ids), None if lens is None else int_array(lens), _ptr(q),
+            _ptr(out), _ptr(lse) if with_lse else None))
+        return (out, lse) if with_lse else out
+
+    def prefill(self, layer: int, seq: int, q, out_dtype=torch.float32, with_lse: bool = False, out=None):
+        """Causal attention of the n_new newest tokens of `seq` (bf16 cache).
+        q [n_new, Hq, 128] bf16 (rotated) -> out [n_new, Hq, 128]."""
+        c = self.config
+        n_new = q.shape[0]
+        _dev(q, "q", self.device, dtype=torch.bfloat16, numel=n_new * c.n_heads * HEAD_DIM)
+        if out is None:
+            out = torch.empty(n_new, c.n_heads, HEAD_DIM, dtype=out_dtype, device=q.device)
+        lse = torch.empty(n_new, c.n_heads, dtype=torch.float32, device=q.device) if with_lse else None
+        self._bind_stream()
+        check(self._ctx, self._L.oomattn_prefill(self._ctx, layer, seq, n_new, _ptr(q), _ptr(out),
+                                                 _DT[out.dtype], _ptr(lse)))
+        return (out, lse) if with_lse else out
+
+    def merge_partials(self, parts: torch.Tensor, lses: torch.Tensor):
+        """LSE merge of split-context partials: parts [P, R, 128], lses [P, R] -> (out [R, 128], lse [R])."""
+        P, R = lses.shape
+        _dev(parts, "parts", self.device, dtype=torch.float32, numel=P * R * HEAD_DIM)
+        _dev(lses, "lses", self.device, dtype=torch.float32)
+        out = torch.empty(R, HEAD_DIM, dtype=torch.float32, device=parts.device)
+        lse = torch.empty(R, dtype=torch.float32, device=parts.device)
+        self._bind_stream()
+        check(self._ctx, self._L.oomattn_merge_partials(self._ctx, P, R, _ptr(parts), _ptr(lses), _ptr(out),
+                                                        _ptr(lse)))
+        return out, lse
+
+    # ------------------------------------------------------------ the layer step
+    def attention_forward_with_bias(self, layer_idx: int, x, wq, wk, wv, wo, bq=None, bk=None, bv=None):
+        """TurboEngine::attention_forward_with_bias (src/oomllama_turbo.rs:618-723).
+        x [B, S, hidden] f32, weights [out, in] f32 -> [B, S, o_out] f32."""
+        c = self.config
+        B, S, H = x.shape
+        if H != c.hidden_size:
+            raise ValueError(f"hidden size {H} != config {c.hidden_size}")
+        o_out = wo.shape[0]
+        _dev(x, "x", self.device, dtype=torch.float32)
+        for name, w, n in (("wq", wq, c.n_heads), ("wk", wk, c.n_kv_heads), ("wv", wv, c.n_kv_heads)):
+            _dev(w, name, self.device, dtype=torch.float32, numel=n * HEAD_DIM * H)
+        _dev(wo, "wo", self.device, dtype=torch.float32, numel=o_out * c.n_heads * HEAD_DIM)
+        for name, b, n in (("bq", bq, c.n_heads), ("bk", bk, c.n_kv_heads), ("bv", bv, c.n_kv_heads)):
+            if b is not None:
+                _dev(b, name, self.device, dtype=torch.float32, numel=n * HEAD_DIM)
+        out = torch.empty(B, S, o_out, dtype=torch.float32, device=x.device)
+        self._bind_stream()
+        check(self._ctx, self._L.oomattn_attention_forward_with_bias(
+            self._ctx, layer_idx, B, S, _ptr(x), _ptr(wq), _ptr(wk), _ptr(wv), _ptr(wo), o_out, _ptr(bq), _ptr(bk),
+            _ptr(bv), _ptr(out)))
+        return out
+
+
+def _alias(ptr: int, shape, dtype, device: int) -> torch.Tensor:
+    """A torch tensor viewing library-owned device memory (no copy, no ownership)."""
+    numel = 1
+    for s in shape:
+        numel *= s
+    esize = torch.tensor([], dtype=dtype).element_size()
+
+    class _Holder:
+        __cuda_array_interface__ = {
+            "shape": (numel * esize,), "typestr": "|u1", "data": (ptr, False), "version": 3, "strides": None,
+        }
+
+    with torch.cuda.device(device):
+        raw = torch.as_tensor(_Holder(), device=f"cuda:{device}")
+    return raw.view(dtype).view(*shape)

@@ -1,0 +1,228 @@
+"""numpy front-end of the C oracle (oracle/attn_ref.c).
+
+TEST INFRASTRUCTURE ONLY: imported by tests/, by ``__graft_entry__.smoke()`` and
+by the CPU-baseline leg of ``bench.py``.  The product package never imports it.
+
+Parity status: UNPINNED -- the Rust reference cannot be built or run here and
+its tests hold no golden vectors for this path; see the header of attn_ref.c.
+Every function cites the reference code it restates (paths are relative to the
+jaspertvdm/oomllama project root).
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_SO = os.path.join(_HERE, "liboomattn_oracle.so")
+_lib = None
+
+ROPE_SPLIT_HALF = 0
+ROPE_INTERLEAVED = 1
+
+_f32p = np.ctypeslib.ndpointer(dtype=np.float32, flags="C_CONTIGUOUS")
+_i32p = np.ctypeslib.ndpointer(dtype=np.int32, flags="C_CONTIGUOUS")
+_i64p = np.ctypeslib.ndpointer(dtype=np.int64, flags="C_CONTIGUOUS")
+_u16p = np.ctypeslib.ndpointer(dtype=np.uint16, flags="C_CONTIGUOUS")
+
+
+def build(force: bool = False) -> str:
+    """Compile attn_ref.c with the committed Makefile (no-op when up to date)."""
+    src = os.path.join(_HERE, "attn_ref.c")
+    if force or not os.path.exists(_SO) or os.path.getmtime(_SO) < os.path.getmtime(src):
+        subprocess.run(["make", "-s", "-C", _HERE], check=True)
+    return _SO
+
+
+def lib():
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(_SO):
+        build()
+    L = ctypes.CDLL(_SO)
+    c_int, c_float, c_void = ctypes.c_int, ctypes.c_float, None
+    L.oracle_rope_table.argtypes = [c_float, c_int, c_int, c_int, _f32p, _f32p]
+    L.oracle_rope_apply.argtypes = [_f32p, c_int, c_int, _f32p, _f32p, c_int]
+    L.oracle_matvec_bias.argtypes = [_f32p, _f32p, ctypes.c_void_p, c_int, c_int, _f32p]
+    L.oracle_attention_head.argtypes = [_f32p, _f32p, _f32p, c_int, c_int, c_float, _f32p, _f32p]
+    L.oracle_attention_head.restype = c_float
+    L.oracle_gqa_attention.argtypes = [_f32p, _f32p, _f32p, c_int, c_int, c_int, c_int, c_int, c_float, c_int,
+                                       _f32p, ctypes.c_void_p]
+    L.oracle_gqa_attention_rows.argtypes = [_f32p, _f32p, _f32p, c_int, c_int, c_int, c_int, c_int, c_float,
+                                            c_int, c_int, _i32p, _i32p, _f32p]
+    L.oracle_decode_batch.argtypes = [_f32p, _f32p, _f32p, _i64p, _i32p, c_int, c_int, c_int, c_int, c_float,
+                                      c_int, _f32p]
+    L.oracle_merge_partials.argtypes = [_f32p, _f32p, c_int, c_int, c_int, _f32p, ctypes.c_void_p]
+    L.oracle_layer_attention.argtypes = [_f32p, c_int, c_int, c_int, _f32p, _f32p, _f32p, ctypes.c_void_p,
+                                         ctypes.c_void_p, ctypes.c_void_p, c_int, c_int, c_int, c_int, _f32p,
+                                         _f32p, c_int, _f32p, _f32p, c_int, c_float, _f32p]
+    L.oracle_round_bf16.argtypes = [_f32p, ctypes.c_int64]
+    L.oracle_f32_to_bf16.argtypes = [c_float]
+    L.oracle_f32_to_bf16.restype = ctypes.c_uint16
+    L.oracle_bf16_to_f32.argtypes = [ctypes.c_uint16]
+    L.oracle_bf16_to_f32.restype = c_float
+    L.oracle_omp_max_threads.restype = c_int
+    _lib = L
+    return L
+
+
+def _c(a, dt=np.float32):
+    return np.ascontiguousarray(a, dtype=dt)
+
+
+def _ptr(a):
+    return None if a is None else a.ctypes.data_as(ctypes.c_void_p)
+
+
+def rope_table(theta: float, head_dim: int, n_pos: int, pos0: int = 0):
+    """cos, sin tables [n_pos, head_dim/2] (oomllama_turbo.rs:753-761, :376-396)."""
+    half = head_dim // 2
+    c = np.empty((n_pos, half), np.float32)
+    s = np.empty((n_pos, half), np.float32)
+    lib().oracle_rope_table(float(theta), head_dim, pos0, n_pos, c, s)
+    return c, s
+
+
+def rope_apply(x, cos_row, sin_row, variant: int):
+    """Rotate x [n_heads, d] (one token) -- apply_rope (interleaved,
+    oomllama_turbo.rs:402-438) or split-half (:443-467, :773-783)."""
+    x = _c(x).copy()
+    nh, d = x.shape
+    lib().oracle_rope_apply(x, nh, d, _c(cos_row), _c(sin_row), variant)
+    return x
+
+
+def rope_tokens(x, positions, cos_t, sin_t, variant: int):
+    """Rotate x [T, n_heads, d], token t at positions[t]."""
+    x = _c(x).copy()
+    T, nh, d = x.shape
+    L = lib()
+    for t in range(T):
+        row = x[t]
+        L.oracle_rope_apply(row, nh, d, _c(cos_t[positions[t]]), _c(sin_t[positions[t]]), variant)
+        x[t] = row
+    return x
+
+
+def matvec_bias(x, w, b=None):
+    """y = x @ W^T + b for one row x (oom_inference.rs:168-180; bias :648-656)."""
+    w = _c(w)
+    out_f, in_f = w.shape
+    y = np.empty(out_f, np.float32)
+    bb = None if b is None else _c(b)
+    lib().oracle_matvec_bias(_c(x), w, _ptr(bb), out_f, in_f, y)
+    return y
+
+
+def attention_head(q, k, v, scale=None):
+    """oom_inference.rs:240-272: one head over k, v [L, d]; returns (out, lse)."""
+    k = _c(k)
+    L_, d = k.shape
+    scale = 1.0 / np.sqrt(np.float32(d)) if scale is None else scale
+    out = np.empty(d, np.float32)
+    ws = np.empty(max(L_, 1), np.float32)
+    lse = lib().oracle_attention_head(_c(q), k, _c(v), L_, d, np.float32(scale), ws, out)
+    return out, lse
+
+
+def gqa_attention(q, k, v, causal=True, scale=None, with_lse=False):
+    """flash_attention_forward semantics (oomllama_turbo.rs:304-369).
+    q [n_q, Hq, d]; k, v [Hkv, L, d]; returns out [n_q, Hq, d] (and lse [n_q, Hq])."""
+    q, k, v = _c(q), _c(k), _c(v)
+    n_q, hq, d = q.shape
+    hkv, L_, _ = k.shape
+    scale = float(1.0 / np.sqrt(np.float32(d))) if scale is None else scale
+    out = np.empty((n_q, hq, d), np.float32)
+    lse = np.empty((n_q, hq), np.float32) if with_lse else None
+    lib().oracle_gqa_attention(q, k, v, n_q, L_, hq, hkv, d, np.float32(scale), int(causal), out, _ptr(lse))
+    return (out, lse) if with_lse else out
+
+
+def gqa_attention_rows(q, k, v, rows, heads, causal=True, scale=None):
+    """gqa_attention for sampled (row, head) pairs only; returns [n_pairs, d]."""
+    q, k, v = _c(q), _c(k), _c(v)
+    n_q, hq, d = q.shape
+    hkv, L_, _ = k.shape
+    scale = float(1.0 / np.sqrt(np.float32(d))) if scale is None else scale
+    rows, heads = _c(rows, np.int32), _c(heads, np.int32)
+    out = np.empty((len(rows), d), np.float32)
+    lib().oracle_gqa_attention_rows(q, k, v, n_q, L_, hq, hkv, d, np.float32(scale), int(causal), len(rows),
+                                    rows, heads, out)
+    return out
+
+
+def decode_batch(q, k_list, v_list, n_threads=1, scale=None):
+    """Batched one-token decode (oom_inference.rs:240-272 per (seq, head)).
+    q [B, Hq, d]; k_list[b], v_list[b]: [Hkv, L_b, d]."""
+    q = _c(q)
+    B, hq, d = q.shape
+    hkv = k_list[0].shape[0]
+    Ls = np.array([k.shape[1] for k in k_list], np.int32)
+    offs = np.zeros(B, np.int64)
+    offs[1:] = np.cumsum([k.size for k in k_list])[:-1]
+    K = np.concatenate([_c(k).ravel() for k in k_list])
+    V = np.concatenate([_c(v).ravel() for v in v_list])
+    scale = float(1.0 / np.sqrt(np.float32(d))) if scale is None else scale
+    out = np.empty_like(q)
+    lib().oracle_decode_batch(q, K, V, offs, Ls, B, hq, hkv, d, np.float32(scale), int(n_threads), out)
+    return out
+
+
+def merge_partials(parts, lses):
+    """LSE merge of split-context partials: parts [P, R, d], lses [P, R]."""
+    parts, lses = _c(parts), _c(lses)
+    P, R, d = parts.shape
+    out = np.empty((R, d), np.float32)
+    lse = np.empty(R, np.float32)
+    lib().oracle_merge_partials(parts, lses, P, R, d, out, _ptr(lse))
+    return out, lse
+
+
+def layer_attention(x, wq, wk, wv, bq, bk, bv, n_heads, n_kv, kc, vc, cos_t, sin_t, variant, kv_bf16=False):
+    """TurboEngine::attention_forward_with_bias (oomllama_turbo.rs:618-723)
+    up to the o_proj.  x [B, S, H]; kc, vc [B, Hkv, P, d] cache before the
+    append.  Returns (out [B, S, Hq*d], kc_new, vc_new [B, Hkv, P+S, d])."""
+    x = _c(x)
+    B, S, H = x.shape
+    _, _, P, d = kc.shape
+    L_ = P + S
+    kn = np.zeros((B, n_kv, L_, d), np.float32)
+    vn = np.zeros((B, n_kv, L_, d), np.float32)
+    kn[:, :, :P] = kc
+    vn[:, :, :P] = vc
+    out = np.empty((B, S, n_heads * d), np.float32)
+    bq_, bk_, bv_ = [None if b is None else _c(b) for b in (bq, bk, bv)]
+    scale = np.float32(1.0 / np.sqrt(np.float32(d)))
+    lib().oracle_layer_attention(x, B, S, H, _c(wq), _c(wk), _c(wv), _ptr(bq_), _ptr(bk_), _ptr(bv_), n_heads,
+                                 n_kv, d, P, kn, vn, int(kv_bf16), _c(cos_t), _c(sin_t), variant, scale, out)
+    return out, kn, vn
+
+
+def round_bf16(x):
+    """Round f32 values to bf16 precision (RNE), returned as f32."""
+    x = _c(x).copy()
+    lib().oracle_round_bf16(x.reshape(-1), x.size)
+    return x
+
+
+def f32_to_bf16_bits(x):
+    """f32 -> bf16 bit patterns (uint16), round to nearest even."""
+    x = _c(x)
+    u = x.view(np.uint32).astype(np.uint64)
+    nan = ((u & 0x7F800000) == 0x7F800000) & ((u & 0x007FFFFF) != 0)
+    r = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+    r[nan] = ((u[nan] >> 16) | 0x40).astype(np.uint16)
+    return r
+
+
+def bf16_bits_to_f32(h):
+    """bf16 bit patterns -> f32 by a 16-bit shift (safetensors2oom.rs:32-39)."""
+    return (np.asarray(h, np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def omp_max_threads() -> int:
+    return int(lib().oracle_omp_max_threads())

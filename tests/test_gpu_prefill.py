@@ -1,0 +1,72 @@
+"""K-C parity: the tcgen05/TMEM causal prefill vs the oracle
+(flash_attention_forward with causal=true, oomllama_turbo.rs:304-369; mask
+aligned to the end of the cache).  Q is bf16 after RoPE by contract, the
+cache is bf16; the oracle sees the same bf16 values."""
+import numpy as np
+import pytest
+import torch
+
+from helpers import BF16_ATOL, BF16_RTOL, as_f32_np, assert_close, make_engine, randn
+
+pytestmark = pytest.mark.gpu
+
+
+def _prefill_case(oracle, n_heads, n_kv, prefix, n_new, seed, rows=None, out_dtype=torch.float32):
+    L = prefix + n_new
+    eng = make_engine(n_heads, n_kv, [L], kv_dtype="bf16", shuffle_seed=seed)
+    k = randn((L, n_kv, 128), seed + 1, torch.bfloat16)
+    v = randn((L, n_kv, 128), seed + 2, torch.bfloat16)
+    eng.kv_write(0, 0, k.cuda(), v.cuda())
+    q = randn((n_new, n_heads, 128), seed + 3, torch.bfloat16)
+    out, lse = eng.prefill(0, 0, q.cuda(), out_dtype=out_dtype, with_lse=True)
+    eng.sync()
+    kf = as_f32_np(k).transpose(1, 0, 2).copy()
+    vf = as_f32_np(v).transpose(1, 0, 2).copy()
+    qf = as_f32_np(q)
+    out = as_f32_np(out)
+    if rows is None:
+        ref, ref_lse = oracle.gqa_attention(qf, kf, vf, causal=True, with_lse=True)
+        eng.close()
+        return out, ref, lse.cpu().numpy(), ref_lse
+    r, h = rows
+    ref = oracle.gqa_attention_rows(qf, kf, vf, r, h, causal=True)
+    eng.close()
+    return out[r, h], ref, None, None
+
+
+@pytest.mark.parametrize("n_new", [1, 100, 128, 129, 256, 300, 512])
+def test_prefill_small(oracle, n_new):
+    out, ref, lse, ref_lse = _prefill_case(oracle, 28, 4, 0, n_new, seed=n_new)
+    assert_close(out, ref, BF16_ATOL, BF16_RTOL, what=f"prefill n={n_new}")
+    assert_close(lse, ref_lse, 2e-3, what="prefill lse")
+
+
+@pytest.mark.parametrize("prefix,n_new", [(16, 100), (200, 300), (1000, 257)])
+def test_prefill_chunk_on_cached_prefix(oracle, prefix, n_new):
+    out, ref, lse, ref_lse = _prefill_case(oracle, 28, 4, prefix, n_new, seed=prefix)
+    assert_close(out, ref, BF16_ATOL, BF16_RTOL, what=f"chunked prefill P={prefix} n={n_new}")
+
+
+def test_prefill_llama_heads_bf16_out(oracle):
+    out, ref, _, _ = _prefill_case(oracle, 32, 8, 0, 384, seed=5, out_dtype=torch.bfloat16)
+    # bf16 output adds one rounding of |out| < 1 (<= 2^-9 relative)
+    assert_close(out, ref, BF16_ATOL + 4e-3, BF16_RTOL, what="prefill 32q/8kv bf16 out")
+
+
+def test_prefill_full_size_sampled_rows(oracle):
+    # Qwen2.5-7B causal prefill at 4096 tokens; oracle on 384 sampled (row, head) pairs
+    rng = np.random.default_rng(6)
+    rows = np.concatenate([[0, 1, 127, 128, 255, 256, 4095], rng.integers(0, 4096, 377)]).astype(np.int32)
+    heads = rng.integers(0, 28, rows.size).astype(np.int32)
+    out, ref, _, _ = _prefill_case(oracle, 28, 4, 0, 4096, seed=7, rows=(rows, heads))
+    assert_close(out, ref, BF16_ATOL, BF16_RTOL, what="prefill 4096 sampled rows")
+
+
+def test_prefill_rejects_f32_cache():
+    from oomllama_b200._lib import OomAttnError
+    eng = make_engine(28, 4, [32], kv_dtype="f32")
+    eng.kv_write(0, 0, torch.zeros(8, 4, 128, device="cuda"), torch.zeros(8, 4, 128, device="cuda"))
+    with pytest.raises(OomAttnError) as e:
+        eng.prefill(0, 0, torch.zeros(8, 28, 128, dtype=torch.bfloat16, device="cuda"))
+    assert e.value.code == 8
+    eng.close()
