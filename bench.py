@@ -191,15 +191,30 @@ def bench_prefill(args, dist_, torch):
     eng.sync()
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    dist_.barrier()
-    torch.cuda.synchronize()
+
+    def load_for(seconds):
+        # untimed steps around the timed region so the 200 ms clock sampler
+        # sees this kernel's clocks under load
+        end = time.perf_counter() + seconds
+        i = 0
+        while time.perf_counter() < end:
+            step(i)
+            i += 1
+            if i % 32 == 0:
+                torch.cuda.synchronize()
+        torch.cuda.synchronize()
+
     with ClockSampler(dev) as clk:
+        load_for(0.7)
+        dist_.barrier()
+        torch.cuda.synchronize()
         t0.record()
         for i in range(args.steps):
             step(i, evs[i])
         t1.record()
         torch.cuda.synchronize()
-    dist_.barrier()
+        dist_.barrier()
+        load_for(0.5)
     eng.sync()
     ms = t0.elapsed_time(t1) / args.steps
     kern_ms = sum(a.elapsed_time(b) for a, b in evs) / args.steps

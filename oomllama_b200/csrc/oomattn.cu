@@ -72,6 +72,7 @@ struct oomattn_ctx {
   int* d_status = nullptr;
   CUtensorMap kmap{}, vmap{};
   bool have_maps = false;
+  int prefill_regs = 0;  // compiled register count of the prefill kernel
   // host mirrors (authoritative for lengths; updated at enqueue time)
   std::vector<int> h_block_table;  // [max_seqs][max_pages_per_seq]
   std::vector<int> h_len;          // [n_layers][max_seqs]
@@ -418,6 +419,9 @@ int oomattn_create(const oomattn_config* cfg, int device, void* stream, oomattn_
       cudaFuncSetAttribute(prefill_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kPfSmemBytes) !=
           cudaSuccess)
     return bail(OOMATTN_ERR_CUDA);
+  cudaFuncAttributes fa;
+  if (cudaFuncGetAttributes(&fa, prefill_bf16_kernel) != cudaSuccess) return bail(OOMATTN_ERR_CUDA);
+  ctx->prefill_regs = fa.numRegs;
   if (cudaDeviceSynchronize() != cudaSuccess) return bail(OOMATTN_ERR_CUDA);
   *out = ctx;
   return OOMATTN_OK;
@@ -757,6 +761,10 @@ int oomattn_prefill(oomattn_ctx* ctx, int32_t layer, int32_t seq, int32_t n_new,
   if (rc) return rc;
   if (ctx->cfg.kv_dtype != OOMATTN_DTYPE_BF16)
     return fail(ctx, OOMATTN_ERR_UNSUPPORTED, "the tensor-core prefill needs a bf16 cache");
+  // The kernel's register split (setmaxnreg) balances only at this launch count.
+  if (ctx->prefill_regs != kPfLaunchRegs)
+    return fail(ctx, OOMATTN_ERR_UNSUPPORTED, "prefill kernel compiled with %d registers per thread, expected %d",
+                ctx->prefill_regs, kPfLaunchRegs);
   if (reinterpret_cast<uintptr_t>(q) % 16 != 0) return fail(ctx, OOMATTN_ERR_INVALID_ARG, "q must be 16-byte aligned");
   const int L = ctx->h_len[(size_t)layer * ctx->cfg.max_seqs + seq];
   if (n_new > L) return fail(ctx, OOMATTN_ERR_OUT_OF_RANGE, "n_new %d exceeds the cached length %d", n_new, L);

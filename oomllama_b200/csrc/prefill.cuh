@@ -36,6 +36,11 @@ constexpr int kTileBytes = 128 * kHeadDim * 2;    // 32 KB: one 128 x 128 bf16 o
 constexpr int kHalfTileBytes = kTileBytes / 2;    // one 64-column half
 constexpr int kPfSmemBytes = 2 * kTileBytes + kPfStages * 2 * kTileBytes + 1024 + 256;
 constexpr float kRescaleThreshold = 8.0f;         // log2 units: rescale O only when the max grows by > 256x
+constexpr int kPfLaunchRegs = 168;                // 65536 / 384, rounded down to a multiple of 8
+constexpr int kPfProducerRegs = 56;
+constexpr int kPfSoftmaxRegs = 224;
+static_assert(128 * kPfProducerRegs + 256 * kPfSoftmaxRegs <= kPfThreads * kPfLaunchRegs,
+              "register split exceeds the launch allocation");
 
 struct PrefillArgs {
   void* out;           // [n_new][n_heads][128]
@@ -192,9 +197,17 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // Register split: the kernel launches with kPfLaunchRegs per thread (the host
+  // checks the compiled count before launching); warpgroup 0 (TMA, MMA and two
+  // idle warps) gives (168-56)*128 registers back at the top of its branches and
+  // the two softmax warpgroups take (224-168)*256 -- the same number, so the
+  // increase never waits.
+#define OOMATTN_REGS_DEC() asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kPfProducerRegs))
+#define OOMATTN_REGS_INC() asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kPfSoftmaxRegs))
 
   if (warp == 0) {
     // ------------------------------------------------ TMA producer
+    OOMATTN_REGS_DEC();
     if (lane == 0) {
       prefetch_tensormap(&qmap);
       prefetch_tensormap(&kmap);
@@ -238,6 +251,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------ MMA issuer
+    OOMATTN_REGS_DEC();
     if (lane == 0) {
       constexpr uint32_t idesc_qk = make_idesc_bf16(false);
       constexpr uint32_t idesc_pv = make_idesc_bf16(true);
@@ -314,8 +328,11 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       tc_commit(mma_done);
       mbar_wait(mma_done, 0, a.status, a.timeout_ns);
     }
-  } else if (warp >= 4) {
+  } else if (warp < 4) {
+    OOMATTN_REGS_DEC();  // warps 2-3: no role
+  } else {
     // ------------------------------------------------ softmax / epilogue
+    OOMATTN_REGS_INC();
     const int i = (warp - 4) >> 2;           // q tile
     const int quarter = warp & 3;            // TMEM lane quarter of this warp
     const int r = quarter * 32 + lane;       // row within the tile
@@ -341,9 +358,16 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         for (int c = 0; c < 128; ++c)
           if (c > lim) sr[c] = __float_as_uint(-INFINITY);
       }
-      float mx = -INFINITY;
+      // row max: 8 independent 3-input max chains, then a short tree
+      float mv[8];
 #pragma unroll
-      for (int c = 0; c < 128; ++c) mx = fmaxf(mx, __uint_as_float(sr[c]));
+      for (int k = 0; k < 8; ++k) mv[k] = fmaxf(__uint_as_float(sr[2 * k]), __uint_as_float(sr[2 * k + 1]));
+#pragma unroll
+      for (int c = 16; c < 128; c += 16)
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          mv[k] = max3f(mv[k], __uint_as_float(sr[c + 2 * k]), __uint_as_float(sr[c + 2 * k + 1]));
+      const float mx = max3f(max3f(mv[0], mv[1], mv[2]), max3f(mv[3], mv[4], mv[5]), fmaxf(mv[6], mv[7]));
       const float mxs = mx * cl;
       bool need = false;
       float alpha = 1.f;
@@ -355,31 +379,38 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         m_used = mxs;
         l *= alpha;
       }
-      // P = P_hi + P_lo, both bf16: P_hi into S columns [0,64), P_lo into [64,128)
-      // (the scores there are already in registers).  Two bf16 MMAs then carry P
-      // to ~16 significant bits, so P's rounding stays far below the bf16-KV
-      // tolerance.  P_hi is packed in place (step c reads sr[2c], sr[2c+1],
-      // writes sr[c], c <= 2c); P_lo goes to its own array, so the live set
-      // stays near 130 registers.
-      float lsum = 0.f;
+      // P = P_hi + P_lo, both bf16: P_hi (p truncated to bf16) into S columns
+      // [0,64), P_lo = bf16(p - P_hi) into [64,128) (the scores there are already
+      // in registers).  Two bf16 MMAs then carry p to ~16 significant bits, far
+      // below the bf16-KV tolerance.  P_hi is packed in place (step c reads
+      // sr[2c], sr[2c+1], writes sr[c], c <= 2c); P_lo goes to its own array,
+      // so the live set stays near 130 registers.  The scale-and-shift and the
+      // row sum run as packed f32x2 FMA-pipe instructions, the exponential on
+      // the MUFU pipe.
+      const uint64_t cl2 = f2_pack(cl, cl);
+      const uint64_t nm2 = f2_pack(-m_used, -m_used);
+      uint64_t acc[4] = {0, 0, 0, 0};
 #pragma unroll
       for (int half = 0; half < 2; ++half) {
         uint32_t plo[32];
 #pragma unroll
         for (int cc = 0; cc < 32; ++cc) {
           const int c = half * 32 + cc;
-          const float p0 = exp2f(fmaf(__uint_as_float(sr[2 * c]), cl, -m_used));
-          const float p1 = exp2f(fmaf(__uint_as_float(sr[2 * c + 1]), cl, -m_used));
-          uint32_t hi, lo;
-          split_bf16x2(p0, p1, hi, lo);
-          lsum += p0 + p1;
+          const uint64_t t = f2_fma(f2_pack(__uint_as_float(sr[2 * c]), __uint_as_float(sr[2 * c + 1])), cl2, nm2);
+          const float p0 = ex2_ftz(f2_lo(t)), p1 = ex2_ftz(f2_hi(t));
+          const uint32_t hi = trunc_bf16x2(p0, p1);
+          const uint64_t p2 = f2_pack(p0, p1);
+          const uint64_t rem = f2_sub(p2, f2_pack(__uint_as_float(__float_as_uint(p0) & 0xffff0000u),
+                                                  __uint_as_float(__float_as_uint(p1) & 0xffff0000u)));
+          acc[cc & 3] = f2_add(acc[cc & 3], p2);
           sr[c] = hi;
-          plo[cc] = lo;
+          plo[cc] = pack_bf16(f2_lo(rem), f2_hi(rem));
         }
         OOMATTN_TMEM_ST32((tmem + i * 128) + lane_off + half * 32, (sr + half * 32));
         OOMATTN_TMEM_ST32((tmem + i * 128) + lane_off + 64 + half * 32, plo);
       }
-      l += lsum;
+      const uint64_t acc2 = f2_add(f2_add(acc[0], acc[1]), f2_add(acc[2], acc[3]));
+      l += f2_lo(acc2) + f2_hi(acc2);
       if (__any_sync(0xffffffffu, need)) {
 #pragma unroll
         for (int ch = 0; ch < 4; ++ch) {
