@@ -31,14 +31,15 @@
 namespace oomattn {
 
 constexpr int kPfThreads = 384;
-constexpr int kPfStages = 2;
+constexpr int kPfKStages = 3;                     // K ring: a stage frees once both S MMAs of its tile finish
+constexpr int kPfVStages = 2;                     // V ring: a stage frees once both P.V MMAs finish
 constexpr int kTileBytes = 128 * kHeadDim * 2;    // 32 KB: one 128 x 128 bf16 operand tile
 constexpr int kHalfTileBytes = kTileBytes / 2;    // one 64-column half
-constexpr int kPfSmemBytes = 2 * kTileBytes + kPfStages * 2 * kTileBytes + 1024 + 256;
+constexpr int kPfSmemBytes = (2 + kPfKStages + kPfVStages) * kTileBytes + 1024 + 256;
 constexpr float kRescaleThreshold = 8.0f;         // log2 units: rescale O only when the max grows by > 256x
 constexpr int kPfLaunchRegs = 168;                // 65536 / 384, rounded down to a multiple of 8
-constexpr int kPfProducerRegs = 56;
-constexpr int kPfSoftmaxRegs = 224;
+constexpr int kPfProducerRegs = 88;
+constexpr int kPfSoftmaxRegs = 208;
 static_assert(128 * kPfProducerRegs + 256 * kPfSoftmaxRegs <= kPfThreads * kPfLaunchRegs,
               "register split exceeds the launch allocation");
 
@@ -84,6 +85,29 @@ __device__ __forceinline__ void mma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// Same two MMAs with each descriptor given as 32-bit halves (lo carries the
+// start address), so callers advance only a 32-bit register per k-step.
+__device__ __forceinline__ void mma_ss_lh(uint32_t d_tmem, uint32_t a_lo, uint32_t a_hi, uint32_t b_lo, uint32_t b_hi,
+                                          uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t.reg .b64 da, db;\n\t"
+      "setp.ne.b32 p, %6, 0;\n\t"
+      "mov.b64 da, {%1, %2};\n\t"
+      "mov.b64 db, {%3, %4};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], da, db, %5, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_lo), "r"(a_hi), "r"(b_lo), "r"(b_hi), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void mma_ts_lh(uint32_t d_tmem, uint32_t a_tmem, uint32_t b_lo, uint32_t b_hi,
+                                          uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t.reg .b64 db;\n\t"
+      "setp.ne.b32 p, %5, 0;\n\t"
+      "mov.b64 db, {%2, %3};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], db, %4, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "r"(b_lo), "r"(b_hi), "r"(idesc), "r"(accumulate)
       : "memory");
 }
 // D[tmem] (+)= A[tmem] * B[smem desc]
@@ -146,14 +170,15 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;                                // [2 tiles][2 halves][128][128 B]
-  uint8_t* sK = smem + 2 * kTileBytes;               // [stage][2 halves][128][128 B]
-  uint8_t* sV = sK + kPfStages * kTileBytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + kPfStages * kTileBytes);
+  uint8_t* sK = smem + 2 * kTileBytes;               // [K stage][2 halves][128][128 B]
+  uint8_t* sV = sK + kPfKStages * kTileBytes;        // [V stage][2 halves][128][128 B]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + kPfVStages * kTileBytes);
   uint64_t* q_full = bars + 0;
-  uint64_t* k_full = bars + 1;                       // [kPfStages]
-  uint64_t* v_full = k_full + kPfStages;             // [kPfStages]
-  uint64_t* kv_empty = v_full + kPfStages;           // [kPfStages]
-  uint64_t* s_full = kv_empty + kPfStages;           // [2]
+  uint64_t* k_full = bars + 1;                       // [kPfKStages]
+  uint64_t* k_empty = k_full + kPfKStages;           // [kPfKStages]
+  uint64_t* v_full = k_empty + kPfKStages;           // [kPfVStages]
+  uint64_t* v_empty = v_full + kPfVStages;           // [kPfVStages]
+  uint64_t* s_full = v_empty + kPfVStages;           // [2]
   uint64_t* p_full = s_full + 2;                     // [2]
   uint64_t* o_full = p_full + 2;                     // [2]
   uint64_t* mma_done = o_full + 2;
@@ -176,10 +201,13 @@ __global__ void __launch_bounds__(kPfThreads, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int s = 0; s < kPfStages; ++s) {
+    for (int s = 0; s < kPfKStages; ++s) {
       mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+    }
+    for (int s = 0; s < kPfVStages; ++s) {
       mbar_init(&v_full[s], 1);
-      mbar_init(&kv_empty[s], 1);
+      mbar_init(&v_empty[s], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
@@ -199,8 +227,8 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   const uint32_t tmem = *tmem_slot;
   // Register split: the kernel launches with kPfLaunchRegs per thread (the host
   // checks the compiled count before launching); warpgroup 0 (TMA, MMA and two
-  // idle warps) gives (168-56)*128 registers back at the top of its branches and
-  // the two softmax warpgroups take (224-168)*256 -- the same number, so the
+  // idle warps) gives (168-88)*128 registers back at the top of its branches and
+  // the two softmax warpgroups take (208-168)*256 -- the same number, so the
   // increase never waits.
 #define OOMATTN_REGS_DEC() asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kPfProducerRegs))
 #define OOMATTN_REGS_INC() asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kPfSoftmaxRegs))
@@ -218,35 +246,55 @@ __global__ void __launch_bounds__(kPfThreads, 1)
           tma_load_3d(sQ + i * kTileBytes + c * kHalfTileBytes, &qmap, q_full, c * 64, h, q0 + 128 * i);
       const int* bt = pool.block_table + (size_t)a.seq * pool.max_pages_per_seq;
       const int null_page = pool.n_pool_pages - 1;
-      bool ok = true;
-      for (int j = 0; j < n_kv_tiles && ok; ++j) {
-        const int s = j % kPfStages;
-        if (j >= kPfStages) ok = mbar_wait(&kv_empty[s], ((j / kPfStages) - 1) & 1, a.status, a.timeout_ns);
-        if (!ok) break;
-        mbar_arrive_expect_tx(&k_full[s], kTileBytes);
-        mbar_arrive_expect_tx(&v_full[s], kTileBytes);
+      // The pool rows of a 128-key tile: its 8 pages' block-table entries, read
+      // together (one latency per tile, shared by K and V; the next tile's are
+      // fetched while this tile's copies are issued).
+      auto tile_rows = [&](int j, int* rows) {
+        int pages[8];
+#pragma unroll
         for (int p = 0; p < 8; ++p) {
           const int lp = j * 8 + p;
-          int page = lp < pool.max_pages_per_seq ? __ldg(bt + lp) : null_page;
+          pages[p] = lp < pool.max_pages_per_seq ? __ldg(bt + lp) : null_page;
+        }
+#pragma unroll
+        for (int p = 0; p < 8; ++p) {
+          int page = pages[p];
           if ((unsigned)page >= (unsigned)pool.n_pool_pages) {
             report_error(a.status, kDevErrBounds);
             page = null_page;
           }
-          const int row = ((a.layer * pool.n_pool_pages + page) * pool.n_kv + g) * kPageSize;
-          uint8_t* kd = sK + s * kTileBytes + p * 2048;
-          uint8_t* vd = sV + s * kTileBytes + p * 2048;
-          tma_load_2d(kd, &kmap, &k_full[s], 0, row);
-          tma_load_2d(kd + kHalfTileBytes, &kmap, &k_full[s], 64, row);
-          tma_load_2d(vd, &vmap, &v_full[s], 0, row);
-          tma_load_2d(vd + kHalfTileBytes, &vmap, &v_full[s], 64, row);
+          rows[p] = ((a.layer * pool.n_pool_pages + page) * pool.n_kv + g) * kPageSize;
         }
+      };
+      // one 128-key tile = 8 pages x two 64-column boxes of 16 rows, stacked at 2 KB steps
+      auto load_tile = [&](uint8_t* dst, const CUtensorMap* map, uint64_t* bar, const int* rows) {
+        mbar_arrive_expect_tx(bar, kTileBytes);
+#pragma unroll
+        for (int p = 0; p < 8; ++p) {
+          tma_load_2d(dst + p * 2048, map, bar, 0, rows[p]);
+          tma_load_2d(dst + p * 2048 + kHalfTileBytes, map, bar, 64, rows[p]);
+        }
+      };
+      bool ok = true;
+      int rows[8], next_rows[8];
+      if (n_kv_tiles > 0) tile_rows(0, rows);
+      for (int j = 0; j < n_kv_tiles && ok; ++j) {
+        const int sk = j % kPfKStages, sv = j % kPfVStages;
+        if (j >= kPfKStages) ok = mbar_wait(&k_empty[sk], ((j / kPfKStages) - 1) & 1, a.status, a.timeout_ns);
+        if (!ok) break;
+        load_tile(sK + sk * kTileBytes, &kmap, &k_full[sk], rows);
+        if (j + 1 < n_kv_tiles) tile_rows(j + 1, next_rows);
+        if (j >= kPfVStages) ok = mbar_wait(&v_empty[sv], ((j / kPfVStages) - 1) & 1, a.status, a.timeout_ns);
+        if (!ok) break;
+        load_tile(sV + sv * kTileBytes, &vmap, &v_full[sv], rows);
+#pragma unroll
+        for (int p = 0; p < 8; ++p) rows[p] = next_rows[p];
       }
       // drain: the last loads this lane issued land before the CTA can exit
-      for (int j = max(0, n_kv_tiles - kPfStages); j < n_kv_tiles; ++j) {
-        const int s = j % kPfStages;
-        mbar_wait(&k_full[s], (j / kPfStages) & 1, a.status, a.timeout_ns);
-        mbar_wait(&v_full[s], (j / kPfStages) & 1, a.status, a.timeout_ns);
-      }
+      for (int j = max(0, n_kv_tiles - kPfKStages); j < n_kv_tiles; ++j)
+        mbar_wait(&k_full[j % kPfKStages], (j / kPfKStages) & 1, a.status, a.timeout_ns);
+      for (int j = max(0, n_kv_tiles - kPfVStages); j < n_kv_tiles; ++j)
+        mbar_wait(&v_full[j % kPfVStages], (j / kPfVStages) & 1, a.status, a.timeout_ns);
       mbar_wait(q_full, 0, a.status, a.timeout_ns);
     }
   } else if (warp == 1) {
@@ -257,45 +305,61 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       constexpr uint32_t idesc_pv = make_idesc_bf16(true);
       bool ok = mbar_wait(q_full, 0, a.status, a.timeout_ns);
       tc_fence_after();
-      const uint32_t q_addr = smem_u32(sQ), k_addr = smem_u32(sK), v_addr = smem_u32(sV);
+      // Descriptor bases are built once; each MMA only adds a compile-time
+      // offset (in 16-byte units) to the start-address field, which cannot
+      // carry out of its 14 bits because shared memory ends below 256 KB.  This
+      // keeps the single issuing thread at a few instructions per MMA, ahead of
+      // the 64-cycle MMA rate even while it shares its scheduler with softmax warps.
+      const uint64_t dq = make_sdesc(smem_u32(sQ), 16, 1024);
+      const uint64_t dk = make_sdesc(smem_u32(sK), 16, 1024);
+      const uint64_t dv = make_sdesc(smem_u32(sV), kHalfTileBytes, 1024);
+      const uint32_t dq_hi = (uint32_t)(dq >> 32), dk_hi = (uint32_t)(dk >> 32), dv_hi = (uint32_t)(dv >> 32);
       // S_i(j) = Q_i K_j^T : 8 k-steps of 16 dims; halves at +16 KB, steps +32 B inside a half
       auto issue_s = [&](int i, int j) {
-        const int s = j % kPfStages;
+        const uint32_t a0 = (uint32_t)dq + i * (kTileBytes >> 4);
+        const uint32_t b0 = (uint32_t)dk + (j % kPfKStages) * (kTileBytes >> 4);
+        const uint32_t d = tmem + i * 128;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
-          const uint32_t off = (kk >> 2) * kHalfTileBytes + (kk & 3) * 32;
-          const uint64_t ad = make_sdesc(q_addr + i * kTileBytes + off, 16, 1024);
-          const uint64_t bd = make_sdesc(k_addr + s * kTileBytes + off, 16, 1024);
-          mma_ss((tmem + i * 128), ad, bd, idesc_qk, kk > 0 ? 1u : 0u);
+          const uint32_t off = (kk >> 2) * (kHalfTileBytes >> 4) + (kk & 3) * 2;
+          mma_ss_lh(d, a0 + off, dq_hi, b0 + off, dk_hi, idesc_qk, kk > 0 ? 1u : 0u);
         }
       };
       // O_i (+)= (P_hi + P_lo)_i V_j : 8 k-steps of 16 keys; P_hi / P_lo from TMEM
       // (8 columns per step, P_lo 64 columns after P_hi); V N-major: LBO = 16 KB
       // between 64-dim halves, SBO = 1 KB between 8-key groups
       auto issue_pv = [&](int i, int j) {
-        const int s = j % kPfStages;
+        const uint32_t b0 = (uint32_t)dv + (j % kPfVStages) * (kTileBytes >> 4);
+        const uint32_t d = tmem + 256 + i * 128, p = tmem + i * 128;
+        const uint32_t first = j > 0 ? 1u : 0u;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
-          const uint64_t bd = make_sdesc(v_addr + s * kTileBytes + kk * 2048, kHalfTileBytes, 1024);
-          mma_ts((tmem + 256 + i * 128), (tmem + i * 128) + kk * 8, bd, idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
-          mma_ts((tmem + 256 + i * 128), (tmem + i * 128) + 64 + kk * 8, bd, idesc_pv, 1u);
+          const uint32_t bl = b0 + kk * (2048 >> 4);
+          mma_ts_lh(d, p + kk * 8, bl, dv_hi, idesc_pv, kk > 0 ? 1u : first);
+          mma_ts_lh(d, p + 64 + kk * 8, bl, dv_hi, idesc_pv, 1u);
         }
       };
       int k_waited = -1, v_waited = -1;
       auto wait_k = [&](int j) {
         if (ok && j > k_waited) {
-          ok = mbar_wait(&k_full[j % kPfStages], (j / kPfStages) & 1, a.status, a.timeout_ns);
+          ok = mbar_wait(&k_full[j % kPfKStages], (j / kPfKStages) & 1, a.status, a.timeout_ns);
           tc_fence_after();
           k_waited = j;
         }
       };
       auto wait_v = [&](int j) {
         if (ok && j > v_waited) {
-          ok = mbar_wait(&v_full[j % kPfStages], (j / kPfStages) & 1, a.status, a.timeout_ns);
+          ok = mbar_wait(&v_full[j % kPfVStages], (j / kPfVStages) & 1, a.status, a.timeout_ns);
           tc_fence_after();
           v_waited = j;
         }
       };
+      // tile i uses K/V tile j when j < ntile[i]; ntile[1] >= ntile[0] unless Q1 is empty,
+      // so the last user of a tile in issue order is Q1 when Q1 uses it, else Q0
+      auto last_user = [&](int j) { return j < ntile[1] ? 1 : 0; };
+      // Each commit tracks every MMA issued before it, so committing a ring's
+      // "empty" barrier right after the last MMA that reads the stage frees it
+      // as soon as those MMAs finish.
       if (ok && n_kv_tiles > 0) {
         wait_k(0);
         for (int i = 0; i < 2 && ok; ++i)
@@ -303,6 +367,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             issue_s(i, 0);
             tc_commit(&s_full[i]);
           }
+        tc_commit(&k_empty[0]);
       }
       for (int j = 0; j < n_kv_tiles && ok; ++j) {
         for (int i = 0; i < 2 && ok; ++i) {
@@ -313,16 +378,17 @@ __global__ void __launch_bounds__(kPfThreads, 1)
           wait_v(j);
           if (!ok) break;
           issue_pv(i, j);
+          if (i == last_user(j)) tc_commit(&v_empty[j % kPfVStages]);
           if (j + 1 < (i ? ntile[1] : ntile[0])) {
             wait_k(j + 1);
             if (!ok) break;
             issue_s(i, j + 1);
             tc_commit(&s_full[i]);
+            if (i == last_user(j + 1)) tc_commit(&k_empty[(j + 1) % kPfKStages]);
           } else {
             tc_commit(&o_full[i]);
           }
         }
-        tc_commit(&kv_empty[j % kPfStages]);
       }
       // every MMA this lane issued has completed before TMEM can be released
       tc_commit(mma_done);
