@@ -14,6 +14,7 @@ enum : int {
   kDevErrTimeout = 1,      // a bounded wait on an mbarrier gave up
   kDevErrBounds = 2,       // a page / position index failed its device check
   kDevErrTmem = 4,         // tensor-memory allocation returned an unusable address
+  kDevErrRange = 8,        // a cached V value of magnitude >= 65536 met the fp16 P.V product
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -191,6 +192,22 @@ __device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
   uint64_t d;
   asm("sub.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
   return d;
+}
+// fp16 pair (round to nearest even): a in the low half, b in the high half.
+__device__ __forceinline__ uint32_t pack_f16(float a, float b) {
+  uint32_t d;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(b), "f"(a));
+  return d;
+}
+// bf16 pair -> fp16 pair (exact for |x| < 65536; larger magnitudes become inf).
+__device__ __forceinline__ uint32_t bf16x2_to_f16x2(uint32_t x) {
+  return pack_f16(__uint_as_float(x << 16), __uint_as_float(x & 0xffff0000u));
+}
+// Largest bf16 exponent field (bits 14..7 of a half, as 0x0000..0x7f80) among
+// the eight bf16 values of four packed pairs.
+__device__ __forceinline__ uint32_t max_exp_bf16x8(uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  const uint32_t m = __vmaxu2(__vmaxu2(a & 0x7f807f80u, b & 0x7f807f80u), __vmaxu2(c & 0x7f807f80u, d & 0x7f807f80u));
+  return max(m & 0xffffu, m >> 16);
 }
 // bf16 pair holding the upper 16 bits (truncation) of a (low half) and b (high half).
 __device__ __forceinline__ uint32_t trunc_bf16x2(float a, float b) {

@@ -455,6 +455,9 @@ int oomattn_sync(oomattn_ctx* ctx) {
   if (st) {
     CK(cudaMemset(ctx->d_status, 0, sizeof(int)));
     if (st & kDevErrTimeout) return fail(ctx, OOMATTN_ERR_TIMEOUT, "a device-side wait timed out (status %d)", st);
+    if (st & kDevErrRange)
+      return fail(ctx, OOMATTN_ERR_DEVICE_CHECK,
+                  "prefill met a cached V value of magnitude >= 65536, outside the fp16 P.V product (status %d)", st);
     return fail(ctx, OOMATTN_ERR_DEVICE_CHECK, "a device-side index check failed (status %d)", st);
   }
   return OOMATTN_OK;

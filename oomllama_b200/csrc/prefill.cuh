@@ -4,25 +4,27 @@
 // for the n_new newest tokens of one sequence: query i (cache slot
 // P + i, P = cache length before the chunk) sees key slots 0..P+i, scale
 // 1/sqrt(128), GQA grouping h -> h / group.  Scores and softmax statistics are
-// f32; Q, K, V and P enter the tensor cores as bf16 (f32 accumulate).
+// f32.  S = Q K^T runs as bf16 x bf16 (the cache and q are bf16 by contract);
+// O += P V runs as fp16 x fp16 with V converted exactly from bf16 and P
+// rounded to fp16 (11 significant bits), f32 accumulate throughout.
 //
 // CTA work unit: one q head and 256 query rows held as two 128-row tiles
 // (Q0, Q1).  Warp roles (384 threads):
 //   warp 0      TMA producer: Q0/Q1 once, then K_j and V_j (128 keys each,
-//               gathered page by page from the paged pool) into a 2-stage ring
+//               gathered page by page from the paged pool) into a 3-stage K
+//               ring and a 2-stage V ring
 //   warp 1      MMA issuer (one lane): S_i = Q_i K_j^T and O_i += P_i V_j
+//   warps 2-3   rewrite each landed V tile in place from bf16 to fp16
 //   warps 4-7   softmax of tile Q0, warps 8-11 softmax of tile Q1: one query
 //               row per thread, read from TMEM, online softmax with a lazily
 //               rescaled O (only when the running max grows by > 2^8), P
-//               written back into TMEM over the S columns as a bf16 hi/lo pair
-//               (P = P_hi + P_lo; two MMAs keep P's rounding ~2^-17), then the
+//               written back into TMEM over the S columns as fp16, then the
 //               final O / l epilogue
 // The two softmax groups ping-pong: while one computes exponentials the tensor
 // core runs the other tile's MMAs.
 // TMEM (512 columns): S0 [0,128) S1 [128,256) O0 [256,384) O1 [384,512);
-// P_hi of tile i aliases columns [0,64) of S_i and P_lo columns [64,128)
-// (two bf16 per column).
-// Shared memory: Q0, Q1 (2 x 32 KB) + 2 stages x (K 32 KB + V 32 KB), all
+// P of tile i aliases columns [0,64) of S_i (two fp16 per column).
+// Shared memory: Q0, Q1 (2 x 32 KB) + 3 K stages + 2 V stages of 32 KB, all
 // 128-byte swizzled; each operand is two 64-column halves of [128 rows][128 B].
 #pragma once
 #include "common.cuh"
@@ -31,6 +33,7 @@
 namespace oomattn {
 
 constexpr int kPfThreads = 384;
+constexpr int kPfConvThreads = 64;                // warps 2-3 convert V tiles bf16 -> fp16
 constexpr int kPfKStages = 3;                     // K ring: a stage frees once both S MMAs of its tile finish
 constexpr int kPfVStages = 2;                     // V ring: a stage frees once both P.V MMAs finish
 constexpr int kTileBytes = 128 * kHeadDim * 2;    // 32 KB: one 128 x 128 bf16 operand tile
@@ -156,12 +159,14 @@ __device__ __forceinline__ uint64_t make_sdesc(uint32_t saddr, uint32_t lbo_byte
   return d;
 }
 
-// Instruction descriptor, kind::f16: f32 accumulate, bf16 A and B, M = 128,
-// N = 128; b_mn_major selects an N-contiguous B operand (V in P.V).
-__host__ __device__ constexpr uint32_t make_idesc_bf16(bool b_mn_major) {
-  return (1u << 4) | (1u << 7) | (1u << 10) | ((b_mn_major ? 1u : 0u) << 16) | ((128u >> 3) << 17) |
-         ((128u >> 4) << 24);
+// Instruction descriptor, kind::f16: f32 accumulate, A and B both bf16 (or
+// both fp16), M = 128, N = 128; b_mn_major selects an N-contiguous B operand
+// (V in P.V).
+__host__ __device__ constexpr uint32_t make_idesc_f16kind(bool bf16, bool b_mn_major) {
+  return (1u << 4) | ((bf16 ? 1u : 0u) << 7) | ((bf16 ? 1u : 0u) << 10) | ((b_mn_major ? 1u : 0u) << 16) |
+         ((128u >> 3) << 17) | ((128u >> 4) << 24);
 }
+__host__ __device__ constexpr uint32_t make_idesc_bf16(bool b_mn_major) { return make_idesc_f16kind(true, b_mn_major); }
 
 // ------------------------------------------------------------ the kernel
 __global__ void __launch_bounds__(kPfThreads, 1)
@@ -178,7 +183,8 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   uint64_t* k_empty = k_full + kPfKStages;           // [kPfKStages]
   uint64_t* v_full = k_empty + kPfKStages;           // [kPfVStages]
   uint64_t* v_empty = v_full + kPfVStages;           // [kPfVStages]
-  uint64_t* s_full = v_empty + kPfVStages;           // [2]
+  uint64_t* v_conv = v_empty + kPfVStages;           // [kPfVStages]: V stage converted to fp16
+  uint64_t* s_full = v_conv + kPfVStages;            // [2]
   uint64_t* p_full = s_full + 2;                     // [2]
   uint64_t* o_full = p_full + 2;                     // [2]
   uint64_t* mma_done = o_full + 2;
@@ -208,6 +214,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     for (int s = 0; s < kPfVStages; ++s) {
       mbar_init(&v_full[s], 1);
       mbar_init(&v_empty[s], 1);
+      mbar_init(&v_conv[s], kPfConvThreads);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
@@ -302,7 +309,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     OOMATTN_REGS_DEC();
     if (lane == 0) {
       constexpr uint32_t idesc_qk = make_idesc_bf16(false);
-      constexpr uint32_t idesc_pv = make_idesc_bf16(true);
+      constexpr uint32_t idesc_pv = make_idesc_f16kind(false, true);  // P fp16 x V fp16
       bool ok = mbar_wait(q_full, 0, a.status, a.timeout_ns);
       tc_fence_after();
       // Descriptor bases are built once; each MMA only adds a compile-time
@@ -325,19 +332,16 @@ __global__ void __launch_bounds__(kPfThreads, 1)
           mma_ss_lh(d, a0 + off, dq_hi, b0 + off, dk_hi, idesc_qk, kk > 0 ? 1u : 0u);
         }
       };
-      // O_i (+)= (P_hi + P_lo)_i V_j : 8 k-steps of 16 keys; P_hi / P_lo from TMEM
-      // (8 columns per step, P_lo 64 columns after P_hi); V N-major: LBO = 16 KB
-      // between 64-dim halves, SBO = 1 KB between 8-key groups
+      // O_i (+)= P_i V_j in fp16 x fp16 : 8 k-steps of 16 keys; P from TMEM
+      // (8 columns per step); V (converted to fp16 in place) N-major: LBO =
+      // 16 KB between 64-dim halves, SBO = 1 KB between 8-key groups
       auto issue_pv = [&](int i, int j) {
         const uint32_t b0 = (uint32_t)dv + (j % kPfVStages) * (kTileBytes >> 4);
         const uint32_t d = tmem + 256 + i * 128, p = tmem + i * 128;
         const uint32_t first = j > 0 ? 1u : 0u;
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          const uint32_t bl = b0 + kk * (2048 >> 4);
-          mma_ts_lh(d, p + kk * 8, bl, dv_hi, idesc_pv, kk > 0 ? 1u : first);
-          mma_ts_lh(d, p + 64 + kk * 8, bl, dv_hi, idesc_pv, 1u);
-        }
+        for (int kk = 0; kk < 8; ++kk)
+          mma_ts_lh(d, p + kk * 8, b0 + kk * (2048 >> 4), dv_hi, idesc_pv, kk > 0 ? 1u : first);
       };
       int k_waited = -1, v_waited = -1;
       auto wait_k = [&](int j) {
@@ -349,7 +353,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       };
       auto wait_v = [&](int j) {
         if (ok && j > v_waited) {
-          ok = mbar_wait(&v_full[j % kPfVStages], (j / kPfVStages) & 1, a.status, a.timeout_ns);
+          ok = mbar_wait(&v_conv[j % kPfVStages], (j / kPfVStages) & 1, a.status, a.timeout_ns);
           tc_fence_after();
           v_waited = j;
         }
@@ -395,7 +399,34 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       mbar_wait(mma_done, 0, a.status, a.timeout_ns);
     }
   } else if (warp < 4) {
-    OOMATTN_REGS_DEC();  // warps 2-3: no role
+    // ------------------------------------------------ V converters (warps 2-3)
+    // Each V tile lands as bf16; these 64 threads rewrite it in place as fp16
+    // (exact for |v| < 65536) so that P.V runs as an fp16 x fp16 MMA with P
+    // carrying 11 significant bits.  A bf16 value of magnitude >= 65536 has no
+    // fp16 image: it is reported through the status word.
+    OOMATTN_REGS_DEC();
+    const int ct = threadIdx.x - 64;  // 0..63
+    bool ok = true;
+    uint32_t big = 0;
+    for (int j = 0; j < n_kv_tiles && ok; ++j) {
+      const int s = j % kPfVStages;
+      ok = mbar_wait(&v_full[s], (j / kPfVStages) & 1, a.status, a.timeout_ns);
+      if (!ok) break;
+      uint4* tile = reinterpret_cast<uint4*>(sV + s * kTileBytes);
+#pragma unroll 4
+      for (int c = ct; c < kTileBytes / 16; c += kPfConvThreads) {
+        uint4 w = tile[c];
+        big = max(big, max_exp_bf16x8(w.x, w.y, w.z, w.w));
+        w.x = bf16x2_to_f16x2(w.x);
+        w.y = bf16x2_to_f16x2(w.y);
+        w.z = bf16x2_to_f16x2(w.z);
+        w.w = bf16x2_to_f16x2(w.w);
+        tile[c] = w;
+      }
+      fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor core
+      mbar_arrive(&v_conv[s]);
+    }
+    if (big >= 0x4780u) report_error(a.status, kDevErrRange);
   } else {
     // ------------------------------------------------ softmax / epilogue
     OOMATTN_REGS_INC();
@@ -445,36 +476,23 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         m_used = mxs;
         l *= alpha;
       }
-      // P = P_hi + P_lo, both bf16: P_hi (p truncated to bf16) into S columns
-      // [0,64), P_lo = bf16(p - P_hi) into [64,128) (the scores there are already
-      // in registers).  Two bf16 MMAs then carry p to ~16 significant bits, far
-      // below the bf16-KV tolerance.  P_hi is packed in place (step c reads
-      // sr[2c], sr[2c+1], writes sr[c], c <= 2c); P_lo goes to its own array,
-      // so the live set stays near 130 registers.  The scale-and-shift and the
-      // row sum run as packed f32x2 FMA-pipe instructions, the exponential on
-      // the MUFU pipe.
+      // P in fp16 (11 significant bits, 8x finer than bf16; p <= 2^8 after the
+      // lazy rescale, far inside fp16 range) packed in place over the scores
+      // (step c reads sr[2c], sr[2c+1] and writes sr[c], c <= 2c), then stored
+      // into S columns [0,64).  The scale-and-shift and the row sum run as
+      // packed f32x2 FMA-pipe instructions, the exponential on the MUFU pipe.
       const uint64_t cl2 = f2_pack(cl, cl);
       const uint64_t nm2 = f2_pack(-m_used, -m_used);
       uint64_t acc[4] = {0, 0, 0, 0};
 #pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        uint32_t plo[32];
-#pragma unroll
-        for (int cc = 0; cc < 32; ++cc) {
-          const int c = half * 32 + cc;
-          const uint64_t t = f2_fma(f2_pack(__uint_as_float(sr[2 * c]), __uint_as_float(sr[2 * c + 1])), cl2, nm2);
-          const float p0 = ex2_ftz(f2_lo(t)), p1 = ex2_ftz(f2_hi(t));
-          const uint32_t hi = trunc_bf16x2(p0, p1);
-          const uint64_t p2 = f2_pack(p0, p1);
-          const uint64_t rem = f2_sub(p2, f2_pack(__uint_as_float(__float_as_uint(p0) & 0xffff0000u),
-                                                  __uint_as_float(__float_as_uint(p1) & 0xffff0000u)));
-          acc[cc & 3] = f2_add(acc[cc & 3], p2);
-          sr[c] = hi;
-          plo[cc] = pack_bf16(f2_lo(rem), f2_hi(rem));
-        }
-        OOMATTN_TMEM_ST32((tmem + i * 128) + lane_off + half * 32, (sr + half * 32));
-        OOMATTN_TMEM_ST32((tmem + i * 128) + lane_off + 64 + half * 32, plo);
+      for (int c = 0; c < 64; ++c) {
+        const uint64_t t = f2_fma(f2_pack(__uint_as_float(sr[2 * c]), __uint_as_float(sr[2 * c + 1])), cl2, nm2);
+        const float p0 = ex2_ftz(f2_lo(t)), p1 = ex2_ftz(f2_hi(t));
+        acc[c & 3] = f2_add(acc[c & 3], f2_pack(p0, p1));
+        sr[c] = pack_f16(p0, p1);
       }
+      OOMATTN_TMEM_ST32((tmem + i * 128) + lane_off + 0, (sr + 0));
+      OOMATTN_TMEM_ST32((tmem + i * 128) + lane_off + 32, (sr + 32));
       const uint64_t acc2 = f2_add(f2_add(acc[0], acc[1]), f2_add(acc[2], acc[3]));
       l += f2_lo(acc2) + f2_hi(acc2);
       if (__any_sync(0xffffffffu, need)) {
