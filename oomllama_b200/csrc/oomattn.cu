@@ -302,6 +302,35 @@ AppendArgs base_append_args(oomattn_ctx* ctx, int layer, int n_new) {
   return ap;
 }
 
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Vectorised K-A epilogue over T tokens (one template instance per input /
+// q-output / cache dtype combination).
+int launch_rope_append(oomattn_ctx* ctx, const AppendArgs& ap, const SeqBatch& sb, int T) {
+  const void* ptrs[] = {ap.q, ap.k, ap.v, ap.q_out, ap.bq, ap.bk, ap.bv};
+  for (const void* p : ptrs)
+    if (p && !aligned16(p)) return fail(ctx, OOMATTN_ERR_INVALID_ARG, "tensors and biases must be 16-byte aligned");
+  const int hq = ctx->cfg.n_heads, hkv = ctx->cfg.n_kv_heads;
+  const long long units = (long long)T * ((hq + 2 * hkv) * 8 - (ap.q ? 0 : hq * 8));
+  const int grid = (int)std::max<long long>(1, std::min<long long>((units + 255) / 256, (long long)ctx->num_sms * 16));
+  const KVPool pool = make_pool(ctx);
+  const int combo = (ap.in_bf16 ? 4 : 0) | (ap.q_out_bf16 ? 2 : 0) | (pool.kv_bf16 ? 1 : 0);
+#define OOMATTN_RA(I, Q, K) rope_append_kernel<I, Q, K><<<grid, 256, 0, ctx->stream>>>(ap, pool, sb, T)
+  switch (combo) {
+    case 0: OOMATTN_RA(false, false, false); break;
+    case 1: OOMATTN_RA(false, false, true); break;
+    case 2: OOMATTN_RA(false, true, false); break;
+    case 3: OOMATTN_RA(false, true, true); break;
+    case 4: OOMATTN_RA(true, false, false); break;
+    case 5: OOMATTN_RA(true, false, true); break;
+    case 6: OOMATTN_RA(true, true, false); break;
+    default: OOMATTN_RA(true, true, true); break;
+  }
+#undef OOMATTN_RA
+  CKLAUNCH();
+  return OOMATTN_OK;
+}
+
 int launch_decode_rows(oomattn_ctx* ctx, int layer, const SeqBatch& sb, const float* q, float* out, float* lse) {
   const int n_kv = ctx->cfg.n_kv_heads;
   long long unit_pages = 0;
@@ -537,7 +566,8 @@ int oomattn_kv_write(oomattn_ctx* ctx, int32_t layer, int32_t seq, const void* k
   ap.in_bf16 = src_dtype == OOMATTN_DTYPE_BF16;
   ap.rope_k = 0;  // K is stored as given: no rotation
   DeviceGuard dg(ctx->device);
-  rope_append_kernel<<<n, 256, 0, ctx->stream>>>(ap, make_pool(ctx), sb);
+  rc = launch_rope_append(ctx, ap, sb, n);
+  if (rc) return rc;
   CKLAUNCH();
   commit_append(ctx, layer, sb, n);
   return OOMATTN_OK;
@@ -617,7 +647,8 @@ int oomattn_rope_append(oomattn_ctx* ctx, int32_t layer, int32_t n_seqs, const i
     ap.bq = bq;
     ap.bk = bk;
     ap.bv = bv;
-    rope_append_kernel<<<n * n_new, 256, 0, ctx->stream>>>(ap, make_pool(ctx), sb);
+    rc = launch_rope_append(ctx, ap, sb, n * n_new);
+    if (rc) return rc;
     CKLAUNCH();
     commit_append(ctx, layer, sb, n_new);
   }

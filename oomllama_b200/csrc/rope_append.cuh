@@ -85,30 +85,120 @@ __device__ __forceinline__ void emit_pair(const AppendArgs& ap, const KVPool& po
   }
 }
 
-// Epilogue-only K-A.  grid.x = T tokens, block = 256 threads.
-__global__ void __launch_bounds__(256)
-    rope_append_kernel(const AppendArgs ap, const KVPool pool, const __grid_constant__ SeqBatch sb) {
-  const int t = blockIdx.x;
-  const int nq = ap.n_heads * 64, nk = pool.n_kv * 64;
-  const int total = nq + 2 * nk;
-  const int first = ap.q ? 0 : nq;  // no q: K/V rows only
-  for (int item = first + threadIdx.x; item < total; item += blockDim.x) {
-    const int sec = item < nq ? 0 : (item < nq + nk ? 1 : 2);
-    const int local = sec == 0 ? item : (sec == 1 ? item - nq : item - nq - nk);
-    const int head = local / 64, i = local % 64;
-    const int i0 = (ap.variant == 1 || sec == 2) ? 2 * i : i;
-    const int i1 = (ap.variant == 1 || sec == 2) ? 2 * i + 1 : i + 64;
-    const void* src = sec == 0 ? ap.q : (sec == 1 ? ap.k : ap.v);
-    const int nh = sec == 0 ? ap.n_heads : pool.n_kv;
-    const size_t base = ((size_t)t * nh + head) * kHeadDim;
-    float x0 = load_elem(src, base + i0, ap.in_bf16);
-    float x1 = load_elem(src, base + i1, ap.in_bf16);
-    const float* b = sec == 0 ? ap.bq : (sec == 1 ? ap.bk : ap.bv);
-    if (b) {
-      x0 = __fadd_rn(x0, b[head * kHeadDim + i0]);
-      x1 = __fadd_rn(x1, b[head * kHeadDim + i1]);
+// 8 consecutive elements of a bf16 or f32 row as f32 (one or two 128-bit loads).
+template <bool BF16>
+__device__ __forceinline__ void load8(const void* p, size_t i, float* x) {
+  if (BF16) {
+    const uint4 w = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(p) + i);
+    const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      x[2 * k] = bf16_lo_f32(u[k]);
+      x[2 * k + 1] = bf16_hi_f32(u[k]);
     }
-    emit_pair(ap, pool, sb, t, item, x0, x1);
+  } else {
+    const float4 a = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p) + i);
+    const float4 b = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p) + i + 4);
+    x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w; x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
+  }
+}
+
+template <bool BF16>
+__device__ __forceinline__ void store8(void* p, size_t i, const float* x) {
+  if (BF16) {
+    uint4 w;
+    w.x = pack_bf16(x[0], x[1]);
+    w.y = pack_bf16(x[2], x[3]);
+    w.z = pack_bf16(x[4], x[5]);
+    w.w = pack_bf16(x[6], x[7]);
+    *reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(p) + i) = w;
+  } else {
+    *reinterpret_cast<float4*>(reinterpret_cast<float*>(p) + i) = make_float4(x[0], x[1], x[2], x[3]);
+    *reinterpret_cast<float4*>(reinterpret_cast<float*>(p) + i + 4) = make_float4(x[4], x[5], x[6], x[7]);
+  }
+}
+
+__device__ __forceinline__ void add_bias8(float* x, const float* b) {
+  const float4 u = *reinterpret_cast<const float4*>(b), v = *reinterpret_cast<const float4*>(b + 4);
+  x[0] = __fadd_rn(x[0], u.x); x[1] = __fadd_rn(x[1], u.y); x[2] = __fadd_rn(x[2], u.z); x[3] = __fadd_rn(x[3], u.w);
+  x[4] = __fadd_rn(x[4], v.x); x[5] = __fadd_rn(x[5], v.y); x[6] = __fadd_rn(x[6], v.z); x[7] = __fadd_rn(x[7], v.w);
+}
+
+// Epilogue-only K-A, vectorised.  A unit is 16 elements of one head that close
+// under the RoPE pairing -- 8 pairs i = 8c..8c+7:
+//   interleaved: elements [16c, 16c+16) (pair i = (2i, 2i+1))
+//   split-half:  elements [8c, 8c+8) and [64+8c, 64+8c+8) (pair i = (i, i+64))
+//   V:           elements [16c, 16c+16), copied
+// so every thread moves 128-bit vectors and reads its 8 cos/sin values as two
+// float4s.  The rotation arithmetic is rope_pair's, bit for bit.
+// grid-stride over T tokens x (n_heads + 2 n_kv) heads x 8 units.
+template <bool IN_BF16, bool Q_BF16, bool KV_BF16>
+__global__ void __launch_bounds__(256)
+    rope_append_kernel(const AppendArgs ap, const KVPool pool, const __grid_constant__ SeqBatch sb, int T) {
+  const int hq = ap.n_heads, hkv = pool.n_kv;
+  const int units_tok = (hq + 2 * hkv) * 8;
+  const int first = ap.q ? 0 : hq * 8;  // no q: K/V rows only
+  const int per_tok = units_tok - first;
+  const long long total = (long long)T * per_tok;
+  for (long long w = blockIdx.x * (long long)blockDim.x + threadIdx.x; w < total;
+       w += (long long)gridDim.x * blockDim.x) {
+    const int t = (int)(w / per_tok);
+    const int u = first + (int)(w % per_tok);
+    const int sec = u < hq * 8 ? 0 : (u < (hq + hkv) * 8 ? 1 : 2);
+    const int lu = sec == 0 ? u : (sec == 1 ? u - hq * 8 : u - (hq + hkv) * 8);
+    const int head = lu >> 3, c = lu & 7;
+    const bool split = ap.variant == 0 && sec < 2;
+    const int e0 = split ? 8 * c : 16 * c;         // first element of the first 8
+    const int e1 = split ? 64 + 8 * c : 16 * c + 8;  // first element of the second 8
+    const void* src = sec == 0 ? ap.q : (sec == 1 ? ap.k : ap.v);
+    const size_t base = ((size_t)t * (sec == 0 ? hq : hkv) + head) * kHeadDim;
+    float a[8], b[8];
+    load8<IN_BF16>(src, base + e0, a);
+    load8<IN_BF16>(src, base + e1, b);
+    const float* bias = sec == 0 ? ap.bq : (sec == 1 ? ap.bk : ap.bv);
+    if (bias) {
+      add_bias8(a, bias + head * kHeadDim + e0);
+      add_bias8(b, bias + head * kHeadDim + e1);
+    }
+    const int row = t / ap.n_new, s = t % ap.n_new;
+    if (sec == 0 || (sec == 1 && ap.rope_k)) {
+      const int pos = sb.pos[row] + s;
+      if ((unsigned)pos >= (unsigned)ap.max_pos) {
+        report_error(ap.status, kDevErrBounds);
+        continue;
+      }
+      const float4* cp = reinterpret_cast<const float4*>(ap.cos_t + (size_t)pos * 64 + 8 * c);
+      const float4* sp = reinterpret_cast<const float4*>(ap.sin_t + (size_t)pos * 64 + 8 * c);
+      const float4 c0 = cp[0], c1 = cp[1], s0 = sp[0], s1 = sp[1];
+      const float cs[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+      const float sn[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+      if (split) {
+        // pair k: (a[k], b[k])
+#pragma unroll
+        for (int k = 0; k < 8; ++k) rope_pair(a[k], b[k], cs[k], sn[k], a[k], b[k]);
+      } else {
+        // pairs 0..3 in a (a[2k], a[2k+1]), pairs 4..7 in b
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          rope_pair(a[2 * k], a[2 * k + 1], cs[k], sn[k], a[2 * k], a[2 * k + 1]);
+          rope_pair(b[2 * k], b[2 * k + 1], cs[k + 4], sn[k + 4], b[2 * k], b[2 * k + 1]);
+        }
+      }
+    }
+    if (sec == 0) {
+      const size_t o = ((size_t)t * hq + head) * kHeadDim;
+      store8<Q_BF16>(ap.q_out, o + e0, a);
+      store8<Q_BF16>(ap.q_out, o + e1, b);
+    } else {
+      size_t off;
+      if (!cache_offset(pool, ap.layer, sb.seq[row], sb.len[row] + s, head, off)) {
+        report_error(ap.status, kDevErrBounds);
+        continue;
+      }
+      void* dst = sec == 1 ? pool.k : pool.v;
+      store8<KV_BF16>(dst, off + e0, a);
+      store8<KV_BF16>(dst, off + e1, b);
+    }
   }
 }
 

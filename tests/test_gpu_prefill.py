@@ -64,6 +64,23 @@ def test_prefill_full_size_sampled_rows(oracle):
     assert_close(out, ref, BF16_ATOL, BF16_RTOL, what="prefill 4096 sampled rows")
 
 
+def test_prefill_reports_v_outside_fp16_range():
+    # P.V runs in fp16; a cached V of magnitude >= 65536 has no fp16 image and
+    # must surface as a device-check error, not as a silent inf.
+    from oomllama_b200._lib import OomAttnError
+    eng = make_engine(28, 4, [128], kv_dtype="bf16")
+    k = randn((128, 4, 128), 1, torch.bfloat16)
+    v = randn((128, 4, 128), 2, torch.bfloat16)
+    v[5, 1, 7] = 70000.0
+    eng.kv_write(0, 0, k.cuda(), v.cuda())
+    eng.prefill(0, 0, randn((128, 28, 128), 3, torch.bfloat16).cuda())
+    with pytest.raises(OomAttnError) as e:
+        eng.sync()
+    assert e.value.code == 9
+    eng.sync()  # the status word is cleared after it is reported
+    eng.close()
+
+
 def test_prefill_rejects_f32_cache():
     from oomllama_b200._lib import OomAttnError
     eng = make_engine(28, 4, [32], kv_dtype="f32")
