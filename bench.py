@@ -40,9 +40,10 @@ sys.path.insert(0, ROOT)
 S_PREFILL, HQ, HKV, D = 4096, 28, 4, 128
 PREFILL_FLOPS = 4 * D * HQ * S_PREFILL * (S_PREFILL + 1) // 2   # 120,288,444,416 per sequence
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
-# dram__bytes_read.sum + dram__bytes_write.sum per launch from ncu captures of
-# this workload (summaries in profiles/); None until captured.
-NCU_TRAFFIC_BYTES = {"prefill_bf16_kernel": None, "decode_bf16_kernel": None}
+# dram__bytes_read.sum + dram__bytes_write.sum per launch from one ncu capture
+# of each kernel on these workloads (profiles/prefill_bf16_kernel_qwen7b_s4096.md,
+# profiles/decode_bf16_kernel_llama8b_ctx32k.md).
+NCU_TRAFFIC_BYTES = {"prefill_bf16_kernel": 37_828_096 + 6_703_360, "decode_bf16_kernel": 1_074_328_000 + 5_611_008}
 
 
 def parse():
@@ -469,7 +470,8 @@ def main():
                 "bytes_per_step": r["total_bytes"], "split_context_merge": r["merge"],
                 "roofline": {"bound": "hbm", "kernel": "decode_bf16_kernel", "achieved": kern_gbs,
                              "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": kern_gbs / peaks["hbm_gbs"],
-                             "traffic": NCU_TRAFFIC_BYTES["decode_bf16_kernel"]},
+                             "traffic": NCU_TRAFFIC_BYTES["decode_bf16_kernel"] if name == "llama-32k" and W == 1
+                             else None},
             }
         line["decode"] = dec
     if dist_.rank == 0 and W == 1 and not args.no_cpu_baseline:
