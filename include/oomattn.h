@@ -184,6 +184,36 @@ int oomattn_decode(oomattn_ctx* ctx, int32_t layer, int32_t n_rows, const int32_
 int oomattn_merge_partials(oomattn_ctx* ctx, int32_t n_parts, int32_t n_rows, const float* parts, const float* lses,
                            float* out, float* lse_out);
 
+/* Decode for callers that cannot allocate device memory.  No counterpart in
+ * the reference.  Some hosts cannot call cudaMalloc while decoding: their
+ * device memory belongs to another allocator (a serving arena, a framework
+ * that hands a plugin only tensors), or an allocation in their token loop
+ * could synchronise the GPU or fail under memory pressure.  This entry point
+ * needs no context and allocates nothing: it runs the split-KV decode kernels
+ * over the caller's own paged K/V memory and keeps the split partials in a
+ * fixed 8.1 MiB array inside the library's device image (every GPU that loads
+ * the library holds one copy until the process exits).
+ *   device, stream: the GPU and cudaStream_t to run on
+ *   kv_dtype: OOMATTN_DTYPE_BF16 or OOMATTN_DTYPE_F32
+ *   k_pool, v_pool: [n_pool_pages][n_kv_heads][16][128] in kv_dtype, 16-byte aligned
+ *   block_table: device int32 [*][max_pages_per_seq]; every page id a row
+ *     reaches must be < n_pool_pages (ids are not validated on the host)
+ *   q, out: f32 [n_rows][n_heads][128]; lse: f32 [n_rows][n_heads] or NULL
+ *   seq_ids, lens (host): row z attends to the first lens[z] slots of block-table row seq_ids[z]
+ *   errbuf (host, optional): receives a message when the call fails
+ * Limits: n_rows <= 128, n_kv_heads <= 64, n_heads / n_kv_heads <= 8; larger
+ * requests return OOMATTN_ERR_OUT_OF_RANGE.  The split count is capped so
+ * that n_rows * n_heads * splits <= 16384.  The first call on a device looks
+ * up the array's address and must come before any stream capture on that
+ * device.  All calls on a device share the array: calls whose GPU work
+ * overlaps (different streams, other host threads) race and must be ordered
+ * by the caller. */
+int oomattn_decode_static_scratch(int device, void* stream, int32_t kv_dtype, const void* k_pool, const void* v_pool,
+                                  int32_t n_pool_pages, const int32_t* block_table, int32_t max_pages_per_seq,
+                                  int32_t n_heads, int32_t n_kv_heads, float softmax_scale, int32_t n_rows,
+                                  const int32_t* seq_ids /* host */, const int32_t* lens /* host */, const float* q,
+                                  float* out, float* lse, char* errbuf /* host, may be NULL */, int32_t errbuf_len);
+
 /* ---------------------------------------------------------------- K-C */
 
 /* Causal prefill of the n_new newest tokens of `seq` (bf16 cache only):

@@ -25,7 +25,7 @@ EXPORTS = (
     "oomattn_sync", "oomattn_reset", "oomattn_seq_len", "oomattn_set_block_table", "oomattn_set_position_offset",
     "oomattn_set_seq_len", "oomattn_kv_pool", "oomattn_kv_write", "oomattn_kv_read", "oomattn_rope_table",
     "oomattn_compute_rope_table", "oomattn_rope_append", "oomattn_qkv_rope_append", "oomattn_decode", "oomattn_merge_partials",
-    "oomattn_prefill", "oomattn_attention_forward_with_bias",
+    "oomattn_prefill", "oomattn_attention_forward_with_bias", "oomattn_decode_static_scratch",
 )
 
 
@@ -83,6 +83,8 @@ def load():
         "oomattn_merge_partials": ([P, I, I, P, P, P, P], ctypes.c_int),
         "oomattn_prefill": ([P, I, I, I, P, P, I, P], ctypes.c_int),
         "oomattn_attention_forward_with_bias": ([P, I, I, I, P, P, P, P, P, I, P, P, P, P], ctypes.c_int),
+        "oomattn_decode_static_scratch": ([ctypes.c_int, P, I, P, P, I, P, I, I, I, F, I, IP, IP, P, P, P,
+                                           ctypes.c_char_p, I], ctypes.c_int),
     }
     for name, (args, res) in sig.items():
         fn = getattr(L, name)

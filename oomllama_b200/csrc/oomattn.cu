@@ -896,3 +896,187 @@ int oomattn_attention_forward_with_bias(oomattn_ctx* ctx, int32_t layer, int32_t
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Decode with no device allocation.
+//
+// Some callers cannot call cudaMalloc on the decode path: a host whose device
+// memory is owned by another allocator (an inference server's pooled arena, a
+// framework plugin that is handed only tensors), or a latency-critical loop in
+// which an allocation could synchronise the device or fail under memory
+// pressure.  oomattn_decode_static_scratch serves them: it runs the same
+// split-KV decode kernels over KV memory the caller owns, and keeps the
+// split-KV partials in a fixed array that is part of this library's device
+// image instead of in allocated scratch.  It creates no context and calls no
+// allocating routine (no cudaMalloc, cudaFree, cuBLAS or torch).
+// ---------------------------------------------------------------------------
+#include <mutex>
+
+namespace {
+
+constexpr int kStaticPartSlots = 16384;  // (row, q head, split) partials held at once
+constexpr int kStaticMaxKv = 64;         // kv heads per launch covered by the counters
+constexpr size_t kStaticPartOBytes = (size_t)kStaticPartSlots * kHeadDim * sizeof(float);  // 8 MiB
+constexpr size_t kStaticPartLseBytes = (size_t)kStaticPartSlots * sizeof(float);          // 64 KiB
+constexpr size_t kStaticCounterBytes = (size_t)kMaxBatch * kStaticMaxKv * sizeof(unsigned);  // 32 KiB
+constexpr size_t kStaticScratchBytes = kStaticPartOBytes + kStaticPartLseBytes + kStaticCounterBytes;
+constexpr int kStaticMaxDevices = 64;
+
+// The scratch: every GPU that loads this library holds one copy until the
+// process exits.  All calls on a device share it.
+static __device__ __align__(256) unsigned char g_decode_scratch[kStaticScratchBytes];
+
+std::mutex g_static_mu;
+void* g_static_scratch[kStaticMaxDevices] = {};
+
+int static_fail(char* buf, int32_t len, int code, const char* fmt, ...) {
+  if (buf && len > 0) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, (size_t)len, fmt, ap);
+    va_end(ap);
+  }
+  return code;
+}
+
+}  // namespace
+
+extern "C" int oomattn_decode_static_scratch(int device, void* stream, int32_t kv_dtype, const void* k_pool,
+                                             const void* v_pool, int32_t n_pool_pages, const int32_t* block_table,
+                                             int32_t max_pages_per_seq, int32_t n_heads, int32_t n_kv_heads,
+                                             float softmax_scale, int32_t n_rows, const int32_t* seq_ids,
+                                             const int32_t* lens, const float* q, float* out, float* lse,
+                                             char* errbuf, int32_t errbuf_len) {
+  if (errbuf && errbuf_len > 0) errbuf[0] = '\0';
+  if (!k_pool || !v_pool || !block_table || !seq_ids || !lens || !q || !out)
+    return static_fail(errbuf, errbuf_len, OOMATTN_ERR_INVALID_ARG, "null pointer argument");
+  if (kv_dtype != OOMATTN_DTYPE_F32 && kv_dtype != OOMATTN_DTYPE_BF16)
+    return static_fail(errbuf, errbuf_len, OOMATTN_ERR_INVALID_ARG, "unknown kv dtype %d", kv_dtype);
+  if (device < 0 || device >= kStaticMaxDevices)
+    return static_fail(errbuf, errbuf_len, OOMATTN_ERR_OUT_OF_RANGE, "device %d outside [0, %d)", device,
+                       kStaticMaxDevices);
+  if (n_heads <= 0 || n_kv_heads <= 0 || n_heads % n_kv_heads || n_heads / n_kv_heads > kMaxGroup)
+    return static_fail(errbuf, errbuf_len, OOMATTN_ERR_BAD_CONFIG, "n_heads %d / n_kv_heads %d unsupported",
+                       n_heads, n_kv_heads);
+  if (n_rows <= 0 || n_rows > kMaxBatch)
+    return static_fail(errbuf, errbuf_len, OOMATTN_ERR_OUT_OF_RANGE,
+                       "n_rows %d outside [1, %d]: the static scratch serves at most %d rows per call", n_rows,
+                       kMaxBatch, kMaxBatch);
+  if (n_kv_heads > kStaticMaxKv)
+    return static_fail(errbuf, errbuf_len, OOMATTN_ERR_OUT_OF_RANGE,
+                       "n_kv_heads %d exceeds the static scratch's %d", n_kv_heads, kStaticMaxKv);
+  if (n_pool_pages <= 0 || max_pages_per_seq <= 0 ||
+      (long long)n_pool_pages * n_kv_heads * kPageSize >= (1ll << 31))
+    return static_fail(errbuf, errbuf_len, OOMATTN_ERR_OUT_OF_RANGE, "pool of %d pages unsupported", n_pool_pages);
+  if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(out)) & 15u)
+    return static_fail(errbuf, errbuf_len, OOMATTN_ERR_INVALID_ARG, "q and out must be 16-byte aligned");
+  int max_pages = 0;
+  long long unit_pages = 0;
+  SeqBatch sb;
+  sb.n = n_rows;
+  for (int z = 0; z < n_rows; ++z) {
+    if (lens[z] < 0 || lens[z] > max_pages_per_seq * kPageSize)
+      return static_fail(errbuf, errbuf_len, OOMATTN_ERR_OUT_OF_RANGE, "row %d: length %d outside [0, %d]", z,
+                         lens[z], max_pages_per_seq * kPageSize);
+    if (seq_ids[z] < 0)
+      return static_fail(errbuf, errbuf_len, OOMATTN_ERR_OUT_OF_RANGE, "row %d: negative sequence id", z);
+    sb.seq[z] = seq_ids[z];
+    sb.len[z] = lens[z];
+    sb.pos[z] = 0;
+    const int pages = (lens[z] + kPageSize - 1) / kPageSize;
+    max_pages = std::max(max_pages, pages);
+    unit_pages += (long long)pages * n_kv_heads;
+  }
+
+  DeviceGuard dg(device);
+  int num_sms = 148;
+  cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, device);
+  void* scratch = nullptr;
+  {
+    // Set-up, once per device with that device current: the array's device
+    // address (its name in host code is only a host-side stand-in) and the
+    // decode kernel's shared-memory limit.
+    std::lock_guard<std::mutex> lock(g_static_mu);
+    if (!g_static_scratch[device]) {
+      void* p = nullptr;
+      cudaError_t e = cudaGetSymbolAddress(&p, g_decode_scratch);
+      if (e != cudaSuccess || !p)
+        return static_fail(errbuf, errbuf_len, OOMATTN_ERR_CUDA, "cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+      e = cudaFuncSetAttribute(decode_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kDecSmemBytes);
+      if (e != cudaSuccess)
+        return static_fail(errbuf, errbuf_len, OOMATTN_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+      g_static_scratch[device] = p;
+    }
+    scratch = g_static_scratch[device];
+  }
+  float* part_o = reinterpret_cast<float*>(scratch);
+  float* part_lse = reinterpret_cast<float*>(static_cast<unsigned char*>(scratch) + kStaticPartOBytes);
+  unsigned* counters =
+      reinterpret_cast<unsigned*>(static_cast<unsigned char*>(scratch) + kStaticPartOBytes + kStaticPartLseBytes);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+
+  // Split plan as in oomattn_decode, capped so that every (row, q head, split)
+  // partial fits the static array: nsplit <= slots / (rows * heads).
+  const int cap_splits = std::max(1, kStaticPartSlots / (n_rows * n_heads));
+  long long target = (unit_pages + (long long)num_sms * 8 - 1) / ((long long)num_sms * 8);
+  int pps = (int)std::max<long long>(8, (target + 3) / 4 * 4);
+  pps = std::max(pps, (max_pages + cap_splits - 1) / cap_splits);
+  const int nsplit = std::max(1, (max_pages + pps - 1) / pps);
+
+  // The counters must start at zero; a previous call that ended early could
+  // have left some set, so they are cleared on every call.
+  cudaError_t e = cudaMemsetAsync(counters, 0, (size_t)n_rows * n_kv_heads * sizeof(unsigned), st);
+  if (e != cudaSuccess)
+    return static_fail(errbuf, errbuf_len, OOMATTN_ERR_CUDA, "cudaMemsetAsync: %s", cudaGetErrorString(e));
+
+  KVPool pool;
+  pool.k = const_cast<void*>(k_pool);
+  pool.v = const_cast<void*>(v_pool);
+  pool.block_table = block_table;
+  pool.max_pages_per_seq = max_pages_per_seq;
+  pool.n_pool_pages = n_pool_pages;
+  pool.n_kv = n_kv_heads;
+  pool.kv_bf16 = kv_dtype == OOMATTN_DTYPE_BF16;
+  DecodeArgs a;
+  a.q = q;
+  a.out = out;
+  a.lse = lse;
+  a.layer = 0;
+  a.n_heads = n_heads;
+  a.group = n_heads / n_kv_heads;
+  a.pages_per_split = pps;
+  a.max_splits = nsplit;
+  a.qscale = (softmax_scale > 0.f ? softmax_scale : 1.0f / sqrtf((float)kHeadDim)) * 1.4426950408889634f;
+  a.part_o = part_o;
+  a.part_lse = part_lse;
+  a.counters = counters;
+  a.status = nullptr;
+  a.timeout_ns = kDefaultTimeoutNs;
+  dim3 grid(nsplit, n_kv_heads, n_rows);
+  if (pool.kv_bf16) {
+    // Tensor maps are encoded on the host into kernel parameters: no allocation.
+    EncodeTiledFn enc = get_encode_fn();
+    if (!enc) return static_fail(errbuf, errbuf_len, OOMATTN_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+    CUtensorMap maps[2];
+    const void* bases[2] = {k_pool, v_pool};
+    for (int m = 0; m < 2; ++m) {
+      cuuint64_t dims[2] = {(cuuint64_t)kHeadDim, (cuuint64_t)n_pool_pages * n_kv_heads * kPageSize};
+      cuuint64_t strides[1] = {(cuuint64_t)kHeadDim * 2};
+      cuuint32_t box[2] = {64, (cuuint32_t)kPageSize};
+      cuuint32_t estr[2] = {1, 1};
+      CUresult r = enc(&maps[m], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(bases[m]), dims, strides,
+                       box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                       CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+      if (r != CUDA_SUCCESS)
+        return static_fail(errbuf, errbuf_len, OOMATTN_ERR_INVALID_ARG,
+                           "pool pointer rejected by cuTensorMapEncodeTiled (%d): it must be 16-byte aligned", (int)r);
+    }
+    decode_bf16_kernel<<<grid, (kDecWarps + 1) * 32, kDecSmemBytes, st>>>(maps[0], maps[1], pool, a, sb);
+  } else {
+    decode_f32_kernel<<<grid, kDecWarps * 32, 0, st>>>(pool, a, sb);
+  }
+  e = cudaGetLastError();
+  if (e != cudaSuccess)
+    return static_fail(errbuf, errbuf_len, OOMATTN_ERR_CUDA, "kernel launch: %s", cudaGetErrorString(e));
+  return OOMATTN_OK;
+}
