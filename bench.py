@@ -274,16 +274,12 @@ def bench_decode(args, dist_, torch, name):
         hq, hkv, B, variant, theta = 28, 4, 64, "interleaved", 1e6
         lens = np.random.default_rng(2).integers(1024, 8193, size=B).tolist()
         lens = [L + 1 for L in lens]  # cached tokens + the new one
-    groups = min(W, hkv)              # kv-head groups
-    ctx_split = W // groups           # context slices when GPUs > kv heads
-    grp, cs = r // ctx_split, r % ctx_split
-    l_hkv, l_hq = hkv // groups, hq // groups
-    # this rank's slice of every sequence: whole pages [c0, c1)
-    slices = []
-    for L in lens:
-        pages = -(-L // 16)
-        p0, p1 = pages * cs // ctx_split, pages * (cs + 1) // ctx_split
-        slices.append((p0 * 16, min(L, p1 * 16)))
+    from oomllama_b200.shard import DecodeShardPlan, gather_partials, new_group_comms
+    plan = DecodeShardPlan(hq, hkv, W, r)
+    ctx_split = plan.ctx_split
+    l_hkv, l_hq = len(plan.kv_heads), len(plan.q_heads)
+    # this rank's slice of every sequence: whole pages
+    slices = [plan.context_slice(L) for L in lens]
     local = [b - a for a, b in slices]
     n_pages = sum(-(-x // 16) for x in local)
     cfg = TurboConfig(n_layers=1, hidden_size=0, n_heads=l_hq, n_kv_heads=l_hkv, max_seq_len=max(lens) + 16,
@@ -306,15 +302,10 @@ def bench_decode(args, dist_, torch, name):
     outb = torch.empty(B, l_hq, D, device="cuda")
     lse = torch.empty(B, l_hq, device="cuda")
     merge = ctx_split > 1
-    if merge:
+    comm = None
+    if dist_.pg:
         import torch.distributed as tdist
-        gparts = torch.empty(W, B * l_hq * D, device="cuda")
-        glses = torch.empty(W, B * l_hq, device="cuda")
-        sub = None  # ranks of this kv-head group gather each other's partials
-        groups_pg = [tdist.new_group(list(range(g_ * ctx_split, (g_ + 1) * ctx_split))) for g_ in range(groups)]
-        sub = groups_pg[grp]
-        gparts = torch.empty(ctx_split, B * l_hq * D, device="cuda")
-        glses = torch.empty(ctx_split, B * l_hq, device="cuda")
+        comm = new_group_comms(plan, tdist)[plan.group]  # every rank creates every group, in order
 
     def step(ev=None):
         if ev is not None:
@@ -323,10 +314,10 @@ def bench_decode(args, dist_, torch, name):
         if ev is not None:
             ev[1].record()
         if merge:
+            # K-D: all-gather the group's (O, lse) partials over NCCL, then the K-B2 merge
             import torch.distributed as tdist
-            tdist.all_gather_into_tensor(gparts, outb.view(-1), group=sub)
-            tdist.all_gather_into_tensor(glses, lse.view(-1), group=sub)
-            eng.merge_partials(gparts.view(ctx_split, B * l_hq, D), glses)
+            parts, lses = gather_partials(outb, lse, plan, tdist, comm)
+            eng.merge_partials(parts, lses)
 
     steps = max(5, args.steps)
     for _ in range(args.warmup):
@@ -363,7 +354,7 @@ def cpu_prefill_sample(seconds_budget=8.0, threads=None):
     q = rng.standard_normal((S_PREFILL, HQ, D), dtype=np.float32)
     k = rng.standard_normal((HKV, S_PREFILL, D), dtype=np.float32)
     v = rng.standard_normal((HKV, S_PREFILL, D), dtype=np.float32)
-    nt = O.omp_max_threads() if threads is None else threads
+    nt = O.set_threads(O.host_cores() if threads is None else threads)
     n_pairs = 64 * nt
     while True:
         rows = rng.integers(0, S_PREFILL, n_pairs).astype(np.int32)
@@ -386,7 +377,7 @@ def reference_arm(args):
         return
     from oracle import oracle as O
     O.build()
-    nt = O.omp_max_threads()
+    nt = O.set_threads(O.host_cores())
     rng = np.random.default_rng(0)
     q = rng.standard_normal((S_PREFILL, HQ, D), dtype=np.float32)
     k = rng.standard_normal((HKV, S_PREFILL, D), dtype=np.float32)

@@ -1,5 +1,5 @@
 // Shared device helpers for the sm_100a attention kernels: mbarriers with
-// bounded waits, TMA tile loads (no multicast), legacy-MMA fragments for the
+// bounded waits, TMA tile loads into the issuing CTA only, legacy-MMA fragments for the
 // decode path, bf16 packing, and the error-status word every kernel reports to.
 #pragma once
 #include <cuda.h>
@@ -86,7 +86,8 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* s
 // ---------------------------------------------------------------- TMA loads
 // 2D tiled bulk-tensor load into this CTA's shared memory, completing on `bar`.
 // x is the innermost coordinate; callers keep x * element size a multiple of
-// 16 bytes.  No multicast form is used anywhere in this library.
+// 16 bytes.  Every TMA load in this library lands in the issuing CTA's own
+// shared memory and reads this GPU's own memory.
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(

@@ -307,6 +307,16 @@ void oracle_layer_attention(const float* x, int B, int S, int H, const float* wq
     free(vt);
 }
 
+/* Host threads used by the OpenMP loops (launchers such as torchrun preset
+ * OMP_NUM_THREADS=1 per process). */
+void oracle_set_threads(int n) {
+#ifdef _OPENMP
+    if (n > 0) omp_set_num_threads(n);
+#else
+    (void)n;
+#endif
+}
+
 int oracle_omp_max_threads(void) {
 #ifdef _OPENMP
     return omp_get_max_threads();

@@ -226,3 +226,19 @@ def bf16_bits_to_f32(h):
 
 def omp_max_threads() -> int:
     return int(lib().oracle_omp_max_threads())
+
+
+def set_threads(n: int) -> int:
+    """Use n host threads in the OpenMP loops; returns the new maximum."""
+    L = lib()
+    L.oracle_set_threads.argtypes = [ctypes.c_int]
+    L.oracle_set_threads(int(n))
+    return omp_max_threads()
+
+
+def host_cores() -> int:
+    """Cores this process may run on."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
