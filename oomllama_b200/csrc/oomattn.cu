@@ -331,6 +331,31 @@ int launch_rope_append(oomattn_ctx* ctx, const AppendArgs& ap, const SeqBatch& s
   return OOMATTN_OK;
 }
 
+// Pages per split-KV CTA.  Candidates are multiples of 4 (one page per consumer
+// warp per stage) that keep the split count within the partial scratch; each
+// is scored by the makespan it implies on the resident CTA slots,
+//   ceil(ctas / slots) * (pps + fill),
+// with `fill` pages standing for a CTA's pipeline fill and merge.  This avoids
+// a nearly empty last wave (e.g. 1216 CTAs on 296 slots) and very short CTAs.
+int plan_pages_per_split(const SeqBatch& sb, int n_kv, int max_pages, int max_splits, int num_sms,
+                         int ctas_per_sm) {
+  const long long slots = (long long)num_sms * ctas_per_sm;
+  const int fill = 6;
+  const int lo = std::max(8, (max_pages + max_splits - 1) / max_splits);
+  int best = std::max(lo, (max_pages + 3) / 4 * 4);
+  double best_cost = 1e30;
+  for (int pps = (lo + 3) / 4 * 4; pps <= std::max(8, (max_pages + 3) / 4 * 4); pps += 4) {
+    long long ctas = 0;
+    for (int z = 0; z < sb.n; ++z) ctas += (long long)((sb.len[z] + kPageSize * pps - 1) / (kPageSize * pps)) * n_kv;
+    const double cost = (double)((ctas + slots - 1) / slots) * (pps + fill);
+    if (cost < best_cost) {
+      best_cost = cost;
+      best = pps;
+    }
+  }
+  return best;
+}
+
 int launch_decode_rows(oomattn_ctx* ctx, int layer, const SeqBatch& sb, const float* q, float* out, float* lse) {
   const int n_kv = ctx->cfg.n_kv_heads;
   long long unit_pages = 0;
@@ -340,12 +365,10 @@ int launch_decode_rows(oomattn_ctx* ctx, int layer, const SeqBatch& sb, const fl
     unit_pages += (long long)pages * n_kv;
     max_pages = std::max(max_pages, pages);
   }
-  // Split size: ~8 CTAs per SM in total, at least 8 pages (one per consumer
-  // warp per two stages) and few enough splits to fit the partial scratch.
-  long long target = (unit_pages + (long long)ctx->num_sms * 8 - 1) / ((long long)ctx->num_sms * 8);
-  int pps = (int)std::max<long long>(8, (target + 3) / 4 * 4);
-  pps = std::max(pps, (max_pages + kMaxSplits - 1) / kMaxSplits);
+  const int pps = plan_pages_per_split(sb, n_kv, max_pages, kMaxSplits, ctx->num_sms,
+                                       ctx->cfg.kv_dtype == OOMATTN_DTYPE_BF16 ? 2 : 8);
   const int nsplit = std::max(1, (max_pages + pps - 1) / pps);
+  (void)unit_pages;
   DecodeArgs a;
   a.q = q;
   a.out = out;
