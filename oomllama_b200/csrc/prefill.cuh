@@ -185,8 +185,8 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   uint64_t* v_empty = v_full + kPfVStages;           // [kPfVStages]
   uint64_t* v_conv = v_empty + kPfVStages;           // [kPfVStages]: V stage converted to fp16
   uint64_t* s_full = v_conv + kPfVStages;            // [2]
-  uint64_t* p_full = s_full + 2;                     // [2]
-  uint64_t* o_full = p_full + 2;                     // [2]
+  uint64_t* p_full = s_full + 2;                     // [2 tiles][2 halves of P]
+  uint64_t* o_full = p_full + 4;                     // [2]
   uint64_t* mma_done = o_full + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
 
@@ -218,7 +218,8 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], 128);
+      mbar_init(&p_full[2 * i], 4);      // one elected lane per softmax warp
+      mbar_init(&p_full[2 * i + 1], 4);
       mbar_init(&o_full[i], 1);
     }
     mbar_init(mma_done, 1);
@@ -335,13 +336,16 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       // O_i (+)= P_i V_j in fp16 x fp16 : 8 k-steps of 16 keys; P from TMEM
       // (8 columns per step); V (converted to fp16 in place) N-major: LBO =
       // 16 KB between 64-dim halves, SBO = 1 KB between 8-key groups
-      auto issue_pv = [&](int i, int j) {
+      // one half = keys [64*half, 64*half+64): k-steps 4*half .. 4*half+3
+      auto issue_pv_half = [&](int i, int j, int half) {
         const uint32_t b0 = (uint32_t)dv + (j % kPfVStages) * (kTileBytes >> 4);
         const uint32_t d = tmem + 256 + i * 128, p = tmem + i * 128;
-        const uint32_t first = j > 0 ? 1u : 0u;
+        const uint32_t first = (j > 0 || half > 0) ? 1u : 0u;
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk)
-          mma_ts_lh(d, p + kk * 8, b0 + kk * (2048 >> 4), dv_hi, idesc_pv, kk > 0 ? 1u : first);
+        for (int k4 = 0; k4 < 4; ++k4) {
+          const int kk = half * 4 + k4;
+          mma_ts_lh(d, p + kk * 8, b0 + kk * (2048 >> 4), dv_hi, idesc_pv, k4 > 0 ? 1u : first);
+        }
       };
       int k_waited = -1, v_waited = -1;
       auto wait_k = [&](int j) {
@@ -376,12 +380,16 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       for (int j = 0; j < n_kv_tiles && ok; ++j) {
         for (int i = 0; i < 2 && ok; ++i) {
           if (j >= (i ? ntile[1] : ntile[0])) continue;
-          ok = mbar_wait(&p_full[i], j & 1, a.status, a.timeout_ns);
-          if (!ok) break;
-          tc_fence_after();
           wait_v(j);
           if (!ok) break;
-          issue_pv(i, j);
+          ok = mbar_wait(&p_full[2 * i], j & 1, a.status, a.timeout_ns);
+          if (!ok) break;
+          tc_fence_after();
+          issue_pv_half(i, j, 0);
+          ok = mbar_wait(&p_full[2 * i + 1], j & 1, a.status, a.timeout_ns);
+          if (!ok) break;
+          tc_fence_after();
+          issue_pv_half(i, j, 1);
           if (i == last_user(j)) tc_commit(&v_empty[j % kPfVStages]);
           if (j + 1 < (i ? ntile[1] : ntile[0])) {
             wait_k(j + 1);
@@ -476,25 +484,8 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         m_used = mxs;
         l *= alpha;
       }
-      // P in fp16 (11 significant bits, 8x finer than bf16; p <= 2^8 after the
-      // lazy rescale, far inside fp16 range) packed in place over the scores
-      // (step c reads sr[2c], sr[2c+1] and writes sr[c], c <= 2c), then stored
-      // into S columns [0,64).  The scale-and-shift and the row sum run as
-      // packed f32x2 FMA-pipe instructions, the exponential on the MUFU pipe.
-      const uint64_t cl2 = f2_pack(cl, cl);
-      const uint64_t nm2 = f2_pack(-m_used, -m_used);
-      uint64_t acc[4] = {0, 0, 0, 0};
-#pragma unroll
-      for (int c = 0; c < 64; ++c) {
-        const uint64_t t = f2_fma(f2_pack(__uint_as_float(sr[2 * c]), __uint_as_float(sr[2 * c + 1])), cl2, nm2);
-        const float p0 = ex2_ftz(f2_lo(t)), p1 = ex2_ftz(f2_hi(t));
-        acc[c & 3] = f2_add(acc[c & 3], f2_pack(p0, p1));
-        sr[c] = pack_f16(p0, p1);
-      }
-      OOMATTN_TMEM_ST32((tmem + i * 128) + lane_off + 0, (sr + 0));
-      OOMATTN_TMEM_ST32((tmem + i * 128) + lane_off + 32, (sr + 32));
-      const uint64_t acc2 = f2_add(f2_add(acc[0], acc[1]), f2_add(acc[2], acc[3]));
-      l += f2_lo(acc2) + f2_hi(acc2);
+      // O must be rescaled before the first P.V of this tile: that MMA is
+      // released with P's first half below.  (Rare: lazy rescale.)
       if (__any_sync(0xffffffffu, need)) {
 #pragma unroll
         for (int ch = 0; ch < 4; ++ch) {
@@ -506,9 +497,35 @@ __global__ void __launch_bounds__(kPfThreads, 1)
           OOMATTN_TMEM_ST32((tmem + 256 + i * 128) + lane_off + ch * 32, orr);
         }
       }
-      tmem_wait_st();
-      tc_fence_before();
-      mbar_arrive(&p_full[i]);
+      // P in fp16 (11 significant bits, 8x finer than bf16; p <= 2^8 after the
+      // lazy rescale, far inside fp16 range) packed in place over the scores
+      // (step c reads sr[2c], sr[2c+1] and writes sr[c], c <= 2c) and stored
+      // into S columns [0,64) in two halves of 64 keys.  Each half is released
+      // to the MMA thread on its own barrier, so the P.V of keys 0..63 runs
+      // while keys 64..127 are still being exponentiated.  One elected lane per
+      // warp arrives (barrier count 4).  The scale-and-shift and the row sum
+      // run as packed f32x2 FMA-pipe instructions, the exponential on MUFU.
+      const uint64_t cl2 = f2_pack(cl, cl);
+      const uint64_t nm2 = f2_pack(-m_used, -m_used);
+      uint64_t acc[4] = {0, 0, 0, 0};
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+#pragma unroll
+        for (int cc = 0; cc < 32; ++cc) {
+          const int c = half * 32 + cc;
+          const uint64_t t = f2_fma(f2_pack(__uint_as_float(sr[2 * c]), __uint_as_float(sr[2 * c + 1])), cl2, nm2);
+          const float p0 = ex2_ftz(f2_lo(t)), p1 = ex2_ftz(f2_hi(t));
+          acc[c & 3] = f2_add(acc[c & 3], f2_pack(p0, p1));
+          sr[c] = pack_f16(p0, p1);
+        }
+        OOMATTN_TMEM_ST32((tmem + i * 128) + lane_off + half * 32, (sr + half * 32));
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_full[2 * i + half]);
+      }
+      const uint64_t acc2 = f2_add(f2_add(acc[0], acc[1]), f2_add(acc[2], acc[3]));
+      l += f2_lo(acc2) + f2_hi(acc2);
     }
     if (ok && (i ? ntile[1] : ntile[0]) > 0) {
       ok = mbar_wait(&o_full[i], 0, a.status, a.timeout_ns);
