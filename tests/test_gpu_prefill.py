@@ -89,3 +89,24 @@ def test_prefill_rejects_f32_cache():
         eng.prefill(0, 0, torch.zeros(8, 28, 128, dtype=torch.bfloat16, device="cuda"))
     assert e.value.code == 8
     eng.close()
+
+
+@pytest.mark.parametrize("prefix,n_new", [(0, 700), (300, 513)])
+def test_prefill_growing_scores_rescales_o(oracle, prefix, n_new):
+    # Keys grow in magnitude along the sequence, so a row's running maximum
+    # climbs by far more than 2^8 across its key tiles and the lazy O rescale
+    # runs in most steps (both key halves of a row must agree on it).
+    L = prefix + n_new
+    eng = make_engine(8, 1, [L], kv_dtype="bf16", shuffle_seed=11)
+    growth = torch.linspace(1.0, 24.0, L).reshape(L, 1, 1)
+    k = (randn((L, 1, 128), 12, torch.float32) * growth).to(torch.bfloat16)
+    v = randn((L, 1, 128), 13, torch.bfloat16)
+    eng.kv_write(0, 0, k.cuda(), v.cuda())
+    q = randn((n_new, 8, 128), 14, torch.bfloat16)
+    out, lse = eng.prefill(0, 0, q.cuda(), with_lse=True)
+    eng.sync()
+    ref, ref_lse = oracle.gqa_attention(as_f32_np(q), as_f32_np(k).transpose(1, 0, 2).copy(),
+                                        as_f32_np(v).transpose(1, 0, 2).copy(), causal=True, with_lse=True)
+    eng.close()
+    assert_close(as_f32_np(out), ref, BF16_ATOL, BF16_RTOL, what=f"growing-score prefill P={prefix} n={n_new}")
+    assert_close(lse.cpu().numpy(), ref_lse, 2e-3 * 24, BF16_RTOL, what="growing-score prefill lse")
