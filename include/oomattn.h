@@ -237,6 +237,49 @@ int oomattn_attention_forward_with_bias(oomattn_ctx* ctx, int32_t layer, int32_t
                                         const float* wo, int32_t o_out, const float* bq, const float* bk,
                                         const float* bv, float* out);
 
+/* ------------------------------------------- K-E: GPU-resident Q8 weights */
+
+/* A Q8 matrix W [rows][cols] resident on the device, row-major ([out][in], the
+ * HF layout of the projections and MLP weights).  Values are quantised in
+ * blocks of 256 consecutive values of the row-major flattening, as the .oom
+ * writer cuts them (src/gguf2oom.rs:719-770); block b covers values
+ * [256 b, 256 b + 256):
+ *   W[r][c] = min[b] + (float)q[r * cols + c] * scale[b],  b = (r * cols + c) / 256
+ * (BlockQ8View::dequantize_fast, src/quant.rs:201-224).
+ *   q: uint8 [rows * cols] (16-byte aligned); scale, min: f32 [ceil(rows*cols/256)].
+ * It replaces the reference's per-call path, OomLoader::dequantize_tensor
+ * (src/quant.rs:413-468) into an f32 host buffer and its upload in
+ * GhostLayer::materialize (src/oomllama.rs:425-439). */
+typedef struct oomattn_q8_matrix {
+  const uint8_t* q;
+  const float* scale;
+  const float* min;
+  int32_t rows;
+  int32_t cols;
+} oomattn_q8_matrix;
+
+/* Unpack the block stream of one .oom Q8 tensor -- the bytes that follow its
+ * header, n_blocks = ceil(n_values / 256) blocks of [f32 scale][f32 min]
+ * [u32 len][len bytes q], little endian (src/gguf2oom.rs:823-826) -- into host
+ * arrays q_out[n_values], scale_out[n_blocks] and min_out[n_blocks].  The walk
+ * is OomLoader::dequantize_tensor_into's (src/quant.rs:431-463); every block
+ * must hold min(256, values left) bytes and lie inside the stream, otherwise
+ * OOMATTN_ERR_INVALID_ARG.  Host only: needs no context or GPU. */
+int oomattn_q8_unpack(const uint8_t* stream /* host */, uint64_t stream_bytes, int64_t n_values,
+                      uint8_t* q_out /* host */, float* scale_out /* host */, float* min_out /* host */,
+                      char* errbuf /* host, may be NULL */, int32_t errbuf_len);
+
+/* y[t][r] = sum_c x[t][c] * W[r][c]  (+ bias[r] when bias is not NULL), for
+ * t < n_tokens: the reference's matvec (src/oom_inference.rs:168-180) and
+ * candle's x @ W^T (src/oomllama_turbo.rs:643-645) on dequantised weights,
+ * without materialising them.  f32 activations: x [n_tokens][cols],
+ * y [n_tokens][rows], bias [rows] -- all device pointers.  rows must be a
+ * multiple of 16 and cols of 64; |x| < 65504 (x enters the tensor cores as an
+ * fp16 hi/lo pair; larger values are reported by oomattn_sync as
+ * OOMATTN_ERR_DEVICE_CHECK). */
+int oomattn_q8_linear(oomattn_ctx* ctx, const oomattn_q8_matrix* w /* host struct */, const float* x,
+                      int32_t n_tokens, const float* bias, float* y);
+
 #ifdef __cplusplus
 }
 #endif

@@ -26,6 +26,7 @@ EXPORTS = (
     "oomattn_set_seq_len", "oomattn_kv_pool", "oomattn_kv_write", "oomattn_kv_read", "oomattn_rope_table",
     "oomattn_compute_rope_table", "oomattn_rope_append", "oomattn_qkv_rope_append", "oomattn_decode", "oomattn_merge_partials",
     "oomattn_prefill", "oomattn_attention_forward_with_bias", "oomattn_decode_static_scratch",
+    "oomattn_q8_unpack", "oomattn_q8_linear",
 )
 
 
@@ -45,6 +46,12 @@ class Config(ctypes.Structure):
         ("kv_dtype", ctypes.c_int32), ("rope_variant", ctypes.c_int32), ("rope_theta", ctypes.c_float),
         ("softmax_scale", ctypes.c_float),
     ]
+
+
+class Q8Matrix(ctypes.Structure):
+    """oomattn_q8_matrix: device pointers of a resident Q8 matrix [rows][cols]."""
+    _fields_ = [("q", ctypes.c_void_p), ("scale", ctypes.c_void_p), ("min", ctypes.c_void_p),
+                ("rows", ctypes.c_int32), ("cols", ctypes.c_int32)]
 
 
 _lib = None
@@ -85,6 +92,8 @@ def load():
         "oomattn_attention_forward_with_bias": ([P, I, I, I, P, P, P, P, P, I, P, P, P, P], ctypes.c_int),
         "oomattn_decode_static_scratch": ([ctypes.c_int, P, I, P, P, I, P, I, I, I, F, I, IP, IP, P, P, P,
                                            ctypes.c_char_p, I], ctypes.c_int),
+        "oomattn_q8_unpack": ([P, ctypes.c_uint64, ctypes.c_int64, P, P, P, ctypes.c_char_p, I], ctypes.c_int),
+        "oomattn_q8_linear": ([P, ctypes.POINTER(Q8Matrix), P, I, P, P], ctypes.c_int),
     }
     for name, (args, res) in sig.items():
         fn = getattr(L, name)

@@ -21,6 +21,7 @@
 #include "decode.cuh"
 #include "params.cuh"
 #include "prefill.cuh"
+#include "q8_linear.cuh"
 #include "rope_append.cuh"
 
 using namespace oomattn;
@@ -82,6 +83,12 @@ struct oomattn_ctx {
   cublasHandle_t cublas = nullptr;
   float* d_scratch = nullptr;
   size_t scratch_bytes = 0;
+  // Q8 linear: activation splits and split-K partials, and per-row-tile
+  // arrival counters (zero between launches)
+  uint8_t* d_q8_scratch = nullptr;
+  size_t q8_scratch_bytes = 0;
+  unsigned* d_q8_counters = nullptr;
+  int q8_counters_n = 0;
 };
 
 namespace {
@@ -485,7 +492,8 @@ int oomattn_destroy(oomattn_ctx* ctx) {
   if (ctx->stream) cudaStreamSynchronize(ctx->stream);
   if (ctx->cublas) cublasDestroy(ctx->cublas);
   void* ptrs[] = {ctx->kpool,     ctx->vpool,      ctx->d_block_table, ctx->d_cos,    ctx->d_sin,
-                  ctx->d_part_o,  ctx->d_part_lse, ctx->d_counters,    ctx->d_status, ctx->d_scratch};
+                  ctx->d_part_o,  ctx->d_part_lse, ctx->d_counters,    ctx->d_status, ctx->d_scratch,
+                  ctx->d_q8_scratch, ctx->d_q8_counters};
   for (void* p : ptrs)
     if (p) cudaFree(p);
   delete ctx;
@@ -510,6 +518,9 @@ int oomattn_sync(oomattn_ctx* ctx) {
     if (st & kDevErrRange)
       return fail(ctx, OOMATTN_ERR_DEVICE_CHECK,
                   "prefill met a cached V value of magnitude >= 65536, outside the fp16 P.V product (status %d)", st);
+    if (st & kDevErrX16)
+      return fail(ctx, OOMATTN_ERR_DEVICE_CHECK,
+                  "q8_linear met an activation of magnitude >= 65504, outside its fp16 hi/lo split (status %d)", st);
     return fail(ctx, OOMATTN_ERR_DEVICE_CHECK, "a device-side index check failed (status %d)", st);
   }
   return OOMATTN_OK;
@@ -1101,5 +1112,144 @@ extern "C" int oomattn_decode_static_scratch(int device, void* stream, int32_t k
   e = cudaGetLastError();
   if (e != cudaSuccess)
     return static_fail(errbuf, errbuf_len, OOMATTN_ERR_CUDA, "kernel launch: %s", cudaGetErrorString(e));
+  return OOMATTN_OK;
+}
+
+// ------------------------------------------------------------------ K-E: Q8 weights
+
+extern "C" int oomattn_q8_unpack(const uint8_t* stream, uint64_t stream_bytes, int64_t n_values, uint8_t* q_out,
+                                 float* scale_out, float* min_out, char* errbuf, int32_t errbuf_len) {
+  auto err = [&](const char* what, long long block, long long val) {
+    if (errbuf && errbuf_len > 0) snprintf(errbuf, (size_t)errbuf_len, "block %lld: %s (%lld)", block, what, val);
+    return OOMATTN_ERR_INVALID_ARG;
+  };
+  if (!stream || !q_out || !scale_out || !min_out || n_values < 0) return err("null pointer or negative size", -1, n_values);
+  // OomLoader::dequantize_tensor_into (src/quant.rs:431-463): per block
+  // [f32 scale][f32 min][u32 len][len bytes], min(256, values left) values each
+  uint64_t off = 0;
+  int64_t pos = 0;
+  for (int64_t b = 0; pos < n_values; ++b) {
+    if (off > stream_bytes || stream_bytes - off < 12) return err("header past the end of the stream, offset", b, (long long)off);
+    float sc, mn;
+    uint32_t len;
+    memcpy(&sc, stream + off, 4);
+    memcpy(&mn, stream + off + 4, 4);
+    memcpy(&len, stream + off + 8, 4);
+    off += 12;
+    const int64_t want = std::min<int64_t>(256, n_values - pos);
+    if ((int64_t)len != want) return err("length is not min(256, values left), length", b, (long long)len);
+    if (stream_bytes - off < len) return err("data past the end of the stream, offset", b, (long long)off);
+    memcpy(q_out + pos, stream + off, len);
+    scale_out[b] = sc;
+    min_out[b] = mn;
+    off += len;
+    pos += len;
+  }
+  return OOMATTN_OK;
+}
+
+namespace {
+
+int ensure_q8_scratch(oomattn_ctx* ctx, size_t bytes, int row_tiles) {
+  if (bytes > ctx->q8_scratch_bytes) {
+    if (ctx->d_q8_scratch) {
+      cudaStreamSynchronize(ctx->stream);
+      cudaFree(ctx->d_q8_scratch);
+      ctx->d_q8_scratch = nullptr;
+      ctx->q8_scratch_bytes = 0;
+    }
+    if (cudaMalloc(&ctx->d_q8_scratch, bytes) != cudaSuccess)
+      return fail(ctx, OOMATTN_ERR_NO_MEMORY, "q8 scratch allocation of %zu bytes failed", bytes);
+    ctx->q8_scratch_bytes = bytes;
+  }
+  if (row_tiles > ctx->q8_counters_n) {
+    if (ctx->d_q8_counters) {
+      cudaStreamSynchronize(ctx->stream);
+      cudaFree(ctx->d_q8_counters);
+      ctx->d_q8_counters = nullptr;
+      ctx->q8_counters_n = 0;
+    }
+    if (cudaMalloc(&ctx->d_q8_counters, sizeof(unsigned) * row_tiles) != cudaSuccess)
+      return fail(ctx, OOMATTN_ERR_NO_MEMORY, "q8 counter allocation failed");
+    CK(cudaMemsetAsync(ctx->d_q8_counters, 0, sizeof(unsigned) * row_tiles, ctx->stream));
+    ctx->q8_counters_n = row_tiles;
+  }
+  return OOMATTN_OK;
+}
+
+template <int NT, int MT>
+void launch_q8_linear(const Q8Args& a, int row_blocks, cudaStream_t st) {
+  q8_linear_kernel<NT, MT><<<dim3(a.splits, row_blocks), kQ8Warps * 32, 0, st>>>(a);
+}
+
+}  // namespace
+
+extern "C" int oomattn_q8_linear(oomattn_ctx* ctx, const oomattn_q8_matrix* w, const float* x, int32_t n_tokens,
+                                 const float* bias, float* y) {
+  if (!ctx) return OOMATTN_ERR_INVALID_ARG;
+  if (!w || !x || !y || !w->q || !w->scale || !w->min) return fail(ctx, OOMATTN_ERR_INVALID_ARG, "null pointer");
+  if (n_tokens < 0 || w->rows <= 0 || w->cols <= 0) return fail(ctx, OOMATTN_ERR_INVALID_ARG, "bad shape");
+  if (w->rows % 16 || w->cols % kQ8Chunk)
+    return fail(ctx, OOMATTN_ERR_UNSUPPORTED, "q8_linear needs rows %% 16 == 0 and cols %% 64 == 0 (got %d x %d)",
+                w->rows, w->cols);
+  if (reinterpret_cast<uintptr_t>(w->q) % 16 || reinterpret_cast<uintptr_t>(x) % 16)
+    return fail(ctx, OOMATTN_ERR_INVALID_ARG, "q and x must be 16-byte aligned");
+  if (n_tokens == 0) return OOMATTN_OK;
+  DeviceGuard dg(ctx->device);
+  const int rows = w->rows, cols = w->cols;
+  const int nchunks = cols / kQ8Chunk;
+  // Tokens run in passes of up to 16 (two tiles of 8); the weights are re-read
+  // per pass.  A pass of up to 8 tokens uses row blocks of 32 rows (two row
+  // tiles per warp share each x fragment), a pass of 9-16 tokens 16 rows.
+  const int group = 16;
+  const int mt = n_tokens <= 8 ? 2 : 1;
+  const int row_blocks = (rows + 16 * mt - 1) / (16 * mt);
+  // split-K so that the grid covers the SMs about four times over, keeping at
+  // least one chunk per warp of a CTA
+  const int want = std::max(1, (4 * ctx->num_sms + row_blocks - 1) / row_blocks);
+  int splits = std::max(1, std::min(want, nchunks / kQ8Warps));
+  const int cps = (nchunks + splits - 1) / splits;
+  splits = (nchunks + cps - 1) / cps;
+  const int tp_max = std::min(group, (n_tokens + 7) / 8 * 8);
+  const size_t xw = (size_t)tp_max * (cols / 2);
+  const size_t bytes = 2 * xw * 4 + (size_t)tp_max * nchunks * 4 + (size_t)splits * tp_max * rows * 4 + 256;
+  int rc = ensure_q8_scratch(ctx, bytes, row_blocks);
+  if (rc) return rc;
+  uint32_t* xh = reinterpret_cast<uint32_t*>(ctx->d_q8_scratch);
+  uint32_t* xl = xh + xw;
+  float* xsum = reinterpret_cast<float*>(xl + xw);
+  float* part = xsum + (size_t)tp_max * nchunks;
+  for (int t0 = 0; t0 < n_tokens; t0 += group) {
+    const int nt = std::min(group, n_tokens - t0);
+    const int ntile = nt <= 8 ? 1 : 2;
+    const long long prep_warps = (long long)nt * nchunks;
+    q8_prep_x_kernel<<<(unsigned)((prep_warps + 7) / 8), 256, 0, ctx->stream>>>(x + (size_t)t0 * cols, nt, cols, xh, xl,
+                                                                                  xsum, ctx->d_status);
+    CKLAUNCH();
+    Q8Args a;
+    a.q = w->q;
+    a.scale = w->scale;
+    a.min = w->min;
+    a.rows = rows;
+    a.cols = cols;
+    a.xh = xh;
+    a.xl = xl;
+    a.xsum = xsum;
+    a.n_tokens = nt;
+    a.bias = bias;
+    a.y = y + (size_t)t0 * rows;
+    a.part = part;
+    a.counters = ctx->d_q8_counters;
+    a.splits = splits;
+    a.chunks_per_split = cps;
+    a.status = ctx->d_status;
+    if (mt == 2)
+      launch_q8_linear<1, 2>(a, row_blocks, ctx->stream);
+    else if (ntile == 1)
+      launch_q8_linear<1, 1>(a, row_blocks, ctx->stream);
+    else
+      launch_q8_linear<2, 1>(a, row_blocks, ctx->stream);
+    CKLAUNCH();
+  }
   return OOMATTN_OK;
 }

@@ -1,0 +1,265 @@
+// K-E: x @ W^T for GPU-resident Q8 weights, without materialising W.
+//
+// Semantics: y[t][r] = sum_c x[t][c] * W[r][c] (+ bias[r]) with
+// W[r][c] = min_b + q[r][c] * scale_b, b the 256-value block of the row-major
+// flattening (BlockQ8View::dequantize_fast, src/quant.rs:201-224; the matvec
+// src/oom_inference.rs:168-180).  The block's affine map is applied after the
+// dot product, per 64-column chunk (a chunk never straddles a block because
+// cols is a multiple of 64):
+//   sum_k x_k (min + q_k s) = s * sum_k q_k x_k + min * sum_k x_k.
+//
+// Tensor-core form (mma.sync m16n8k16, fp16 in, f32 accumulate):
+//  - A = 1024 + q as fp16: the bit pattern 0x6400 | q, built from the weight
+//    bytes with one byte permute per two values; exact for q <= 255.
+//  - B = x split into fp16 hi + lo (about 22 significant bits), two MMAs per
+//    k-step; products are exact in the f32 accumulator.
+//  - D = sum (1024 + q) x, so the chunk's contribution is
+//      s * D + (min - 1024 s) * X,   X = sum_k x_k over the chunk.
+//  - The k order inside a chunk is permuted so that each thread's A values
+//    are 16 consecutive weight bytes of a row and its B values 16 consecutive
+//    x values of a token (the dot product does not depend on the order).
+// A warp covers 16 * MT rows x 64 columns per chunk and all tokens in tiles of
+// 8, reading the next chunk's operands while it computes the current one; a
+// CTA's 8 warps split its column range and reduce in shared memory, and
+// split-K CTAs of the same rows merge through a partial buffer: the last CTA
+// to arrive (a per-row-block counter) sums the splits in order, so results do
+// not depend on CTA timing.
+//
+// Roofline: HBM-bound for decode-sized token counts; algorithmic bytes per
+// launch = rows * cols (q) + 8 * ceil(rows * cols / 256) (scale, min)
+// + 4 * (n_tokens * cols + n_tokens * rows) (x, y).
+#pragma once
+#include <cuda_fp16.h>
+
+#include "common.cuh"
+
+namespace oomattn {
+
+constexpr int kQ8Warps = 8;            // warps per CTA
+constexpr int kQ8Chunk = 64;           // columns per chunk
+
+struct Q8Args {
+  const uint8_t* q;
+  const float* scale;
+  const float* min;
+  int rows;
+  int cols;
+  const uint32_t* xh;   // [n_tokens][cols / 2] fp16 pairs: x rounded to fp16
+  const uint32_t* xl;   // [n_tokens][cols / 2] fp16 pairs: x - hi rounded to fp16
+  const float* xsum;    // [n_tokens][cols / 64]
+  int n_tokens;
+  const float* bias;    // [rows] or null
+  float* y;             // [n_tokens][rows]
+  float* part;          // [splits][8 * token tiles][rows]: split-K partial sums
+  unsigned* counters;   // [row blocks]: arrivals per row block, zero between launches
+  int splits;
+  int chunks_per_split;
+  int* status;
+};
+
+// x -> (hi, lo) fp16 pairs and per-chunk sums.  One warp per (token, 64-column
+// chunk): lane l owns columns 2l, 2l+1.  The chunk sum is a fixed shuffle
+// tree, so it does not depend on timing.  |x| >= 65504 has no fp16 image: it
+// is reported through the status word.
+__global__ void q8_prep_x_kernel(const float* __restrict__ x, int n_tokens, int cols, uint32_t* xh, uint32_t* xl,
+                                 float* xsum, int* status) {
+  const int lane = threadIdx.x & 31;
+  const int nchunks = cols / kQ8Chunk;
+  const long long w = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (w >= (long long)n_tokens * nchunks) return;
+  const int t = (int)(w / nchunks), ch = (int)(w % nchunks);
+  const float2 v = *reinterpret_cast<const float2*>(x + (size_t)t * cols + ch * kQ8Chunk + 2 * lane);
+  const __half2 hi = __floats2half2_rn(v.x, v.y);
+  const float2 hf = __half22float2(hi);
+  const __half2 lo = __floats2half2_rn(v.x - hf.x, v.y - hf.y);
+  if (!(fabsf(v.x) < 65504.f) || !(fabsf(v.y) < 65504.f)) report_error(status, kDevErrX16);
+  const size_t o = (size_t)t * (cols / 2) + ch * (kQ8Chunk / 2) + lane;
+  xh[o] = *reinterpret_cast<const uint32_t*>(&hi);
+  xl[o] = *reinterpret_cast<const uint32_t*>(&lo);
+  float s = v.x + v.y;
+#pragma unroll
+  for (int d = 16; d > 0; d >>= 1) s += __shfl_xor_sync(0xffffffffu, s, d);
+  if (lane == 0) xsum[(size_t)t * nchunks + ch] = s;
+}
+
+// 16 weight bytes of a row, streamed past L1 (each byte is read once).
+__device__ __forceinline__ uint4 ldg_stream16(const uint8_t* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+// D(16x8, f32) += A(16x16, f16, row) * B(16x8, f16, col)
+__device__ __forceinline__ void mma_f16_16816(float* d, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                              uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// fp16 pair (1024 + byte 2i, 1024 + byte 2i + 1) of a word of four weight bytes.
+__device__ __forceinline__ uint32_t q8_pair(uint32_t w, uint32_t sel) { return __byte_perm(w, 0x64646464u, sel); }
+
+// Everything one warp reads for one 64-column chunk: the weight bytes of its
+// MT row tiles, their blocks' scale and min, and the x fragments and chunk
+// sums of its NT token tiles.  Loaded one chunk ahead of use.
+template <int NT, int MT>
+struct Q8Chunk {
+  uint4 qa[MT], qb[MT];          // rows g and g + 8 of each row tile: 16 bytes each
+  float sa[MT], ma[MT], sb[MT], mb[MT];
+  uint32_t bh[NT][8], bl[NT][8];  // x hi / lo pairs of token 8n + g, the thread's 16 columns
+  float x0[NT], x1[NT];           // chunk sums of tokens 8n + 2c and 8n + 2c + 1
+};
+
+template <int NT, int MT>
+__device__ __forceinline__ void q8_load_chunk(const Q8Args& a, int ch, int row0, int g, int c, Q8Chunk<NT, MT>& d) {
+  const int nchunks = a.cols / kQ8Chunk;
+#pragma unroll
+  for (int m = 0; m < MT; ++m) {
+    if (row0 + 16 * m >= a.rows) {  // a row block's last tile may lie past the matrix
+      d.qa[m] = d.qb[m] = make_uint4(0, 0, 0, 0);
+      d.sa[m] = d.ma[m] = d.sb[m] = d.mb[m] = 0.f;
+      continue;
+    }
+    const long long ra = (long long)(row0 + 16 * m + g) * a.cols, rb = ra + 8LL * a.cols;
+    d.qa[m] = ldg_stream16(a.q + ra + (long long)ch * kQ8Chunk + 16 * c);
+    d.qb[m] = ldg_stream16(a.q + rb + (long long)ch * kQ8Chunk + 16 * c);
+    const long long ba = (ra + (long long)ch * kQ8Chunk) >> 8, bb = (rb + (long long)ch * kQ8Chunk) >> 8;
+    d.sa[m] = __ldg(a.scale + ba);
+    d.ma[m] = __ldg(a.min + ba);
+    d.sb[m] = __ldg(a.scale + bb);
+    d.mb[m] = __ldg(a.min + bb);
+  }
+#pragma unroll
+  for (int n = 0; n < NT; ++n) {
+    const int tok = 8 * n + g;
+    if (tok < a.n_tokens) {  // tokens past n_tokens contribute zero and are not read
+      const size_t xo = (size_t)tok * (a.cols / 2) + ch * (kQ8Chunk / 2) + 8 * c;
+      const uint4 h0 = __ldg(reinterpret_cast<const uint4*>(a.xh + xo));
+      const uint4 h1 = __ldg(reinterpret_cast<const uint4*>(a.xh + xo + 4));
+      const uint4 l0 = __ldg(reinterpret_cast<const uint4*>(a.xl + xo));
+      const uint4 l1 = __ldg(reinterpret_cast<const uint4*>(a.xl + xo + 4));
+      d.bh[n][0] = h0.x; d.bh[n][1] = h0.y; d.bh[n][2] = h0.z; d.bh[n][3] = h0.w;
+      d.bh[n][4] = h1.x; d.bh[n][5] = h1.y; d.bh[n][6] = h1.z; d.bh[n][7] = h1.w;
+      d.bl[n][0] = l0.x; d.bl[n][1] = l0.y; d.bl[n][2] = l0.z; d.bl[n][3] = l0.w;
+      d.bl[n][4] = l1.x; d.bl[n][5] = l1.y; d.bl[n][6] = l1.z; d.bl[n][7] = l1.w;
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) d.bh[n][e] = d.bl[n][e] = 0u;
+    }
+    const int t0 = 8 * n + 2 * c;
+    d.x0[n] = t0 < a.n_tokens ? __ldg(a.xsum + (size_t)t0 * nchunks + ch) : 0.f;
+    d.x1[n] = t0 + 1 < a.n_tokens ? __ldg(a.xsum + (size_t)(t0 + 1) * nchunks + ch) : 0.f;
+  }
+}
+
+// A CTA owns 16 * MT rows and a column range; its 8 warps take the range's
+// chunks round-robin, each chunk for all MT row tiles and NT token tiles.
+template <int NT, int MT>
+__global__ void __launch_bounds__(kQ8Warps * 32) q8_linear_kernel(const Q8Args a) {
+  __shared__ float red[kQ8Warps][MT][NT][4][32];
+  __shared__ int s_last;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, c = lane & 3;
+  const int rb = blockIdx.y, sp = blockIdx.x;
+  const int row0 = rb * 16 * MT;
+  const int nchunks = a.cols / kQ8Chunk;
+  const int c0 = sp * a.chunks_per_split, c1 = min(nchunks, c0 + a.chunks_per_split);
+
+  float acc[MT][NT][4];
+#pragma unroll
+  for (int m = 0; m < MT; ++m)
+#pragma unroll
+    for (int n = 0; n < NT; ++n)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[m][n][e] = 0.f;
+
+  int ch = c0 + warp;
+  Q8Chunk<NT, MT> cur;
+  if (ch < c1) q8_load_chunk<NT, MT>(a, ch, row0, g, c, cur);
+  for (; ch < c1; ch += kQ8Warps) {
+    Q8Chunk<NT, MT> nxt;
+    if (ch + kQ8Warps < c1) q8_load_chunk<NT, MT>(a, ch + kQ8Warps, row0, g, c, nxt);
+#pragma unroll
+    for (int m = 0; m < MT; ++m) {
+      // A fragments of the 4 k-steps: step s takes bytes 4s..4s+3 of the thread's 16
+      const uint32_t wa[4] = {cur.qa[m].x, cur.qa[m].y, cur.qa[m].z, cur.qa[m].w};
+      const uint32_t wb[4] = {cur.qb[m].x, cur.qb[m].y, cur.qb[m].z, cur.qb[m].w};
+      uint32_t af[4][4];
+#pragma unroll
+      for (int s = 0; s < 4; ++s) {
+        af[s][0] = q8_pair(wa[s], 0x4140u);
+        af[s][1] = q8_pair(wb[s], 0x4140u);
+        af[s][2] = q8_pair(wa[s], 0x4342u);
+        af[s][3] = q8_pair(wb[s], 0x4342u);
+      }
+      const float ka = cur.ma[m] - 1024.f * cur.sa[m], kb = cur.mb[m] - 1024.f * cur.sb[m];
+#pragma unroll
+      for (int n = 0; n < NT; ++n) {
+        // hi and lo products accumulate in two independent chains
+        float dh[4] = {0.f, 0.f, 0.f, 0.f}, dl[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int s = 0; s < 4; ++s) {
+          mma_f16_16816(dh, af[s][0], af[s][1], af[s][2], af[s][3], cur.bh[n][2 * s], cur.bh[n][2 * s + 1]);
+          mma_f16_16816(dl, af[s][0], af[s][1], af[s][2], af[s][3], cur.bl[n][2 * s], cur.bl[n][2 * s + 1]);
+        }
+        // rows g, g + 8 x tokens 8n + 2c, 8n + 2c + 1
+        acc[m][n][0] = fmaf(cur.sa[m], dh[0] + dl[0], fmaf(ka, cur.x0[n], acc[m][n][0]));
+        acc[m][n][1] = fmaf(cur.sa[m], dh[1] + dl[1], fmaf(ka, cur.x1[n], acc[m][n][1]));
+        acc[m][n][2] = fmaf(cur.sb[m], dh[2] + dl[2], fmaf(kb, cur.x0[n], acc[m][n][2]));
+        acc[m][n][3] = fmaf(cur.sb[m], dh[3] + dl[3], fmaf(kb, cur.x1[n], acc[m][n][3]));
+      }
+    }
+    cur = nxt;
+  }
+
+  // the CTA's warps cover disjoint chunks of the same rows: sum them in warp order
+#pragma unroll
+  for (int m = 0; m < MT; ++m)
+#pragma unroll
+    for (int n = 0; n < NT; ++n)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) red[warp][m][n][e][lane] = acc[m][n][e];
+  __syncthreads();
+  const int tp = 8 * NT;
+  const int rows_cta = 16 * MT;
+  float* part = a.part + (size_t)sp * tp * a.rows;
+  for (int i = threadIdx.x; i < MT * NT * 128; i += blockDim.x) {
+    const int m = i / (NT * 128), n = (i / 128) % NT, e = (i / 32) & 3, l = i & 31;
+    float v = 0.f;
+#pragma unroll
+    for (int w = 0; w < kQ8Warps; ++w) v += red[w][m][n][e][l];
+    const int row = row0 + 16 * m + (l >> 2) + ((e & 2) ? 8 : 0);
+    const int tok = 8 * n + 2 * (l & 3) + (e & 1);
+    if (row >= a.rows || tok >= a.n_tokens) continue;
+    if (a.splits == 1)
+      a.y[(size_t)tok * a.rows + row] = v + (a.bias ? a.bias[row] : 0.f);
+    else
+      part[(size_t)tok * a.rows + row] = v;
+  }
+  if (a.splits == 1) return;
+  // split-K merge: the last CTA of this row block sums the splits in order
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const unsigned prev = atomicAdd(&a.counters[rb], 1u);
+    s_last = (prev == (unsigned)a.splits - 1);
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  for (int i = threadIdx.x; i < rows_cta * a.n_tokens; i += blockDim.x) {
+    const int tok = i / rows_cta, row = row0 + i % rows_cta;
+    if (row >= a.rows) continue;
+    float v = 0.f;
+    for (int s = 0; s < a.splits; ++s) v += __ldcg(a.part + ((size_t)s * tp + tok) * a.rows + row);
+    a.y[(size_t)tok * a.rows + row] = v + (a.bias ? a.bias[row] : 0.f);
+  }
+  if (threadIdx.x == 0) a.counters[rb] = 0;
+}
+
+}  // namespace oomattn

@@ -317,6 +317,67 @@ class TurboEngine:
         return out
 
 
+    # ------------------------------------------------------------ Q8 weights (K-E)
+    def q8_linear(self, w: "Q8Matrix", x: torch.Tensor, bias=None, out=None):
+        """x @ W^T (+ bias) for a resident Q8 matrix: x [T, cols] f32 -> [T, rows] f32.
+        Replaces dequantize-to-f32-then-matmul (src/quant.rs:413-468, src/oomllama.rs:425-439,
+        src/oom_inference.rs:168-180) without materialising W."""
+        if x.dim() != 2 or x.shape[1] != w.cols:
+            raise ValueError(f"x must be [T, {w.cols}], got {tuple(x.shape)}")
+        _dev(x, "x", self.device, dtype=torch.float32)
+        if bias is not None:
+            _dev(bias, "bias", self.device, dtype=torch.float32, numel=w.rows)
+        T = x.shape[0]
+        if out is None:
+            out = torch.empty(T, w.rows, dtype=torch.float32, device=x.device)
+        else:
+            _dev(out, "out", self.device, dtype=torch.float32, numel=T * w.rows)
+        self._bind_stream()
+        check(self._ctx, self._L.oomattn_q8_linear(self._ctx, ctypes.byref(w.c_struct()), _ptr(x), T, _ptr(bias),
+                                                   _ptr(out)))
+        return out
+
+
+def q8_unpack(stream, n_values: int):
+    """Unpack one .oom Q8 tensor's block stream ([f32 scale][f32 min][u32 len][bytes] per 256 values,
+    src/gguf2oom.rs:823-826) into host arrays (q uint8 [n_values], scale, min f32 [n_blocks])."""
+    import numpy as np
+    buf = np.frombuffer(bytes(stream) if not isinstance(stream, np.ndarray) else stream.tobytes(), dtype=np.uint8)
+    nb = (n_values + 255) // 256
+    q = np.empty(max(1, n_values), np.uint8)
+    scale = np.empty(max(1, nb), np.float32)
+    mn = np.empty(max(1, nb), np.float32)
+    err = ctypes.create_string_buffer(256)
+    rc = _lib.load().oomattn_q8_unpack(buf.ctypes.data_as(ctypes.c_void_p), buf.size, n_values,
+                                       q.ctypes.data_as(ctypes.c_void_p), scale.ctypes.data_as(ctypes.c_void_p),
+                                       mn.ctypes.data_as(ctypes.c_void_p), err, 256)
+    if rc != _lib.OK:
+        raise _lib.OomAttnError(rc, err.value.decode(errors="replace"))
+    return q[:n_values], scale[:nb], mn[:nb]
+
+
+@dataclass
+class Q8Matrix:
+    """A Q8 matrix [rows][cols] ([out][in]) resident on the device: q uint8 [rows*cols], scale and min f32 per
+    256-value block of the row-major flattening (src/quant.rs:201-224)."""
+    q: torch.Tensor
+    scale: torch.Tensor
+    min: torch.Tensor
+    rows: int
+    cols: int
+
+    @staticmethod
+    def from_oom_stream(stream, rows: int, cols: int, device: int = 0) -> "Q8Matrix":
+        """Unpack a .oom Q8 block stream on the host and upload it once."""
+        q, scale, mn = q8_unpack(stream, rows * cols)
+        dev = f"cuda:{device}"
+        return Q8Matrix(torch.from_numpy(q.copy()).to(dev), torch.from_numpy(scale.copy()).to(dev),
+                        torch.from_numpy(mn.copy()).to(dev), rows, cols)
+
+    def c_struct(self) -> _lib.Q8Matrix:
+        return _lib.Q8Matrix(self.q.data_ptr(), self.scale.data_ptr(), self.min.data_ptr(), self.rows, self.cols)
+
+
 def _alias(ptr: int, shape, dtype, device: int) -> torch.Tensor:
     """A torch tensor viewing library-owned device memory (no copy, no ownership)."""
     numel = 1

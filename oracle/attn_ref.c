@@ -309,6 +309,79 @@ void oracle_layer_attention(const float* x, int B, int S, int H, const float* wq
 
 /* Host threads used by the OpenMP loops (launchers such as torchrun preset
  * OMP_NUM_THREADS=1 per process). */
+/* ------------------------------------------------------------------ Q8 weights
+ * The .oom Q8 format.  The writer (src/gguf2oom.rs:719-770, add_tensor_q8)
+ * cuts a tensor's values into blocks of 256 (the last may be shorter); per
+ * block it takes min and max (f32 compares from f32::MAX / f32::MIN), scale =
+ * range / 255 (0 when |range| < 1e-9), q = round((v - min) / scale) with
+ * Rust's round-half-away-from-zero and saturating `as u8` (NaN -> 0), and
+ * writes [f32 scale][f32 min][u32 len][len bytes] little endian.  The reader
+ * (OomLoader::dequantize_tensor_into, src/quant.rs:431-463, with
+ * BlockQ8View::dequantize_fast, src/quant.rs:201-224) gives
+ * min + (f32)q * scale, separately rounded. */
+int64_t oracle_q8_stream_bytes(int64_t n) { return ((n + 255) / 256) * 12 + n; }
+
+void oracle_q8_quantize(const float* v, int64_t n, uint8_t* out) {
+    int64_t off = 0;
+    for (int64_t start = 0; start < n; start += 256) {
+        const int64_t end = start + 256 < n ? start + 256 : n;
+        float mn = 3.40282347e38f, mx = -3.40282347e38f;
+        for (int64_t i = start; i < end; ++i) {
+            if (v[i] < mn) mn = v[i];
+            if (v[i] > mx) mx = v[i];
+        }
+        const float range = mx - mn;
+        const float scale = fabsf(range) < 1e-9f ? 0.0f : range / 255.0f;
+        const uint32_t len = (uint32_t)(end - start);
+        memcpy(out + off, &scale, 4);
+        memcpy(out + off + 4, &mn, 4);
+        memcpy(out + off + 8, &len, 4);
+        off += 12;
+        for (int64_t i = start; i < end; ++i) {
+            uint8_t q = 0;
+            if (scale != 0.0f) {
+                const float r = roundf((v[i] - mn) / scale);
+                q = isnan(r) ? 0 : r <= 0.0f ? 0 : r >= 255.0f ? 255 : (uint8_t)r;
+            }
+            out[off++] = q;
+        }
+    }
+}
+
+/* Returns 0, or -1 for a malformed stream (the reader would read past it). */
+int oracle_q8_dequantize(const uint8_t* stream, int64_t stream_bytes, int64_t n, float* out) {
+    int64_t off = 0, pos = 0;
+    while (pos < n) {
+        if (off + 12 > stream_bytes) return -1;
+        float scale, mn;
+        uint32_t len;
+        memcpy(&scale, stream + off, 4);
+        memcpy(&mn, stream + off + 4, 4);
+        memcpy(&len, stream + off + 8, 4);
+        off += 12;
+        const int64_t num = n - pos < 256 ? n - pos : 256;
+        if ((int64_t)len < num || off + (int64_t)len > stream_bytes) return -1;
+        for (int64_t i = 0; i < num; ++i) out[pos + i] = mn + (float)stream[off + i] * scale;
+        off += len;
+        pos += num;
+    }
+    return 0;
+}
+
+/* y[t][r] = sum_c x[t][c] * W[r][c] (+ b[r]): oom_inference.rs:168-180 per token,
+ * OpenMP over (token, row) pairs. */
+void oracle_linear(const float* x, int T, const float* w, const float* b, int rows, int cols, float* y) {
+#pragma omp parallel for collapse(2) schedule(static)
+    for (int t = 0; t < T; ++t)
+        for (int r = 0; r < rows; ++r) {
+            float sum = 0.0f;
+            const float* wr = w + (size_t)r * cols;
+            const float* xt = x + (size_t)t * cols;
+            for (int c = 0; c < cols; ++c) sum += xt[c] * wr[c];
+            y[(size_t)t * rows + r] = b ? sum + b[r] : sum;
+        }
+}
+
 void oracle_set_threads(int n) {
 #ifdef _OPENMP
     if (n > 0) omp_set_num_threads(n);

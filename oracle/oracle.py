@@ -66,6 +66,13 @@ def lib():
     L.oracle_bf16_to_f32.argtypes = [ctypes.c_uint16]
     L.oracle_bf16_to_f32.restype = c_float
     L.oracle_omp_max_threads.restype = c_int
+    _u8p = np.ctypeslib.ndpointer(dtype=np.uint8, flags="C_CONTIGUOUS")
+    L.oracle_q8_stream_bytes.argtypes = [ctypes.c_int64]
+    L.oracle_q8_stream_bytes.restype = ctypes.c_int64
+    L.oracle_q8_quantize.argtypes = [_f32p, ctypes.c_int64, _u8p]
+    L.oracle_q8_dequantize.argtypes = [_u8p, ctypes.c_int64, ctypes.c_int64, _f32p]
+    L.oracle_q8_dequantize.restype = c_int
+    L.oracle_linear.argtypes = [_f32p, c_int, _f32p, ctypes.c_void_p, c_int, c_int, _f32p]
     _lib = L
     return L
 
@@ -222,6 +229,34 @@ def f32_to_bf16_bits(x):
 def bf16_bits_to_f32(h):
     """bf16 bit patterns -> f32 by a 16-bit shift (safetensors2oom.rs:32-39)."""
     return (np.asarray(h, np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def q8_quantize(values) -> np.ndarray:
+    """The .oom Q8 block stream of a flat f32 tensor (src/gguf2oom.rs:719-770)."""
+    v = _c(values).ravel()
+    out = np.empty(int(lib().oracle_q8_stream_bytes(v.size)), np.uint8)
+    lib().oracle_q8_quantize(v, v.size, out)
+    return out
+
+
+def q8_dequantize(stream, n: int) -> np.ndarray:
+    """Dequantise n values of a Q8 block stream (src/quant.rs:431-463 with :201-224)."""
+    s = np.ascontiguousarray(stream, dtype=np.uint8)
+    out = np.empty(max(1, n), np.float32)
+    if lib().oracle_q8_dequantize(s, s.size, n, out) != 0:
+        raise ValueError("malformed Q8 block stream")
+    return out[:n]
+
+
+def linear(x, w, b=None):
+    """x [T, cols] @ w[rows, cols]^T (+ b): the reference's matvec per token (oom_inference.rs:168-180)."""
+    x, w = _c(x), _c(w)
+    T, cols = x.shape
+    rows = w.shape[0]
+    y = np.empty((T, rows), np.float32)
+    bb = None if b is None else _c(b)
+    lib().oracle_linear(x, T, w, _ptr(bb), rows, cols, y)
+    return y
 
 
 def omp_max_threads() -> int:
