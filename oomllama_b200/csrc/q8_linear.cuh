@@ -115,20 +115,33 @@ struct Q8Chunk {
   float x0[NT], x1[NT];           // chunk sums of tokens 8n + 2c and 8n + 2c + 1
 };
 
+// Per-thread addresses that do not change along the column range.
 template <int NT, int MT>
-__device__ __forceinline__ void q8_load_chunk(const Q8Args& a, int ch, int row0, int g, int c, Q8Chunk<NT, MT>& d) {
-  const int nchunks = a.cols / kQ8Chunk;
+struct Q8Base {
+  long long fa[MT];        // flattened index of row g of each row tile (row g + 8 is 8 rows on)
+  bool live[MT];           // row tile inside the matrix
+  const uint32_t* xh[NT];  // token 8n + g, this thread's 8 words of a chunk (null past n_tokens)
+  const float* xs0[NT];    // chunk sums of token 8n + 2c (8n + 2c + 1 follows a row later)
+  bool has0[NT], has1[NT];
+  long long xlo;           // xl - xh in words
+  long long row8;          // 8 * cols
+  int nchunks;
+};
+
+template <int NT, int MT>
+__device__ __forceinline__ void q8_load_chunk(const Q8Args& a, const Q8Base<NT, MT>& b, int ch,
+                                              Q8Chunk<NT, MT>& d) {
 #pragma unroll
   for (int m = 0; m < MT; ++m) {
-    if (row0 + 16 * m >= a.rows) {  // a row block's last tile may lie past the matrix
+    if (!b.live[m]) {  // a row block's last tile may lie past the matrix
       d.qa[m] = d.qb[m] = make_uint4(0, 0, 0, 0);
       d.sa[m] = d.ma[m] = d.sb[m] = d.mb[m] = 0.f;
       continue;
     }
-    const long long ra = (long long)(row0 + 16 * m + g) * a.cols, rb = ra + 8LL * a.cols;
-    d.qa[m] = ldg_stream16(a.q + ra + (long long)ch * kQ8Chunk + 16 * c);
-    d.qb[m] = ldg_stream16(a.q + rb + (long long)ch * kQ8Chunk + 16 * c);
-    const long long ba = (ra + (long long)ch * kQ8Chunk) >> 8, bb = (rb + (long long)ch * kQ8Chunk) >> 8;
+    const long long f = b.fa[m] + ch * kQ8Chunk;
+    d.qa[m] = ldg_stream16(a.q + f);
+    d.qb[m] = ldg_stream16(a.q + f + b.row8);
+    const long long ba = f >> 8, bb = (f + b.row8) >> 8;
     d.sa[m] = __ldg(a.scale + ba);
     d.ma[m] = __ldg(a.min + ba);
     d.sb[m] = __ldg(a.scale + bb);
@@ -136,13 +149,12 @@ __device__ __forceinline__ void q8_load_chunk(const Q8Args& a, int ch, int row0,
   }
 #pragma unroll
   for (int n = 0; n < NT; ++n) {
-    const int tok = 8 * n + g;
-    if (tok < a.n_tokens) {  // tokens past n_tokens contribute zero and are not read
-      const size_t xo = (size_t)tok * (a.cols / 2) + ch * (kQ8Chunk / 2) + 8 * c;
-      const uint4 h0 = __ldg(reinterpret_cast<const uint4*>(a.xh + xo));
-      const uint4 h1 = __ldg(reinterpret_cast<const uint4*>(a.xh + xo + 4));
-      const uint4 l0 = __ldg(reinterpret_cast<const uint4*>(a.xl + xo));
-      const uint4 l1 = __ldg(reinterpret_cast<const uint4*>(a.xl + xo + 4));
+    if (b.xh[n]) {  // tokens past n_tokens contribute zero and are not read
+      const uint32_t* ph = b.xh[n] + ch * (kQ8Chunk / 2);
+      const uint4 h0 = __ldg(reinterpret_cast<const uint4*>(ph));
+      const uint4 h1 = __ldg(reinterpret_cast<const uint4*>(ph + 4));
+      const uint4 l0 = __ldg(reinterpret_cast<const uint4*>(ph + b.xlo));
+      const uint4 l1 = __ldg(reinterpret_cast<const uint4*>(ph + b.xlo + 4));
       d.bh[n][0] = h0.x; d.bh[n][1] = h0.y; d.bh[n][2] = h0.z; d.bh[n][3] = h0.w;
       d.bh[n][4] = h1.x; d.bh[n][5] = h1.y; d.bh[n][6] = h1.z; d.bh[n][7] = h1.w;
       d.bl[n][0] = l0.x; d.bl[n][1] = l0.y; d.bl[n][2] = l0.z; d.bl[n][3] = l0.w;
@@ -151,16 +163,51 @@ __device__ __forceinline__ void q8_load_chunk(const Q8Args& a, int ch, int row0,
 #pragma unroll
       for (int e = 0; e < 8; ++e) d.bh[n][e] = d.bl[n][e] = 0u;
     }
-    const int t0 = 8 * n + 2 * c;
-    d.x0[n] = t0 < a.n_tokens ? __ldg(a.xsum + (size_t)t0 * nchunks + ch) : 0.f;
-    d.x1[n] = t0 + 1 < a.n_tokens ? __ldg(a.xsum + (size_t)(t0 + 1) * nchunks + ch) : 0.f;
+    d.x0[n] = b.has0[n] ? __ldg(b.xs0[n] + ch) : 0.f;
+    d.x1[n] = b.has1[n] ? __ldg(b.xs0[n] + b.nchunks + ch) : 0.f;
+  }
+}
+
+template <int NT, int MT>
+__device__ __forceinline__ void q8_compute_chunk(const Q8Chunk<NT, MT>& d, float (&acc)[MT][NT][4]) {
+#pragma unroll
+  for (int m = 0; m < MT; ++m) {
+    // A fragments of the 4 k-steps: step s takes bytes 4s..4s+3 of the thread's 16
+    const uint32_t wa[4] = {d.qa[m].x, d.qa[m].y, d.qa[m].z, d.qa[m].w};
+    const uint32_t wb[4] = {d.qb[m].x, d.qb[m].y, d.qb[m].z, d.qb[m].w};
+    uint32_t af[4][4];
+#pragma unroll
+    for (int s = 0; s < 4; ++s) {
+      af[s][0] = q8_pair(wa[s], 0x4140u);
+      af[s][1] = q8_pair(wb[s], 0x4140u);
+      af[s][2] = q8_pair(wa[s], 0x4342u);
+      af[s][3] = q8_pair(wb[s], 0x4342u);
+    }
+    const float ka = d.ma[m] - 1024.f * d.sa[m], kb = d.mb[m] - 1024.f * d.sb[m];
+#pragma unroll
+    for (int n = 0; n < NT; ++n) {
+      // hi and lo products accumulate in two independent chains
+      float dh[4] = {0.f, 0.f, 0.f, 0.f}, dl[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int s = 0; s < 4; ++s) {
+        mma_f16_16816(dh, af[s][0], af[s][1], af[s][2], af[s][3], d.bh[n][2 * s], d.bh[n][2 * s + 1]);
+        mma_f16_16816(dl, af[s][0], af[s][1], af[s][2], af[s][3], d.bl[n][2 * s], d.bl[n][2 * s + 1]);
+      }
+      // rows g, g + 8 x tokens 8n + 2c, 8n + 2c + 1
+      acc[m][n][0] = fmaf(d.sa[m], dh[0] + dl[0], fmaf(ka, d.x0[n], acc[m][n][0]));
+      acc[m][n][1] = fmaf(d.sa[m], dh[1] + dl[1], fmaf(ka, d.x1[n], acc[m][n][1]));
+      acc[m][n][2] = fmaf(d.sb[m], dh[2] + dl[2], fmaf(kb, d.x0[n], acc[m][n][2]));
+      acc[m][n][3] = fmaf(d.sb[m], dh[3] + dl[3], fmaf(kb, d.x1[n], acc[m][n][3]));
+    }
   }
 }
 
 // A CTA owns 16 * MT rows and a column range; its 8 warps take the range's
 // chunks round-robin, each chunk for all MT row tiles and NT token tiles.
+// Two chunk buffers alternate (the loop is unrolled by two), so the next
+// chunk's loads are in flight while the current one is computed.
 template <int NT, int MT>
-__global__ void __launch_bounds__(kQ8Warps * 32) q8_linear_kernel(const Q8Args a) {
+__global__ void __launch_bounds__(kQ8Warps * 32, 2) q8_linear_kernel(const Q8Args a) {
   __shared__ float red[kQ8Warps][MT][NT][4][32];
   __shared__ int s_last;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -170,6 +217,24 @@ __global__ void __launch_bounds__(kQ8Warps * 32) q8_linear_kernel(const Q8Args a
   const int nchunks = a.cols / kQ8Chunk;
   const int c0 = sp * a.chunks_per_split, c1 = min(nchunks, c0 + a.chunks_per_split);
 
+  Q8Base<NT, MT> b;
+  b.row8 = 8LL * a.cols;
+  b.xlo = a.xl - a.xh;
+  b.nchunks = nchunks;
+#pragma unroll
+  for (int m = 0; m < MT; ++m) {
+    b.live[m] = row0 + 16 * m < a.rows;
+    b.fa[m] = (long long)(row0 + 16 * m + g) * a.cols + 16 * c;  // block lookups ignore the low 8 bits
+  }
+#pragma unroll
+  for (int n = 0; n < NT; ++n) {
+    const int tok = 8 * n + g, t0 = 8 * n + 2 * c;
+    b.xh[n] = tok < a.n_tokens ? a.xh + (size_t)tok * (a.cols / 2) + 8 * c : nullptr;
+    b.xs0[n] = a.xsum + (size_t)t0 * nchunks;
+    b.has0[n] = t0 < a.n_tokens;
+    b.has1[n] = t0 + 1 < a.n_tokens;
+  }
+
   float acc[MT][NT][4];
 #pragma unroll
   for (int m = 0; m < MT; ++m)
@@ -178,43 +243,17 @@ __global__ void __launch_bounds__(kQ8Warps * 32) q8_linear_kernel(const Q8Args a
 #pragma unroll
       for (int e = 0; e < 4; ++e) acc[m][n][e] = 0.f;
 
+  Q8Chunk<NT, MT> d0, d1;
   int ch = c0 + warp;
-  Q8Chunk<NT, MT> cur;
-  if (ch < c1) q8_load_chunk<NT, MT>(a, ch, row0, g, c, cur);
-  for (; ch < c1; ch += kQ8Warps) {
-    Q8Chunk<NT, MT> nxt;
-    if (ch + kQ8Warps < c1) q8_load_chunk<NT, MT>(a, ch + kQ8Warps, row0, g, c, nxt);
-#pragma unroll
-    for (int m = 0; m < MT; ++m) {
-      // A fragments of the 4 k-steps: step s takes bytes 4s..4s+3 of the thread's 16
-      const uint32_t wa[4] = {cur.qa[m].x, cur.qa[m].y, cur.qa[m].z, cur.qa[m].w};
-      const uint32_t wb[4] = {cur.qb[m].x, cur.qb[m].y, cur.qb[m].z, cur.qb[m].w};
-      uint32_t af[4][4];
-#pragma unroll
-      for (int s = 0; s < 4; ++s) {
-        af[s][0] = q8_pair(wa[s], 0x4140u);
-        af[s][1] = q8_pair(wb[s], 0x4140u);
-        af[s][2] = q8_pair(wa[s], 0x4342u);
-        af[s][3] = q8_pair(wb[s], 0x4342u);
-      }
-      const float ka = cur.ma[m] - 1024.f * cur.sa[m], kb = cur.mb[m] - 1024.f * cur.sb[m];
-#pragma unroll
-      for (int n = 0; n < NT; ++n) {
-        // hi and lo products accumulate in two independent chains
-        float dh[4] = {0.f, 0.f, 0.f, 0.f}, dl[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-        for (int s = 0; s < 4; ++s) {
-          mma_f16_16816(dh, af[s][0], af[s][1], af[s][2], af[s][3], cur.bh[n][2 * s], cur.bh[n][2 * s + 1]);
-          mma_f16_16816(dl, af[s][0], af[s][1], af[s][2], af[s][3], cur.bl[n][2 * s], cur.bl[n][2 * s + 1]);
-        }
-        // rows g, g + 8 x tokens 8n + 2c, 8n + 2c + 1
-        acc[m][n][0] = fmaf(cur.sa[m], dh[0] + dl[0], fmaf(ka, cur.x0[n], acc[m][n][0]));
-        acc[m][n][1] = fmaf(cur.sa[m], dh[1] + dl[1], fmaf(ka, cur.x1[n], acc[m][n][1]));
-        acc[m][n][2] = fmaf(cur.sb[m], dh[2] + dl[2], fmaf(kb, cur.x0[n], acc[m][n][2]));
-        acc[m][n][3] = fmaf(cur.sb[m], dh[3] + dl[3], fmaf(kb, cur.x1[n], acc[m][n][3]));
-      }
-    }
-    cur = nxt;
+  if (ch < c1) q8_load_chunk<NT, MT>(a, b, ch, d0);
+  while (ch < c1) {
+    if (ch + kQ8Warps < c1) q8_load_chunk<NT, MT>(a, b, ch + kQ8Warps, d1);
+    q8_compute_chunk<NT, MT>(d0, acc);
+    ch += kQ8Warps;
+    if (ch >= c1) break;
+    if (ch + kQ8Warps < c1) q8_load_chunk<NT, MT>(a, b, ch + kQ8Warps, d0);
+    q8_compute_chunk<NT, MT>(d1, acc);
+    ch += kQ8Warps;
   }
 
   // the CTA's warps cover disjoint chunks of the same rows: sum them in warp order

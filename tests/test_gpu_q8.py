@@ -89,6 +89,7 @@ def test_q8_linear_rejects_odd_shapes(oracle, eng):
 
 
 def test_q8_linear_reports_activation_outside_fp16(oracle, eng):
+    # x enters the tensor cores as an fp16 hi / lo pair
     from oomllama_b200._lib import OomAttnError
     wq, _ = _matrix(oracle, 16, 64, seed=9)
     x = torch.zeros(1, 64, device="cuda")
