@@ -365,6 +365,91 @@ def bench_decode(args, dist_, torch, name):
             "merge": merge, "lens_sum": sum(lens), "kern_local_ms": kern_ms}
 
 
+# ---------------------------------------------------------------- Q8 linear (K-E, secondary)
+Q8_LAYER = (("qkv", 4608, 3584), ("o_proj", 3584, 3584), ("gate_up", 37888, 3584), ("down", 3584, 18944))
+
+
+def bench_q8(args, dist_, torch, T):
+    """One Qwen2.5-7B layer's linears from GPU-resident Q8 weights (qkv fused 4608x3584, o_proj 3584x3584,
+    gate+up fused 37888x3584, down 3584x18944) for T decode tokens: the weights a decode step streams
+    (src/oomllama.rs:425-439 dequantises and uploads them per call instead).  Two layers' weights
+    (466 MB) rotate, so no matrix is L2-resident when it is read."""
+    from oomllama_b200 import Q8Matrix, TurboConfig, TurboEngine
+    dev = torch.cuda.current_device()
+    eng = TurboEngine(TurboConfig(n_layers=1, hidden_size=0, n_heads=8, n_kv_heads=1, max_seq_len=16, max_seqs=1,
+                                  kv_dtype="bf16"), device=dev)
+    g = torch.Generator(device="cuda").manual_seed(21 + dist_.rank)
+    layers = []
+    for _ in range(2):
+        mats = []
+        for _, rows, cols in Q8_LAYER:
+            nb = (rows * cols + 255) // 256
+            q = torch.randint(0, 256, (rows * cols,), dtype=torch.uint8, device="cuda", generator=g)
+            mats.append(Q8Matrix(q, torch.rand(nb, device="cuda", generator=g) * 1e-3,
+                                 -torch.rand(nb, device="cuda", generator=g) * 0.1, rows, cols))
+        layers.append(mats)
+    xs = {cols: torch.randn(T, cols, device="cuda", generator=g) for _, _, cols in Q8_LAYER}
+    ys = {rows: torch.empty(T, rows, device="cuda") for _, rows, _ in Q8_LAYER}
+    byts = sum(r * c + 8 * ((r * c + 255) // 256) + 4 * T * (r + c) for _, r, c in Q8_LAYER)
+
+    def step(i):
+        for (name, rows, cols), w in zip(Q8_LAYER, layers[i % 2]):
+            eng.q8_linear(w, xs[cols], out=ys[rows])
+
+    # a decode step is replayed as a CUDA graph (8 launches: x split + linear per matrix), so the
+    # measurement is the kernels and their dependencies, not the Python host loop
+    side = torch.cuda.Stream()
+    graphs = []
+    with torch.cuda.stream(side):
+        for i in range(max(2, args.warmup)):
+            step(i)  # grows the library's scratch before capture
+        for i in range(2):
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr, stream=side):
+                step(i)
+            graphs.append(gr)
+    torch.cuda.synchronize()
+    eng.sync()
+    for i in range(args.warmup):
+        graphs[i % 2].replay()
+    steps = max(10, args.steps)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    dist_.barrier()
+    torch.cuda.synchronize()
+    t0.record()
+    for i in range(steps):
+        graphs[i % 2].replay()
+    t1.record()
+    torch.cuda.synchronize()
+    dist_.barrier()
+    eng.sync()
+    ms = dist_.max(t0.elapsed_time(t1) / steps)
+    del graphs
+    eng.close()
+    del layers
+    return ms, byts
+
+
+def cpu_q8_sample(T, rows_per_matrix=64):
+    """The oracle's Q8 dequantise + matvec (src/quant.rs:201-224, src/oom_inference.rs:168-180) on
+    rows_per_matrix rows of each matrix of the layer; returns GB/s of algorithmic bytes and threads."""
+    from oracle import oracle as O
+    O.build()
+    nt = O.set_threads(O.host_cores())
+    rng = np.random.default_rng(5)
+    total_bytes, total_s = 0, 0.0
+    for _, rows, cols in Q8_LAYER:
+        w = (rng.standard_normal((rows_per_matrix, cols)) * 0.02).astype(np.float32)
+        stream = O.q8_quantize(w)
+        x = rng.standard_normal((T, cols)).astype(np.float32)
+        t = time.perf_counter()
+        wd = O.q8_dequantize(stream, w.size).reshape(w.shape)
+        O.linear(x, wd)
+        total_s += time.perf_counter() - t
+        total_bytes += w.size + 8 * ((w.size + 255) // 256) + 4 * T * (rows_per_matrix + cols)
+    return total_bytes / total_s / 1e9, nt
+
+
 # ---------------------------------------------------------------- CPU baseline (oracle port)
 def cpu_prefill_sample(seconds_budget=8.0, threads=None):
     """Time the oracle's scalar causal attention (oom_inference.rs:240-272 per
@@ -487,6 +572,23 @@ def main():
                              else None},
             }
         line["decode"] = dec
+        q8 = {}
+        for T in (1, 8):
+            ms, byts = bench_q8(args, dist_, torch, T)
+            gbs = W * byts / (ms * 1e-3) / 1e9
+            q8[f"qwen7b-layer-T{T}"] = {
+                "hbm_gbs": gbs, "ms_per_step": ms, "bytes_per_step": byts, "tokens": T,
+                "linears": [f"{n} {r}x{c}" for n, r, c in Q8_LAYER],
+                "roofline": {"bound": "hbm", "kernel": "q8_linear_kernel (with q8_prep_x_kernel)",
+                             "achieved": gbs / W, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                             "frac": gbs / W / peaks["hbm_gbs"], "traffic": None},
+            }
+            if dist_.rank == 0 and W == 1 and not args.no_cpu_baseline:
+                v, nt = cpu_q8_sample(T)
+                q8[f"qwen7b-layer-T{T}"]["cpu_baseline"] = {
+                    "value": v, "unit": "GB/s", "cores": nt, "kind": "port",
+                    "sample": "64 rows of each linear: oracle Q8 dequantise + matvec"}
+        line["q8_linear"] = q8
     if dist_.rank == 0 and W == 1 and not args.no_cpu_baseline:
         v, nt, desc = cpu_prefill_sample()
         line["cpu_baseline"] = {"value": v, "unit": "TFLOP/s", "cores": nt, "kind": "port", "sample": desc}

@@ -1177,9 +1177,22 @@ int ensure_q8_scratch(oomattn_ctx* ctx, size_t bytes, int row_tiles) {
   return OOMATTN_OK;
 }
 
+// The linear kernel is a programmatic dependent of the x-split kernel before
+// it: it launches while that kernel runs, issues its first weight loads, and
+// waits for the split only before it reads x.
 template <int NT, int MT>
-void launch_q8_linear(const Q8Args& a, int row_blocks, cudaStream_t st) {
-  q8_linear_kernel<NT, MT><<<dim3(a.splits, row_blocks), kQ8Warps * 32, 0, st>>>(a);
+cudaError_t launch_q8_linear(const Q8Args& a, int row_blocks, cudaStream_t st) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(a.splits, row_blocks);
+  cfg.blockDim = dim3(kQ8Warps * 32);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, q8_linear_kernel<NT, MT>, a);
 }
 
 }  // namespace
@@ -1198,15 +1211,15 @@ extern "C" int oomattn_q8_linear(oomattn_ctx* ctx, const oomattn_q8_matrix* w, c
   DeviceGuard dg(ctx->device);
   const int rows = w->rows, cols = w->cols;
   const int nchunks = cols / kQ8Chunk;
-  // Tokens run in passes of up to 16 (two tiles of 8); the weights are re-read
-  // per pass.  A pass of up to 8 tokens uses row blocks of 32 rows (two row
-  // tiles per warp share each x fragment), a pass of 9-16 tokens 16 rows.
-  const int group = 16;
-  const int mt = n_tokens <= 8 ? 2 : 1;
+  // Tokens run in passes of up to 8 (one MMA token tile); the weights are
+  // re-read per pass.  Tall matrices use row blocks of 32 rows (two row tiles
+  // per warp share each x fragment), others 16 rows for more CTAs.
+  const int group = 8;
+  const int mt = rows >= 64 * ctx->num_sms ? 2 : 1;
   const int row_blocks = (rows + 16 * mt - 1) / (16 * mt);
-  // split-K so that the grid covers the SMs about four times over, keeping at
-  // least one chunk per warp of a CTA
-  const int want = std::max(1, (4 * ctx->num_sms + row_blocks - 1) / row_blocks);
+  // split-K only when the row blocks alone leave SMs idle, keeping at least one
+  // chunk per warp of a CTA (more, shorter CTAs only add pipeline fill and merge)
+  const int want = std::max(1, (ctx->num_sms + row_blocks - 1) / row_blocks);
   int splits = std::max(1, std::min(want, nchunks / kQ8Warps));
   const int cps = (nchunks + splits - 1) / splits;
   splits = (nchunks + cps - 1) / cps;
@@ -1221,7 +1234,6 @@ extern "C" int oomattn_q8_linear(oomattn_ctx* ctx, const oomattn_q8_matrix* w, c
   float* part = xsum + (size_t)tp_max * nchunks;
   for (int t0 = 0; t0 < n_tokens; t0 += group) {
     const int nt = std::min(group, n_tokens - t0);
-    const int ntile = nt <= 8 ? 1 : 2;
     const long long prep_warps = (long long)nt * nchunks;
     q8_prep_x_kernel<<<(unsigned)((prep_warps + 7) / 8), 256, 0, ctx->stream>>>(x + (size_t)t0 * cols, nt, cols, xh, xl,
                                                                                   xsum, ctx->d_status);
@@ -1243,13 +1255,9 @@ extern "C" int oomattn_q8_linear(oomattn_ctx* ctx, const oomattn_q8_matrix* w, c
     a.splits = splits;
     a.chunks_per_split = cps;
     a.status = ctx->d_status;
-    if (mt == 2)
-      launch_q8_linear<1, 2>(a, row_blocks, ctx->stream);
-    else if (ntile == 1)
-      launch_q8_linear<1, 1>(a, row_blocks, ctx->stream);
-    else
-      launch_q8_linear<2, 1>(a, row_blocks, ctx->stream);
-    CKLAUNCH();
+    const cudaError_t le = mt == 2 ? launch_q8_linear<1, 2>(a, row_blocks, ctx->stream)
+                                   : launch_q8_linear<1, 1>(a, row_blocks, ctx->stream);
+    if (le != cudaSuccess) return fail(ctx, OOMATTN_ERR_CUDA, "q8_linear launch: %s", cudaGetErrorString(le));
   }
   return OOMATTN_OK;
 }

@@ -63,6 +63,9 @@ struct Q8Args {
 // is reported through the status word.
 __global__ void q8_prep_x_kernel(const float* __restrict__ x, int n_tokens, int cols, uint32_t* xh, uint32_t* xl,
                                  float* xsum, int* status) {
+  // let the dependent linear kernel launch now: it waits for this grid's
+  // completion (griddepcontrol.wait) before it reads x
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int lane = threadIdx.x & 31;
   const int nchunks = cols / kQ8Chunk;
   const long long w = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -128,9 +131,9 @@ struct Q8Base {
   int nchunks;
 };
 
+// The weight bytes and their blocks' scale and min (independent of x).
 template <int NT, int MT>
-__device__ __forceinline__ void q8_load_chunk(const Q8Args& a, const Q8Base<NT, MT>& b, int ch,
-                                              Q8Chunk<NT, MT>& d) {
+__device__ __forceinline__ void q8_load_w(const Q8Args& a, const Q8Base<NT, MT>& b, int ch, Q8Chunk<NT, MT>& d) {
 #pragma unroll
   for (int m = 0; m < MT; ++m) {
     if (!b.live[m]) {  // a row block's last tile may lie past the matrix
@@ -147,6 +150,11 @@ __device__ __forceinline__ void q8_load_chunk(const Q8Args& a, const Q8Base<NT, 
     d.sb[m] = __ldg(a.scale + bb);
     d.mb[m] = __ldg(a.min + bb);
   }
+}
+
+// The x fragments and chunk sums (written by the split kernel).
+template <int NT, int MT>
+__device__ __forceinline__ void q8_load_x(const Q8Base<NT, MT>& b, int ch, Q8Chunk<NT, MT>& d) {
 #pragma unroll
   for (int n = 0; n < NT; ++n) {
     if (b.xh[n]) {  // tokens past n_tokens contribute zero and are not read
@@ -245,13 +253,23 @@ __global__ void __launch_bounds__(kQ8Warps * 32, 2) q8_linear_kernel(const Q8Arg
 
   Q8Chunk<NT, MT> d0, d1;
   int ch = c0 + warp;
-  if (ch < c1) q8_load_chunk<NT, MT>(a, b, ch, d0);
+  // the first chunk's weights do not depend on the x split: load them, then
+  // wait for the split kernel (launched before this one) to complete
+  if (ch < c1) q8_load_w<NT, MT>(a, b, ch, d0);
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  if (ch < c1) q8_load_x<NT, MT>(b, ch, d0);
   while (ch < c1) {
-    if (ch + kQ8Warps < c1) q8_load_chunk<NT, MT>(a, b, ch + kQ8Warps, d1);
+    if (ch + kQ8Warps < c1) {
+      q8_load_w<NT, MT>(a, b, ch + kQ8Warps, d1);
+      q8_load_x<NT, MT>(b, ch + kQ8Warps, d1);
+    }
     q8_compute_chunk<NT, MT>(d0, acc);
     ch += kQ8Warps;
     if (ch >= c1) break;
-    if (ch + kQ8Warps < c1) q8_load_chunk<NT, MT>(a, b, ch + kQ8Warps, d0);
+    if (ch + kQ8Warps < c1) {
+      q8_load_w<NT, MT>(a, b, ch + kQ8Warps, d0);
+      q8_load_x<NT, MT>(b, ch + kQ8Warps, d0);
+    }
     q8_compute_chunk<NT, MT>(d1, acc);
     ch += kQ8Warps;
   }
