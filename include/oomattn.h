@@ -280,6 +280,44 @@ int oomattn_q8_unpack(const uint8_t* stream /* host */, uint64_t stream_bytes, i
 int oomattn_q8_linear(oomattn_ctx* ctx, const oomattn_q8_matrix* w /* host struct */, const float* x,
                       int32_t n_tokens, const float* bias, float* y);
 
+/* ------------------------------------------- the layer steps around attention */
+
+/* GhostRMSNorm::forward (src/oomllama.rs:200-211): out[t] = x[t] /
+ * sqrt(mean(x[t]^2) + eps) * weight, f32, x and out [n_tokens][hidden],
+ * weight [hidden]; hidden % 4 == 0, 16-byte aligned rows (device). */
+int oomattn_rmsnorm(oomattn_ctx* ctx, const float* x, const float* weight, float eps, int32_t n_tokens,
+                    int32_t hidden, float* out);
+
+/* GhostMlp::forward (src/oomllama.rs:230-242) on resident Q8 weights, plus
+ * the decoder layer's residual add (src/oomllama.rs:401):
+ *   y = down(silu(gate(x)) * up(x)) (+ residual)
+ * gate, up [inter][hidden]; down [hidden][inter]; x, y, residual
+ * [n_tokens][hidden] f32 (residual may alias y, or be NULL).  The gated
+ * activation is formed while down's input is split, without a buffer of its
+ * own. */
+int oomattn_q8_mlp(oomattn_ctx* ctx, const oomattn_q8_matrix* gate, const oomattn_q8_matrix* up,
+                   const oomattn_q8_matrix* down, const float* x, int32_t n_tokens, const float* residual, float* y);
+
+/* The Q8 weights of one decoder layer (GhostDecoderLayer, src/oomllama.rs:366-402). */
+typedef struct oomattn_q8_layer {
+  oomattn_q8_matrix q, k, v, o;      /* [n_heads*128][hidden], [n_kv*128][hidden] x2, [hidden][n_heads*128] */
+  oomattn_q8_matrix gate, up, down;  /* [inter][hidden] x2, [hidden][inter] */
+  const float* bq;                   /* attention biases (Qwen), f32 or NULL */
+  const float* bk;
+  const float* bv;
+  const float* input_norm;           /* RMSNorm weights [hidden] */
+  const float* post_norm;
+  float eps;                         /* rms_norm_eps */
+} oomattn_q8_layer;
+
+/* GhostDecoderLayer::forward_turbo (src/oomllama.rs:387-402) for one new token
+ * of each of n_seqs sequences (decode), Q8 weights resident on the device:
+ *   h = x + o_proj(attention(rope(qkv(rmsnorm(x)))))      (the token is appended)
+ *   out = h + mlp(rmsnorm(h))
+ * x, out [n_seqs][hidden] f32 (device); sequence seq_ids[b] is batch row b. */
+int oomattn_decoder_layer_q8(oomattn_ctx* ctx, int32_t layer, int32_t n_seqs, const int32_t* seq_ids /* host */,
+                             const float* x, const oomattn_q8_layer* w /* host struct */, float* out);
+
 #ifdef __cplusplus
 }
 #endif

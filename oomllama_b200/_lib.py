@@ -26,7 +26,7 @@ EXPORTS = (
     "oomattn_set_seq_len", "oomattn_kv_pool", "oomattn_kv_write", "oomattn_kv_read", "oomattn_rope_table",
     "oomattn_compute_rope_table", "oomattn_rope_append", "oomattn_qkv_rope_append", "oomattn_decode", "oomattn_merge_partials",
     "oomattn_prefill", "oomattn_attention_forward_with_bias", "oomattn_decode_static_scratch",
-    "oomattn_q8_unpack", "oomattn_q8_linear",
+    "oomattn_q8_unpack", "oomattn_q8_linear", "oomattn_rmsnorm", "oomattn_q8_mlp", "oomattn_decoder_layer_q8",
 )
 
 
@@ -52,6 +52,14 @@ class Q8Matrix(ctypes.Structure):
     """oomattn_q8_matrix: device pointers of a resident Q8 matrix [rows][cols]."""
     _fields_ = [("q", ctypes.c_void_p), ("scale", ctypes.c_void_p), ("min", ctypes.c_void_p),
                 ("rows", ctypes.c_int32), ("cols", ctypes.c_int32)]
+
+
+class Q8Layer(ctypes.Structure):
+    """oomattn_q8_layer: one decoder layer's resident Q8 weights, biases and norm weights."""
+    _fields_ = [("q", Q8Matrix), ("k", Q8Matrix), ("v", Q8Matrix), ("o", Q8Matrix), ("gate", Q8Matrix),
+                ("up", Q8Matrix), ("down", Q8Matrix), ("bq", ctypes.c_void_p), ("bk", ctypes.c_void_p),
+                ("bv", ctypes.c_void_p), ("input_norm", ctypes.c_void_p), ("post_norm", ctypes.c_void_p),
+                ("eps", ctypes.c_float)]
 
 
 _lib = None
@@ -94,6 +102,10 @@ def load():
                                            ctypes.c_char_p, I], ctypes.c_int),
         "oomattn_q8_unpack": ([P, ctypes.c_uint64, ctypes.c_int64, P, P, P, ctypes.c_char_p, I], ctypes.c_int),
         "oomattn_q8_linear": ([P, ctypes.POINTER(Q8Matrix), P, I, P, P], ctypes.c_int),
+        "oomattn_rmsnorm": ([P, P, P, F, I, I, P], ctypes.c_int),
+        "oomattn_q8_mlp": ([P, ctypes.POINTER(Q8Matrix), ctypes.POINTER(Q8Matrix), ctypes.POINTER(Q8Matrix), P, I, P,
+                            P], ctypes.c_int),
+        "oomattn_decoder_layer_q8": ([P, I, I, IP, P, ctypes.POINTER(Q8Layer), P], ctypes.c_int),
     }
     for name, (args, res) in sig.items():
         fn = getattr(L, name)

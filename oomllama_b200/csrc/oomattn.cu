@@ -89,6 +89,9 @@ struct oomattn_ctx {
   size_t q8_scratch_bytes = 0;
   unsigned* d_q8_counters = nullptr;
   int q8_counters_n = 0;
+  // decoder-layer step: normalised activations, projections, MLP intermediates
+  float* d_layer_scratch = nullptr;
+  size_t layer_scratch_bytes = 0;
 };
 
 namespace {
@@ -493,7 +496,7 @@ int oomattn_destroy(oomattn_ctx* ctx) {
   if (ctx->cublas) cublasDestroy(ctx->cublas);
   void* ptrs[] = {ctx->kpool,     ctx->vpool,      ctx->d_block_table, ctx->d_cos,    ctx->d_sin,
                   ctx->d_part_o,  ctx->d_part_lse, ctx->d_counters,    ctx->d_status, ctx->d_scratch,
-                  ctx->d_q8_scratch, ctx->d_q8_counters};
+                  ctx->d_q8_scratch, ctx->d_q8_counters, ctx->d_layer_scratch};
   for (void* p : ptrs)
     if (p) cudaFree(p);
   delete ctx;
@@ -1197,67 +1200,234 @@ cudaError_t launch_q8_linear(const Q8Args& a, int row_blocks, cudaStream_t st) {
 
 }  // namespace
 
-extern "C" int oomattn_q8_linear(oomattn_ctx* ctx, const oomattn_q8_matrix* w, const float* x, int32_t n_tokens,
-                                 const float* bias, float* y) {
-  if (!ctx) return OOMATTN_ERR_INVALID_ARG;
-  if (!w || !x || !y || !w->q || !w->scale || !w->min) return fail(ctx, OOMATTN_ERR_INVALID_ARG, "null pointer");
-  if (n_tokens < 0 || w->rows <= 0 || w->cols <= 0) return fail(ctx, OOMATTN_ERR_INVALID_ARG, "bad shape");
+namespace {
+
+// One output of a Q8 pass: y = x W^T (+ bias) (+ residual).
+struct Q8Job {
+  const oomattn_q8_matrix* w;
+  const float* bias;
+  const float* residual;
+  float* y;
+};
+
+int check_q8_matrix(oomattn_ctx* ctx, const oomattn_q8_matrix* w, int cols) {
+  if (!w || !w->q || !w->scale || !w->min) return fail(ctx, OOMATTN_ERR_INVALID_ARG, "null Q8 matrix pointer");
+  if (w->rows <= 0 || w->cols <= 0) return fail(ctx, OOMATTN_ERR_INVALID_ARG, "bad Q8 matrix shape");
   if (w->rows % 16 || w->cols % kQ8Chunk)
-    return fail(ctx, OOMATTN_ERR_UNSUPPORTED, "q8_linear needs rows %% 16 == 0 and cols %% 64 == 0 (got %d x %d)",
+    return fail(ctx, OOMATTN_ERR_UNSUPPORTED, "Q8 linear needs rows %% 16 == 0 and cols %% 64 == 0 (got %d x %d)",
                 w->rows, w->cols);
-  if (reinterpret_cast<uintptr_t>(w->q) % 16 || reinterpret_cast<uintptr_t>(x) % 16)
-    return fail(ctx, OOMATTN_ERR_INVALID_ARG, "q and x must be 16-byte aligned");
-  if (n_tokens == 0) return OOMATTN_OK;
-  DeviceGuard dg(ctx->device);
-  const int rows = w->rows, cols = w->cols;
+  if (cols >= 0 && w->cols != cols)
+    return fail(ctx, OOMATTN_ERR_INVALID_ARG, "Q8 matrix has %d columns, the input %d", w->cols, cols);
+  if (reinterpret_cast<uintptr_t>(w->q) % 16) return fail(ctx, OOMATTN_ERR_INVALID_ARG, "q must be 16-byte aligned");
+  return OOMATTN_OK;
+}
+
+struct Q8Plan {
+  int mt, row_blocks, splits, cps;
+};
+
+// Tall matrices use row blocks of 32 rows (two row tiles per warp share each x
+// fragment), others 16 rows for more CTAs.  Split-K only when the row blocks
+// alone leave SMs idle, keeping at least one chunk per warp of a CTA (more,
+// shorter CTAs only add pipeline fill and merge).
+Q8Plan plan_q8(const oomattn_ctx* ctx, int rows, int cols) {
+  Q8Plan p;
   const int nchunks = cols / kQ8Chunk;
-  // Tokens run in passes of up to 8 (one MMA token tile); the weights are
-  // re-read per pass.  Tall matrices use row blocks of 32 rows (two row tiles
-  // per warp share each x fragment), others 16 rows for more CTAs.
+  p.mt = rows >= 64 * ctx->num_sms ? 2 : 1;
+  p.row_blocks = (rows + 16 * p.mt - 1) / (16 * p.mt);
+  const int want = std::max(1, (ctx->num_sms + p.row_blocks - 1) / p.row_blocks);
+  p.splits = std::max(1, std::min(want, nchunks / kQ8Warps));
+  p.cps = (nchunks + p.splits - 1) / p.splits;
+  p.splits = (nchunks + p.cps - 1) / p.cps;
+  return p;
+}
+
+// Runs every job on the same input: x, or silu(x) * up when `up` is given.
+// Tokens run in passes of up to 8 (one MMA token tile): one x split per pass,
+// then each job's linear, a programmatic dependent of the kernel before it.
+int q8_run(oomattn_ctx* ctx, const Q8Job* jobs, int n_jobs, const float* x, const float* up, int n_tokens) {
+  if (!x || n_tokens < 0) return fail(ctx, OOMATTN_ERR_INVALID_ARG, "bad Q8 input");
+  if (reinterpret_cast<uintptr_t>(x) % 16 || (up && reinterpret_cast<uintptr_t>(up) % 16))
+    return fail(ctx, OOMATTN_ERR_INVALID_ARG, "x must be 16-byte aligned");
+  const int cols = jobs[0].w ? jobs[0].w->cols : 0;
+  size_t part_floats = 0;
+  int max_blocks = 1;
+  for (int j = 0; j < n_jobs; ++j) {
+    int rc = check_q8_matrix(ctx, jobs[j].w, cols);
+    if (rc) return rc;
+    if (!jobs[j].y) return fail(ctx, OOMATTN_ERR_INVALID_ARG, "null Q8 output");
+    const Q8Plan p = plan_q8(ctx, jobs[j].w->rows, cols);
+    part_floats = std::max(part_floats, (size_t)p.splits * 8 * jobs[j].w->rows);
+    max_blocks = std::max(max_blocks, p.row_blocks);
+  }
+  if (n_tokens == 0) return OOMATTN_OK;
   const int group = 8;
-  const int mt = rows >= 64 * ctx->num_sms ? 2 : 1;
-  const int row_blocks = (rows + 16 * mt - 1) / (16 * mt);
-  // split-K only when the row blocks alone leave SMs idle, keeping at least one
-  // chunk per warp of a CTA (more, shorter CTAs only add pipeline fill and merge)
-  const int want = std::max(1, (ctx->num_sms + row_blocks - 1) / row_blocks);
-  int splits = std::max(1, std::min(want, nchunks / kQ8Warps));
-  const int cps = (nchunks + splits - 1) / splits;
-  splits = (nchunks + cps - 1) / cps;
-  const int tp_max = std::min(group, (n_tokens + 7) / 8 * 8);
-  const size_t xw = (size_t)tp_max * (cols / 2);
-  const size_t bytes = 2 * xw * 4 + (size_t)tp_max * nchunks * 4 + (size_t)splits * tp_max * rows * 4 + 256;
-  int rc = ensure_q8_scratch(ctx, bytes, row_blocks);
+  const int nchunks = cols / kQ8Chunk;
+  const size_t xw = (size_t)group * (cols / 2);
+  const size_t bytes = 2 * xw * 4 + (size_t)group * nchunks * 4 + part_floats * 4 + 256;
+  int rc = ensure_q8_scratch(ctx, bytes, max_blocks);
   if (rc) return rc;
   uint32_t* xh = reinterpret_cast<uint32_t*>(ctx->d_q8_scratch);
   uint32_t* xl = xh + xw;
   float* xsum = reinterpret_cast<float*>(xl + xw);
-  float* part = xsum + (size_t)tp_max * nchunks;
+  float* part = xsum + (size_t)group * nchunks;
   for (int t0 = 0; t0 < n_tokens; t0 += group) {
     const int nt = std::min(group, n_tokens - t0);
     const long long prep_warps = (long long)nt * nchunks;
-    q8_prep_x_kernel<<<(unsigned)((prep_warps + 7) / 8), 256, 0, ctx->stream>>>(x + (size_t)t0 * cols, nt, cols, xh, xl,
-                                                                                  xsum, ctx->d_status);
+    q8_prep_x_kernel<<<(unsigned)((prep_warps + 7) / 8), 256, 0, ctx->stream>>>(
+        x + (size_t)t0 * cols, up ? up + (size_t)t0 * cols : nullptr, nt, cols, xh, xl, xsum, ctx->d_status);
     CKLAUNCH();
-    Q8Args a;
-    a.q = w->q;
-    a.scale = w->scale;
-    a.min = w->min;
-    a.rows = rows;
-    a.cols = cols;
-    a.xh = xh;
-    a.xl = xl;
-    a.xsum = xsum;
-    a.n_tokens = nt;
-    a.bias = bias;
-    a.y = y + (size_t)t0 * rows;
-    a.part = part;
-    a.counters = ctx->d_q8_counters;
-    a.splits = splits;
-    a.chunks_per_split = cps;
-    a.status = ctx->d_status;
-    const cudaError_t le = mt == 2 ? launch_q8_linear<1, 2>(a, row_blocks, ctx->stream)
-                                   : launch_q8_linear<1, 1>(a, row_blocks, ctx->stream);
-    if (le != cudaSuccess) return fail(ctx, OOMATTN_ERR_CUDA, "q8_linear launch: %s", cudaGetErrorString(le));
+    for (int j = 0; j < n_jobs; ++j) {
+      const oomattn_q8_matrix* w = jobs[j].w;
+      const Q8Plan p = plan_q8(ctx, w->rows, cols);
+      Q8Args a;
+      a.q = w->q;
+      a.scale = w->scale;
+      a.min = w->min;
+      a.rows = w->rows;
+      a.cols = cols;
+      a.xh = xh;
+      a.xl = xl;
+      a.xsum = xsum;
+      a.n_tokens = nt;
+      a.bias = jobs[j].bias;
+      a.residual = jobs[j].residual ? jobs[j].residual + (size_t)t0 * w->rows : nullptr;
+      a.y = jobs[j].y + (size_t)t0 * w->rows;
+      a.part = part;
+      a.counters = ctx->d_q8_counters;
+      a.splits = p.splits;
+      a.chunks_per_split = p.cps;
+      a.status = ctx->d_status;
+      const cudaError_t le = p.mt == 2 ? launch_q8_linear<1, 2>(a, p.row_blocks, ctx->stream)
+                                       : launch_q8_linear<1, 1>(a, p.row_blocks, ctx->stream);
+      if (le != cudaSuccess) return fail(ctx, OOMATTN_ERR_CUDA, "q8_linear launch: %s", cudaGetErrorString(le));
+    }
   }
   return OOMATTN_OK;
+}
+
+// Per-context buffers of the layer step (grown on demand).
+float* layer_scratch(oomattn_ctx* ctx, size_t floats, int* rc) {
+  if (floats * 4 > ctx->layer_scratch_bytes) {
+    if (ctx->d_layer_scratch) {
+      cudaStreamSynchronize(ctx->stream);
+      cudaFree(ctx->d_layer_scratch);
+      ctx->d_layer_scratch = nullptr;
+      ctx->layer_scratch_bytes = 0;
+    }
+    if (cudaMalloc(&ctx->d_layer_scratch, floats * 4) != cudaSuccess) {
+      *rc = fail(ctx, OOMATTN_ERR_NO_MEMORY, "layer scratch allocation of %zu bytes failed", floats * 4);
+      return nullptr;
+    }
+    ctx->layer_scratch_bytes = floats * 4;
+  }
+  *rc = OOMATTN_OK;
+  return ctx->d_layer_scratch;
+}
+
+int run_rmsnorm(oomattn_ctx* ctx, const float* x, const float* w, float eps, int n_tokens, int hidden, float* out) {
+  if (!x || !w || !out || n_tokens < 0 || hidden <= 0) return fail(ctx, OOMATTN_ERR_INVALID_ARG, "bad rmsnorm arguments");
+  if (hidden % 4 || !aligned16(x) || !aligned16(w) || !aligned16(out))
+    return fail(ctx, OOMATTN_ERR_INVALID_ARG, "rmsnorm needs hidden %% 4 == 0 and 16-byte aligned rows");
+  if (n_tokens == 0) return OOMATTN_OK;
+  rmsnorm_kernel<<<n_tokens, kNormThreads, 0, ctx->stream>>>(x, w, eps, hidden, out);
+  CKLAUNCH();
+  return OOMATTN_OK;
+}
+
+}  // namespace
+
+extern "C" int oomattn_q8_linear(oomattn_ctx* ctx, const oomattn_q8_matrix* w, const float* x, int32_t n_tokens,
+                                 const float* bias, float* y) {
+  if (!ctx) return OOMATTN_ERR_INVALID_ARG;
+  if (!y) return fail(ctx, OOMATTN_ERR_INVALID_ARG, "null pointer");
+  DeviceGuard dg(ctx->device);
+  const Q8Job job{w, bias, nullptr, y};
+  return q8_run(ctx, &job, 1, x, nullptr, n_tokens);
+}
+
+extern "C" int oomattn_rmsnorm(oomattn_ctx* ctx, const float* x, const float* weight, float eps, int32_t n_tokens,
+                               int32_t hidden, float* out) {
+  if (!ctx) return OOMATTN_ERR_INVALID_ARG;
+  DeviceGuard dg(ctx->device);
+  return run_rmsnorm(ctx, x, weight, eps, n_tokens, hidden, out);
+}
+
+extern "C" int oomattn_q8_mlp(oomattn_ctx* ctx, const oomattn_q8_matrix* gate, const oomattn_q8_matrix* up,
+                              const oomattn_q8_matrix* down, const float* x, int32_t n_tokens, const float* residual,
+                              float* y) {
+  if (!ctx) return OOMATTN_ERR_INVALID_ARG;
+  if (!gate || !up || !down || !y) return fail(ctx, OOMATTN_ERR_INVALID_ARG, "null pointer");
+  if (gate->rows != up->rows || gate->cols != up->cols || down->cols != gate->rows || down->rows != gate->cols)
+    return fail(ctx, OOMATTN_ERR_INVALID_ARG, "MLP shapes disagree: gate %dx%d, up %dx%d, down %dx%d", gate->rows,
+                gate->cols, up->rows, up->cols, down->rows, down->cols);
+  if (n_tokens <= 0) return n_tokens == 0 ? OOMATTN_OK : fail(ctx, OOMATTN_ERR_INVALID_ARG, "negative n_tokens");
+  DeviceGuard dg(ctx->device);
+  int rc;
+  const size_t inter = (size_t)gate->rows;
+  float* g = layer_scratch(ctx, 2 * inter * n_tokens + 64, &rc);
+  if (rc) return rc;
+  float* u = g + inter * n_tokens + 32;  // 128-byte offset keeps both 16-byte aligned
+  const Q8Job gu[2] = {{gate, nullptr, nullptr, g}, {up, nullptr, nullptr, u}};
+  rc = q8_run(ctx, gu, 2, x, nullptr, n_tokens);
+  if (rc) return rc;
+  const Q8Job dn{down, nullptr, residual, y};
+  return q8_run(ctx, &dn, 1, g, u, n_tokens);
+}
+
+extern "C" int oomattn_decoder_layer_q8(oomattn_ctx* ctx, int32_t layer, int32_t n_seqs, const int32_t* seq_ids,
+                                        const float* x, const oomattn_q8_layer* w, float* out) {
+  if (!ctx) return OOMATTN_ERR_INVALID_ARG;
+  if (!seq_ids || !x || !w || !out || n_seqs <= 0)
+    return fail(ctx, OOMATTN_ERR_INVALID_ARG, "bad decoder_layer_q8 arguments");
+  const int H = ctx->cfg.hidden_size, hq = ctx->cfg.n_heads, hkv = ctx->cfg.n_kv_heads;
+  const int nq = hq * kHeadDim, nkv = hkv * kHeadDim;
+  if (w->q.rows != nq || w->k.rows != nkv || w->v.rows != nkv || w->q.cols != H || w->k.cols != H ||
+      w->v.cols != H || w->o.rows != H || w->o.cols != nq || w->gate.cols != H || w->up.cols != H ||
+      w->up.rows != w->gate.rows || w->down.rows != H || w->down.cols != w->gate.rows)
+    return fail(ctx, OOMATTN_ERR_INVALID_ARG, "decoder_layer_q8 weight shapes do not match the configuration");
+  if (!w->input_norm || !w->post_norm) return fail(ctx, OOMATTN_ERR_INVALID_ARG, "null norm weights");
+  int rc = check_layer(ctx, layer);
+  if (rc) return rc;
+  DeviceGuard dg(ctx->device);
+  const size_t B = (size_t)n_seqs, inter = (size_t)w->gate.rows;
+  // scratch: normalised x, q, k, v, rotated q, attention output, residual stream h
+  const size_t need = B * (2 * H + 3 * nq + 2 * nkv) + 8 * 32;
+  float* sb = layer_scratch(ctx, need + 2 * inter * B + 64, &rc);
+  if (rc) return rc;
+  auto carve = [&](size_t n) {
+    float* p = sb;
+    sb += (n + 31) / 32 * 32;  // 128-byte aligned pieces
+    return p;
+  };
+  float* xn = carve(B * H);
+  float* q = carve(B * nq);
+  float* k = carve(B * nkv);
+  float* v = carve(B * nkv);
+  float* qr = carve(B * nq);
+  float* att = carve(B * nq);
+  float* h = carve(B * H);
+  float* g = carve(B * inter);
+  float* u = carve(B * inter);
+  // GhostDecoderLayer::forward_turbo (src/oomllama.rs:387-402): h = x + attn(norm(x)); out = h + mlp(norm(h))
+  rc = run_rmsnorm(ctx, x, w->input_norm, w->eps, n_seqs, H, xn);
+  if (rc) return rc;
+  const Q8Job qkv[3] = {{&w->q, w->bq, nullptr, q}, {&w->k, w->bk, nullptr, k}, {&w->v, w->bv, nullptr, v}};
+  rc = q8_run(ctx, qkv, 3, xn, nullptr, n_seqs);
+  if (rc) return rc;
+  rc = oomattn_rope_append(ctx, layer, n_seqs, seq_ids, 1, q, k, v, OOMATTN_DTYPE_F32, nullptr, nullptr, nullptr, qr,
+                           OOMATTN_DTYPE_F32);
+  if (rc) return rc;
+  rc = oomattn_decode(ctx, layer, n_seqs, seq_ids, nullptr, qr, att, nullptr);
+  if (rc) return rc;
+  const Q8Job o{&w->o, nullptr, x, h};
+  rc = q8_run(ctx, &o, 1, att, nullptr, n_seqs);
+  if (rc) return rc;
+  rc = run_rmsnorm(ctx, h, w->post_norm, w->eps, n_seqs, H, xn);
+  if (rc) return rc;
+  const Q8Job gu[2] = {{&w->gate, nullptr, nullptr, g}, {&w->up, nullptr, nullptr, u}};
+  rc = q8_run(ctx, gu, 2, xn, nullptr, n_seqs);
+  if (rc) return rc;
+  const Q8Job dn{&w->down, nullptr, h, out};
+  return q8_run(ctx, &dn, 1, g, u, n_seqs);
 }

@@ -49,6 +49,7 @@ struct Q8Args {
   const float* xsum;    // [n_tokens][cols / 64]
   int n_tokens;
   const float* bias;    // [rows] or null
+  const float* residual;  // [n_tokens][rows] added to y, or null (may alias y)
   float* y;             // [n_tokens][rows]
   float* part;          // [splits][8 * token tiles][rows]: split-K partial sums
   unsigned* counters;   // [row blocks]: arrivals per row block, zero between launches
@@ -57,12 +58,23 @@ struct Q8Args {
   int* status;
 };
 
+// y = x W^T + bias + residual for one output element (the residual add of a
+// decoder layer, src/oomllama.rs:391, :401).
+__device__ __forceinline__ float q8_epilogue(const Q8Args& a, int tok, int row, float v) {
+  if (a.bias) v += a.bias[row];
+  if (a.residual) v += a.residual[(size_t)tok * a.rows + row];
+  return v;
+}
+
 // x -> (hi, lo) fp16 pairs and per-chunk sums.  One warp per (token, 64-column
 // chunk): lane l owns columns 2l, 2l+1.  The chunk sum is a fixed shuffle
 // tree, so it does not depend on timing.  |x| >= 65504 has no fp16 image: it
 // is reported through the status word.
-__global__ void q8_prep_x_kernel(const float* __restrict__ x, int n_tokens, int cols, uint32_t* xh, uint32_t* xl,
-                                 float* xsum, int* status) {
+// With `up` given, the split input is the MLP's gated activation
+// silu(x) * up = x * sigmoid(x) * up (GhostMlp::forward, src/oomllama.rs:230-242),
+// so the down projection reads it without a separate kernel or buffer.
+__global__ void q8_prep_x_kernel(const float* __restrict__ x, const float* __restrict__ up, int n_tokens, int cols,
+                                 uint32_t* xh, uint32_t* xl, float* xsum, int* status) {
   // let the dependent linear kernel launch now: it waits for this grid's
   // completion (griddepcontrol.wait) before it reads x
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -71,7 +83,12 @@ __global__ void q8_prep_x_kernel(const float* __restrict__ x, int n_tokens, int 
   const long long w = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (w >= (long long)n_tokens * nchunks) return;
   const int t = (int)(w / nchunks), ch = (int)(w % nchunks);
-  const float2 v = *reinterpret_cast<const float2*>(x + (size_t)t * cols + ch * kQ8Chunk + 2 * lane);
+  float2 v = *reinterpret_cast<const float2*>(x + (size_t)t * cols + ch * kQ8Chunk + 2 * lane);
+  if (up) {
+    const float2 u = *reinterpret_cast<const float2*>(up + (size_t)t * cols + ch * kQ8Chunk + 2 * lane);
+    v.x = v.x * (1.f / (1.f + expf(-v.x))) * u.x;
+    v.y = v.y * (1.f / (1.f + expf(-v.y))) * u.y;
+  }
   const __half2 hi = __floats2half2_rn(v.x, v.y);
   const float2 hf = __half22float2(hi);
   const __half2 lo = __floats2half2_rn(v.x - hf.x, v.y - hf.y);
@@ -294,7 +311,7 @@ __global__ void __launch_bounds__(kQ8Warps * 32, 2) q8_linear_kernel(const Q8Arg
     const int tok = 8 * n + 2 * (l & 3) + (e & 1);
     if (row >= a.rows || tok >= a.n_tokens) continue;
     if (a.splits == 1)
-      a.y[(size_t)tok * a.rows + row] = v + (a.bias ? a.bias[row] : 0.f);
+      a.y[(size_t)tok * a.rows + row] = q8_epilogue(a, tok, row, v);
     else
       part[(size_t)tok * a.rows + row] = v;
   }
@@ -314,9 +331,42 @@ __global__ void __launch_bounds__(kQ8Warps * 32, 2) q8_linear_kernel(const Q8Arg
     if (row >= a.rows) continue;
     float v = 0.f;
     for (int s = 0; s < a.splits; ++s) v += __ldcg(a.part + ((size_t)s * tp + tok) * a.rows + row);
-    a.y[(size_t)tok * a.rows + row] = v + (a.bias ? a.bias[row] : 0.f);
+    a.y[(size_t)tok * a.rows + row] = q8_epilogue(a, tok, row, v);
   }
   if (threadIdx.x == 0) a.counters[rb] = 0;
+}
+
+// ------------------------------------------------------------------ RMSNorm
+// out[t] = x[t] / sqrt(mean(x[t]^2) + eps) * w  (GhostRMSNorm::forward,
+// src/oomllama.rs:200-211), f32.  One CTA per token: the sum of squares is a
+// fixed-order block reduction; the division and square root are IEEE.
+constexpr int kNormThreads = 256;
+__global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(const float* __restrict__ x,
+                                                               const float* __restrict__ w, float eps, int hidden,
+                                                               float* __restrict__ out) {
+  __shared__ float part[kNormThreads / 32];
+  const int t = blockIdx.x;
+  const float* xr = x + (size_t)t * hidden;
+  float s = 0.f;
+  for (int i = threadIdx.x * 4; i < hidden; i += kNormThreads * 4) {
+    const float4 v = *reinterpret_cast<const float4*>(xr + i);
+    s += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+  }
+#pragma unroll
+  for (int d = 16; d > 0; d >>= 1) s += __shfl_xor_sync(0xffffffffu, s, d);
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = s;
+  __syncthreads();
+  float tot = 0.f;
+#pragma unroll
+  for (int k = 0; k < kNormThreads / 32; ++k) tot += part[k];
+  const float denom = sqrtf(tot / (float)hidden + eps);
+  float* orow = out + (size_t)t * hidden;
+  for (int i = threadIdx.x * 4; i < hidden; i += kNormThreads * 4) {
+    const float4 v = *reinterpret_cast<const float4*>(xr + i);
+    const float4 g = *reinterpret_cast<const float4*>(w + i);
+    *reinterpret_cast<float4*>(orow + i) =
+        make_float4(v.x / denom * g.x, v.y / denom * g.y, v.z / denom * g.z, v.w / denom * g.w);
+  }
 }
 
 }  // namespace oomattn

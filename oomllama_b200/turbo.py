@@ -338,6 +338,42 @@ class TurboEngine:
         return out
 
 
+    # ------------------------------------------------------------ the layer steps around attention
+    def rmsnorm(self, x: torch.Tensor, weight: torch.Tensor, eps: float, out=None):
+        """GhostRMSNorm::forward (src/oomllama.rs:200-211): x [T, H] f32 -> [T, H]."""
+        T, H = x.shape
+        _dev(x, "x", self.device, dtype=torch.float32)
+        _dev(weight, "weight", self.device, dtype=torch.float32, numel=H)
+        out = torch.empty_like(x) if out is None else _dev(out, "out", self.device, dtype=torch.float32, numel=T * H)
+        self._bind_stream()
+        check(self._ctx, self._L.oomattn_rmsnorm(self._ctx, _ptr(x), _ptr(weight), float(eps), T, H, _ptr(out)))
+        return out
+
+    def q8_mlp(self, gate: "Q8Matrix", up: "Q8Matrix", down: "Q8Matrix", x: torch.Tensor, residual=None, out=None):
+        """GhostMlp::forward (src/oomllama.rs:230-242) plus the residual add: down(silu(gate x) * up x) (+ residual)."""
+        T, H = x.shape
+        _dev(x, "x", self.device, dtype=torch.float32)
+        if residual is not None:
+            _dev(residual, "residual", self.device, dtype=torch.float32, numel=T * down.rows)
+        out = torch.empty(T, down.rows, dtype=torch.float32, device=x.device) if out is None else out
+        self._bind_stream()
+        check(self._ctx, self._L.oomattn_q8_mlp(self._ctx, ctypes.byref(gate.c_struct()), ctypes.byref(up.c_struct()),
+                                                ctypes.byref(down.c_struct()), _ptr(x), T, _ptr(residual), _ptr(out)))
+        return out
+
+    def decoder_layer_q8(self, layer: int, seq_ids, x: torch.Tensor, w: "Q8DecoderLayer", out=None):
+        """GhostDecoderLayer::forward_turbo (src/oomllama.rs:387-402) for one new token per sequence:
+        x [B, hidden] f32 -> [B, hidden]; appends each sequence's token to the cache of `layer`."""
+        B, H = x.shape
+        _dev(x, "x", self.device, dtype=torch.float32)
+        out = torch.empty_like(x) if out is None else _dev(out, "out", self.device, dtype=torch.float32, numel=B * H)
+        self._bind_stream()
+        ids = int_array(seq_ids)
+        check(self._ctx, self._L.oomattn_decoder_layer_q8(self._ctx, layer, B, ids, _ptr(x),
+                                                          ctypes.byref(w.c_struct()), _ptr(out)))
+        return out
+
+
 def q8_unpack(stream, n_values: int):
     """Unpack one .oom Q8 tensor's block stream ([f32 scale][f32 min][u32 len][bytes] per 256 values,
     src/gguf2oom.rs:823-826) into host arrays (q uint8 [n_values], scale, min f32 [n_blocks])."""
@@ -393,3 +429,28 @@ def _alias(ptr: int, shape, dtype, device: int) -> torch.Tensor:
     with torch.cuda.device(device):
         raw = torch.as_tensor(_Holder(), device=f"cuda:{device}")
     return raw.view(dtype).view(*shape)
+
+
+@dataclass
+class Q8DecoderLayer:
+    """One decoder layer's resident weights (GhostDecoderLayer, src/oomllama.rs:366-402): Q8 projections and MLP,
+    f32 attention biases (or None) and RMSNorm weights."""
+    q: Q8Matrix
+    k: Q8Matrix
+    v: Q8Matrix
+    o: Q8Matrix
+    gate: Q8Matrix
+    up: Q8Matrix
+    down: Q8Matrix
+    input_norm: torch.Tensor
+    post_norm: torch.Tensor
+    eps: float
+    bq: torch.Tensor = None
+    bk: torch.Tensor = None
+    bv: torch.Tensor = None
+
+    def c_struct(self) -> _lib.Q8Layer:
+        p = lambda t: None if t is None else t.data_ptr()  # noqa: E731
+        return _lib.Q8Layer(self.q.c_struct(), self.k.c_struct(), self.v.c_struct(), self.o.c_struct(),
+                            self.gate.c_struct(), self.up.c_struct(), self.down.c_struct(), p(self.bq), p(self.bk),
+                            p(self.bv), p(self.input_norm), p(self.post_norm), self.eps)

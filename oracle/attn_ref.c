@@ -382,6 +382,29 @@ void oracle_linear(const float* x, int T, const float* w, const float* b, int ro
         }
 }
 
+/* ------------------------------------------------------------------ RMSNorm, SwiGLU
+ * GhostRMSNorm::forward (src/oomllama.rs:200-211) as candle's ops: sqr,
+ * mean over the last dim (sum / H, summed in index order here), + eps, sqrt,
+ * x / that, * w; f32 throughout. */
+void oracle_rmsnorm(const float* x, const float* w, float eps, int T, int H, float* out) {
+    for (int t = 0; t < T; ++t) {
+        const float* xr = x + (size_t)t * H;
+        float s = 0.0f;
+        for (int i = 0; i < H; ++i) s += xr[i] * xr[i];
+        const float denom = sqrtf(s / (float)H + eps);
+        for (int i = 0; i < H; ++i) out[(size_t)t * H + i] = xr[i] / denom * w[i];
+    }
+}
+
+/* GhostMlp::forward's gated activation (src/oomllama.rs:235-238):
+ * gate * sigmoid(gate) * up, sigmoid(x) = 1 / (1 + exp(-x)). */
+void oracle_swiglu(const float* gate, const float* up, int64_t n, float* out) {
+    for (int64_t i = 0; i < n; ++i) {
+        const float s = 1.0f / (1.0f + expf(-gate[i]));
+        out[i] = gate[i] * s * up[i];
+    }
+}
+
 void oracle_set_threads(int n) {
 #ifdef _OPENMP
     if (n > 0) omp_set_num_threads(n);

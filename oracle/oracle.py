@@ -73,6 +73,8 @@ def lib():
     L.oracle_q8_dequantize.argtypes = [_u8p, ctypes.c_int64, ctypes.c_int64, _f32p]
     L.oracle_q8_dequantize.restype = c_int
     L.oracle_linear.argtypes = [_f32p, c_int, _f32p, ctypes.c_void_p, c_int, c_int, _f32p]
+    L.oracle_rmsnorm.argtypes = [_f32p, _f32p, c_float, c_int, c_int, _f32p]
+    L.oracle_swiglu.argtypes = [_f32p, _f32p, ctypes.c_int64, _f32p]
     _lib = L
     return L
 
@@ -257,6 +259,23 @@ def linear(x, w, b=None):
     bb = None if b is None else _c(b)
     lib().oracle_linear(x, T, w, _ptr(bb), rows, cols, y)
     return y
+
+
+def rmsnorm(x, w, eps):
+    """GhostRMSNorm::forward (src/oomllama.rs:200-211): x [T, H]."""
+    x = _c(x)
+    T, H = x.shape
+    out = np.empty_like(x)
+    lib().oracle_rmsnorm(x, _c(w), np.float32(eps), T, H, out)
+    return out
+
+
+def swiglu(gate, up):
+    """gate * sigmoid(gate) * up (src/oomllama.rs:235-238)."""
+    g, u = _c(gate), _c(up)
+    out = np.empty_like(g)
+    lib().oracle_swiglu(g.ravel(), u.ravel(), g.size, out.reshape(-1))
+    return out
 
 
 def omp_max_threads() -> int:

@@ -81,3 +81,24 @@ def test_unpack_rejects_a_wrong_block_length(g):
     with pytest.raises(OomAttnError) as e:
         q8_unpack(s, g["w"].size)
     assert "length" in str(e.value)
+
+
+def test_oracle_rmsnorm_known_answers(oracle):
+    # a constant row c normalises to sign(c) * w (up to eps); a row scaled by k gives the same output
+    w = np.linspace(-2, 2, 64).astype(np.float32)
+    out = oracle.rmsnorm(np.full((1, 64), 3.0, np.float32), w, 1e-6)[0]
+    assert np.allclose(out, w, rtol=1e-6, atol=1e-6)
+    x = np.random.default_rng(0).standard_normal((3, 64)).astype(np.float32)
+    assert np.allclose(oracle.rmsnorm(x, w, 0.0), oracle.rmsnorm(4.0 * x, w, 0.0), rtol=1e-5, atol=1e-6)
+    # float64 restatement of src/oomllama.rs:200-211
+    ref = x / np.sqrt((x.astype(np.float64) ** 2).mean(-1, keepdims=True) + 1e-6) * w
+    assert np.abs(oracle.rmsnorm(x, w, 1e-6) - ref).max() < 1e-5
+
+
+def test_oracle_swiglu_known_answers(oracle):
+    g = np.array([0.0, 1.0, -1.0, 20.0, -20.0], np.float32)
+    u = np.array([5.0, 1.0, 2.0, 0.5, 1.0], np.float32)
+    out = oracle.swiglu(g, u)
+    ref = g.astype(np.float64) / (1.0 + np.exp(-g.astype(np.float64))) * u
+    assert out[0] == 0.0
+    assert np.abs(out - ref).max() < 1e-6 * max(1.0, np.abs(ref).max())
