@@ -430,6 +430,75 @@ def bench_q8(args, dist_, torch, T):
     return ms, byts
 
 
+def bench_layer_q8(args, dist_, torch, B, ctx_len=2048):
+    """One Qwen2.5-7B decoder layer's decode step on resident Q8 weights (oomattn_decoder_layer_q8:
+    RMSNorm, QKV + bias, RoPE + append, split-KV attention over ctx_len cached bf16 tokens, o_proj +
+    residual, RMSNorm, gated MLP + residual) for B sequences, replayed as a CUDA graph."""
+    from oomllama_b200 import Q8DecoderLayer, Q8Matrix, TurboConfig, TurboEngine
+    dev = torch.cuda.current_device()
+    H, hq, hkv, inter = 3584, 28, 4, 18944
+    pages_per = -(-(ctx_len + 1) // 16)
+    cfg = TurboConfig(n_layers=1, hidden_size=H, n_heads=hq, n_kv_heads=hkv, max_seq_len=ctx_len + 16, max_seqs=B,
+                      n_pages=B * pages_per, kv_dtype="bf16", rope_variant="interleaved", rope_theta=1e6)
+    eng = TurboEngine(cfg, device=dev, assign_pages=False)
+    perm = np.random.default_rng(7 + dist_.rank).permutation(B * pages_per)
+    for b in range(B):
+        eng.set_block_table(b, perm[b * pages_per:(b + 1) * pages_per].tolist())
+        eng.set_seq_len(0, b, ctx_len)
+    g = torch.Generator(device="cuda").manual_seed(31 + dist_.rank)
+    kp, vp = eng.kv_pool()
+    kp.normal_(generator=g)
+    vp.normal_(generator=g)
+    kp[:, -1].zero_()
+    vp[:, -1].zero_()
+
+    def mat(rows, cols):
+        nb = (rows * cols + 255) // 256
+        q = torch.randint(0, 256, (rows * cols,), dtype=torch.uint8, device="cuda", generator=g)
+        return Q8Matrix(q, torch.rand(nb, device="cuda", generator=g) * 2e-4,
+                        -torch.rand(nb, device="cuda", generator=g) * 0.02, rows, cols)
+
+    w = Q8DecoderLayer(q=mat(hq * D, H), k=mat(hkv * D, H), v=mat(hkv * D, H), o=mat(H, hq * D), gate=mat(inter, H),
+                       up=mat(inter, H), down=mat(H, inter), input_norm=torch.ones(H, device="cuda"),
+                       post_norm=torch.ones(H, device="cuda"), eps=1e-6,
+                       bq=torch.zeros(hq * D, device="cuda"), bk=torch.zeros(hkv * D, device="cuda"),
+                       bv=torch.zeros(hkv * D, device="cuda"))
+    x = torch.randn(B, H, device="cuda", generator=g)
+    out = torch.empty_like(x)
+    seqs = list(range(B))
+    side = torch.cuda.Stream()
+    with torch.cuda.stream(side):
+        for _ in range(2):  # grows the scratch; each call appends at the next slot
+            eng.decoder_layer_q8(0, seqs, x, w, out=out)
+        for b in range(B):
+            eng.set_seq_len(0, b, ctx_len)  # replays then overwrite slot ctx_len: the same work every step
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr, stream=side):
+            eng.decoder_layer_q8(0, seqs, x, w, out=out)
+    torch.cuda.synchronize()
+    eng.sync()
+    for _ in range(max(3, args.warmup)):
+        gr.replay()
+    steps = max(10, args.steps)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    dist_.barrier()
+    torch.cuda.synchronize()
+    t0.record()
+    for _ in range(steps):
+        gr.replay()
+    t1.record()
+    torch.cuda.synchronize()
+    dist_.barrier()
+    eng.sync()
+    ms = dist_.max(t0.elapsed_time(t1) / steps)
+    wbytes = sum(r * c + 8 * ((r * c + 255) // 256) for r, c in
+                 [(hq * D, H), (hkv * D, H), (hkv * D, H), (H, hq * D), (inter, H), (inter, H), (H, inter)])
+    kvbytes = B * (ctx_len + 1) * hkv * D * 2 * 2
+    del gr
+    eng.close()
+    return ms, wbytes + kvbytes
+
+
 def cpu_q8_sample(T, rows_per_matrix=64):
     """The oracle's Q8 dequantise + matvec (src/quant.rs:201-224, src/oom_inference.rs:168-180) on
     rows_per_matrix rows of each matrix of the layer; returns GB/s of algorithmic bytes and threads."""
@@ -589,6 +658,19 @@ def main():
                     "value": v, "unit": "GB/s", "cores": nt, "kind": "port",
                     "sample": "64 rows of each linear: oracle Q8 dequantise + matvec"}
         line["q8_linear"] = q8
+        lay = {}
+        for B in (1, 16):
+            ms, byts = bench_layer_q8(args, dist_, torch, B)
+            lay[f"qwen7b-B{B}-ctx2048"] = {
+                "ms_per_step": ms, "tok_s_per_layer": W * B / (ms * 1e-3),
+                "tok_s_28_layers": W * B / (28 * ms * 1e-3), "hbm_gbs": W * byts / (ms * 1e-3) / 1e9,
+                "bytes_per_step": byts,
+                "note": "decode step of one decoder layer (no embedding / LM head); tok_s_28_layers = B / (28 x step)",
+                "roofline": {"bound": "hbm", "kernel": "decoder layer (K-E, K-A, K-B, RMSNorm)",
+                             "achieved": byts / (ms * 1e-3) / 1e9, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                             "frac": byts / (ms * 1e-3) / 1e9 / peaks["hbm_gbs"], "traffic": None},
+            }
+        line["decoder_layer_q8"] = lay
     if dist_.rank == 0 and W == 1 and not args.no_cpu_baseline:
         v, nt, desc = cpu_prefill_sample()
         line["cpu_baseline"] = {"value": v, "unit": "TFLOP/s", "cores": nt, "kind": "port", "sample": desc}
