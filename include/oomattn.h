@@ -318,6 +318,45 @@ typedef struct oomattn_q8_layer {
 int oomattn_decoder_layer_q8(oomattn_ctx* ctx, int32_t layer, int32_t n_seqs, const int32_t* seq_ids /* host */,
                              const float* x, const oomattn_q8_layer* w /* host struct */, float* out);
 
+/* ------------------------------------------------ embedding, LM head, greedy pick */
+
+/* out[t] = row token_ids[t] of the embedding table emb [vocab][hidden],
+ * dequantised (min + (f32)q * scale): embed_w.embedding(tokens) of
+ * OomLlamaModel::forward_turbo (src/oomllama.rs:508-515).  token_ids
+ * [n_tokens] int32 and out [n_tokens][hidden] f32 are device pointers; an id
+ * outside [0, vocab) gives a zero row and OOMATTN_ERR_DEVICE_CHECK at
+ * oomattn_sync. */
+int oomattn_embed_q8(oomattn_ctx* ctx, const oomattn_q8_matrix* emb /* host struct */, const int32_t* token_ids,
+                     int32_t n_tokens, float* out);
+
+/* ids[r] = argmax of logits[r][0..n): the generation loop's greedy pick
+ * (src/oomllama.rs:973-976, :1000-1003; candle's argmax scans from element 0
+ * and moves only to a strictly larger value: lowest index among equal values,
+ * NaN skipped unless in element 0, which then gives 0).  Device pointers. */
+int oomattn_argmax(oomattn_ctx* ctx, const float* logits, int32_t n_rows, int32_t n, int32_t* ids);
+
+/* A whole Q8 model (OomLlamaModel, src/oomllama.rs:462-500). */
+typedef struct oomattn_q8_model {
+  int32_t n_layers;                /* <= the context's n_layers; layer l uses KV layer l */
+  const oomattn_q8_layer* layers;  /* host array [n_layers] */
+  oomattn_q8_matrix embed;         /* [vocab][hidden] */
+  oomattn_q8_matrix lm_head;       /* [vocab][hidden] */
+  const float* final_norm;         /* [hidden] (device) */
+  float eps;
+} oomattn_q8_model;
+
+/* One decode step of the whole model for n_seqs sequences, one new token each
+ * (OomLlamaModel::forward_turbo, src/oomllama.rs:504-553, then the greedy pick
+ * of the generation loop, :1000-1003): embedding of tokens[b], every decoder
+ * layer (each appends the token to its KV cache), the final RMSNorm, the LM
+ * head and argmax into next[b].  tokens, next [n_seqs] int32 (device; next may
+ * alias tokens, so steps chain on the device); logits [n_seqs][vocab] f32
+ * (device) or NULL to keep them in library scratch.  seq_ids [n_seqs] is host
+ * memory, sequence seq_ids[b] is batch row b.  The sequences' lengths grow by
+ * one. */
+int oomattn_decode_step_q8(oomattn_ctx* ctx, const oomattn_q8_model* m /* host struct */, int32_t n_seqs,
+                           const int32_t* seq_ids /* host */, const int32_t* tokens, int32_t* next, float* logits);
+
 #ifdef __cplusplus
 }
 #endif

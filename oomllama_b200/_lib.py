@@ -27,6 +27,7 @@ EXPORTS = (
     "oomattn_compute_rope_table", "oomattn_rope_append", "oomattn_qkv_rope_append", "oomattn_decode", "oomattn_merge_partials",
     "oomattn_prefill", "oomattn_attention_forward_with_bias", "oomattn_decode_static_scratch",
     "oomattn_q8_unpack", "oomattn_q8_linear", "oomattn_rmsnorm", "oomattn_q8_mlp", "oomattn_decoder_layer_q8",
+    "oomattn_embed_q8", "oomattn_argmax", "oomattn_decode_step_q8",
 )
 
 
@@ -60,6 +61,12 @@ class Q8Layer(ctypes.Structure):
                 ("up", Q8Matrix), ("down", Q8Matrix), ("bq", ctypes.c_void_p), ("bk", ctypes.c_void_p),
                 ("bv", ctypes.c_void_p), ("input_norm", ctypes.c_void_p), ("post_norm", ctypes.c_void_p),
                 ("eps", ctypes.c_float)]
+
+
+class Q8Model(ctypes.Structure):
+    """oomattn_q8_model: the layers (host array), embedding, LM head and final norm of a Q8 model."""
+    _fields_ = [("n_layers", ctypes.c_int32), ("layers", ctypes.POINTER(Q8Layer)), ("embed", Q8Matrix),
+                ("lm_head", Q8Matrix), ("final_norm", ctypes.c_void_p), ("eps", ctypes.c_float)]
 
 
 _lib = None
@@ -106,6 +113,9 @@ def load():
         "oomattn_q8_mlp": ([P, ctypes.POINTER(Q8Matrix), ctypes.POINTER(Q8Matrix), ctypes.POINTER(Q8Matrix), P, I, P,
                             P], ctypes.c_int),
         "oomattn_decoder_layer_q8": ([P, I, I, IP, P, ctypes.POINTER(Q8Layer), P], ctypes.c_int),
+        "oomattn_embed_q8": ([P, ctypes.POINTER(Q8Matrix), P, I, P], ctypes.c_int),
+        "oomattn_argmax": ([P, P, I, I, P], ctypes.c_int),
+        "oomattn_decode_step_q8": ([P, ctypes.POINTER(Q8Model), I, IP, P, P, P], ctypes.c_int),
     }
     for name, (args, res) in sig.items():
         fn = getattr(L, name)

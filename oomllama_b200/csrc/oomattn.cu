@@ -92,6 +92,9 @@ struct oomattn_ctx {
   // decoder-layer step: normalised activations, projections, MLP intermediates
   float* d_layer_scratch = nullptr;
   size_t layer_scratch_bytes = 0;
+  // model step: the residual stream between layers and the logits
+  float* d_model_scratch = nullptr;
+  size_t model_scratch_bytes = 0;
 };
 
 namespace {
@@ -496,7 +499,7 @@ int oomattn_destroy(oomattn_ctx* ctx) {
   if (ctx->cublas) cublasDestroy(ctx->cublas);
   void* ptrs[] = {ctx->kpool,     ctx->vpool,      ctx->d_block_table, ctx->d_cos,    ctx->d_sin,
                   ctx->d_part_o,  ctx->d_part_lse, ctx->d_counters,    ctx->d_status, ctx->d_scratch,
-                  ctx->d_q8_scratch, ctx->d_q8_counters, ctx->d_layer_scratch};
+                  ctx->d_q8_scratch, ctx->d_q8_counters, ctx->d_layer_scratch, ctx->d_model_scratch};
   for (void* p : ptrs)
     if (p) cudaFree(p);
   delete ctx;
@@ -1430,4 +1433,74 @@ extern "C" int oomattn_decoder_layer_q8(oomattn_ctx* ctx, int32_t layer, int32_t
   if (rc) return rc;
   const Q8Job dn{&w->down, nullptr, h, out};
   return q8_run(ctx, &dn, 1, g, u, n_seqs);
+}
+
+extern "C" int oomattn_embed_q8(oomattn_ctx* ctx, const oomattn_q8_matrix* emb, const int32_t* token_ids,
+                                int32_t n_tokens, float* out) {
+  if (!ctx) return OOMATTN_ERR_INVALID_ARG;
+  if (!emb || !emb->q || !emb->scale || !emb->min || !token_ids || !out || n_tokens < 0 || emb->rows <= 0 ||
+      emb->cols <= 0)
+    return fail(ctx, OOMATTN_ERR_INVALID_ARG, "bad embed_q8 arguments");
+  if (n_tokens == 0) return OOMATTN_OK;
+  DeviceGuard dg(ctx->device);
+  embed_q8_kernel<<<n_tokens, 256, 0, ctx->stream>>>(emb->q, emb->scale, emb->min, emb->rows, emb->cols, token_ids,
+                                                     out, ctx->d_status);
+  CKLAUNCH();
+  return OOMATTN_OK;
+}
+
+extern "C" int oomattn_argmax(oomattn_ctx* ctx, const float* logits, int32_t n_rows, int32_t n, int32_t* ids) {
+  if (!ctx) return OOMATTN_ERR_INVALID_ARG;
+  if (!logits || !ids || n_rows < 0 || n <= 0) return fail(ctx, OOMATTN_ERR_INVALID_ARG, "bad argmax arguments");
+  if (n_rows == 0) return OOMATTN_OK;
+  DeviceGuard dg(ctx->device);
+  argmax_kernel<<<n_rows, kArgmaxThreads, 0, ctx->stream>>>(logits, n, ids);
+  CKLAUNCH();
+  return OOMATTN_OK;
+}
+
+extern "C" int oomattn_decode_step_q8(oomattn_ctx* ctx, const oomattn_q8_model* m, int32_t n_seqs,
+                                      const int32_t* seq_ids, const int32_t* tokens, int32_t* next, float* logits) {
+  if (!ctx) return OOMATTN_ERR_INVALID_ARG;
+  if (!m || !m->layers || !seq_ids || !tokens || !next || n_seqs <= 0)
+    return fail(ctx, OOMATTN_ERR_INVALID_ARG, "bad decode_step_q8 arguments");
+  if (m->n_layers <= 0 || m->n_layers > ctx->cfg.n_layers)
+    return fail(ctx, OOMATTN_ERR_OUT_OF_RANGE, "model has %d layers, the context %d", m->n_layers, ctx->cfg.n_layers);
+  const int H = ctx->cfg.hidden_size;
+  if (m->embed.cols != H || m->lm_head.cols != H || !m->final_norm)
+    return fail(ctx, OOMATTN_ERR_INVALID_ARG, "embedding / LM head width or final norm does not match hidden %d", H);
+  DeviceGuard dg(ctx->device);
+  const size_t B = (size_t)n_seqs, vocab = (size_t)m->lm_head.rows;
+  const size_t xf = (B * H + 31) / 32 * 32;
+  const size_t need = (3 * xf + (logits ? 0 : B * vocab) + 64) * 4;
+  if (need > ctx->model_scratch_bytes) {
+    if (ctx->d_model_scratch) {
+      cudaStreamSynchronize(ctx->stream);
+      cudaFree(ctx->d_model_scratch);
+      ctx->d_model_scratch = nullptr;
+      ctx->model_scratch_bytes = 0;
+    }
+    if (cudaMalloc(&ctx->d_model_scratch, need) != cudaSuccess)
+      return fail(ctx, OOMATTN_ERR_NO_MEMORY, "model scratch allocation of %zu bytes failed", need);
+    ctx->model_scratch_bytes = need;
+  }
+  float* xa = ctx->d_model_scratch;
+  float* xb = xa + xf;
+  float* xn = xb + xf;
+  float* lg = logits ? logits : xn + xf;
+  // OomLlamaModel::forward_turbo (src/oomllama.rs:504-553) for one new token per sequence, then the greedy
+  // pick of the generation loop (:973-976, :1000-1003)
+  int rc = oomattn_embed_q8(ctx, &m->embed, tokens, n_seqs, xa);
+  if (rc) return rc;
+  for (int l = 0; l < m->n_layers; ++l) {
+    rc = oomattn_decoder_layer_q8(ctx, l, n_seqs, seq_ids, xa, &m->layers[l], xb);
+    if (rc) return rc;
+    std::swap(xa, xb);
+  }
+  rc = run_rmsnorm(ctx, xa, m->final_norm, m->eps, n_seqs, H, xn);
+  if (rc) return rc;
+  const Q8Job head{&m->lm_head, nullptr, nullptr, lg};
+  rc = q8_run(ctx, &head, 1, xn, nullptr, n_seqs);
+  if (rc) return rc;
+  return oomattn_argmax(ctx, lg, n_seqs, (int)vocab, next);
 }

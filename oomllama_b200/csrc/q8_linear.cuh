@@ -369,4 +369,74 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(const float* __re
   }
 }
 
+// ------------------------------------------------------------------ embedding, argmax
+// out[t] = row ids[t] of a Q8 matrix [vocab][hidden], dequantised exactly as
+// the reference reads a Q8 tensor (min + (f32)q * scale, src/quant.rs:201-224),
+// the embedding gather of src/oomllama.rs:508-515.  One CTA per token.  A
+// token id outside [0, vocab) is reported and gives a zero row.
+__global__ void embed_q8_kernel(const uint8_t* __restrict__ q, const float* __restrict__ scale,
+                                const float* __restrict__ mn, int vocab, int hidden, const int* __restrict__ ids,
+                                float* __restrict__ out, int* status) {
+  const int t = blockIdx.x;
+  const int id = ids[t];
+  float* orow = out + (size_t)t * hidden;
+  if ((unsigned)id >= (unsigned)vocab) {
+    if (threadIdx.x == 0) report_error(status, kDevErrBounds);
+    for (int i = threadIdx.x; i < hidden; i += blockDim.x) orow[i] = 0.f;
+    return;
+  }
+  const long long base = (long long)id * hidden;
+  for (int i = threadIdx.x; i < hidden; i += blockDim.x) {
+    const long long f = base + i;
+    orow[i] = __fadd_rn(mn[f >> 8], __fmul_rn((float)q[f], scale[f >> 8]));
+  }
+}
+
+// ids[t] = argmax over logits[t][0..n) (the greedy pick, src/oomllama.rs:973-976,
+// :1000-1003, i.e. candle-core 0.9.1's argmax: a scan from element 0 that moves
+// only to a strictly larger value).  So: the largest value, the lowest index
+// among equal ones, NaN skipped -- except that a NaN in element 0 is never left
+// and gives 0.  One CTA per row.
+constexpr int kArgmaxThreads = 512;
+__global__ void __launch_bounds__(kArgmaxThreads) argmax_kernel(const float* __restrict__ logits, int n,
+                                                                int* __restrict__ ids) {
+  __shared__ float sv[kArgmaxThreads / 32];
+  __shared__ int si[kArgmaxThreads / 32];
+  const float* row = logits + (size_t)blockIdx.x * n;
+  float bv = -INFINITY;
+  int bi = n;  // sentinel: no candidate yet
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const float v = row[i];
+    if (v > bv || (bi == n && v == v)) {  // first non-NaN, then strictly larger (indices ascend)
+      bv = v;
+      bi = i;
+    }
+  }
+  // reduce (value, index): larger value wins, lower index on ties
+#pragma unroll
+  for (int d = 16; d > 0; d >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, d);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, d);
+    if (oi != n && (bi == n || ov > bv || (ov == bv && oi < bi))) {
+      bv = ov;
+      bi = oi;
+    }
+  }
+  if ((threadIdx.x & 31) == 0) {
+    sv[threadIdx.x >> 5] = bv;
+    si[threadIdx.x >> 5] = bi;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float v = sv[0];
+    int i0 = si[0];
+    for (int w = 1; w < kArgmaxThreads / 32; ++w)
+      if (si[w] != n && (i0 == n || sv[w] > v || (sv[w] == v && si[w] < i0))) {
+        v = sv[w];
+        i0 = si[w];
+      }
+    ids[blockIdx.x] = (i0 == n || row[0] != row[0]) ? 0 : i0;
+  }
+}
+
 }  // namespace oomattn

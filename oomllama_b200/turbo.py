@@ -373,6 +373,45 @@ class TurboEngine:
                                                           ctypes.byref(w.c_struct()), _ptr(out)))
         return out
 
+    def embed_q8(self, emb: "Q8Matrix", token_ids: torch.Tensor, out=None):
+        """embed_w.embedding(tokens) (src/oomllama.rs:508-515) on a resident Q8 table: int32 ids [T] ->
+        f32 [T, hidden]."""
+        T = token_ids.numel()
+        _dev(token_ids, "token_ids", self.device, dtype=torch.int32)
+        out = (torch.empty(T, emb.cols, dtype=torch.float32, device=self.device) if out is None
+               else _dev(out, "out", self.device, dtype=torch.float32, numel=T * emb.cols))
+        self._bind_stream()
+        check(self._ctx, self._L.oomattn_embed_q8(self._ctx, ctypes.byref(emb.c_struct()), _ptr(token_ids), T,
+                                                  _ptr(out)))
+        return out
+
+    def argmax(self, logits: torch.Tensor, out=None):
+        """The greedy pick of the generation loop (src/oomllama.rs:1000-1003): f32 [R, n] -> int32 [R]."""
+        R, n = logits.shape
+        _dev(logits, "logits", self.device, dtype=torch.float32)
+        out = (torch.empty(R, dtype=torch.int32, device=self.device) if out is None
+               else _dev(out, "out", self.device, dtype=torch.int32, numel=R))
+        self._bind_stream()
+        check(self._ctx, self._L.oomattn_argmax(self._ctx, _ptr(logits), R, n, _ptr(out)))
+        return out
+
+    def decode_step_q8(self, model: "Q8Model", seq_ids, tokens: torch.Tensor, next_tokens=None, logits=None):
+        """OomLlamaModel::forward_turbo (src/oomllama.rs:504-553) for one new token per sequence plus the greedy
+        pick: int32 tokens [B] -> int32 next [B] (may be `tokens` itself).  `logits` [B, vocab] f32 receives the
+        LM head output when given.  Every layer's cache grows by one token per sequence."""
+        B = tokens.numel()
+        _dev(tokens, "tokens", self.device, dtype=torch.int32)
+        nxt = (torch.empty(B, dtype=torch.int32, device=self.device) if next_tokens is None
+               else _dev(next_tokens, "next_tokens", self.device, dtype=torch.int32, numel=B))
+        if logits is not None:
+            _dev(logits, "logits", self.device, dtype=torch.float32, numel=B * model.lm_head.rows)
+        self._bind_stream()
+        ids = int_array(seq_ids)
+        check(self._ctx, self._L.oomattn_decode_step_q8(self._ctx, ctypes.byref(model.c_struct()), B, ids,
+                                                        _ptr(tokens), _ptr(nxt),
+                                                        None if logits is None else _ptr(logits)))
+        return nxt
+
 
 def q8_unpack(stream, n_values: int):
     """Unpack one .oom Q8 tensor's block stream ([f32 scale][f32 min][u32 len][bytes] per 256 values,
@@ -454,3 +493,21 @@ class Q8DecoderLayer:
         return _lib.Q8Layer(self.q.c_struct(), self.k.c_struct(), self.v.c_struct(), self.o.c_struct(),
                             self.gate.c_struct(), self.up.c_struct(), self.down.c_struct(), p(self.bq), p(self.bk),
                             p(self.bv), p(self.input_norm), p(self.post_norm), self.eps)
+
+
+@dataclass
+class Q8Model:
+    """A whole model's resident weights (OomLlamaModel, src/oomllama.rs:462-500): decoder layers, the Q8
+    embedding table and LM head [vocab][hidden], and the final RMSNorm weight."""
+    layers: list
+    embed: Q8Matrix
+    lm_head: Q8Matrix
+    final_norm: torch.Tensor
+    eps: float
+
+    def c_struct(self) -> _lib.Q8Model:
+        arr = (_lib.Q8Layer * len(self.layers))(*[l.c_struct() for l in self.layers])
+        m = _lib.Q8Model(len(self.layers), ctypes.cast(arr, ctypes.POINTER(_lib.Q8Layer)), self.embed.c_struct(),
+                         self.lm_head.c_struct(), self.final_norm.data_ptr(), self.eps)
+        m._keep = arr  # the layer array lives as long as the struct
+        return m

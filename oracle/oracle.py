@@ -278,6 +278,79 @@ def swiglu(gate, up):
     return out
 
 
+def embedding(stream, vocab: int, hidden: int, ids) -> np.ndarray:
+    """embed_w.embedding(tokens) of OomLlamaModel::forward_turbo (src/oomllama.rs:508-515) on a Q8 table
+    [vocab][hidden] given as its block stream: the dequantised rows ids."""
+    table = q8_dequantize(stream, vocab * hidden).reshape(vocab, hidden)
+    return table[np.asarray(ids, np.int64)].copy()
+
+
+def argmax(logits) -> np.ndarray:
+    """The generation loop's greedy pick (src/oomllama.rs:973-976, :1000-1003), candle-core 0.9.1's argmax over
+    the last axis: a scan from element 0 that moves only to a strictly larger value.  Equivalent vectorised form:
+    NaN never compares larger, so NaNs become -inf and numpy's first-maximum argmax applies, except that a NaN in
+    element 0 is never left."""
+    x = np.array(logits, np.float32, ndmin=2)
+    first_nan = np.isnan(x[:, 0])
+    idx = np.argmax(np.where(np.isnan(x), -np.inf, x), axis=1).astype(np.int32)
+    idx[first_nan] = 0
+    return idx
+
+
+def argmax_scan(row) -> int:
+    """argmax as the literal strict-greater scan from element 0 (small rows; checks the vectorised form)."""
+    best, bi = row[0], 0
+    for i in range(1, len(row)):
+        if row[i] > best:
+            best, bi = row[i], i
+    return bi
+
+
+def decoder_layer_decode(x, w, kc, vc, lens, n_heads, n_kv, cos_t, sin_t, variant, kv_bf16=False):
+    """GhostDecoderLayer::forward_turbo (src/oomllama.rs:387-402) for one new token per sequence:
+    h = x + o(attention(rope(qkv(rmsnorm(x))))), out = h + mlp(rmsnorm(h)).  x [B, H]; w a dict of dequantised
+    matrices q, k, v, o, gate, up, down, biases bq, bk, bv (or None), norms n1, n2 and eps; kc[b], vc[b]
+    [lens[b], n_kv, d] the cached (rotated) keys and values, extended in place by the new token (rounded to
+    bf16 when kv_bf16).  Returns out [B, H]."""
+    x = _c(x)
+    B = x.shape[0]
+    d = w["q"].shape[0] // n_heads
+    store = round_bf16 if kv_bf16 else (lambda a: a)
+    xn = rmsnorm(x, w["n1"], w["eps"])
+    q = linear(xn, w["q"], w.get("bq")).reshape(B, n_heads, d)
+    k = linear(xn, w["k"], w.get("bk")).reshape(B, n_kv, d)
+    v = linear(xn, w["v"], w.get("bv")).reshape(B, n_kv, d)
+    att = np.empty((B, n_heads * d), np.float32)
+    for b in range(B):
+        L = lens[b]
+        qr = rope_apply(q[b], cos_t[L], sin_t[L], variant)
+        kr = rope_apply(k[b], cos_t[L], sin_t[L], variant)
+        kc[b] = store(np.concatenate([kc[b][:L], kr[None]], 0))
+        vc[b] = store(np.concatenate([vc[b][:L], v[b][None]], 0))
+        K = kc[b].transpose(1, 0, 2).copy()
+        V = vc[b].transpose(1, 0, 2).copy()
+        att[b] = gqa_attention(qr[None], K, V, causal=False)[0].reshape(-1)
+    h = linear(att, w["o"]) + x
+    hn = rmsnorm(h, w["n2"], w["eps"])
+    return linear(swiglu(linear(hn, w["gate"]), linear(hn, w["up"])), w["down"]) + h
+
+
+def model_decode_step(tokens, embed, layers, final_norm, lm_head, eps, caches, lens, n_heads, n_kv, cos_t, sin_t,
+                      variant, kv_bf16=False):
+    """OomLlamaModel::forward_turbo (src/oomllama.rs:504-553) for one new token per sequence, then the greedy
+    pick (:1000-1003).  embed, lm_head [vocab, H] dequantised; layers a list of decoder_layer_decode weight dicts;
+    caches[l] = (kc, vc) lists per sequence, extended in place, and lens advanced by one.  Returns
+    (next ids [B], logits [B, vocab])."""
+    x = embed[np.asarray(tokens, np.int64)].astype(np.float32)
+    for l, w in enumerate(layers):
+        x = decoder_layer_decode(x, w, caches[l][0], caches[l][1], lens, n_heads, n_kv, cos_t, sin_t, variant,
+                                 kv_bf16)
+    for b in range(len(lens)):
+        lens[b] += 1
+    logits = linear(rmsnorm(x, final_norm, eps), lm_head)
+    return argmax(logits), logits
+
+
 def omp_max_threads() -> int:
     return int(lib().oracle_omp_max_threads())
 

@@ -81,21 +81,9 @@ def _layer_case(oracle, kv_dtype, variant, theta, lens, seed):
     # the oracle's decode step
     var = oracle.ROPE_INTERLEAVED if variant == "interleaved" else oracle.ROPE_SPLIT_HALF
     cos_t, sin_t = oracle.rope_table(theta, D, max(lens) + 1)
-    xn = oracle.rmsnorm(x, n1, eps)
-    q = oracle.linear(xn, mats["q"][1], bq).reshape(B, hq, D)
-    k = oracle.linear(xn, mats["k"][1], bk).reshape(B, hkv, D)
-    v = oracle.linear(xn, mats["v"][1], bv).reshape(B, hkv, D)
-    store = oracle.round_bf16 if kv_dtype == "bf16" else (lambda a: a)
-    att = np.empty((B, hq * D), np.float32)
-    for b, L in enumerate(lens):
-        qr = oracle.rope_apply(q[b], cos_t[L], sin_t[L], var)
-        kr = oracle.rope_apply(k[b], cos_t[L], sin_t[L], var)
-        K = store(np.concatenate([kc[b], kr[None]], 0)).transpose(1, 0, 2).copy()
-        V = store(np.concatenate([vc[b], v[b][None]], 0)).transpose(1, 0, 2).copy()
-        att[b] = oracle.gqa_attention(qr[None], K, V, causal=False)[0].reshape(-1)
-    h = oracle.linear(att, mats["o"][1]) + x
-    ref = oracle.linear(oracle.swiglu(oracle.linear(oracle.rmsnorm(h, n2, eps), mats["gate"][1]),
-                                      oracle.linear(oracle.rmsnorm(h, n2, eps), mats["up"][1])), mats["down"][1]) + h
+    wd = {name: m[1] for name, m in mats.items()}
+    wd.update(bq=bq, bk=bk, bv=bv, n1=n1, n2=n2, eps=eps)
+    ref = oracle.decoder_layer_decode(x, wd, kc, vc, lens, hq, hkv, cos_t, sin_t, var, kv_dtype == "bf16")
     return out.cpu().numpy(), ref, lens_after
 
 

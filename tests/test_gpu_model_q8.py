@@ -1,0 +1,186 @@
+"""The model ends of the decode step on resident Q8 weights, against the
+oracle: the embedding gather (src/oomllama.rs:508-515), the greedy pick
+(src/oomllama.rs:973-976, :1000-1003; candle's argmax) and the whole-model
+decode step OomLlamaModel::forward_turbo (src/oomllama.rs:504-553) chained
+over several greedy steps on a reduced two-layer model.
+
+Embedding and argmax are bit-exact.  Logits: max-abs <= 1e-4 scaled by their
+magnitude where it exceeds 1 (f32 KV).  Tokens: equal to the oracle's pick
+wherever the oracle's top-two margin exceeds the logit tolerance; the oracle
+then follows the library's token so both stay on one sequence."""
+import numpy as np
+import pytest
+import torch
+
+from helpers import F32_ATOL, assert_close, make_engine
+
+pytestmark = pytest.mark.gpu
+
+
+def _q8(oracle, rows, cols, rng, scale=0.05):
+    from oomllama_b200 import Q8Matrix
+    w = (rng.standard_normal((rows, cols)) * scale).astype(np.float32)
+    stream = oracle.q8_quantize(w)
+    return Q8Matrix.from_oom_stream(stream, rows, cols, device=0), stream
+
+
+@pytest.fixture(scope="module")
+def eng():
+    e = make_engine(2, 1, [16])
+    yield e
+    e.close()
+
+
+@pytest.mark.parametrize("vocab,hidden", [(1000, 256), (517, 320), (64, 3584)])
+def test_embed_q8_bit_exact(oracle, eng, vocab, hidden):
+    rng = np.random.default_rng(vocab + hidden)
+    emb, stream = _q8(oracle, vocab, hidden, rng, scale=1.0)
+    ids = np.concatenate([[0, vocab - 1, 5, 5], rng.integers(0, vocab, 29)]).astype(np.int32)
+    out = eng.embed_q8(emb, torch.from_numpy(ids).cuda())
+    eng.sync()
+    ref = oracle.embedding(stream, vocab, hidden, ids)
+    assert np.array_equal(out.cpu().numpy().view(np.uint32), ref.view(np.uint32))
+
+
+def test_embed_q8_reports_out_of_range_ids(oracle, eng):
+    from oomllama_b200._lib import OomAttnError
+    rng = np.random.default_rng(7)
+    emb, stream = _q8(oracle, 100, 256, rng)
+    ids = torch.tensor([3, 100, -1, 99], dtype=torch.int32, device="cuda")
+    out = eng.embed_q8(emb, ids)
+    with pytest.raises(OomAttnError) as e:
+        eng.sync()
+    assert e.value.code == 9
+    eng.sync()
+    o = out.cpu().numpy()
+    ref = oracle.embedding(stream, 100, 256, [3, 99])
+    assert np.array_equal(o[[0, 3]], ref) and not o[[1, 2]].any()
+
+
+def _argmax_rows():
+    rng = np.random.default_rng(11)
+    rows = []
+    r = rng.standard_normal(1000).astype(np.float32)
+    r[[17, 400, 999]] = 9.0  # tie: lowest index
+    rows.append(r)
+    r = rng.standard_normal(1000).astype(np.float32)
+    r[[3, 500]] = np.nan  # NaN skipped
+    rows.append(r)
+    r = rng.standard_normal(1000).astype(np.float32)
+    r[0] = np.nan  # NaN in element 0 is never left
+    rows.append(r)
+    rows.append(np.full(1000, -np.inf, np.float32))  # all -inf: 0
+    r = np.full(1000, -np.inf, np.float32)
+    r[777] = -1e30
+    rows.append(r)
+    r = rng.standard_normal(1000).astype(np.float32)
+    r[998] = np.inf
+    r[999] = np.inf
+    rows.append(r)
+    r = np.zeros(1000, np.float32)
+    r[5] = -0.0
+    rows.append(r)  # +0 and -0 compare equal: 0
+    return np.stack(rows)
+
+
+def test_argmax_edge_cases(oracle, eng):
+    x = _argmax_rows()
+    ids = eng.argmax(torch.from_numpy(x).cuda())
+    eng.sync()
+    ref = oracle.argmax(x)
+    assert ids.cpu().numpy().tolist() == ref.tolist()
+    assert ref.tolist() == [oracle.argmax_scan(r) for r in x]
+
+
+@pytest.mark.parametrize("R,n", [(1, 1), (3, 513), (16, 152064), (2, 128256)])
+def test_argmax_sizes(oracle, eng, R, n):
+    rng = np.random.default_rng(R * n)
+    x = rng.standard_normal((R, n)).astype(np.float32)
+    x[:, rng.integers(0, n, 4)] = x.max() + 1.0  # a tie at the top of every row
+    ids = eng.argmax(torch.from_numpy(x).cuda())
+    eng.sync()
+    assert ids.cpu().numpy().tolist() == oracle.argmax(x).tolist()
+
+
+def _model(oracle, n_layers, hq, hkv, inter, vocab, seed):
+    from oomllama_b200 import Q8DecoderLayer, Q8Model
+    D = 128
+    H = hq * D
+    rng = np.random.default_rng(seed)
+    dev = lambda a: torch.from_numpy(a).cuda()  # noqa: E731
+    layers, ref_layers = [], []
+    for _ in range(n_layers):
+        mats, deq = {}, {}
+        for name, (r, c) in {"q": (hq * D, H), "k": (hkv * D, H), "v": (hkv * D, H), "o": (H, hq * D),
+                             "gate": (inter, H), "up": (inter, H), "down": (H, inter)}.items():
+            mats[name], stream = _q8(oracle, r, c, rng)
+            deq[name] = oracle.q8_dequantize(stream, r * c).reshape(r, c)
+        bq, bk, bv = [(rng.standard_normal(n) * 0.1).astype(np.float32) for n in (hq * D, hkv * D, hkv * D)]
+        n1, n2 = (1 + 0.1 * rng.standard_normal((2, H))).astype(np.float32)
+        layers.append(Q8DecoderLayer(q=mats["q"], k=mats["k"], v=mats["v"], o=mats["o"], gate=mats["gate"],
+                                     up=mats["up"], down=mats["down"], input_norm=dev(n1), post_norm=dev(n2),
+                                     eps=1e-6, bq=dev(bq), bk=dev(bk), bv=dev(bv)))
+        ref_layers.append(dict(deq, bq=bq, bk=bk, bv=bv, n1=n1, n2=n2, eps=1e-6))
+    emb, es = _q8(oracle, vocab, H, rng, scale=1.0)
+    head, hs = _q8(oracle, vocab, H, rng, scale=0.2)
+    fn = (1 + 0.1 * rng.standard_normal(H)).astype(np.float32)
+    model = Q8Model(layers=layers, embed=emb, lm_head=head, final_norm=dev(fn), eps=1e-6)
+    ref = dict(layers=ref_layers, embed=oracle.q8_dequantize(es, vocab * H).reshape(vocab, H),
+               lm_head=oracle.q8_dequantize(hs, vocab * H).reshape(vocab, H), final_norm=fn)
+    return model, ref
+
+
+@pytest.mark.parametrize("variant,theta,lens", [("interleaved", 1e6, [7, 30, 1]), ("split_half", 5e5, [64])])
+def test_decode_step_q8_greedy_chain(oracle, variant, theta, lens):
+    n_layers, hq, hkv, inter, vocab, steps = 2, 2, 1, 512, 1024, 6
+    model, ref = _model(oracle, n_layers, hq, hkv, inter, vocab, seed=len(lens) * 10 + 1)
+    B, D = len(lens), 128
+    eng = make_engine(hq, hkv, [L + steps for L in lens], kv_dtype="f32", variant=variant, theta=theta,
+                      hidden=hq * D, n_layers=n_layers, shuffle_seed=5)
+    rng = np.random.default_rng(99)
+    caches = []
+    for l in range(n_layers):
+        kc = [rng.standard_normal((L, hkv, D)).astype(np.float32) for L in lens]
+        vc = [rng.standard_normal((L, hkv, D)).astype(np.float32) for L in lens]
+        for b in range(B):
+            eng.kv_write(l, b, torch.from_numpy(kc[b]).cuda(), torch.from_numpy(vc[b]).cuda())
+        caches.append((kc, vc))
+    var = oracle.ROPE_INTERLEAVED if variant == "interleaved" else oracle.ROPE_SPLIT_HALF
+    cos_t, sin_t = oracle.rope_table(theta, D, max(lens) + steps)
+    rl = list(lens)
+    tokens = torch.from_numpy(rng.integers(0, vocab, B).astype(np.int32)).cuda()
+    logits = torch.empty(B, vocab, device="cuda")
+    for step in range(steps):
+        tok_in = tokens.cpu().numpy()
+        eng.decode_step_q8(model, list(range(B)), tokens, next_tokens=tokens, logits=logits)  # chained in place
+        eng.sync()
+        got, lg = tokens.cpu().numpy(), logits.cpu().numpy()
+        want, ref_lg = oracle.model_decode_step(tok_in, ref["embed"], ref["layers"], ref["final_norm"],
+                                                ref["lm_head"], 1e-6, caches, rl, hq, hkv, cos_t, sin_t, var)
+        tol = F32_ATOL * max(1.0, np.abs(ref_lg).max())
+        assert_close(lg, ref_lg, tol, what=f"logits step {step}")
+        assert got.tolist() == oracle.argmax(lg).tolist(), "the pick is not the argmax of the library's logits"
+        top2 = np.sort(ref_lg, axis=1)[:, -2:]
+        clear = (top2[:, 1] - top2[:, 0]) > 2 * tol
+        assert (got[clear] == want[clear]).all(), f"step {step}: picks {got} vs oracle {want}"
+    assert [eng.seq_len(l, b) for l in range(n_layers) for b in range(B)] == [L + steps for _ in range(n_layers)
+                                                                               for L in lens]
+    eng.close()
+
+
+def test_decode_step_q8_rejects_mismatched_models(oracle):
+    from oomllama_b200 import Q8Model
+    from oomllama_b200._lib import OomAttnError
+    model, _ = _model(oracle, 2, 2, 1, 256, 64, seed=3)
+    eng = make_engine(2, 1, [8], kv_dtype="f32", hidden=256, n_layers=1)
+    tok = torch.zeros(1, dtype=torch.int32, device="cuda")
+    with pytest.raises(OomAttnError) as e:  # two layers, a one-layer context
+        eng.decode_step_q8(model, [0], tok)
+    assert e.value.code == 3
+    rng = np.random.default_rng(0)
+    bad = Q8Model(layers=model.layers[:1], embed=_q8(oracle, 64, 128, rng)[0], lm_head=model.lm_head,
+                  final_norm=model.final_norm, eps=1e-6)
+    with pytest.raises(OomAttnError) as e:  # embedding width 128, hidden 256
+        eng.decode_step_q8(bad, [0], tok)
+    assert e.value.code == 1
+    eng.close()

@@ -102,3 +102,22 @@ def test_oracle_swiglu_known_answers(oracle):
     ref = g.astype(np.float64) / (1.0 + np.exp(-g.astype(np.float64))) * u
     assert out[0] == 0.0
     assert np.abs(out - ref).max() < 1e-6 * max(1.0, np.abs(ref).max())
+
+
+def test_oracle_argmax_matches_the_scan(oracle):
+    # the vectorised argmax against the literal strict-greater scan from element 0
+    rng = np.random.default_rng(5)
+    x = rng.integers(-3, 4, (64, 40)).astype(np.float32)  # many ties
+    x[rng.random(x.shape) < 0.05] = np.nan
+    x[::7, 0] = np.nan
+    x[3] = -np.inf
+    x[5, 10:] = np.inf
+    assert oracle.argmax(x).tolist() == [oracle.argmax_scan(r) for r in x]
+
+
+def test_oracle_embedding_rows(oracle):
+    w = np.random.default_rng(2).standard_normal((37, 96)).astype(np.float32)  # blocks straddle rows
+    s = oracle.q8_quantize(w)
+    full = oracle.q8_dequantize(s, w.size).reshape(37, 96)
+    ids = [36, 0, 5, 5]
+    assert np.array_equal(oracle.embedding(s, 37, 96, ids), full[ids])
