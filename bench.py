@@ -499,6 +499,100 @@ def bench_layer_q8(args, dist_, torch, B, ctx_len=2048):
     return ms, wbytes + kvbytes
 
 
+def q8_random_matrix(torch, rows, cols, g, std=0.02, chunk=1 << 26):
+    """A Q8 matrix of weights ~N(0, std) quantised on the device the way the .oom writer does
+    (src/gguf2oom.rs:719-770: per 256-value block min, scale = range / 255, q = round((v - min) / scale));
+    rows * cols must be a multiple of 256."""
+    from oomllama_b200 import Q8Matrix
+    n = rows * cols
+    q = torch.empty(n, dtype=torch.uint8, device="cuda")
+    scale = torch.empty(n // 256, device="cuda")
+    mn = torch.empty(n // 256, device="cuda")
+    for o in range(0, n, chunk):
+        m = min(chunk, n - o)
+        v = (torch.randn(m, device="cuda", generator=g) * std).view(-1, 256)
+        lo, hi = v.min(1).values, v.max(1).values
+        sc = (hi - lo) / 255.0
+        sc = torch.where((hi - lo).abs() < 1e-9, torch.zeros_like(sc), sc)
+        qq = torch.where(sc[:, None] > 0, torch.floor((v - lo[:, None]) / sc[:, None].clamp_min(1e-30) + 0.5),
+                         torch.zeros_like(v)).clamp_(0, 255)
+        q[o:o + m] = qq.view(-1).to(torch.uint8)
+        scale[o // 256:(o + m) // 256] = sc
+        mn[o // 256:(o + m) // 256] = lo
+    return Q8Matrix(q, scale, mn, rows, cols)
+
+
+def bench_model_q8(args, dist_, torch, B=16, prompt=2048, gen=256, n_layers=28):
+    """Greedy decode of the whole Qwen2.5-7B-shaped model on resident Q8 weights (oomattn_decode_step_q8:
+    embedding, 28 decoder layers, final RMSNorm, LM head 152064 x 3584, argmax; each step's ids feed the
+    next on the device and are copied to pinned host memory) for B sequences: gen steps after a prompt of
+    `prompt` tokens whose KV entries are synthetic ~N(0, 1) bf16 (the prompt's prefill is not run)."""
+    from oomllama_b200 import Q8DecoderLayer, Q8Model, TurboConfig, TurboEngine
+    dev = torch.cuda.current_device()
+    H, hq, hkv, inter, vocab = 3584, 28, 4, 18944, 152064
+    cap = prompt + gen + 8
+    pages_per = -(-cap // 16)
+    cfg = TurboConfig(n_layers=n_layers, hidden_size=H, n_heads=hq, n_kv_heads=hkv, max_seq_len=cap, max_seqs=B,
+                      n_pages=B * pages_per, kv_dtype="bf16", rope_variant="interleaved", rope_theta=1e6)
+    eng = TurboEngine(cfg, device=dev, assign_pages=False)
+    perm = np.random.default_rng(9 + dist_.rank).permutation(B * pages_per)
+    for b in range(B):
+        eng.set_block_table(b, perm[b * pages_per:(b + 1) * pages_per].tolist())
+    g = torch.Generator(device="cuda").manual_seed(4 + dist_.rank)
+    kp, vp = eng.kv_pool()
+    kp.normal_(generator=g)
+    vp.normal_(generator=g)
+    bias = lambda n: torch.randn(n, device="cuda", generator=g) * 0.02  # noqa: E731
+    layers = [Q8DecoderLayer(q=q8_random_matrix(torch, hq * D, H, g), k=q8_random_matrix(torch, hkv * D, H, g),
+                             v=q8_random_matrix(torch, hkv * D, H, g), o=q8_random_matrix(torch, H, hq * D, g),
+                             gate=q8_random_matrix(torch, inter, H, g), up=q8_random_matrix(torch, inter, H, g),
+                             down=q8_random_matrix(torch, H, inter, g), input_norm=torch.ones(H, device="cuda"),
+                             post_norm=torch.ones(H, device="cuda"), eps=1e-6, bq=bias(hq * D), bk=bias(hkv * D),
+                             bv=bias(hkv * D)) for _ in range(n_layers)]
+    model = Q8Model(layers=layers, embed=q8_random_matrix(torch, vocab, H, g),
+                    lm_head=q8_random_matrix(torch, vocab, H, g), final_norm=torch.ones(H, device="cuda"), eps=1e-6)
+    seqs = list(range(B))
+    first = torch.randint(0, vocab, (B,), dtype=torch.int32, device="cuda", generator=g)
+    tokens = first.clone()
+    out_host = torch.empty(gen, B, dtype=torch.int32).pin_memory()
+
+    def reset():
+        for l in range(n_layers):
+            for b in range(B):
+                eng.set_seq_len(l, b, prompt)
+        tokens.copy_(first)
+
+    reset()
+    for _ in range(max(3, args.warmup)):
+        eng.decode_step_q8(model, seqs, tokens, next_tokens=tokens)
+    eng.sync()
+    reset()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    stream = torch.cuda.current_stream()
+    dist_.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(dev) as clk:
+        t0.record(stream)
+        for i in range(gen):
+            eng.decode_step_q8(model, seqs, tokens, next_tokens=tokens)
+            out_host[i].copy_(tokens, non_blocking=True)
+        t1.record(stream)
+        torch.cuda.synchronize()
+    clocks = clk.summary()
+    dist_.barrier()
+    eng.sync()
+    ms = dist_.max(t0.elapsed_time(t1))
+    ids = out_host.numpy()
+    lens_ok = all(eng.seq_len(l, b) == prompt + gen for l in (0, n_layers - 1) for b in range(B))
+    wbytes = sum(m.rows * m.cols + 8 * (m.rows * m.cols // 256) for lay in layers
+                 for m in (lay.q, lay.k, lay.v, lay.o, lay.gate, lay.up, lay.down))
+    wbytes += vocab * H + 8 * (vocab * H // 256)  # LM head (the embedding reads B rows)
+    kv_per_step = sum(B * (prompt + i + 1) * hkv * D * 2 * 2 * n_layers for i in range(gen)) / gen
+    eng.close()
+    return {"ms": ms, "ids": ids, "lens_ok": lens_ok, "weight_bytes": wbytes, "kv_bytes_per_step": kv_per_step,
+            "clocks": clocks}
+
+
 def cpu_q8_sample(T, rows_per_matrix=64):
     """The oracle's Q8 dequantise + matvec (src/quant.rs:201-224, src/oom_inference.rs:168-180) on
     rows_per_matrix rows of each matrix of the layer; returns GB/s of algorithmic bytes and threads."""
@@ -642,7 +736,7 @@ def main():
             }
         line["decode"] = dec
         q8 = {}
-        for T in (1, 8):
+        for T in (1, 8, 16):
             ms, byts = bench_q8(args, dist_, torch, T)
             gbs = W * byts / (ms * 1e-3) / 1e9
             q8[f"qwen7b-layer-T{T}"] = {
@@ -671,6 +765,21 @@ def main():
                              "frac": byts / (ms * 1e-3) / 1e9 / peaks["hbm_gbs"], "traffic": None},
             }
         line["decoder_layer_q8"] = lay
+        B, P, G = 16, 2048, 256
+        r = bench_model_q8(args, dist_, torch, B, P, G)
+        step_ms = r["ms"] / G
+        step_bytes = r["weight_bytes"] + r["kv_bytes_per_step"]
+        line["model_q8"] = {
+            "workload": f"Qwen2.5-7B-shaped 28 layers, Q8 weights ~N(0,0.02), B={B}, prompt {P}, {G} greedy steps",
+            "tok_s": W * B * G / (r["ms"] * 1e-3), "decode_ms": r["ms"], "ms_per_step": step_ms,
+            "bytes_per_step": step_bytes, "hbm_gbs": step_bytes / (step_ms * 1e-3) / 1e9,
+            "frac_of_hbm": step_bytes / (step_ms * 1e-3) / 1e9 / peaks["hbm_gbs"],
+            "prompt": "KV of the prompt synthetic ~N(0,1) bf16; its prefill is not run",
+            "api": "TurboEngine.decode_step_q8 per step, ids copied to pinned host memory each step",
+            "distinct_ids": int(len(np.unique(r["ids"]))), "lens_ok": r["lens_ok"], "clocks": r["clocks"],
+            "cpu_baseline": None,
+            "cpu_baseline_note": "not run: the full-size CPU reference model is infeasible on the host",
+        }
     if dist_.rank == 0 and W == 1 and not args.no_cpu_baseline:
         v, nt, desc = cpu_prefill_sample()
         line["cpu_baseline"] = {"value": v, "unit": "TFLOP/s", "cores": nt, "kind": "port", "sample": desc}

@@ -1186,7 +1186,7 @@ int ensure_q8_scratch(oomattn_ctx* ctx, size_t bytes, int row_tiles) {
 // The linear kernel is a programmatic dependent of the x-split kernel before
 // it: it launches while that kernel runs, issues its first weight loads, and
 // waits for the split only before it reads x.
-template <int NT, int MT>
+template <int NT, int MT, int S, bool XA>
 cudaError_t launch_q8_linear(const Q8Args& a, int row_blocks, cudaStream_t st) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(a.splits, row_blocks);
@@ -1198,7 +1198,7 @@ cudaError_t launch_q8_linear(const Q8Args& a, int row_blocks, cudaStream_t st) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, q8_linear_kernel<NT, MT>, a);
+  return cudaLaunchKernelEx(&cfg, q8_linear_kernel<NT, MT, S, XA>, a);
 }
 
 }  // namespace
@@ -1233,10 +1233,12 @@ struct Q8Plan {
 // fragment), others 16 rows for more CTAs.  Split-K only when the row blocks
 // alone leave SMs idle, keeping at least one chunk per warp of a CTA (more,
 // shorter CTAs only add pipeline fill and merge).
-Q8Plan plan_q8(const oomattn_ctx* ctx, int rows, int cols) {
+Q8Plan plan_q8(const oomattn_ctx* ctx, int rows, int cols, int nt) {
   Q8Plan p;
   const int nchunks = cols / kQ8Chunk;
-  p.mt = rows >= 64 * ctx->num_sms ? 2 : 1;
+  // two row tiles per warp for large matrices; a 16-token pass has no
+  // registers left for the second
+  p.mt = (nt == 1 && rows >= 64 * ctx->num_sms) ? 2 : 1;
   p.row_blocks = (rows + 16 * p.mt - 1) / (16 * p.mt);
   const int want = std::max(1, (ctx->num_sms + p.row_blocks - 1) / p.row_blocks);
   p.splits = std::max(1, std::min(want, nchunks / kQ8Warps));
@@ -1246,8 +1248,9 @@ Q8Plan plan_q8(const oomattn_ctx* ctx, int rows, int cols) {
 }
 
 // Runs every job on the same input: x, or silu(x) * up when `up` is given.
-// Tokens run in passes of up to 8 (one MMA token tile): one x split per pass,
-// then each job's linear, a programmatic dependent of the kernel before it.
+// Tokens run in passes of up to 16 (two MMA token tiles; each weight byte is
+// read once per pass): one x split per pass, then each job's linear, a
+// programmatic dependent of the kernel before it.
 int q8_run(oomattn_ctx* ctx, const Q8Job* jobs, int n_jobs, const float* x, const float* up, int n_tokens) {
   if (!x || n_tokens < 0) return fail(ctx, OOMATTN_ERR_INVALID_ARG, "bad Q8 input");
   if (reinterpret_cast<uintptr_t>(x) % 16 || (up && reinterpret_cast<uintptr_t>(up) % 16))
@@ -1259,12 +1262,14 @@ int q8_run(oomattn_ctx* ctx, const Q8Job* jobs, int n_jobs, const float* x, cons
     int rc = check_q8_matrix(ctx, jobs[j].w, cols);
     if (rc) return rc;
     if (!jobs[j].y) return fail(ctx, OOMATTN_ERR_INVALID_ARG, "null Q8 output");
-    const Q8Plan p = plan_q8(ctx, jobs[j].w->rows, cols);
-    part_floats = std::max(part_floats, (size_t)p.splits * 8 * jobs[j].w->rows);
-    max_blocks = std::max(max_blocks, p.row_blocks);
+    for (int nt = 1; nt <= 2; ++nt) {
+      const Q8Plan p = plan_q8(ctx, jobs[j].w->rows, cols, nt);
+      part_floats = std::max(part_floats, (size_t)p.splits * 8 * nt * jobs[j].w->rows);
+      max_blocks = std::max(max_blocks, p.row_blocks);
+    }
   }
   if (n_tokens == 0) return OOMATTN_OK;
-  const int group = 8;
+  const int group = 16;
   const int nchunks = cols / kQ8Chunk;
   const size_t xw = (size_t)group * (cols / 2);
   const size_t bytes = 2 * xw * 4 + (size_t)group * nchunks * 4 + part_floats * 4 + 256;
@@ -1280,9 +1285,10 @@ int q8_run(oomattn_ctx* ctx, const Q8Job* jobs, int n_jobs, const float* x, cons
     q8_prep_x_kernel<<<(unsigned)((prep_warps + 7) / 8), 256, 0, ctx->stream>>>(
         x + (size_t)t0 * cols, up ? up + (size_t)t0 * cols : nullptr, nt, cols, xh, xl, xsum, ctx->d_status);
     CKLAUNCH();
+    const int ntiles = nt > 8 ? 2 : 1;
     for (int j = 0; j < n_jobs; ++j) {
       const oomattn_q8_matrix* w = jobs[j].w;
-      const Q8Plan p = plan_q8(ctx, w->rows, cols);
+      const Q8Plan p = plan_q8(ctx, w->rows, cols, ntiles);
       Q8Args a;
       a.q = w->q;
       a.scale = w->scale;
@@ -1301,8 +1307,10 @@ int q8_run(oomattn_ctx* ctx, const Q8Job* jobs, int n_jobs, const float* x, cons
       a.splits = p.splits;
       a.chunks_per_split = p.cps;
       a.status = ctx->d_status;
-      const cudaError_t le = p.mt == 2 ? launch_q8_linear<1, 2>(a, p.row_blocks, ctx->stream)
-                                       : launch_q8_linear<1, 1>(a, p.row_blocks, ctx->stream);
+      // one token tile: x read a chunk ahead; two: a 3-deep weight ring, x read at use
+      const cudaError_t le = ntiles == 2 ? launch_q8_linear<2, 1, 3, false>(a, p.row_blocks, ctx->stream)
+                             : p.mt == 2 ? launch_q8_linear<1, 2, 2, true>(a, p.row_blocks, ctx->stream)
+                                         : launch_q8_linear<1, 1, 2, true>(a, p.row_blocks, ctx->stream);
       if (le != cudaSuccess) return fail(ctx, OOMATTN_ERR_CUDA, "q8_linear launch: %s", cudaGetErrorString(le));
     }
   }

@@ -124,15 +124,21 @@ __device__ __forceinline__ void mma_f16_16816(float* d, uint32_t a0, uint32_t a1
 // fp16 pair (1024 + byte 2i, 1024 + byte 2i + 1) of a word of four weight bytes.
 __device__ __forceinline__ uint32_t q8_pair(uint32_t w, uint32_t sel) { return __byte_perm(w, 0x64646464u, sel); }
 
-// Everything one warp reads for one 64-column chunk: the weight bytes of its
-// MT row tiles, their blocks' scale and min, and the x fragments and chunk
-// sums of its NT token tiles.  Loaded one chunk ahead of use.
-template <int NT, int MT>
-struct Q8Chunk {
-  uint4 qa[MT], qb[MT];          // rows g and g + 8 of each row tile: 16 bytes each
+// The weight bytes of one 64-column chunk for a warp's MT row tiles (rows g
+// and g + 8 of each: 16 bytes each), and their blocks' scale and min.
+template <int MT>
+struct Q8W {
+  uint4 qa[MT], qb[MT];
   float sa[MT], ma[MT], sb[MT], mb[MT];
-  uint32_t bh[NT][8], bl[NT][8];  // x hi / lo pairs of token 8n + g, the thread's 16 columns
-  float x0[NT], x1[NT];           // chunk sums of tokens 8n + 2c and 8n + 2c + 1
+};
+
+// The x fragments of one chunk for NT token tiles: hi / lo pairs of token
+// 8n + g (the thread's 16 columns) and the chunk sums of tokens 8n + 2c and
+// 8n + 2c + 1.
+template <int NT>
+struct Q8X {
+  uint32_t bh[NT][8], bl[NT][8];
+  float x0[NT], x1[NT];
 };
 
 // Per-thread addresses that do not change along the column range.
@@ -150,7 +156,7 @@ struct Q8Base {
 
 // The weight bytes and their blocks' scale and min (independent of x).
 template <int NT, int MT>
-__device__ __forceinline__ void q8_load_w(const Q8Args& a, const Q8Base<NT, MT>& b, int ch, Q8Chunk<NT, MT>& d) {
+__device__ __forceinline__ void q8_load_w(const Q8Args& a, const Q8Base<NT, MT>& b, int ch, Q8W<MT>& d) {
 #pragma unroll
   for (int m = 0; m < MT; ++m) {
     if (!b.live[m]) {  // a row block's last tile may lie past the matrix
@@ -169,9 +175,9 @@ __device__ __forceinline__ void q8_load_w(const Q8Args& a, const Q8Base<NT, MT>&
   }
 }
 
-// The x fragments and chunk sums (written by the split kernel).
+// The x fragments and chunk sums (written by the split kernel; cache hits).
 template <int NT, int MT>
-__device__ __forceinline__ void q8_load_x(const Q8Base<NT, MT>& b, int ch, Q8Chunk<NT, MT>& d) {
+__device__ __forceinline__ void q8_load_x(const Q8Base<NT, MT>& b, int ch, Q8X<NT>& d) {
 #pragma unroll
   for (int n = 0; n < NT; ++n) {
     if (b.xh[n]) {  // tokens past n_tokens contribute zero and are not read
@@ -194,12 +200,12 @@ __device__ __forceinline__ void q8_load_x(const Q8Base<NT, MT>& b, int ch, Q8Chu
 }
 
 template <int NT, int MT>
-__device__ __forceinline__ void q8_compute_chunk(const Q8Chunk<NT, MT>& d, float (&acc)[MT][NT][4]) {
+__device__ __forceinline__ void q8_compute_chunk(const Q8W<MT>& w, const Q8X<NT>& d, float (&acc)[MT][NT][4]) {
 #pragma unroll
   for (int m = 0; m < MT; ++m) {
     // A fragments of the 4 k-steps: step s takes bytes 4s..4s+3 of the thread's 16
-    const uint32_t wa[4] = {d.qa[m].x, d.qa[m].y, d.qa[m].z, d.qa[m].w};
-    const uint32_t wb[4] = {d.qb[m].x, d.qb[m].y, d.qb[m].z, d.qb[m].w};
+    const uint32_t wa[4] = {w.qa[m].x, w.qa[m].y, w.qa[m].z, w.qa[m].w};
+    const uint32_t wb[4] = {w.qb[m].x, w.qb[m].y, w.qb[m].z, w.qb[m].w};
     uint32_t af[4][4];
 #pragma unroll
     for (int s = 0; s < 4; ++s) {
@@ -208,7 +214,7 @@ __device__ __forceinline__ void q8_compute_chunk(const Q8Chunk<NT, MT>& d, float
       af[s][2] = q8_pair(wa[s], 0x4342u);
       af[s][3] = q8_pair(wb[s], 0x4342u);
     }
-    const float ka = d.ma[m] - 1024.f * d.sa[m], kb = d.mb[m] - 1024.f * d.sb[m];
+    const float ka = w.ma[m] - 1024.f * w.sa[m], kb = w.mb[m] - 1024.f * w.sb[m];
 #pragma unroll
     for (int n = 0; n < NT; ++n) {
       // hi and lo products accumulate in two independent chains
@@ -219,20 +225,24 @@ __device__ __forceinline__ void q8_compute_chunk(const Q8Chunk<NT, MT>& d, float
         mma_f16_16816(dl, af[s][0], af[s][1], af[s][2], af[s][3], d.bl[n][2 * s], d.bl[n][2 * s + 1]);
       }
       // rows g, g + 8 x tokens 8n + 2c, 8n + 2c + 1
-      acc[m][n][0] = fmaf(d.sa[m], dh[0] + dl[0], fmaf(ka, d.x0[n], acc[m][n][0]));
-      acc[m][n][1] = fmaf(d.sa[m], dh[1] + dl[1], fmaf(ka, d.x1[n], acc[m][n][1]));
-      acc[m][n][2] = fmaf(d.sb[m], dh[2] + dl[2], fmaf(kb, d.x0[n], acc[m][n][2]));
-      acc[m][n][3] = fmaf(d.sb[m], dh[3] + dl[3], fmaf(kb, d.x1[n], acc[m][n][3]));
+      acc[m][n][0] = fmaf(w.sa[m], dh[0] + dl[0], fmaf(ka, d.x0[n], acc[m][n][0]));
+      acc[m][n][1] = fmaf(w.sa[m], dh[1] + dl[1], fmaf(ka, d.x1[n], acc[m][n][1]));
+      acc[m][n][2] = fmaf(w.sb[m], dh[2] + dl[2], fmaf(kb, d.x0[n], acc[m][n][2]));
+      acc[m][n][3] = fmaf(w.sb[m], dh[3] + dl[3], fmaf(kb, d.x1[n], acc[m][n][3]));
     }
   }
 }
 
 // A CTA owns 16 * MT rows and a column range; its 8 warps take the range's
 // chunks round-robin, each chunk for all MT row tiles and NT token tiles.
-// Two chunk buffers alternate (the loop is unrolled by two), so the next
-// chunk's loads are in flight while the current one is computed.
-template <int NT, int MT>
+// Each warp keeps the weights of its next S - 1 chunks in flight in a
+// register ring (the loop is unrolled by S so ring slots are static).  The x
+// fragments are cache hits: with XA they are read one chunk ahead into a
+// second buffer (S even, so buffer indices stay static), otherwise just
+// before use, which leaves the registers to the weight ring.
+template <int NT, int MT, int S, bool XA>
 __global__ void __launch_bounds__(kQ8Warps * 32, 2) q8_linear_kernel(const Q8Args a) {
+  static_assert(S >= 2 && (!XA || S % 2 == 0), "ring depth");
   __shared__ float red[kQ8Warps][MT][NT][4][32];
   __shared__ int s_last;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -268,27 +278,31 @@ __global__ void __launch_bounds__(kQ8Warps * 32, 2) q8_linear_kernel(const Q8Arg
 #pragma unroll
       for (int e = 0; e < 4; ++e) acc[m][n][e] = 0.f;
 
-  Q8Chunk<NT, MT> d0, d1;
+  Q8W<MT> w[S];
+  Q8X<NT> xf[XA ? 2 : 1];
   int ch = c0 + warp;
-  // the first chunk's weights do not depend on the x split: load them, then
-  // wait for the split kernel (launched before this one) to complete
-  if (ch < c1) q8_load_w<NT, MT>(a, b, ch, d0);
+  // the first S - 1 chunks' weights do not depend on the x split: load them,
+  // then wait for the split kernel (launched before this one) to complete
+#pragma unroll
+  for (int s = 0; s < S - 1; ++s)
+    if (ch + s * kQ8Warps < c1) q8_load_w<NT, MT>(a, b, ch + s * kQ8Warps, w[s]);
   asm volatile("griddepcontrol.wait;" ::: "memory");
-  if (ch < c1) q8_load_x<NT, MT>(b, ch, d0);
+  if (XA && ch < c1) q8_load_x<NT, MT>(b, ch, xf[0]);
   while (ch < c1) {
-    if (ch + kQ8Warps < c1) {
-      q8_load_w<NT, MT>(a, b, ch + kQ8Warps, d1);
-      q8_load_x<NT, MT>(b, ch + kQ8Warps, d1);
+#pragma unroll
+    for (int s = 0; s < S; ++s) {
+      if (ch >= c1) break;
+      const int nx = ch + (S - 1) * kQ8Warps;
+      if (nx < c1) q8_load_w<NT, MT>(a, b, nx, w[(s + S - 1) % S]);
+      if (XA) {
+        if (ch + kQ8Warps < c1) q8_load_x<NT, MT>(b, ch + kQ8Warps, xf[(s + 1) & 1]);
+        q8_compute_chunk<NT, MT>(w[s], xf[s & 1], acc);
+      } else {
+        q8_load_x<NT, MT>(b, ch, xf[0]);
+        q8_compute_chunk<NT, MT>(w[s], xf[0], acc);
+      }
+      ch += kQ8Warps;
     }
-    q8_compute_chunk<NT, MT>(d0, acc);
-    ch += kQ8Warps;
-    if (ch >= c1) break;
-    if (ch + kQ8Warps < c1) {
-      q8_load_w<NT, MT>(a, b, ch + kQ8Warps, d0);
-      q8_load_x<NT, MT>(b, ch + kQ8Warps, d0);
-    }
-    q8_compute_chunk<NT, MT>(d1, acc);
-    ch += kQ8Warps;
   }
 
   // the CTA's warps cover disjoint chunks of the same rows: sum them in warp order
@@ -306,7 +320,7 @@ __global__ void __launch_bounds__(kQ8Warps * 32, 2) q8_linear_kernel(const Q8Arg
     const int m = i / (NT * 128), n = (i / 128) % NT, e = (i / 32) & 3, l = i & 31;
     float v = 0.f;
 #pragma unroll
-    for (int w = 0; w < kQ8Warps; ++w) v += red[w][m][n][e][l];
+    for (int w8 = 0; w8 < kQ8Warps; ++w8) v += red[w8][m][n][e][l];
     const int row = row0 + 16 * m + (l >> 2) + ((e & 2) ? 8 : 0);
     const int tok = 8 * n + 2 * (l & 3) + (e & 1);
     if (row >= a.rows || tok >= a.n_tokens) continue;
