@@ -1247,26 +1247,33 @@ Q8Plan plan_q8(const oomattn_ctx* ctx, int rows, int cols, int nt) {
   return p;
 }
 
-// Runs every job on the same input: x, or silu(x) * up when `up` is given.
-// Tokens run in passes of up to 16 (two MMA token tiles; each weight byte is
-// read once per pass): one x split per pass, then each job's linear, a
-// programmatic dependent of the kernel before it.
+// Runs every job (up to kQ8MaxMats, all of the same width) on the same input:
+// x, or silu(x) * up when `up` is given.  Tokens run in passes of up to 16
+// (two MMA token tiles; each weight byte is read once per pass): one x split
+// per pass, then one linear launch over all jobs' row blocks, a programmatic
+// dependent of the split.
 int q8_run(oomattn_ctx* ctx, const Q8Job* jobs, int n_jobs, const float* x, const float* up, int n_tokens) {
   if (!x || n_tokens < 0) return fail(ctx, OOMATTN_ERR_INVALID_ARG, "bad Q8 input");
   if (reinterpret_cast<uintptr_t>(x) % 16 || (up && reinterpret_cast<uintptr_t>(up) % 16))
     return fail(ctx, OOMATTN_ERR_INVALID_ARG, "x must be 16-byte aligned");
+  if (n_jobs < 1 || n_jobs > kQ8MaxMats) return fail(ctx, OOMATTN_ERR_INVALID_ARG, "bad Q8 job count");
   const int cols = jobs[0].w ? jobs[0].w->cols : 0;
-  size_t part_floats = 0;
-  int max_blocks = 1;
+  int total_rows = 0;
   for (int j = 0; j < n_jobs; ++j) {
     int rc = check_q8_matrix(ctx, jobs[j].w, cols);
     if (rc) return rc;
     if (!jobs[j].y) return fail(ctx, OOMATTN_ERR_INVALID_ARG, "null Q8 output");
-    for (int nt = 1; nt <= 2; ++nt) {
-      const Q8Plan p = plan_q8(ctx, jobs[j].w->rows, cols, nt);
-      part_floats = std::max(part_floats, (size_t)p.splits * 8 * nt * jobs[j].w->rows);
-      max_blocks = std::max(max_blocks, p.row_blocks);
-    }
+    total_rows += jobs[j].w->rows;
+  }
+  // all jobs run in one launch per pass, planned on their rows together
+  size_t part_floats = 0;
+  int max_blocks = 1;
+  for (int nt = 1; nt <= 2; ++nt) {
+    const Q8Plan p = plan_q8(ctx, total_rows, cols, nt);
+    int blocks = 0;
+    for (int j = 0; j < n_jobs; ++j) blocks += (jobs[j].w->rows + 16 * p.mt - 1) / (16 * p.mt);
+    part_floats = std::max(part_floats, (size_t)p.splits * 8 * nt * total_rows);
+    max_blocks = std::max(max_blocks, blocks);
   }
   if (n_tokens == 0) return OOMATTN_OK;
   const int group = 16;
@@ -1286,33 +1293,41 @@ int q8_run(oomattn_ctx* ctx, const Q8Job* jobs, int n_jobs, const float* x, cons
         x + (size_t)t0 * cols, up ? up + (size_t)t0 * cols : nullptr, nt, cols, xh, xl, xsum, ctx->d_status);
     CKLAUNCH();
     const int ntiles = nt > 8 ? 2 : 1;
+    const Q8Plan p = plan_q8(ctx, total_rows, cols, ntiles);
+    Q8Args a;
+    memset(&a, 0, sizeof(a));
+    a.n_mats = n_jobs;
+    a.cols = cols;
+    a.xh = xh;
+    a.xl = xl;
+    a.xsum = xsum;
+    a.n_tokens = nt;
+    a.counters = ctx->d_q8_counters;
+    a.splits = p.splits;
+    a.chunks_per_split = p.cps;
+    a.status = ctx->d_status;
+    int blocks = 0;
+    size_t row_prefix = 0;
     for (int j = 0; j < n_jobs; ++j) {
       const oomattn_q8_matrix* w = jobs[j].w;
-      const Q8Plan p = plan_q8(ctx, w->rows, cols, ntiles);
-      Q8Args a;
-      a.q = w->q;
-      a.scale = w->scale;
-      a.min = w->min;
-      a.rows = w->rows;
-      a.cols = cols;
-      a.xh = xh;
-      a.xl = xl;
-      a.xsum = xsum;
-      a.n_tokens = nt;
-      a.bias = jobs[j].bias;
-      a.residual = jobs[j].residual ? jobs[j].residual + (size_t)t0 * w->rows : nullptr;
-      a.y = jobs[j].y + (size_t)t0 * w->rows;
-      a.part = part;
-      a.counters = ctx->d_q8_counters;
-      a.splits = p.splits;
-      a.chunks_per_split = p.cps;
-      a.status = ctx->d_status;
-      // one token tile: x read a chunk ahead; two: a 3-deep weight ring, x read at use
-      const cudaError_t le = ntiles == 2 ? launch_q8_linear<2, 1, 3, false>(a, p.row_blocks, ctx->stream)
-                             : p.mt == 2 ? launch_q8_linear<1, 2, 2, true>(a, p.row_blocks, ctx->stream)
-                                         : launch_q8_linear<1, 1, 2, true>(a, p.row_blocks, ctx->stream);
-      if (le != cudaSuccess) return fail(ctx, OOMATTN_ERR_CUDA, "q8_linear launch: %s", cudaGetErrorString(le));
+      Q8Mat& m = a.m[j];
+      m.q = w->q;
+      m.scale = w->scale;
+      m.min = w->min;
+      m.rows = w->rows;
+      m.rb_begin = blocks;
+      m.bias = jobs[j].bias;
+      m.residual = jobs[j].residual ? jobs[j].residual + (size_t)t0 * w->rows : nullptr;
+      m.y = jobs[j].y + (size_t)t0 * w->rows;
+      m.part = part + (size_t)p.splits * 8 * ntiles * row_prefix;
+      blocks += (w->rows + 16 * p.mt - 1) / (16 * p.mt);
+      row_prefix += w->rows;
     }
+    // one token tile: x read a chunk ahead; two: a 3-deep weight ring, x read at use
+    const cudaError_t le = ntiles == 2 ? launch_q8_linear<2, 1, 3, false>(a, blocks, ctx->stream)
+                           : p.mt == 2 ? launch_q8_linear<1, 2, 2, true>(a, blocks, ctx->stream)
+                                       : launch_q8_linear<1, 1, 2, true>(a, blocks, ctx->stream);
+    if (le != cudaSuccess) return fail(ctx, OOMATTN_ERR_CUDA, "q8_linear launch: %s", cudaGetErrorString(le));
   }
   return OOMATTN_OK;
 }

@@ -38,29 +38,78 @@ namespace oomattn {
 constexpr int kQ8Warps = 8;            // warps per CTA
 constexpr int kQ8Chunk = 64;           // columns per chunk
 
-struct Q8Args {
+// One matrix of a launch: its weights, epilogue operands and output.  A
+// launch runs up to kQ8MaxMats matrices of the same width on the same x (the
+// q, k and v projections; gate and up); matrix i owns the grid's row blocks
+// from rb_begin.
+constexpr int kQ8MaxMats = 3;
+struct Q8Mat {
   const uint8_t* q;
   const float* scale;
   const float* min;
   int rows;
+  int rb_begin;
+  const float* bias;      // [rows] or null
+  const float* residual;  // [n_tokens][rows] added to y, or null (may alias y)
+  float* y;               // [n_tokens][rows]
+  float* part;            // [splits][8 * token tiles][rows]: split-K partial sums
+};
+
+struct Q8Args {
+  Q8Mat m[kQ8MaxMats];
+  int n_mats;
   int cols;
   const uint32_t* xh;   // [n_tokens][cols / 2] fp16 pairs: x rounded to fp16
   const uint32_t* xl;   // [n_tokens][cols / 2] fp16 pairs: x - hi rounded to fp16
   const float* xsum;    // [n_tokens][cols / 64]
   int n_tokens;
-  const float* bias;    // [rows] or null
-  const float* residual;  // [n_tokens][rows] added to y, or null (may alias y)
-  float* y;             // [n_tokens][rows]
-  float* part;          // [splits][8 * token tiles][rows]: split-K partial sums
   unsigned* counters;   // [row blocks]: arrivals per row block, zero between launches
   int splits;
   int chunks_per_split;
   int* status;
 };
 
+// What one CTA uses: its matrix's fields and the launch's shared ones.
+struct Q8View {
+  const uint8_t* q;
+  const float* scale;
+  const float* min;
+  int rows;
+  int rb;  // row block within the matrix
+  const float* bias;
+  const float* residual;
+  float* y;
+  float* part;
+  int cols;
+  int n_tokens;
+  int splits;
+};
+
+// Field-wise selects keep the parameter array in constant space (a dynamic
+// index would copy it to local memory).
+__device__ __forceinline__ Q8View q8_view(const Q8Args& A, int rbg) {
+  const int j = (A.n_mats > 1 && rbg >= A.m[1].rb_begin) + (A.n_mats > 2 && rbg >= A.m[2].rb_begin);
+#define Q8_SEL(f) (j == 0 ? A.m[0].f : (j == 1 ? A.m[1].f : A.m[2].f))
+  Q8View v;
+  v.q = Q8_SEL(q);
+  v.scale = Q8_SEL(scale);
+  v.min = Q8_SEL(min);
+  v.rows = Q8_SEL(rows);
+  v.rb = rbg - Q8_SEL(rb_begin);
+  v.bias = Q8_SEL(bias);
+  v.residual = Q8_SEL(residual);
+  v.y = Q8_SEL(y);
+  v.part = Q8_SEL(part);
+#undef Q8_SEL
+  v.cols = A.cols;
+  v.n_tokens = A.n_tokens;
+  v.splits = A.splits;
+  return v;
+}
+
 // y = x W^T + bias + residual for one output element (the residual add of a
 // decoder layer, src/oomllama.rs:391, :401).
-__device__ __forceinline__ float q8_epilogue(const Q8Args& a, int tok, int row, float v) {
+__device__ __forceinline__ float q8_epilogue(const Q8View& a, int tok, int row, float v) {
   if (a.bias) v += a.bias[row];
   if (a.residual) v += a.residual[(size_t)tok * a.rows + row];
   return v;
@@ -156,7 +205,7 @@ struct Q8Base {
 
 // The weight bytes and their blocks' scale and min (independent of x).
 template <int NT, int MT>
-__device__ __forceinline__ void q8_load_w(const Q8Args& a, const Q8Base<NT, MT>& b, int ch, Q8W<MT>& d) {
+__device__ __forceinline__ void q8_load_w(const Q8View& a, const Q8Base<NT, MT>& b, int ch, Q8W<MT>& d) {
 #pragma unroll
   for (int m = 0; m < MT; ++m) {
     if (!b.live[m]) {  // a row block's last tile may lie past the matrix
@@ -241,20 +290,21 @@ __device__ __forceinline__ void q8_compute_chunk(const Q8W<MT>& w, const Q8X<NT>
 // second buffer (S even, so buffer indices stay static), otherwise just
 // before use, which leaves the registers to the weight ring.
 template <int NT, int MT, int S, bool XA>
-__global__ void __launch_bounds__(kQ8Warps * 32, 2) q8_linear_kernel(const Q8Args a) {
+__global__ void __launch_bounds__(kQ8Warps * 32, 2) q8_linear_kernel(const Q8Args args) {
   static_assert(S >= 2 && (!XA || S % 2 == 0), "ring depth");
   __shared__ float red[kQ8Warps][MT][NT][4][32];
   __shared__ int s_last;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, c = lane & 3;
-  const int rb = blockIdx.y, sp = blockIdx.x;
+  const Q8View a = q8_view(args, blockIdx.y);
+  const int rb = a.rb, sp = blockIdx.x;
   const int row0 = rb * 16 * MT;
   const int nchunks = a.cols / kQ8Chunk;
-  const int c0 = sp * a.chunks_per_split, c1 = min(nchunks, c0 + a.chunks_per_split);
+  const int c0 = sp * args.chunks_per_split, c1 = min(nchunks, c0 + args.chunks_per_split);
 
   Q8Base<NT, MT> b;
   b.row8 = 8LL * a.cols;
-  b.xlo = a.xl - a.xh;
+  b.xlo = args.xl - args.xh;
   b.nchunks = nchunks;
 #pragma unroll
   for (int m = 0; m < MT; ++m) {
@@ -264,8 +314,8 @@ __global__ void __launch_bounds__(kQ8Warps * 32, 2) q8_linear_kernel(const Q8Arg
 #pragma unroll
   for (int n = 0; n < NT; ++n) {
     const int tok = 8 * n + g, t0 = 8 * n + 2 * c;
-    b.xh[n] = tok < a.n_tokens ? a.xh + (size_t)tok * (a.cols / 2) + 8 * c : nullptr;
-    b.xs0[n] = a.xsum + (size_t)t0 * nchunks;
+    b.xh[n] = tok < a.n_tokens ? args.xh + (size_t)tok * (a.cols / 2) + 8 * c : nullptr;
+    b.xs0[n] = args.xsum + (size_t)t0 * nchunks;
     b.has0[n] = t0 < a.n_tokens;
     b.has1[n] = t0 + 1 < a.n_tokens;
   }
@@ -334,7 +384,7 @@ __global__ void __launch_bounds__(kQ8Warps * 32, 2) q8_linear_kernel(const Q8Arg
   __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) {
-    const unsigned prev = atomicAdd(&a.counters[rb], 1u);
+    const unsigned prev = atomicAdd(&args.counters[blockIdx.y], 1u);
     s_last = (prev == (unsigned)a.splits - 1);
   }
   __syncthreads();
@@ -347,7 +397,7 @@ __global__ void __launch_bounds__(kQ8Warps * 32, 2) q8_linear_kernel(const Q8Arg
     for (int s = 0; s < a.splits; ++s) v += __ldcg(a.part + ((size_t)s * tp + tok) * a.rows + row);
     a.y[(size_t)tok * a.rows + row] = q8_epilogue(a, tok, row, v);
   }
-  if (threadIdx.x == 0) a.counters[rb] = 0;
+  if (threadIdx.x == 0) args.counters[blockIdx.y] = 0;
 }
 
 // ------------------------------------------------------------------ RMSNorm
