@@ -1,11 +1,14 @@
 // K-B / K-B2: split-KV GQA flash-decode over the paged cache, with the
 // log-sum-exp merge of the splits done by the last CTA of each (row, kv head).
 //
-// Work unit: one CTA per (split, kv head g, row z).  The CTA streams pages
-// [split*pps, (split+1)*pps) of row z's block table and serves all `group`
-// q heads that read kv head g (q head h -> kv head h / group, the
-// repeat_interleave grouping of oomllama_turbo.rs:313-316), so each KV byte is
-// read from HBM once per step instead of `group` times.
+// Work unit: one CTA per item (row z, kv head g, split) of a DecodeSched.  The
+// CTA streams pages [split*pps, (split+1)*pps) of row z's block table, pps =
+// ceil(pages / nsplit), and serves all `group` q heads that read kv head g
+// (q head h -> kv head h / group, the repeat_interleave grouping of
+// oomllama_turbo.rs:313-316), so each KV byte is read from HBM once per step
+// instead of `group` times.  Items come longest first, so the block scheduler,
+// which hands CTAs out in grid order to whichever slot frees first, runs a
+// longest-processing-time list schedule over rows of different lengths.
 //
 // bf16 cache (decode_bf16_kernel): a producer warp moves each (page, kv head)
 // chunk -- 16 tokens x 128 dims, two 2 KB TMA boxes with the 128-byte swizzle --
@@ -123,6 +126,30 @@ __device__ __forceinline__ void combine_and_store(const MergeSmem& ms, const Dec
 }
 
 // A row with no visible keys gets O = 0 and lse = -inf (written by split 0).
+// Item i of the schedule: the last row slot whose items start at or before i.
+struct DecodeItem {
+  int z, g, split, nsplit, pb, pe;
+};
+__device__ __forceinline__ DecodeItem decode_item(const DecodeSched& s, const SeqBatch& sb, int i) {
+  int lo = 0, hi = s.n - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (s.item0[mid] <= i) lo = mid; else hi = mid - 1;
+  }
+  DecodeItem it;
+  it.z = s.order[lo];
+  const int ns = s.nsplit[lo];
+  const int j = i - s.item0[lo];
+  it.g = j / ns;
+  it.split = j - it.g * ns;
+  const int n_pages = (sb.len[it.z] + kPageSize - 1) / kPageSize;
+  const int pps = n_pages > 0 ? (n_pages + ns - 1) / ns : 0;
+  it.pb = it.split * pps;
+  it.pe = min(it.pb + pps, n_pages);
+  it.nsplit = pps > 0 ? (n_pages + pps - 1) / pps : 1;
+  return it;
+}
+
 __device__ __forceinline__ void write_empty_row(const DecodeArgs& a, int z, int g) {
   for (int i = threadIdx.x; i < a.group * kHeadDim; i += blockDim.x) {
     const int h = g * a.group + i / kHeadDim;
@@ -133,24 +160,24 @@ __device__ __forceinline__ void write_empty_row(const DecodeArgs& a, int z, int 
 
 __global__ void __launch_bounds__((kDecWarps + 1) * 32, 2)
     decode_bf16_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
-                       const KVPool pool, const DecodeArgs a, const __grid_constant__ SeqBatch sb) {
+                       const KVPool pool, const DecodeArgs a, const __grid_constant__ SeqBatch sb,
+                       const __grid_constant__ DecodeSched sched) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kDecStages * kDecStageBytes);
   uint64_t* empty = full + kDecStages;
   int* s_last = reinterpret_cast<int*>(empty + kDecStages);
 
-  const int split = blockIdx.x, g = blockIdx.y, z = blockIdx.z;
+  const DecodeItem item = decode_item(sched, sb, blockIdx.x);
+  const int split = item.split, g = item.g, z = item.z;
   const int seq = sb.seq[z];
   const int L = sb.len[z];
-  const int n_pages = (L + kPageSize - 1) / kPageSize;
-  const int pb = split * a.pages_per_split;
-  const int pe = min(pb + a.pages_per_split, n_pages);
+  const int pb = item.pb, pe = item.pe;
   if (pb >= pe) {
     if (L <= 0 && split == 0) write_empty_row(a, z, g);
     return;
   }
-  const int nsplit = (n_pages + a.pages_per_split - 1) / a.pages_per_split;
+  const int nsplit = item.nsplit;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_iter = (pe - pb + kDecWarps - 1) / kDecWarps;
 
@@ -300,20 +327,20 @@ __global__ void __launch_bounds__((kDecWarps + 1) * 32, 2)
 }
 
 __global__ void __launch_bounds__(kDecWarps * 32)
-    decode_f32_kernel(const KVPool pool, const DecodeArgs a, const __grid_constant__ SeqBatch sb) {
+    decode_f32_kernel(const KVPool pool, const DecodeArgs a, const __grid_constant__ SeqBatch sb,
+                      const __grid_constant__ DecodeSched sched) {
   __shared__ MergeSmem ms;
   __shared__ int s_last;
-  const int split = blockIdx.x, g = blockIdx.y, z = blockIdx.z;
+  const DecodeItem item = decode_item(sched, sb, blockIdx.x);
+  const int split = item.split, g = item.g, z = item.z;
   const int seq = sb.seq[z];
   const int L = sb.len[z];
-  const int n_pages = (L + kPageSize - 1) / kPageSize;
-  const int pb = split * a.pages_per_split;
-  const int pe = min(pb + a.pages_per_split, n_pages);
+  const int pb = item.pb, pe = item.pe;
   if (pb >= pe) {
     if (L <= 0 && split == 0) write_empty_row(a, z, g);
     return;
   }
-  const int nsplit = (n_pages + a.pages_per_split - 1) / a.pages_per_split;
+  const int nsplit = item.nsplit;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const float* kp = reinterpret_cast<const float*>(pool.k);
   const float* vp = reinterpret_cast<const float*>(pool.v);

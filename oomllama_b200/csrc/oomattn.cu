@@ -95,6 +95,11 @@ struct oomattn_ctx {
   // model step: the residual stream between layers and the logits
   float* d_model_scratch = nullptr;
   size_t model_scratch_bytes = 0;
+  // the last decode schedule and the page counts it was planned for (every
+  // layer of a step, and every step until a row crosses a page, reuses it)
+  std::vector<int> sched_key;
+  DecodeSched sched;
+  int sched_items = 0;
 };
 
 namespace {
@@ -344,44 +349,117 @@ int launch_rope_append(oomattn_ctx* ctx, const AppendArgs& ap, const SeqBatch& s
   return OOMATTN_OK;
 }
 
-// Pages per split-KV CTA.  Candidates are multiples of 4 (one page per consumer
-// warp per stage) that keep the split count within the partial scratch; each
-// is scored by the makespan it implies on the resident CTA slots,
-//   ceil(ctas / slots) * (pps + fill),
-// with `fill` pages standing for a CTA's pipeline fill and merge.  This avoids
-// a nearly empty last wave (e.g. 1216 CTAs on 296 slots) and very short CTAs.
-int plan_pages_per_split(const SeqBatch& sb, int n_kv, int max_pages, int max_splits, int num_sms,
-                         int ctas_per_sm) {
-  const long long slots = (long long)num_sms * ctas_per_sm;
-  const int fill = 6;
-  const int lo = std::max(8, (max_pages + max_splits - 1) / max_splits);
-  int best = std::max(lo, (max_pages + 3) / 4 * 4);
-  double best_cost = 1e30;
-  for (int pps = (lo + 3) / 4 * 4; pps <= std::max(8, (max_pages + 3) / 4 * 4); pps += 4) {
-    long long ctas = 0;
-    for (int z = 0; z < sb.n; ++z) ctas += (long long)((sb.len[z] + kPageSize * pps - 1) / (kPageSize * pps)) * n_kv;
-    const double cost = (double)((ctas + slots - 1) / slots) * (pps + fill);
-    if (cost < best_cost) {
-      best_cost = cost;
-      best = pps;
+// Split-KV decode schedule.  Row z's pages are split into ns_z = ceil(pages_z
+// / t) near-equal ranges (at most max_splits) for each kv head, and the rows
+// are ordered by range size, longest first, so that the block scheduler's
+// in-order hand-out of CTAs to free slots is a longest-processing-time list
+// schedule.  t is the best of three candidates -- the smallest t that gives at
+// most 1, 2 or 3 waves of CTAs on the resident slots -- judged by simulating
+// that list schedule with kDecodeFillPages pages of fixed cost per CTA
+// (pipeline fill and merge).  Returns the number of items (the grid size).
+constexpr int kDecodeFillPages = 12;
+constexpr int kDecodeMaxSimSlots = 2048;
+
+long long lpt_makespan(const int* size, const int* count, int groups, int slots, long long* heap) {
+  // min-heap of slot finish times, in pages
+  for (int i = 0; i < slots; ++i) heap[i] = 0;
+  for (int gi = 0; gi < groups; ++gi) {
+    for (int k = 0; k < count[gi]; ++k) {
+      heap[0] += size[gi] + kDecodeFillPages;  // the earliest free slot takes the item; sift it down
+      int i = 0;
+      for (;;) {
+        const int l = 2 * i + 1, r = l + 1;
+        int m = i;
+        if (l < slots && heap[l] < heap[m]) m = l;
+        if (r < slots && heap[r] < heap[m]) m = r;
+        if (m == i) break;
+        std::swap(heap[i], heap[m]);
+        i = m;
+      }
     }
   }
-  return best;
+  long long mx = 0;
+  for (int i = 0; i < slots; ++i) mx = std::max(mx, heap[i]);
+  return mx;
+}
+
+int plan_decode(const SeqBatch& sb, int n_kv, int slots, int max_splits, DecodeSched& sched) {
+  slots = std::max(1, std::min(slots, kDecodeMaxSimSlots));
+  int pages[kMaxBatch];
+  int mp = 0;
+  for (int z = 0; z < sb.n; ++z) {
+    pages[z] = sb.len[z] > 0 ? (sb.len[z] + kPageSize - 1) / kPageSize : 0;
+    mp = std::max(mp, pages[z]);
+  }
+  const int t_lo = std::max(1, (mp + max_splits - 1) / max_splits);
+  const int t_hi = std::max(t_lo, mp);
+  auto ns_of = [&](int p, int t) { return p > 0 ? (p + t - 1) / t : 1; };
+  auto ctas_of = [&](int t) {
+    long long c = 0;
+    for (int z = 0; z < sb.n; ++z) c += (long long)ns_of(pages[z], t) * n_kv;
+    return c;
+  };
+  int cand[3];
+  for (int w = 1; w <= 3; ++w) {  // smallest t with ctas(t) <= w * slots (ctas falls as t grows)
+    int lo = t_lo, hi = t_hi;
+    while (lo < hi) {
+      const int mid = lo + (hi - lo) / 2;
+      if (ctas_of(mid) <= (long long)w * slots) hi = mid; else lo = mid + 1;
+    }
+    cand[w - 1] = lo;
+  }
+  long long heap[kDecodeMaxSimSlots];
+  int order[kMaxBatch], size[kMaxBatch], count[kMaxBatch];
+  int best_t = cand[0];
+  long long best_cost = -1;
+  for (int ci = 0; ci < 3; ++ci) {
+    const int t = cand[ci];
+    if (ci > 0 && (t == cand[ci - 1])) continue;
+    for (int z = 0; z < sb.n; ++z) order[z] = z;
+    auto range = [&](int z) { const int p = pages[z]; return p > 0 ? (p + ns_of(p, t) - 1) / ns_of(p, t) : 0; };
+    std::sort(order, order + sb.n, [&](int x, int y) { return range(x) > range(y); });
+    for (int r = 0; r < sb.n; ++r) {
+      size[r] = range(order[r]);
+      count[r] = ns_of(pages[order[r]], t) * n_kv;
+    }
+    const long long cost = lpt_makespan(size, count, sb.n, slots, heap);
+    if (best_cost < 0 || cost < best_cost) {
+      best_cost = cost;
+      best_t = t;
+    }
+  }
+  // the chosen schedule
+  sched.n = sb.n;
+  for (int z = 0; z < sb.n; ++z) order[z] = z;
+  auto range_best = [&](int z) {
+    const int p = pages[z];
+    return p > 0 ? (p + ns_of(p, best_t) - 1) / ns_of(p, best_t) : 0;
+  };
+  std::sort(order, order + sb.n, [&](int x, int y) { return range_best(x) > range_best(y); });
+  int items = 0;
+  for (int r = 0; r < sb.n; ++r) {
+    sched.order[r] = order[r];
+    sched.nsplit[r] = ns_of(pages[order[r]], best_t);
+    sched.item0[r] = items;
+    items += sched.nsplit[r] * n_kv;
+  }
+  sched.item0[sb.n] = items;
+  return items;
 }
 
 int launch_decode_rows(oomattn_ctx* ctx, int layer, const SeqBatch& sb, const float* q, float* out, float* lse) {
   const int n_kv = ctx->cfg.n_kv_heads;
-  long long unit_pages = 0;
-  int max_pages = 0;
-  for (int z = 0; z < sb.n; ++z) {
-    const int pages = (sb.len[z] + kPageSize - 1) / kPageSize;
-    unit_pages += (long long)pages * n_kv;
-    max_pages = std::max(max_pages, pages);
+  const int slots = ctx->num_sms * (ctx->cfg.kv_dtype == OOMATTN_DTYPE_BF16 ? 2 : 8);
+  int key[kMaxBatch + 1];
+  key[0] = sb.n;
+  for (int z = 0; z < sb.n; ++z) key[z + 1] = sb.len[z] > 0 ? (sb.len[z] + kPageSize - 1) / kPageSize : 0;
+  if (ctx->sched_key.size() != (size_t)sb.n + 1 || !std::equal(key, key + sb.n + 1, ctx->sched_key.begin())) {
+    ctx->sched_items = plan_decode(sb, n_kv, slots, kMaxSplits, ctx->sched);
+    ctx->sched_key.assign(key, key + sb.n + 1);
   }
-  const int pps = plan_pages_per_split(sb, n_kv, max_pages, kMaxSplits, ctx->num_sms,
-                                       ctx->cfg.kv_dtype == OOMATTN_DTYPE_BF16 ? 2 : 8);
-  const int nsplit = std::max(1, (max_pages + pps - 1) / pps);
-  (void)unit_pages;
+  const DecodeSched& sched = ctx->sched;
+  const int n_items = ctx->sched_items;
+  if (n_items == 0) return OOMATTN_OK;
   DecodeArgs a;
   a.q = q;
   a.out = out;
@@ -389,7 +467,6 @@ int launch_decode_rows(oomattn_ctx* ctx, int layer, const SeqBatch& sb, const fl
   a.layer = layer;
   a.n_heads = ctx->cfg.n_heads;
   a.group = ctx->group;
-  a.pages_per_split = pps;
   a.max_splits = kMaxSplits;
   a.qscale = ctx->scale * 1.4426950408889634f;
   a.part_o = ctx->d_part_o;
@@ -398,11 +475,11 @@ int launch_decode_rows(oomattn_ctx* ctx, int layer, const SeqBatch& sb, const fl
   a.status = ctx->d_status;
   a.timeout_ns = ctx->timeout_ns;
   KVPool pool = make_pool(ctx);
-  dim3 grid(nsplit, n_kv, sb.n);
   if (ctx->cfg.kv_dtype == OOMATTN_DTYPE_BF16) {
-    decode_bf16_kernel<<<grid, (kDecWarps + 1) * 32, kDecSmemBytes, ctx->stream>>>(ctx->kmap, ctx->vmap, pool, a, sb);
+    decode_bf16_kernel<<<n_items, (kDecWarps + 1) * 32, kDecSmemBytes, ctx->stream>>>(ctx->kmap, ctx->vmap, pool, a,
+                                                                                      sb, sched);
   } else {
-    decode_f32_kernel<<<grid, kDecWarps * 32, 0, ctx->stream>>>(pool, a, sb);
+    decode_f32_kernel<<<n_items, kDecWarps * 32, 0, ctx->stream>>>(pool, a, sb, sched);
   }
   CKLAUNCH();
   return OOMATTN_OK;
@@ -1010,8 +1087,6 @@ extern "C" int oomattn_decode_static_scratch(int device, void* stream, int32_t k
     return static_fail(errbuf, errbuf_len, OOMATTN_ERR_OUT_OF_RANGE, "pool of %d pages unsupported", n_pool_pages);
   if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(out)) & 15u)
     return static_fail(errbuf, errbuf_len, OOMATTN_ERR_INVALID_ARG, "q and out must be 16-byte aligned");
-  int max_pages = 0;
-  long long unit_pages = 0;
   SeqBatch sb;
   sb.n = n_rows;
   for (int z = 0; z < n_rows; ++z) {
@@ -1023,9 +1098,6 @@ extern "C" int oomattn_decode_static_scratch(int device, void* stream, int32_t k
     sb.seq[z] = seq_ids[z];
     sb.len[z] = lens[z];
     sb.pos[z] = 0;
-    const int pages = (lens[z] + kPageSize - 1) / kPageSize;
-    max_pages = std::max(max_pages, pages);
-    unit_pages += (long long)pages * n_kv_heads;
   }
 
   DeviceGuard dg(device);
@@ -1057,11 +1129,11 @@ extern "C" int oomattn_decode_static_scratch(int device, void* stream, int32_t k
 
   // Split plan as in oomattn_decode, capped so that every (row, q head, split)
   // partial fits the static array: nsplit <= slots / (rows * heads).
-  const int cap_splits = std::max(1, kStaticPartSlots / (n_rows * n_heads));
-  long long target = (unit_pages + (long long)num_sms * 8 - 1) / ((long long)num_sms * 8);
-  int pps = (int)std::max<long long>(8, (target + 3) / 4 * 4);
-  pps = std::max(pps, (max_pages + cap_splits - 1) / cap_splits);
-  const int nsplit = std::max(1, (max_pages + pps - 1) / pps);
+  const int cap_splits = std::max(1, std::min(kMaxSplits, kStaticPartSlots / (n_rows * n_heads)));
+  DecodeSched sched;
+  const int n_items = plan_decode(sb, n_kv_heads, num_sms * (kv_dtype == OOMATTN_DTYPE_BF16 ? 2 : 8), cap_splits,
+                                  sched);
+  if (n_items == 0) return OOMATTN_OK;
 
   // The counters must start at zero; a previous call that ended early could
   // have left some set, so they are cleared on every call.
@@ -1084,15 +1156,13 @@ extern "C" int oomattn_decode_static_scratch(int device, void* stream, int32_t k
   a.layer = 0;
   a.n_heads = n_heads;
   a.group = n_heads / n_kv_heads;
-  a.pages_per_split = pps;
-  a.max_splits = nsplit;
+  a.max_splits = cap_splits;
   a.qscale = (softmax_scale > 0.f ? softmax_scale : 1.0f / sqrtf((float)kHeadDim)) * 1.4426950408889634f;
   a.part_o = part_o;
   a.part_lse = part_lse;
   a.counters = counters;
   a.status = nullptr;
   a.timeout_ns = kDefaultTimeoutNs;
-  dim3 grid(nsplit, n_kv_heads, n_rows);
   if (pool.kv_bf16) {
     // Tensor maps are encoded on the host into kernel parameters: no allocation.
     EncodeTiledFn enc = get_encode_fn();
@@ -1111,9 +1181,9 @@ extern "C" int oomattn_decode_static_scratch(int device, void* stream, int32_t k
         return static_fail(errbuf, errbuf_len, OOMATTN_ERR_INVALID_ARG,
                            "pool pointer rejected by cuTensorMapEncodeTiled (%d): it must be 16-byte aligned", (int)r);
     }
-    decode_bf16_kernel<<<grid, (kDecWarps + 1) * 32, kDecSmemBytes, st>>>(maps[0], maps[1], pool, a, sb);
+    decode_bf16_kernel<<<n_items, (kDecWarps + 1) * 32, kDecSmemBytes, st>>>(maps[0], maps[1], pool, a, sb, sched);
   } else {
-    decode_f32_kernel<<<grid, kDecWarps * 32, 0, st>>>(pool, a, sb);
+    decode_f32_kernel<<<n_items, kDecWarps * 32, 0, st>>>(pool, a, sb, sched);
   }
   e = cudaGetLastError();
   if (e != cudaSuccess)

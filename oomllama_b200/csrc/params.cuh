@@ -43,14 +43,24 @@ struct DecodeArgs {
   int layer;
   int n_heads;
   int group;            // n_heads / n_kv
-  int pages_per_split;
-  int max_splits;
+  int max_splits;       // partial slots per (row, q head)
   float qscale;         // softmax scale * log2(e)
   float* part_o;        // [rows][n_heads][max_splits][128]
   float* part_lse;      // [rows][n_heads][max_splits], base 2
   unsigned* counters;   // [rows][n_kv], zero between launches
   int* status;
   unsigned long long timeout_ns;
+};
+
+// The split-KV decode grid as a list of work items, longest first: row slot r
+// is row order[r], whose pages are split into nsplit[r] near-equal ranges
+// (ceil(pages / nsplit) each) for every kv head; its items are
+// [item0[r], item0[r + 1]), kv head major.
+struct DecodeSched {
+  int n;                      // row slots
+  int order[kMaxBatch];
+  int nsplit[kMaxBatch];
+  int item0[kMaxBatch + 1];
 };
 
 struct AppendArgs {

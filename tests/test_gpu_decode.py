@@ -77,6 +77,22 @@ def test_decode_lse_and_empty_row(oracle):
     assert_close(lse[1], ref_lse[1], 1e-3, what="lse")
 
 
+@pytest.mark.parametrize("kv_dtype", ["bf16", "f32"])
+def test_decode_ragged_rows_longest_first(oracle, kv_dtype):
+    # rows of very different lengths, empty ones among them: the work items are
+    # reordered longest first and each row's pages split into near-equal ranges
+    lens = [0, 5000, 17, 1, 0, 800, 3000, 16, 33, 12000, 2]
+    (out, lse), ref, ref_lse = _run_decode(oracle, 28, 4, lens, kv_dtype, seed=8, with_lse=True)
+    out, lse = out.cpu().numpy(), lse.cpu().numpy()
+    tol = (BF16_ATOL, BF16_RTOL) if kv_dtype == "bf16" else (F32_ATOL, None)
+    for r, L in enumerate(lens):
+        if L == 0:
+            assert (out[r] == 0).all() and np.isneginf(lse[r]).all()
+        else:
+            assert_close(out[r], ref[r], *tol, what=f"{kv_dtype} ragged row {r} (len {L})")
+            assert_close(lse[r], ref_lse[r], 1e-3, what=f"lse row {r}")
+
+
 def test_decode_gqa_marker():
     # q head h must read kv head h // group: V of kv head 2 is 5, others 0
     eng = make_engine(28, 4, [40], kv_dtype="bf16")
