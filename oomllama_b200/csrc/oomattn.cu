@@ -95,6 +95,9 @@ struct oomattn_ctx {
   // model step: the residual stream between layers and the logits
   float* d_model_scratch = nullptr;
   size_t model_scratch_bytes = 0;
+  // argmax: per-(row, chunk) (value, index) partials
+  void* d_argmax_part = nullptr;
+  size_t argmax_part_bytes = 0;
   // the last decode schedule and the page counts it was planned for (every
   // layer of a step, and every step until a row crosses a page, reuses it)
   std::vector<int> sched_key;
@@ -576,7 +579,8 @@ int oomattn_destroy(oomattn_ctx* ctx) {
   if (ctx->cublas) cublasDestroy(ctx->cublas);
   void* ptrs[] = {ctx->kpool,     ctx->vpool,      ctx->d_block_table, ctx->d_cos,    ctx->d_sin,
                   ctx->d_part_o,  ctx->d_part_lse, ctx->d_counters,    ctx->d_status, ctx->d_scratch,
-                  ctx->d_q8_scratch, ctx->d_q8_counters, ctx->d_layer_scratch, ctx->d_model_scratch};
+                  ctx->d_q8_scratch, ctx->d_q8_counters, ctx->d_layer_scratch, ctx->d_model_scratch,
+                  ctx->d_argmax_part};
   for (void* p : ptrs)
     if (p) cudaFree(p);
   delete ctx;
@@ -1322,9 +1326,11 @@ Q8Plan plan_q8(const oomattn_ctx* ctx, int rows, int cols, int nt) {
 // (two MMA token tiles; each weight byte is read once per pass): one x split
 // per pass, then one linear launch over all jobs' row blocks, a programmatic
 // dependent of the split.
-int q8_run(oomattn_ctx* ctx, const Q8Job* jobs, int n_jobs, const float* x, const float* up, int n_tokens) {
+int q8_run(oomattn_ctx* ctx, const Q8Job* jobs, int n_jobs, const float* x, const float* up, int n_tokens,
+           const float* norm_w = nullptr, float eps = 0.f) {
   if (!x || n_tokens < 0) return fail(ctx, OOMATTN_ERR_INVALID_ARG, "bad Q8 input");
-  if (reinterpret_cast<uintptr_t>(x) % 16 || (up && reinterpret_cast<uintptr_t>(up) % 16))
+  if (reinterpret_cast<uintptr_t>(x) % 16 || (up && reinterpret_cast<uintptr_t>(up) % 16) ||
+      (norm_w && reinterpret_cast<uintptr_t>(norm_w) % 16))
     return fail(ctx, OOMATTN_ERR_INVALID_ARG, "x must be 16-byte aligned");
   if (n_jobs < 1 || n_jobs > kQ8MaxMats) return fail(ctx, OOMATTN_ERR_INVALID_ARG, "bad Q8 job count");
   const int cols = jobs[0].w ? jobs[0].w->cols : 0;
@@ -1358,9 +1364,14 @@ int q8_run(oomattn_ctx* ctx, const Q8Job* jobs, int n_jobs, const float* x, cons
   float* part = xsum + (size_t)group * nchunks;
   for (int t0 = 0; t0 < n_tokens; t0 += group) {
     const int nt = std::min(group, n_tokens - t0);
-    const long long prep_warps = (long long)nt * nchunks;
-    q8_prep_x_kernel<<<(unsigned)((prep_warps + 7) / 8), 256, 0, ctx->stream>>>(
-        x + (size_t)t0 * cols, up ? up + (size_t)t0 * cols : nullptr, nt, cols, xh, xl, xsum, ctx->d_status);
+    if (norm_w) {
+      rmsnorm_prep_x_kernel<<<nt, kNormThreads, 0, ctx->stream>>>(x + (size_t)t0 * cols, norm_w, eps, cols, xh, xl,
+                                                                  xsum, ctx->d_status);
+    } else {
+      const long long prep_warps = (long long)nt * nchunks;
+      q8_prep_x_kernel<<<(unsigned)((prep_warps + 7) / 8), 256, 0, ctx->stream>>>(
+          x + (size_t)t0 * cols, up ? up + (size_t)t0 * cols : nullptr, nt, cols, xh, xl, xsum, ctx->d_status);
+    }
     CKLAUNCH();
     const int ntiles = nt > 8 ? 2 : 1;
     const Q8Plan p = plan_q8(ctx, total_rows, cols, ntiles);
@@ -1487,8 +1498,8 @@ extern "C" int oomattn_decoder_layer_q8(oomattn_ctx* ctx, int32_t layer, int32_t
   if (rc) return rc;
   DeviceGuard dg(ctx->device);
   const size_t B = (size_t)n_seqs, inter = (size_t)w->gate.rows;
-  // scratch: normalised x, q, k, v, rotated q, attention output, residual stream h
-  const size_t need = B * (2 * H + 3 * nq + 2 * nkv) + 8 * 32;
+  // scratch: q, k, v, rotated q, attention output, residual stream h
+  const size_t need = B * (H + 3 * nq + 2 * nkv) + 8 * 32;
   float* sb = layer_scratch(ctx, need + 2 * inter * B + 64, &rc);
   if (rc) return rc;
   auto carve = [&](size_t n) {
@@ -1496,7 +1507,6 @@ extern "C" int oomattn_decoder_layer_q8(oomattn_ctx* ctx, int32_t layer, int32_t
     sb += (n + 31) / 32 * 32;  // 128-byte aligned pieces
     return p;
   };
-  float* xn = carve(B * H);
   float* q = carve(B * nq);
   float* k = carve(B * nkv);
   float* v = carve(B * nkv);
@@ -1506,10 +1516,9 @@ extern "C" int oomattn_decoder_layer_q8(oomattn_ctx* ctx, int32_t layer, int32_t
   float* g = carve(B * inter);
   float* u = carve(B * inter);
   // GhostDecoderLayer::forward_turbo (src/oomllama.rs:387-402): h = x + attn(norm(x)); out = h + mlp(norm(h))
-  rc = run_rmsnorm(ctx, x, w->input_norm, w->eps, n_seqs, H, xn);
-  if (rc) return rc;
+  // (the RMSNorms run inside the x splits of the linears that read them)
   const Q8Job qkv[3] = {{&w->q, w->bq, nullptr, q}, {&w->k, w->bk, nullptr, k}, {&w->v, w->bv, nullptr, v}};
-  rc = q8_run(ctx, qkv, 3, xn, nullptr, n_seqs);
+  rc = q8_run(ctx, qkv, 3, x, nullptr, n_seqs, w->input_norm, w->eps);
   if (rc) return rc;
   rc = oomattn_rope_append(ctx, layer, n_seqs, seq_ids, 1, q, k, v, OOMATTN_DTYPE_F32, nullptr, nullptr, nullptr, qr,
                            OOMATTN_DTYPE_F32);
@@ -1519,10 +1528,8 @@ extern "C" int oomattn_decoder_layer_q8(oomattn_ctx* ctx, int32_t layer, int32_t
   const Q8Job o{&w->o, nullptr, x, h};
   rc = q8_run(ctx, &o, 1, att, nullptr, n_seqs);
   if (rc) return rc;
-  rc = run_rmsnorm(ctx, h, w->post_norm, w->eps, n_seqs, H, xn);
-  if (rc) return rc;
   const Q8Job gu[2] = {{&w->gate, nullptr, nullptr, g}, {&w->up, nullptr, nullptr, u}};
-  rc = q8_run(ctx, gu, 2, xn, nullptr, n_seqs);
+  rc = q8_run(ctx, gu, 2, h, nullptr, n_seqs, w->post_norm, w->eps);
   if (rc) return rc;
   const Q8Job dn{&w->down, nullptr, h, out};
   return q8_run(ctx, &dn, 1, g, u, n_seqs);
@@ -1547,7 +1554,28 @@ extern "C" int oomattn_argmax(oomattn_ctx* ctx, const float* logits, int32_t n_r
   if (!logits || !ids || n_rows < 0 || n <= 0) return fail(ctx, OOMATTN_ERR_INVALID_ARG, "bad argmax arguments");
   if (n_rows == 0) return OOMATTN_OK;
   DeviceGuard dg(ctx->device);
-  argmax_kernel<<<n_rows, kArgmaxThreads, 0, ctx->stream>>>(logits, n, ids);
+  // about 4 CTAs per SM over all rows, at least 2048 logits per CTA
+  const int want = std::max(1, (4 * ctx->num_sms + n_rows - 1) / n_rows);
+  const int chunks = std::max(1, std::min({want, (n + 2047) / 2048, 1024}));
+  const int chunk = (n + chunks - 1) / chunks;
+  const int n_chunks = (n + chunk - 1) / chunk;
+  const size_t need = (size_t)n_rows * n_chunks * 8;
+  if (need > ctx->argmax_part_bytes) {
+    if (ctx->d_argmax_part) {
+      cudaStreamSynchronize(ctx->stream);
+      cudaFree(ctx->d_argmax_part);
+      ctx->d_argmax_part = nullptr;
+      ctx->argmax_part_bytes = 0;
+    }
+    if (cudaMalloc(&ctx->d_argmax_part, need) != cudaSuccess)
+      return fail(ctx, OOMATTN_ERR_NO_MEMORY, "argmax scratch allocation of %zu bytes failed", need);
+    ctx->argmax_part_bytes = need;
+  }
+  float* pv = static_cast<float*>(ctx->d_argmax_part);
+  int* pi = reinterpret_cast<int*>(pv + (size_t)n_rows * n_chunks);
+  argmax_partial_kernel<<<dim3(n_chunks, n_rows), kArgmaxThreads, 0, ctx->stream>>>(logits, n, chunk, pv, pi);
+  CKLAUNCH();
+  argmax_final_kernel<<<n_rows, kArgmaxThreads, 0, ctx->stream>>>(logits, n, n_chunks, pv, pi, ids);
   CKLAUNCH();
   return OOMATTN_OK;
 }
@@ -1565,7 +1593,7 @@ extern "C" int oomattn_decode_step_q8(oomattn_ctx* ctx, const oomattn_q8_model* 
   DeviceGuard dg(ctx->device);
   const size_t B = (size_t)n_seqs, vocab = (size_t)m->lm_head.rows;
   const size_t xf = (B * H + 31) / 32 * 32;
-  const size_t need = (3 * xf + (logits ? 0 : B * vocab) + 64) * 4;
+  const size_t need = (2 * xf + (logits ? 0 : B * vocab) + 64) * 4;
   if (need > ctx->model_scratch_bytes) {
     if (ctx->d_model_scratch) {
       cudaStreamSynchronize(ctx->stream);
@@ -1579,8 +1607,7 @@ extern "C" int oomattn_decode_step_q8(oomattn_ctx* ctx, const oomattn_q8_model* 
   }
   float* xa = ctx->d_model_scratch;
   float* xb = xa + xf;
-  float* xn = xb + xf;
-  float* lg = logits ? logits : xn + xf;
+  float* lg = logits ? logits : xb + xf;
   // OomLlamaModel::forward_turbo (src/oomllama.rs:504-553) for one new token per sequence, then the greedy
   // pick of the generation loop (:973-976, :1000-1003)
   int rc = oomattn_embed_q8(ctx, &m->embed, tokens, n_seqs, xa);
@@ -1590,10 +1617,8 @@ extern "C" int oomattn_decode_step_q8(oomattn_ctx* ctx, const oomattn_q8_model* 
     if (rc) return rc;
     std::swap(xa, xb);
   }
-  rc = run_rmsnorm(ctx, xa, m->final_norm, m->eps, n_seqs, H, xn);
-  if (rc) return rc;
   const Q8Job head{&m->lm_head, nullptr, nullptr, lg};
-  rc = q8_run(ctx, &head, 1, xn, nullptr, n_seqs);
+  rc = q8_run(ctx, &head, 1, xa, nullptr, n_seqs, m->final_norm, m->eps);
   if (rc) return rc;
   return oomattn_argmax(ctx, lg, n_seqs, (int)vocab, next);
 }

@@ -433,6 +433,53 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(const float* __re
   }
 }
 
+// RMSNorm fused into the x split of the linear that reads it: one CTA per
+// token forms the row's sum of squares exactly as rmsnorm_kernel does, then
+// its warps split the normalised row x / sqrt(mean(x^2) + eps) * w chunk by
+// chunk exactly as q8_prep_x_kernel does.  The normalised row itself is not
+// stored: only the linears read it (src/oomllama.rs:389, :395, :549).
+__global__ void __launch_bounds__(kNormThreads) rmsnorm_prep_x_kernel(const float* __restrict__ x,
+                                                                      const float* __restrict__ w, float eps,
+                                                                      int cols, uint32_t* xh, uint32_t* xl,
+                                                                      float* xsum, int* status) {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  __shared__ float part[kNormThreads / 32];
+  const int t = blockIdx.x;
+  const float* xr = x + (size_t)t * cols;
+  float s = 0.f;
+  for (int i = threadIdx.x * 4; i < cols; i += kNormThreads * 4) {
+    const float4 v = *reinterpret_cast<const float4*>(xr + i);
+    s += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+  }
+#pragma unroll
+  for (int d = 16; d > 0; d >>= 1) s += __shfl_xor_sync(0xffffffffu, s, d);
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = s;
+  __syncthreads();
+  float tot = 0.f;
+#pragma unroll
+  for (int k = 0; k < kNormThreads / 32; ++k) tot += part[k];
+  const float denom = sqrtf(tot / (float)cols + eps);
+  const int lane = threadIdx.x & 31;
+  const int nchunks = cols / kQ8Chunk;
+  for (int ch = threadIdx.x >> 5; ch < nchunks; ch += kNormThreads / 32) {
+    const int c = ch * kQ8Chunk + 2 * lane;
+    const float2 xv = *reinterpret_cast<const float2*>(xr + c);
+    const float2 g = *reinterpret_cast<const float2*>(w + c);
+    const float2 v = make_float2(xv.x / denom * g.x, xv.y / denom * g.y);
+    const __half2 hi = __floats2half2_rn(v.x, v.y);
+    const float2 hf = __half22float2(hi);
+    const __half2 lo = __floats2half2_rn(v.x - hf.x, v.y - hf.y);
+    if (!(fabsf(v.x) < 65504.f) || !(fabsf(v.y) < 65504.f)) report_error(status, kDevErrX16);
+    const size_t o = (size_t)t * (cols / 2) + ch * (kQ8Chunk / 2) + lane;
+    xh[o] = *reinterpret_cast<const uint32_t*>(&hi);
+    xl[o] = *reinterpret_cast<const uint32_t*>(&lo);
+    float cs = v.x + v.y;
+#pragma unroll
+    for (int d = 16; d > 0; d >>= 1) cs += __shfl_xor_sync(0xffffffffu, cs, d);
+    if (lane == 0) xsum[(size_t)t * nchunks + ch] = cs;
+  }
+}
+
 // ------------------------------------------------------------------ embedding, argmax
 // out[t] = row ids[t] of a Q8 matrix [vocab][hidden], dequantised exactly as
 // the reference reads a Q8 tensor (min + (f32)q * scale, src/quant.rs:201-224),
@@ -456,50 +503,72 @@ __global__ void embed_q8_kernel(const uint8_t* __restrict__ q, const float* __re
   }
 }
 
-// ids[t] = argmax over logits[t][0..n) (the greedy pick, src/oomllama.rs:973-976,
+// ids[r] = argmax over logits[r][0..n) (the greedy pick, src/oomllama.rs:973-976,
 // :1000-1003, i.e. candle-core 0.9.1's argmax: a scan from element 0 that moves
 // only to a strictly larger value).  So: the largest value, the lowest index
 // among equal ones, NaN skipped -- except that a NaN in element 0 is never left
-// and gives 0.  One CTA per row.
-constexpr int kArgmaxThreads = 512;
-__global__ void __launch_bounds__(kArgmaxThreads) argmax_kernel(const float* __restrict__ logits, int n,
-                                                                int* __restrict__ ids) {
+// and gives 0.  Two stages: CTAs (chunk, row) reduce ranges of a row to
+// (value, index) pairs, then one CTA per row reduces those.  "Larger value,
+// then lower index" is associative and commutative, so the result does not
+// depend on how the row is cut.
+constexpr int kArgmaxThreads = 256;
+
+__device__ __forceinline__ void argmax_take(float& bv, int& bi, float v, int i, int none) {
+  if (i != none && (bi == none || v > bv || (v == bv && i < bi))) {
+    bv = v;
+    bi = i;
+  }
+}
+
+// (value, index) of the whole block; valid in thread 0.  `none` marks "no candidate".
+__device__ __forceinline__ void argmax_block(float& bv, int& bi, int none) {
   __shared__ float sv[kArgmaxThreads / 32];
   __shared__ int si[kArgmaxThreads / 32];
-  const float* row = logits + (size_t)blockIdx.x * n;
-  float bv = -INFINITY;
-  int bi = n;  // sentinel: no candidate yet
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    const float v = row[i];
-    if (v > bv || (bi == n && v == v)) {  // first non-NaN, then strictly larger (indices ascend)
-      bv = v;
-      bi = i;
-    }
-  }
-  // reduce (value, index): larger value wins, lower index on ties
 #pragma unroll
   for (int d = 16; d > 0; d >>= 1) {
     const float ov = __shfl_xor_sync(0xffffffffu, bv, d);
     const int oi = __shfl_xor_sync(0xffffffffu, bi, d);
-    if (oi != n && (bi == n || ov > bv || (ov == bv && oi < bi))) {
-      bv = ov;
-      bi = oi;
-    }
+    argmax_take(bv, bi, ov, oi, none);
   }
   if ((threadIdx.x & 31) == 0) {
     sv[threadIdx.x >> 5] = bv;
     si[threadIdx.x >> 5] = bi;
   }
   __syncthreads();
+  if (threadIdx.x == 0)
+    for (int k = 1; k < (int)(blockDim.x >> 5); ++k) argmax_take(bv, bi, sv[k], si[k], none);
+}
+
+__global__ void __launch_bounds__(kArgmaxThreads) argmax_partial_kernel(const float* __restrict__ logits, int n,
+                                                                        int chunk, float* part_v, int* part_i) {
+  const int r = blockIdx.y, c = blockIdx.x;
+  const float* row = logits + (size_t)r * n;
+  const int b = c * chunk, e = min(n, b + chunk);
+  float bv = -INFINITY;
+  int bi = n;  // none yet
+  for (int i = b + threadIdx.x; i < e; i += blockDim.x) {
+    const float v = row[i];
+    if (v == v) argmax_take(bv, bi, v, i, n);  // NaN is never larger
+  }
+  argmax_block(bv, bi, n);
   if (threadIdx.x == 0) {
-    float v = sv[0];
-    int i0 = si[0];
-    for (int w = 1; w < kArgmaxThreads / 32; ++w)
-      if (si[w] != n && (i0 == n || sv[w] > v || (sv[w] == v && si[w] < i0))) {
-        v = sv[w];
-        i0 = si[w];
-      }
-    ids[blockIdx.x] = (i0 == n || row[0] != row[0]) ? 0 : i0;
+    part_v[(size_t)r * gridDim.x + c] = bv;
+    part_i[(size_t)r * gridDim.x + c] = bi;
+  }
+}
+
+__global__ void __launch_bounds__(kArgmaxThreads) argmax_final_kernel(const float* __restrict__ logits, int n,
+                                                                      int chunks, const float* part_v,
+                                                                      const int* part_i, int* __restrict__ ids) {
+  const int r = blockIdx.x;
+  float bv = -INFINITY;
+  int bi = n;
+  for (int c = threadIdx.x; c < chunks; c += blockDim.x)
+    argmax_take(bv, bi, part_v[(size_t)r * chunks + c], part_i[(size_t)r * chunks + c], n);
+  argmax_block(bv, bi, n);
+  if (threadIdx.x == 0) {
+    const float first = logits[(size_t)r * n];
+    ids[r] = (bi == n || first != first) ? 0 : bi;
   }
 }
 

@@ -57,34 +57,41 @@ def test_embed_q8_reports_out_of_range_ids(oracle, eng):
     assert np.array_equal(o[[0, 3]], ref) and not o[[1, 2]].any()
 
 
-def _argmax_rows():
+def _argmax_rows(n):
     rng = np.random.default_rng(11)
     rows = []
-    r = rng.standard_normal(1000).astype(np.float32)
-    r[[17, 400, 999]] = 9.0  # tie: lowest index
+    r = rng.standard_normal(n).astype(np.float32)
+    r[[17, n // 2 - 1, n // 2, n - 1]] = 9.0  # tie: lowest index (across the row's chunks for large n)
     rows.append(r)
-    r = rng.standard_normal(1000).astype(np.float32)
-    r[[3, 500]] = np.nan  # NaN skipped
+    r = rng.standard_normal(n).astype(np.float32)
+    r[[3, n // 2]] = np.nan  # NaN skipped
     rows.append(r)
-    r = rng.standard_normal(1000).astype(np.float32)
+    r = rng.standard_normal(n).astype(np.float32)
     r[0] = np.nan  # NaN in element 0 is never left
     rows.append(r)
-    rows.append(np.full(1000, -np.inf, np.float32))  # all -inf: 0
-    r = np.full(1000, -np.inf, np.float32)
-    r[777] = -1e30
+    rows.append(np.full(n, -np.inf, np.float32))  # all -inf: 0
+    r = np.full(n, -np.inf, np.float32)
+    r[n - 223] = -1e30
     rows.append(r)
-    r = rng.standard_normal(1000).astype(np.float32)
-    r[998] = np.inf
-    r[999] = np.inf
+    r = rng.standard_normal(n).astype(np.float32)
+    r[n - 2] = np.inf
+    r[n - 1] = np.inf
     rows.append(r)
-    r = np.zeros(1000, np.float32)
+    r = np.zeros(n, np.float32)
     r[5] = -0.0
     rows.append(r)  # +0 and -0 compare equal: 0
+    r = np.full(n, np.nan, np.float32)
+    r[n - 1] = -5.0
+    rows.append(r)  # NaN in element 0: 0, even though a number follows
+    r = np.full(n, np.nan, np.float32)
+    r[0] = 1.0
+    rows.append(r)  # only element 0 is a number
     return np.stack(rows)
 
 
-def test_argmax_edge_cases(oracle, eng):
-    x = _argmax_rows()
+@pytest.mark.parametrize("n", [1000, 20000])
+def test_argmax_edge_cases(oracle, eng, n):
+    x = _argmax_rows(n)
     ids = eng.argmax(torch.from_numpy(x).cuda())
     eng.sync()
     ref = oracle.argmax(x)
