@@ -40,6 +40,7 @@ sys.path.insert(0, ROOT)
 S_PREFILL, HQ, HKV, D = 4096, 28, 4, 128
 PREFILL_FLOPS = 4 * D * HQ * S_PREFILL * (S_PREFILL + 1) // 2   # 120,288,444,416 per sequence
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+SPEC_PEAKS = {"hbm_gbs": 7700.0, "bf16_tflops": 2250.0}  # nominal B200 (HGX HBM3e; dense bf16), for context
 # dram__bytes_read.sum + dram__bytes_write.sum per launch from one ncu capture
 # of each kernel on these workloads (profiles/prefill_bf16_kernel_qwen7b_s4096.md,
 # profiles/decode_bf16_kernel_llama8b_ctx32k.md).
@@ -499,6 +500,82 @@ def bench_layer_q8(args, dist_, torch, B, ctx_len=2048):
     return ms, wbytes + kvbytes
 
 
+def bench_c1(args, dist_, torch, n_sets=4, cached=512):
+    """C1: one Qwen2.5-7B layer's f32 attention step for one sequence with 512 cached tokens:
+    K-A GEMV over f32 Wq/Wk/Wv (66 MB) + bias + interleaved RoPE + append at slot 512, then the
+    f32 K-B decode over 513 tokens.  n_sets layers, each with its own weights and cache, rotate so
+    the 4 x 68 MB working set exceeds L2; replayed as a CUDA graph (slot 512 rewritten every step)."""
+    from oomllama_b200 import TurboConfig, TurboEngine
+    dev = torch.cuda.current_device()
+    H, hq, hkv = 3584, 28, 4
+    cfg = TurboConfig(n_layers=n_sets, hidden_size=H, n_heads=hq, n_kv_heads=hkv, max_seq_len=cached + 16,
+                      max_seqs=1, kv_dtype="f32", rope_variant="interleaved", rope_theta=1e6)
+    eng = TurboEngine(cfg, device=dev)
+    g = torch.Generator(device="cuda").manual_seed(0 + dist_.rank)
+    ws = []
+    for l in range(n_sets):
+        eng.kv_write(l, 0, torch.randn(cached, hkv, D, device="cuda", generator=g),
+                     torch.randn(cached, hkv, D, device="cuda", generator=g))
+        ws.append([torch.randn(n * D, H, device="cuda", generator=g) * 0.02 for n in (hq, hkv, hkv)])
+    bq, bk, bv = (torch.zeros(n * D, device="cuda") for n in (hq, hkv, hkv))
+    x = torch.randn(1, H, device="cuda", generator=g)
+    out = torch.empty(1, hq, D, device="cuda")
+    side = torch.cuda.Stream()
+    with torch.cuda.stream(side):
+        for l in range(n_sets):  # warm the scratch on this stream
+            q = eng.qkv_rope_append(l, [0], x, *ws[l], bq, bk, bv)
+            eng.decode(l, [0], q, out=out)
+            eng.set_seq_len(l, 0, cached)
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr, stream=side):
+            for l in range(n_sets):
+                q = eng.qkv_rope_append(l, [0], x, *ws[l], bq, bk, bv)
+                eng.decode(l, [0], q, out=out)
+    torch.cuda.synchronize()
+    eng.sync()
+    for _ in range(max(3, args.warmup)):
+        gr.replay()
+    reps = max(10, args.steps)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    dist_.barrier()
+    torch.cuda.synchronize()
+    t0.record()
+    for _ in range(reps):
+        gr.replay()
+    t1.record()
+    torch.cuda.synchronize()
+    dist_.barrier()
+    eng.sync()
+    ms = dist_.max(t0.elapsed_time(t1) / (reps * n_sets))
+    L = cached + 1
+    byts = ((hq + 2 * hkv) * D * H * 4 + (hq + 2 * hkv) * D * 4 + H * 4  # weights, biases, x
+            + 2 * hkv * L * D * 4 + 2 * hkv * D * 4 + 2 * hq * D * 4)  # K/V read, K/V append, q and O
+    del gr
+    eng.close()
+    return ms, byts
+
+
+def cpu_c1_sample(threads=None, reps=5):
+    """The oracle's f32 layer attention (QKV matvec + bias + interleaved RoPE + append + GQA
+    attention, oomllama_turbo.rs:618-723 up to o_proj) for the C1 shape; returns (tok/s, threads)."""
+    from oracle import oracle as O
+    O.build()
+    nt = O.set_threads(O.host_cores() if threads is None else threads)
+    rng = np.random.default_rng(0)
+    H, hq, hkv, P = 3584, 28, 4, 512
+    x = rng.standard_normal((1, 1, H), dtype=np.float32)
+    wq, wk, wv = (rng.standard_normal((n * D, H), dtype=np.float32) * np.float32(0.02) for n in (hq, hkv, hkv))
+    kc = rng.standard_normal((1, hkv, P, D), dtype=np.float32)
+    vc = rng.standard_normal((1, hkv, P, D), dtype=np.float32)
+    cos_t, sin_t = O.rope_table(1e6, D, P + 1)
+    best = 1e30
+    for _ in range(reps):
+        t = time.perf_counter()
+        O.layer_attention(x, wq, wk, wv, None, None, None, hq, hkv, kc, vc, cos_t, sin_t, O.ROPE_INTERLEAVED)
+        best = min(best, time.perf_counter() - t)
+    return 1.0 / best, nt
+
+
 def q8_random_matrix(torch, rows, cols, g, std=0.02, chunk=1 << 26):
     """A Q8 matrix of weights ~N(0, std) quantised on the device the way the .oom writer does
     (src/gguf2oom.rs:719-770: per 256-value block min, scale = range / 255, q = round((v - min) / scale));
@@ -711,6 +788,7 @@ def main():
         "config": workload_config(W),
         "roofline": {"bound": "tensor", "kernel": "prefill_bf16_kernel", "achieved": achieved,
                      "peak": peaks[peak_key], "unit": "TFLOP/s", "frac": achieved / peaks[peak_key],
+                     "frac_of_spec": achieved / SPEC_PEAKS["bf16_tflops"],
                      "peak_source": f"{peak_src} {peak_key}",
                      "traffic": NCU_TRAFFIC_BYTES["prefill_bf16_kernel"],
                      "algorithmic_flops_per_launch": PREFILL_FLOPS},
@@ -731,10 +809,27 @@ def main():
                 "bytes_per_step": r["total_bytes"], "split_context_merge": r["merge"],
                 "roofline": {"bound": "hbm", "kernel": "decode_bf16_kernel", "achieved": kern_gbs,
                              "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": kern_gbs / peaks["hbm_gbs"],
+                             "frac_of_spec": kern_gbs / SPEC_PEAKS["hbm_gbs"],
                              "traffic": NCU_TRAFFIC_BYTES["decode_bf16_kernel"] if name == "llama-32k" and W == 1
                              else None},
             }
         line["decode"] = dec
+        ms, byts = bench_c1(args, dist_, torch)
+        gbs = byts / (ms * 1e-3) / 1e9
+        line["c1_decode_f32"] = {
+            "workload": "one Qwen2.5-7B layer's f32 attention step, B=1, 512 cached + 1 new: K-A GEMV over f32 "
+                        "Wq/Wk/Wv (66 MB) + bias + interleaved RoPE + append, then f32 K-B decode",
+            "tok_s": W / (ms * 1e-3), "ms_per_step": ms, "bytes_per_step": byts, "hbm_gbs": W * gbs,
+            "roofline": {"bound": "hbm", "kernel": "qkv_gemv_rope_append_kernel + decode_f32_kernel",
+                         "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": gbs / peaks["hbm_gbs"],
+                         "frac_of_spec": gbs / SPEC_PEAKS["hbm_gbs"], "traffic": None},
+            "l2": "4 layers' weights and caches rotate (4 x 68 MB > 126 MB L2)",
+        }
+        if dist_.rank == 0 and W == 1 and not args.no_cpu_baseline:
+            v, nt = cpu_c1_sample()
+            line["c1_decode_f32"]["cpu_baseline"] = {
+                "value": v, "unit": "tok/s", "cores": nt, "kind": "port",
+                "sample": "the whole C1 step: oracle QKV matvec + RoPE + append + GQA attention, best of 5"}
         q8 = {}
         for T in (1, 8, 16):
             ms, byts = bench_q8(args, dist_, torch, T)
@@ -782,7 +877,9 @@ def main():
         }
     if dist_.rank == 0 and W == 1 and not args.no_cpu_baseline:
         v, nt, desc = cpu_prefill_sample()
-        line["cpu_baseline"] = {"value": v, "unit": "TFLOP/s", "cores": nt, "kind": "port", "sample": desc}
+        v1, _, desc1 = cpu_prefill_sample(seconds_budget=3.0, threads=1)
+        line["cpu_baseline"] = {"value": v, "unit": "TFLOP/s", "cores": nt, "kind": "port", "sample": desc,
+                                "single_thread": {"value": v1, "cores": 1, "sample": desc1}}
     if dist_.rank == 0:
         print(json.dumps(line))
     dist_.close()

@@ -35,6 +35,7 @@ constexpr int kChunkBytes = kPageSize * kHeadDim * 2;           // one (page, kv
 constexpr int kDecStageBytes = 2 * kDecWarps * kChunkBytes;     // K and V of 4 pages: 32 KB
 constexpr int kDecSmemBytes = kDecStages * kDecStageBytes + 1024 + 2 * kDecStages * 8 + 64;
 
+constexpr int kF32Tok = 4;                 // f32 path: tokens loaded and scored together
 constexpr int kMergeStride = kHeadDim + 4;  // padded row of the per-warp O staging area
 struct MergeSmem {
   float m[kDecWarps][kMaxGroup];
@@ -361,32 +362,62 @@ __global__ void __launch_bounds__(kDecWarps * 32)
     m[j] = -INFINITY;
     l[j] = 0.f;
   }
-  for (int pi = pb + warp; pi < pe; pi += kDecWarps) {
+  // the CTA's tokens in groups of kF32Tok (a group never crosses a page),
+  // dealt to the warps in turn; a group's loads issue together and its scores
+  // reduce as independent shuffle chains; the running max and sums are
+  // updated once per group
+  const int tok_end = min(pe * kPageSize, L);
+  for (int g0 = pb * kPageSize + warp * kF32Tok; g0 < tok_end; g0 += kDecWarps * kF32Tok) {
+    const int pi = g0 / kPageSize;
     int page = __ldg(bt + pi);
     if ((unsigned)page >= (unsigned)pool.n_pool_pages) {
       if (lane == 0) report_error(a.status, kDevErrBounds);
       page = pool.n_pool_pages - 1;
     }
     const size_t base = ((size_t)(a.layer * pool.n_pool_pages + page) * pool.n_kv + g) * kPageSize * kHeadDim;
-    const int nt = min(kPageSize, L - pi * kPageSize);
-    for (int t = 0; t < nt; ++t) {
-      const float4 kv = __ldg(reinterpret_cast<const float4*>(kp + base + t * kHeadDim) + lane);
-      const float4 vv = __ldg(reinterpret_cast<const float4*>(vp + base + t * kHeadDim) + lane);
+    const int t0 = g0 - pi * kPageSize;             // first slot of the group in its page
+    const int nt = min(kPageSize, tok_end - pi * kPageSize);  // valid slots of the page
+    {
+      float4 kv[kF32Tok], vv[kF32Tok];
+#pragma unroll
+      for (int u = 0; u < kF32Tok; ++u) {
+        const int t = min(t0 + u, nt - 1);  // past the last token: reloaded, then masked
+        kv[u] = __ldg(reinterpret_cast<const float4*>(kp + base + t * kHeadDim) + lane);
+        vv[u] = __ldg(reinterpret_cast<const float4*>(vp + base + t * kHeadDim) + lane);
+      }
 #pragma unroll
       for (int j = 0; j < kMaxGroup; ++j) {
         if (j < a.group) {
-          float s = q[j].x * kv.x + q[j].y * kv.y + q[j].z * kv.z + q[j].w * kv.w;
+          float sc[kF32Tok];
 #pragma unroll
-          for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
-          const float mn = fmaxf(m[j], s);
+          for (int u = 0; u < kF32Tok; ++u)
+            sc[u] = q[j].x * kv[u].x + q[j].y * kv[u].y + q[j].z * kv[u].z + q[j].w * kv[u].w;
+#pragma unroll
+          for (int off = 16; off > 0; off >>= 1)
+#pragma unroll
+            for (int u = 0; u < kF32Tok; ++u) sc[u] += __shfl_xor_sync(0xffffffffu, sc[u], off);
+          float mn = m[j];
+#pragma unroll
+          for (int u = 0; u < kF32Tok; ++u)
+            if (t0 + u < nt) mn = fmaxf(mn, sc[u]);
           const float al = exp2f(m[j] - mn);
-          const float p = exp2f(s - mn);
           m[j] = mn;
-          l[j] = l[j] * al + p;
-          o[j].x = o[j].x * al + p * vv.x;
-          o[j].y = o[j].y * al + p * vv.y;
-          o[j].z = o[j].z * al + p * vv.z;
-          o[j].w = o[j].w * al + p * vv.w;
+          l[j] *= al;
+          o[j].x *= al;
+          o[j].y *= al;
+          o[j].z *= al;
+          o[j].w *= al;
+#pragma unroll
+          for (int u = 0; u < kF32Tok; ++u) {
+            if (t0 + u < nt) {
+              const float p = exp2f(sc[u] - mn);
+              l[j] += p;
+              o[j].x += p * vv[u].x;
+              o[j].y += p * vv[u].y;
+              o[j].z += p * vv[u].z;
+              o[j].w += p * vv[u].w;
+            }
+          }
         }
       }
     }

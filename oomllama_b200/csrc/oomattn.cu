@@ -360,15 +360,16 @@ int launch_rope_append(oomattn_ctx* ctx, const AppendArgs& ap, const SeqBatch& s
 // most 1, 2 or 3 waves of CTAs on the resident slots -- judged by simulating
 // that list schedule with kDecodeFillPages pages of fixed cost per CTA
 // (pipeline fill and merge).  Returns the number of items (the grid size).
-constexpr int kDecodeFillPages = 12;
+constexpr int kDecodeFillPages = 12;     // bf16 cache
+constexpr int kDecodeFillPagesF32 = 12;  // f32 cache (measured insensitive: 4 to 200 chose the same plans on C1)
 constexpr int kDecodeMaxSimSlots = 2048;
 
-long long lpt_makespan(const int* size, const int* count, int groups, int slots, long long* heap) {
+long long lpt_makespan(const int* size, const int* count, int groups, int slots, int fill, long long* heap) {
   // min-heap of slot finish times, in pages
   for (int i = 0; i < slots; ++i) heap[i] = 0;
   for (int gi = 0; gi < groups; ++gi) {
     for (int k = 0; k < count[gi]; ++k) {
-      heap[0] += size[gi] + kDecodeFillPages;  // the earliest free slot takes the item; sift it down
+      heap[0] += size[gi] + fill;  // the earliest free slot takes the item; sift it down
       int i = 0;
       for (;;) {
         const int l = 2 * i + 1, r = l + 1;
@@ -386,7 +387,7 @@ long long lpt_makespan(const int* size, const int* count, int groups, int slots,
   return mx;
 }
 
-int plan_decode(const SeqBatch& sb, int n_kv, int slots, int max_splits, DecodeSched& sched) {
+int plan_decode(const SeqBatch& sb, int n_kv, int slots, int max_splits, int fill, DecodeSched& sched) {
   slots = std::max(1, std::min(slots, kDecodeMaxSimSlots));
   int pages[kMaxBatch];
   int mp = 0;
@@ -402,22 +403,30 @@ int plan_decode(const SeqBatch& sb, int n_kv, int slots, int max_splits, DecodeS
     for (int z = 0; z < sb.n; ++z) c += (long long)ns_of(pages[z], t) * n_kv;
     return c;
   };
-  int cand[3];
-  for (int w = 1; w <= 3; ++w) {  // smallest t with ctas(t) <= w * slots (ctas falls as t grows)
+  // candidates: the smallest t giving at most 1, 2 or 3 waves (ctas falls as
+  // t grows), and for batches too small to fill one wave, whole rows cut in
+  // 1, 2, 4 or 8 ranges
+  int cand[7];
+  int n_cand = 0;
+  for (int w = 1; w <= 3; ++w) {
     int lo = t_lo, hi = t_hi;
     while (lo < hi) {
       const int mid = lo + (hi - lo) / 2;
       if (ctas_of(mid) <= (long long)w * slots) hi = mid; else lo = mid + 1;
     }
-    cand[w - 1] = lo;
+    cand[n_cand++] = lo;
+  }
+  for (int k = 1; k <= 8; k *= 2) {
+    const int t = std::max(t_lo, (mp + k - 1) / k);
+    if (t > cand[0]) cand[n_cand++] = t;
   }
   long long heap[kDecodeMaxSimSlots];
   int order[kMaxBatch], size[kMaxBatch], count[kMaxBatch];
   int best_t = cand[0];
   long long best_cost = -1;
-  for (int ci = 0; ci < 3; ++ci) {
+  for (int ci = 0; ci < n_cand; ++ci) {
     const int t = cand[ci];
-    if (ci > 0 && (t == cand[ci - 1])) continue;
+    if (std::find(cand, cand + ci, t) != cand + ci) continue;
     for (int z = 0; z < sb.n; ++z) order[z] = z;
     auto range = [&](int z) { const int p = pages[z]; return p > 0 ? (p + ns_of(p, t) - 1) / ns_of(p, t) : 0; };
     std::sort(order, order + sb.n, [&](int x, int y) { return range(x) > range(y); });
@@ -425,7 +434,7 @@ int plan_decode(const SeqBatch& sb, int n_kv, int slots, int max_splits, DecodeS
       size[r] = range(order[r]);
       count[r] = ns_of(pages[order[r]], t) * n_kv;
     }
-    const long long cost = lpt_makespan(size, count, sb.n, slots, heap);
+    const long long cost = lpt_makespan(size, count, sb.n, slots, fill, heap);
     if (best_cost < 0 || cost < best_cost) {
       best_cost = cost;
       best_t = t;
@@ -452,12 +461,14 @@ int plan_decode(const SeqBatch& sb, int n_kv, int slots, int max_splits, DecodeS
 
 int launch_decode_rows(oomattn_ctx* ctx, int layer, const SeqBatch& sb, const float* q, float* out, float* lse) {
   const int n_kv = ctx->cfg.n_kv_heads;
-  const int slots = ctx->num_sms * (ctx->cfg.kv_dtype == OOMATTN_DTYPE_BF16 ? 2 : 8);
+  const int slots = ctx->num_sms * (ctx->cfg.kv_dtype == OOMATTN_DTYPE_BF16 ? 2 : 3);
   int key[kMaxBatch + 1];
   key[0] = sb.n;
   for (int z = 0; z < sb.n; ++z) key[z + 1] = sb.len[z] > 0 ? (sb.len[z] + kPageSize - 1) / kPageSize : 0;
   if (ctx->sched_key.size() != (size_t)sb.n + 1 || !std::equal(key, key + sb.n + 1, ctx->sched_key.begin())) {
-    ctx->sched_items = plan_decode(sb, n_kv, slots, kMaxSplits, ctx->sched);
+    ctx->sched_items = plan_decode(sb, n_kv, slots, kMaxSplits,
+                                   ctx->cfg.kv_dtype == OOMATTN_DTYPE_BF16 ? kDecodeFillPages : kDecodeFillPagesF32,
+                                   ctx->sched);
     ctx->sched_key.assign(key, key + sb.n + 1);
   }
   const DecodeSched& sched = ctx->sched;
@@ -1135,8 +1146,8 @@ extern "C" int oomattn_decode_static_scratch(int device, void* stream, int32_t k
   // partial fits the static array: nsplit <= slots / (rows * heads).
   const int cap_splits = std::max(1, std::min(kMaxSplits, kStaticPartSlots / (n_rows * n_heads)));
   DecodeSched sched;
-  const int n_items = plan_decode(sb, n_kv_heads, num_sms * (kv_dtype == OOMATTN_DTYPE_BF16 ? 2 : 8), cap_splits,
-                                  sched);
+  const int n_items = plan_decode(sb, n_kv_heads, num_sms * (kv_dtype == OOMATTN_DTYPE_BF16 ? 2 : 3), cap_splits,
+                                  kv_dtype == OOMATTN_DTYPE_BF16 ? kDecodeFillPages : kDecodeFillPagesF32, sched);
   if (n_items == 0) return OOMATTN_OK;
 
   // The counters must start at zero; a previous call that ended early could

@@ -231,47 +231,65 @@ __global__ void __launch_bounds__(256)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int H = ga.hidden;
 
+  // the warp's two rows stream together: twice the loads in flight, and each
+  // x vector is read once for both
+  size_t wrow[2];
+#pragma unroll
   for (int rr = 0; rr < 2; ++rr) {
     const int r = warp * 2 + rr;  // 0..15
     const int drow = split_half ? (r < 8 ? c * 8 + r : 64 + c * 8 + (r - 8)) : c * 16 + r;
-    const size_t wrow = (size_t)(head * kHeadDim + drow) * H;
-    float acc[T];
+    wrow[rr] = (size_t)(head * kHeadDim + drow) * H;
+  }
+  float acc[2][T];
 #pragma unroll
-    for (int t = 0; t < T; ++t) acc[t] = 0.f;
-    if (WBF16) {
-      const uint16_t* wp = reinterpret_cast<const uint16_t*>(W) + wrow;
-      for (int j = lane * 8; j < H; j += 256) {
-        const uint4 wv = __ldcs(reinterpret_cast<const uint4*>(wp + j));
-        const float w[8] = {bf16_lo_f32(wv.x), bf16_hi_f32(wv.x), bf16_lo_f32(wv.y), bf16_hi_f32(wv.y),
-                            bf16_lo_f32(wv.z), bf16_hi_f32(wv.z), bf16_lo_f32(wv.w), bf16_hi_f32(wv.w)};
+  for (int rr = 0; rr < 2; ++rr)
 #pragma unroll
-        for (int t = 0; t < T; ++t) {
-          const float4 x0 = __ldg(reinterpret_cast<const float4*>(ga.x + (size_t)t * H + j));
-          const float4 x1 = __ldg(reinterpret_cast<const float4*>(ga.x + (size_t)t * H + j + 4));
-          acc[t] += x0.x * w[0] + x0.y * w[1] + x0.z * w[2] + x0.w * w[3] + x1.x * w[4] + x1.y * w[5] +
-                    x1.z * w[6] + x1.w * w[7];
-        }
-      }
-    } else {
-      const float* wp = reinterpret_cast<const float*>(W) + wrow;
-#pragma unroll 4
-      for (int j = lane * 4; j < H; j += 128) {
-        const float4 w = __ldcs(reinterpret_cast<const float4*>(wp + j));
+    for (int t = 0; t < T; ++t) acc[rr][t] = 0.f;
+  if (WBF16) {
+    const uint16_t* wp0 = reinterpret_cast<const uint16_t*>(W) + wrow[0];
+    const uint16_t* wp1 = reinterpret_cast<const uint16_t*>(W) + wrow[1];
+#pragma unroll 2
+    for (int j = lane * 8; j < H; j += 256) {
+      const uint4 wa = __ldcs(reinterpret_cast<const uint4*>(wp0 + j));
+      const uint4 wb = __ldcs(reinterpret_cast<const uint4*>(wp1 + j));
+      const float w0[8] = {bf16_lo_f32(wa.x), bf16_hi_f32(wa.x), bf16_lo_f32(wa.y), bf16_hi_f32(wa.y),
+                           bf16_lo_f32(wa.z), bf16_hi_f32(wa.z), bf16_lo_f32(wa.w), bf16_hi_f32(wa.w)};
+      const float w1[8] = {bf16_lo_f32(wb.x), bf16_hi_f32(wb.x), bf16_lo_f32(wb.y), bf16_hi_f32(wb.y),
+                           bf16_lo_f32(wb.z), bf16_hi_f32(wb.z), bf16_lo_f32(wb.w), bf16_hi_f32(wb.w)};
 #pragma unroll
-        for (int t = 0; t < T; ++t) {
-          const float4 x = __ldg(reinterpret_cast<const float4*>(ga.x + (size_t)t * H + j));
-          acc[t] += x.x * w.x + x.y * w.y + x.z * w.z + x.w * w.w;
-        }
+      for (int t = 0; t < T; ++t) {
+        const float4 x0 = __ldg(reinterpret_cast<const float4*>(ga.x + (size_t)t * H + j));
+        const float4 x1 = __ldg(reinterpret_cast<const float4*>(ga.x + (size_t)t * H + j + 4));
+        acc[0][t] += x0.x * w0[0] + x0.y * w0[1] + x0.z * w0[2] + x0.w * w0[3] + x1.x * w0[4] + x1.y * w0[5] +
+                     x1.z * w0[6] + x1.w * w0[7];
+        acc[1][t] += x0.x * w1[0] + x0.y * w1[1] + x0.z * w1[2] + x0.w * w1[3] + x1.x * w1[4] + x1.y * w1[5] +
+                     x1.z * w1[6] + x1.w * w1[7];
       }
     }
+  } else {
+    const float* wp0 = reinterpret_cast<const float*>(W) + wrow[0];
+    const float* wp1 = reinterpret_cast<const float*>(W) + wrow[1];
+#pragma unroll 4
+    for (int j = lane * 4; j < H; j += 128) {
+      const float4 wa = __ldcs(reinterpret_cast<const float4*>(wp0 + j));
+      const float4 wb = __ldcs(reinterpret_cast<const float4*>(wp1 + j));
 #pragma unroll
-    for (int t = 0; t < T; ++t) {
-      float v = acc[t];
-#pragma unroll
-      for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
-      if (lane == 0) y[r][t] = v;
+      for (int t = 0; t < T; ++t) {
+        const float4 x = __ldg(reinterpret_cast<const float4*>(ga.x + (size_t)t * H + j));
+        acc[0][t] += x.x * wa.x + x.y * wa.y + x.z * wa.z + x.w * wa.w;
+        acc[1][t] += x.x * wb.x + x.y * wb.y + x.z * wb.z + x.w * wb.w;
+      }
     }
   }
+#pragma unroll
+  for (int rr = 0; rr < 2; ++rr)
+#pragma unroll
+    for (int t = 0; t < T; ++t) {
+      float v = acc[rr][t];
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+      if (lane == 0) y[warp * 2 + rr][t] = v;
+    }
   __syncthreads();
   // epilogue: 8 pairs x T tokens
   for (int idx = threadIdx.x; idx < 8 * ga.T; idx += blockDim.x) {
