@@ -670,6 +670,78 @@ def bench_model_q8(args, dist_, torch, B=16, prompt=2048, gen=256, n_layers=28):
             "clocks": clocks}
 
 
+def synthetic_q8_stream(rows, cols, seed=6):
+    """A valid .oom Q8 block stream of rows*cols values (a multiple of 256): per block
+    [f32 scale][f32 min][u32 256][256 random bytes] (src/gguf2oom.rs:782-829 layout)."""
+    n = rows * cols
+    nb = n // 256
+    rng = np.random.default_rng(seed)
+    blk = np.empty((nb, 268), np.uint8)
+    blk[:, 0:4] = (rng.random(nb, dtype=np.float32) * 1e-3).view(np.uint8).reshape(nb, 4)
+    blk[:, 4:8] = (-rng.random(nb, dtype=np.float32) * 0.05).view(np.uint8).reshape(nb, 4)
+    blk[:, 8:12] = np.frombuffer(np.uint32(256).tobytes(), np.uint8)
+    blk[:, 12:] = rng.integers(0, 256, (nb, 256), dtype=np.uint8)
+    return blk.reshape(-1)
+
+
+def bench_oom_repack(args, dist_, torch, rows=18944, cols=3584):
+    """The .oom loader path for one Qwen2.5-7B gate matrix (Q8, 67.9 M values, a 70.5 MB block stream):
+    the device repack from a resident stream (oomattn_q8_repack), and end to end from pinned host memory
+    (one H2D copy + the repack).  Returns (device ms, e2e ms, stream bytes, device bytes moved)."""
+    from oomllama_b200 import TurboConfig, TurboEngine
+    dev = torch.cuda.current_device()
+    eng = TurboEngine(TurboConfig(n_layers=1, hidden_size=0, n_heads=8, n_kv_heads=1, max_seq_len=16, max_seqs=1),
+                      device=dev)
+    host = torch.from_numpy(synthetic_q8_stream(rows, cols)).pin_memory()
+    n = rows * cols
+    d_stream = host.to("cuda")
+    w = eng.q8_repack(d_stream, n, rows, cols)  # allocates the outputs once
+    for _ in range(3):
+        eng.q8_repack(d_stream, n, rows, cols)
+    eng.sync()
+    reps = max(10, args.steps)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    dist_.barrier()
+    torch.cuda.synchronize()
+    t0.record()
+    for _ in range(reps):
+        eng.q8_repack(d_stream, n, rows, cols)
+    t1.record()
+    torch.cuda.synchronize()
+    ms = dist_.max(t0.elapsed_time(t1) / reps)
+    t0.record()
+    for _ in range(reps):
+        d_stream.copy_(host, non_blocking=True)
+        eng.q8_repack(d_stream, n, rows, cols)
+    t1.record()
+    torch.cuda.synchronize()
+    e2e_ms = dist_.max(t0.elapsed_time(t1) / reps)
+    eng.sync()
+    byts = host.numel()
+    moved = byts + n + 8 * (n // 256)
+    del w
+    eng.close()
+    return ms, e2e_ms, byts, moved
+
+
+def cpu_oom_sample(rows=2048, cols=3584):
+    """The reference's loader work on the host for a sample of the same stream: the block walk that
+    dequantises to f32 (OomLoader::dequantize_tensor_into, src/quant.rs:431-463; the oracle's restatement),
+    and this library's host unpack (oomattn_q8_unpack).  Returns GB/s of stream bytes for each."""
+    from oracle import oracle as O
+    from oomllama_b200 import q8_unpack
+    O.build()
+    s = synthetic_q8_stream(rows, cols)
+    n = rows * cols
+    t = time.perf_counter()
+    O.q8_dequantize(s, n)
+    deq = s.size / (time.perf_counter() - t) / 1e9
+    t = time.perf_counter()
+    q8_unpack(s, n)
+    unp = s.size / (time.perf_counter() - t) / 1e9
+    return deq, unp
+
+
 def cpu_q8_sample(T, rows_per_matrix=64):
     """The oracle's Q8 dequantise + matvec (src/quant.rs:201-224, src/oom_inference.rs:168-180) on
     rows_per_matrix rows of each matrix of the layer; returns GB/s of algorithmic bytes and threads."""
@@ -860,6 +932,23 @@ def main():
                              "frac": byts / (ms * 1e-3) / 1e9 / peaks["hbm_gbs"], "traffic": None},
             }
         line["decoder_layer_q8"] = lay
+        ms, e2e_ms, sb, moved = bench_oom_repack(args, dist_, torch)
+        rp = {
+            "workload": "device repack of a Qwen2.5-7B gate matrix's .oom Q8 block stream (18944 x 3584, 70.5 MB)",
+            "stream_gbs": W * sb / (ms * 1e-3) / 1e9, "ms": ms,
+            "roofline": {"bound": "hbm", "kernel": "q8_repack_kernel", "achieved": moved / (ms * 1e-3) / 1e9,
+                         "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": moved / (ms * 1e-3) / 1e9 / peaks["hbm_gbs"], "traffic": None,
+                         "algorithmic_bytes": moved},
+            "e2e": {"value": W * sb / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s of stream", "h2d_bytes_per_step": sb,
+                    "d2h_bytes_per_step": 0, "api": "H2D copy from pinned memory + TurboEngine.q8_repack"},
+        }
+        if dist_.rank == 0 and W == 1 and not args.no_cpu_baseline:
+            deq, unp = cpu_oom_sample()
+            rp["cpu_baseline"] = {"value": deq, "unit": "GB/s of stream", "cores": 1, "kind": "port",
+                                  "sample": "2048 x 3584 of the same stream: the oracle's block walk to f32",
+                                  "host_unpack_gbs": unp}
+        line["oom_repack"] = rp
         B, P, G = 16, 2048, 256
         r = bench_model_q8(args, dist_, torch, B, P, G)
         step_ms = r["ms"] / G

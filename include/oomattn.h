@@ -318,6 +318,40 @@ typedef struct oomattn_q8_layer {
 int oomattn_decoder_layer_q8(oomattn_ctx* ctx, int32_t layer, int32_t n_seqs, const int32_t* seq_ids /* host */,
                              const float* x, const oomattn_q8_layer* w /* host struct */, float* out);
 
+/* ------------------------------------------------------------------ .oom files */
+
+/* One tensor of an .oom file: OomTensorMeta (src/quant.rs:307-312) plus where
+ * its name and blocks lie in the file image.  quant_type: 0 f32 (one block of
+ * raw values), 8 Q8, 4 Q4, 2 Q2. */
+typedef struct oomattn_oom_tensor {
+  uint64_t name_offset;  /* the name's bytes (not terminated) */
+  uint32_t name_len;
+  uint32_t quant_type;
+  uint32_t num_blocks;
+  uint32_t total_values;
+  uint64_t data_offset;  /* first block header: OomTensorMeta::offset */
+  uint64_t data_bytes;   /* all its blocks: headers and data */
+} oomattn_oom_tensor;
+
+/* OomLoader::load's scan (src/quant.rs:320-367) of a file image in host
+ * memory: "OOML", u32 version, u32 tensor count, then per tensor u32 name
+ * length, name, u8 quant type, u32 blocks, u32 values and its blocks
+ * (src/gguf2oom.rs:708-716, :782-829).  Fills out[0..min(count, max_tensors))
+ * and *n_tensors = count.  A field or block past the end of the image is
+ * OOMATTN_ERR_INVALID_ARG (the reference stops silently).  Host only. */
+int oomattn_oom_scan(const uint8_t* file /* host */, uint64_t bytes, oomattn_oom_tensor* out /* host */,
+                     int32_t max_tensors, int32_t* n_tensors /* host */, char* errbuf /* host, may be NULL */,
+                     int32_t errbuf_len);
+
+/* The device-side repack of one Q8 tensor: its block stream (the bytes at
+ * data_offset, data_bytes long, already in device memory, at any byte
+ * alignment and readable to the next 4-byte boundary past its end) into the
+ * resident layout q [n_values], scale and min [ceil(n_values / 256)] that
+ * oomattn_q8_unpack produces on the host.  A block whose length field is not
+ * min(256, values left) is reported by oomattn_sync as OOMATTN_ERR_DEVICE_CHECK. */
+int oomattn_q8_repack(oomattn_ctx* ctx, const uint8_t* blocks, uint64_t bytes, int64_t n_values, uint8_t* q,
+                      float* scale, float* min);
+
 /* ------------------------------------------------ embedding, LM head, greedy pick */
 
 /* out[t] = row token_ids[t] of the embedding table emb [vocab][hidden],

@@ -3,7 +3,7 @@
 The compute path is liboomattn.so (C ABI in include/oomattn.h); this package is
 its host-side mirror of the reference's TurboEngine interface.
 """
-from .turbo import (Q8DecoderLayer, Q8Matrix, Q8Model, TurboConfig, TurboEngine, compute_rope_freqs,  # noqa: F401
-                    q8_unpack)
+from .turbo import (OomFile, Q8DecoderLayer, Q8Matrix, Q8Model, TurboConfig, TurboEngine,  # noqa: F401
+                    compute_rope_freqs, oom_scan, q8_unpack)
 
-__all__ = ["TurboConfig", "TurboEngine", "compute_rope_freqs", "Q8Matrix", "Q8DecoderLayer", "Q8Model", "q8_unpack"]
+__all__ = ["TurboConfig", "TurboEngine", "compute_rope_freqs", "Q8Matrix", "Q8DecoderLayer", "Q8Model", "q8_unpack", "OomFile", "oom_scan"]

@@ -27,7 +27,7 @@ EXPORTS = (
     "oomattn_compute_rope_table", "oomattn_rope_append", "oomattn_qkv_rope_append", "oomattn_decode", "oomattn_merge_partials",
     "oomattn_prefill", "oomattn_attention_forward_with_bias", "oomattn_decode_static_scratch",
     "oomattn_q8_unpack", "oomattn_q8_linear", "oomattn_rmsnorm", "oomattn_q8_mlp", "oomattn_decoder_layer_q8",
-    "oomattn_embed_q8", "oomattn_argmax", "oomattn_decode_step_q8",
+    "oomattn_embed_q8", "oomattn_argmax", "oomattn_decode_step_q8", "oomattn_oom_scan", "oomattn_q8_repack",
 )
 
 
@@ -61,6 +61,13 @@ class Q8Layer(ctypes.Structure):
                 ("up", Q8Matrix), ("down", Q8Matrix), ("bq", ctypes.c_void_p), ("bk", ctypes.c_void_p),
                 ("bv", ctypes.c_void_p), ("input_norm", ctypes.c_void_p), ("post_norm", ctypes.c_void_p),
                 ("eps", ctypes.c_float)]
+
+
+class OomTensor(ctypes.Structure):
+    """oomattn_oom_tensor: one tensor of an .oom file image (OomTensorMeta plus name and block extents)."""
+    _fields_ = [("name_offset", ctypes.c_uint64), ("name_len", ctypes.c_uint32), ("quant_type", ctypes.c_uint32),
+                ("num_blocks", ctypes.c_uint32), ("total_values", ctypes.c_uint32), ("data_offset", ctypes.c_uint64),
+                ("data_bytes", ctypes.c_uint64)]
 
 
 class Q8Model(ctypes.Structure):
@@ -116,6 +123,9 @@ def load():
         "oomattn_embed_q8": ([P, ctypes.POINTER(Q8Matrix), P, I, P], ctypes.c_int),
         "oomattn_argmax": ([P, P, I, I, P], ctypes.c_int),
         "oomattn_decode_step_q8": ([P, ctypes.POINTER(Q8Model), I, IP, P, P, P], ctypes.c_int),
+        "oomattn_oom_scan": ([P, ctypes.c_uint64, ctypes.POINTER(OomTensor), I, ctypes.POINTER(ctypes.c_int32),
+                              ctypes.c_char_p, I], ctypes.c_int),
+        "oomattn_q8_repack": ([P, P, ctypes.c_uint64, ctypes.c_int64, P, P, P], ctypes.c_int),
     }
     for name, (args, res) in sig.items():
         fn = getattr(L, name)

@@ -16,6 +16,7 @@ enum : int {
   kDevErrTmem = 4,         // tensor-memory allocation returned an unusable address
   kDevErrRange = 8,        // a cached V value of magnitude >= 65536 met the fp16 P.V product
   kDevErrX16 = 16,         // a Q8-linear activation of magnitude >= 65504 met its fp16 hi/lo split
+  kDevErrFormat = 32,      // a .oom Q8 block's length field disagrees with its position in the tensor
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {

@@ -616,6 +616,9 @@ int oomattn_sync(oomattn_ctx* ctx) {
     if (st & kDevErrRange)
       return fail(ctx, OOMATTN_ERR_DEVICE_CHECK,
                   "prefill met a cached V value of magnitude >= 65536, outside the fp16 P.V product (status %d)", st);
+    if (st & kDevErrFormat)
+      return fail(ctx, OOMATTN_ERR_DEVICE_CHECK,
+                  "q8_repack met a block whose length field disagrees with its position (status %d)", st);
     if (st & kDevErrX16)
       return fail(ctx, OOMATTN_ERR_DEVICE_CHECK,
                   "q8_linear met an activation of magnitude >= 65504, outside its fp16 hi/lo split (status %d)", st);
@@ -1632,4 +1635,84 @@ extern "C" int oomattn_decode_step_q8(oomattn_ctx* ctx, const oomattn_q8_model* 
   rc = q8_run(ctx, &head, 1, xa, nullptr, n_seqs, m->final_norm, m->eps);
   if (rc) return rc;
   return oomattn_argmax(ctx, lg, n_seqs, (int)vocab, next);
+}
+
+// ------------------------------------------------------------------ .oom files
+namespace {
+bool rd_u32(const uint8_t* f, uint64_t bytes, uint64_t off, uint32_t* v) {
+  if (off + 4 > bytes) return false;
+  memcpy(v, f + off, 4);  // little endian, as the writer stores it
+  return true;
+}
+}  // namespace
+
+// OomLoader::load's metadata scan (src/quant.rs:320-367) over a file image,
+// with every field and block bounds-checked (the reference stops silently at
+// a truncated tensor; here that is an error).
+extern "C" int oomattn_oom_scan(const uint8_t* file, uint64_t bytes, oomattn_oom_tensor* out, int32_t max_tensors,
+                                int32_t* n_tensors, char* errbuf, int32_t errbuf_len) {
+  auto bad = [&](const char* fmt, long long a, long long b) {
+    if (errbuf && errbuf_len > 0) snprintf(errbuf, (size_t)errbuf_len, fmt, a, b);
+    return OOMATTN_ERR_INVALID_ARG;
+  };
+  if (!file || !n_tensors || (max_tensors > 0 && !out)) return bad("null argument (%lld %lld)", 0, 0);
+  if (bytes < 12 || memcmp(file, "OOML", 4) != 0) return bad("not an .oom file (%lld bytes, magic %lld)", (long long)bytes, 0);
+  uint32_t version = 0, count = 0;
+  rd_u32(file, bytes, 4, &version);
+  rd_u32(file, bytes, 8, &count);
+  *n_tensors = (int32_t)count;
+  uint64_t off = 12;
+  for (uint32_t t = 0; t < count; ++t) {
+    uint32_t name_len = 0, num_blocks = 0, total = 0;
+    if (!rd_u32(file, bytes, off, &name_len) || off + 4 + name_len + 9 > bytes)
+      return bad("tensor %lld: header past the end of the file (offset %lld)", t, (long long)off);
+    const uint64_t name_off = off + 4;
+    off = name_off + name_len;
+    const uint8_t qt = file[off];
+    off += 1;
+    rd_u32(file, bytes, off, &num_blocks);
+    rd_u32(file, bytes, off + 4, &total);
+    off += 8;
+    const uint64_t data_off = off;
+    for (uint32_t b = 0; b < num_blocks; ++b) {
+      uint32_t len = 0;
+      if (!rd_u32(file, bytes, off + 8, &len) || off + 12 + (uint64_t)len > bytes)
+        return bad("tensor %lld: block %lld past the end of the file", t, b);
+      off += 12 + (uint64_t)len;
+    }
+    if ((int32_t)t < max_tensors) {
+      oomattn_oom_tensor& m = out[t];
+      m.name_offset = name_off;
+      m.name_len = name_len;
+      m.quant_type = qt;
+      m.num_blocks = num_blocks;
+      m.total_values = total;
+      m.data_offset = data_off;
+      m.data_bytes = off - data_off;
+    }
+  }
+  (void)version;
+  return OOMATTN_OK;
+}
+
+extern "C" int oomattn_q8_repack(oomattn_ctx* ctx, const uint8_t* blocks, uint64_t bytes, int64_t n_values,
+                                 uint8_t* q, float* scale, float* min) {
+  if (!ctx) return OOMATTN_ERR_INVALID_ARG;
+  if (!blocks || !q || !scale || !min || n_values <= 0) return fail(ctx, OOMATTN_ERR_INVALID_ARG, "bad q8_repack arguments");
+  const long long nb = (n_values + 255) / 256;
+  const uint64_t expect = (uint64_t)nb * 12 + (uint64_t)n_values;
+  if (bytes != expect)
+    return fail(ctx, OOMATTN_ERR_INVALID_ARG, "a Q8 stream of %lld values has %llu bytes, not %llu", (long long)n_values,
+                (unsigned long long)bytes, (unsigned long long)expect);
+  if (reinterpret_cast<uintptr_t>(q) % 8 || reinterpret_cast<uintptr_t>(scale) % 4 ||
+      reinterpret_cast<uintptr_t>(min) % 4)
+    return fail(ctx, OOMATTN_ERR_INVALID_ARG, "q must be 8-byte and scale/min 4-byte aligned");
+  DeviceGuard dg(ctx->device);
+  const uintptr_t p = reinterpret_cast<uintptr_t>(blocks);
+  const uint32_t* base_w = reinterpret_cast<const uint32_t*>(p & ~uintptr_t(3));
+  const int warps = 8;
+  q8_repack_kernel<<<(unsigned)((nb + warps - 1) / warps), warps * 32, 0, ctx->stream>>>(
+      base_w, (uint32_t)(p & 3), n_values, nb, q, scale, min, ctx->d_status);
+  CKLAUNCH();
+  return OOMATTN_OK;
 }

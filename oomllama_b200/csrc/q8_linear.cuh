@@ -480,6 +480,51 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_prep_x_kernel(const floa
   }
 }
 
+// ---------------------------------------------------------- .oom block repack
+// A Q8 tensor's block stream as the .oom writer lays it down
+// (src/gguf2oom.rs:782-829): block b = [f32 scale][f32 min][u32 len][len bytes]
+// with len = min(256, n - 256 b), so block b starts at byte 268 b.  One warp
+// per block: lane l moves bytes 8l..8l+7 of the block's data into q and lane 0
+// the scale and min.  The stream may start at any byte (a tensor inside a
+// whole uploaded file): words are read 4-byte aligned and funnel-shifted.  A
+// length field that disagrees with the block's position is reported.
+constexpr int kQ8BlockBytes = 12 + 256;
+
+__device__ __forceinline__ uint32_t oom_word(const uint32_t* base_w, uint32_t shift, long long byte_off) {
+  // 4 bytes starting at byte_off of a stream whose first byte lies `shift` bytes into base_w[0]
+  const long long b = byte_off + shift;
+  const uint32_t lo = base_w[b >> 2];
+  if ((b & 3) == 0) return lo;  // the next word is read only when the 4 bytes reach into it
+  return __funnelshift_r(lo, base_w[(b >> 2) + 1], (uint32_t)(b & 3) * 8);
+}
+
+__global__ void q8_repack_kernel(const uint32_t* __restrict__ base_w, uint32_t shift, long long n_values,
+                                 long long n_blocks, uint8_t* __restrict__ q, float* __restrict__ scale,
+                                 float* __restrict__ mn, int* status) {
+  const long long blk = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (blk >= n_blocks) return;
+  const int lane = threadIdx.x & 31;
+  const long long off = blk * kQ8BlockBytes;
+  const int len = (int)min(256LL, n_values - blk * 256);
+  if (lane == 0) {
+    scale[blk] = __uint_as_float(oom_word(base_w, shift, off));
+    mn[blk] = __uint_as_float(oom_word(base_w, shift, off + 4));
+    if ((int)oom_word(base_w, shift, off + 8) != len) report_error(status, kDevErrFormat);
+  }
+  const int b0 = lane * 8;
+  if (b0 >= len) return;
+  uint8_t* dst = q + blk * 256 + b0;
+  if (b0 + 8 <= len) {
+    const uint32_t w0 = oom_word(base_w, shift, off + 12 + b0), w1 = oom_word(base_w, shift, off + 16 + b0);
+    *reinterpret_cast<uint2*>(dst) = make_uint2(w0, w1);  // q is 8-byte aligned per lane (blocks of 256)
+  } else {
+    for (int i = b0; i < len; ++i) {
+      const long long b = off + 12 + i + shift;
+      dst[i - b0] = (uint8_t)(base_w[b >> 2] >> ((b & 3) * 8));
+    }
+  }
+}
+
 // ------------------------------------------------------------------ embedding, argmax
 // out[t] = row ids[t] of a Q8 matrix [vocab][hidden], dequantised exactly as
 // the reference reads a Q8 tensor (min + (f32)q * scale, src/quant.rs:201-224),

@@ -373,6 +373,19 @@ class TurboEngine:
                                                           ctypes.byref(w.c_struct()), _ptr(out)))
         return out
 
+    def q8_repack(self, blocks: torch.Tensor, n_values: int, rows: int = None, cols: int = None):
+        """Device-side repack of one Q8 tensor's .oom block stream (uint8 device tensor, any offset) into a
+        resident Q8Matrix [rows][cols] (src/gguf2oom.rs:782-829 layout; the result equals q8_unpack's)."""
+        _dev(blocks, "blocks", self.device, dtype=torch.uint8)
+        nb = (n_values + 255) // 256
+        q = torch.empty(n_values, dtype=torch.uint8, device=self.device)
+        scale = torch.empty(nb, dtype=torch.float32, device=self.device)
+        mn = torch.empty(nb, dtype=torch.float32, device=self.device)
+        self._bind_stream()
+        check(self._ctx, self._L.oomattn_q8_repack(self._ctx, _ptr(blocks), blocks.numel(), n_values, _ptr(q),
+                                                   _ptr(scale), _ptr(mn)))
+        return Q8Matrix(q, scale, mn, rows if rows is not None else 1, cols if cols is not None else n_values)
+
     def embed_q8(self, emb: "Q8Matrix", token_ids: torch.Tensor, out=None):
         """embed_w.embedding(tokens) (src/oomllama.rs:508-515) on a resident Q8 table: int32 ids [T] ->
         f32 [T, hidden]."""
@@ -429,6 +442,72 @@ def q8_unpack(stream, n_values: int):
     if rc != _lib.OK:
         raise _lib.OomAttnError(rc, err.value.decode(errors="replace"))
     return q[:n_values], scale[:nb], mn[:nb]
+
+
+def oom_scan(image):
+    """OomLoader::load's metadata scan (src/quant.rs:320-367) of an .oom file image (bytes, or a uint8 numpy
+    array / memory map): {name: OomTensor} in file order."""
+    import numpy as np
+    buf = image if isinstance(image, np.ndarray) else np.frombuffer(image, dtype=np.uint8)
+    L = _lib.load()
+    err = ctypes.create_string_buffer(256)
+    n = ctypes.c_int32(0)
+    rc = L.oomattn_oom_scan(buf.ctypes.data_as(ctypes.c_void_p), buf.size, None, 0, ctypes.byref(n), err, 256)
+    if rc != _lib.OK:
+        raise _lib.OomAttnError(rc, err.value.decode(errors="replace"))
+    metas = (_lib.OomTensor * max(1, n.value))()
+    rc = L.oomattn_oom_scan(buf.ctypes.data_as(ctypes.c_void_p), buf.size, metas, n.value, ctypes.byref(n), err, 256)
+    if rc != _lib.OK:
+        raise _lib.OomAttnError(rc, err.value.decode(errors="replace"))
+    out = {}
+    for m in metas[:n.value]:
+        name = bytes(buf[m.name_offset:m.name_offset + m.name_len]).decode("utf-8")
+        out[name] = m
+    return out
+
+
+class OomFile:
+    """An .oom file for GPU-resident inference: the metadata scan of OomLoader::load (src/quant.rs:320-367) and,
+    per tensor, one upload of its block stream followed by the device repack into a resident Q8Matrix -- the
+    weights are never dequantised to f32 (src/oomllama.rs:425-439 dequantises and uploads on every call)."""
+
+    def __init__(self, path_or_image):
+        import os
+        import numpy as np
+        if isinstance(path_or_image, (str, os.PathLike)):
+            self.image = np.memmap(path_or_image, dtype=np.uint8, mode="r")
+        elif isinstance(path_or_image, (bytes, bytearray)):
+            self.image = np.frombuffer(path_or_image, dtype=np.uint8)
+        else:
+            self.image = path_or_image
+        self.tensors = oom_scan(self.image)
+
+    def blocks(self, name: str):
+        m = self.tensors[name]
+        return self.image[m.data_offset:m.data_offset + m.data_bytes]
+
+    def q8_matrix(self, engine: "TurboEngine", name: str, rows: int, cols: int) -> "Q8Matrix":
+        """Upload the tensor's blocks (padded to a 4-byte multiple) and repack them on the device."""
+        m = self.tensors[name]
+        if m.quant_type != 8:
+            raise ValueError(f"{name}: quant type {m.quant_type}, not Q8")
+        if m.total_values != rows * cols:
+            raise ValueError(f"{name}: {m.total_values} values, not {rows} x {cols}")
+        import numpy as np
+        raw = self.blocks(name)
+        dev = torch.empty((raw.size + 3) // 4 * 4, dtype=torch.uint8, device=engine.device)
+        dev[:raw.size].copy_(torch.from_numpy(np.ascontiguousarray(raw)))
+        return engine.q8_repack(dev[:raw.size], rows * cols, rows, cols)
+
+    def f32_tensor(self, name: str, device=None) -> torch.Tensor:
+        """A raw f32 tensor (norms, biases): one block whose data are the values (src/gguf2oom.rs:835-861)."""
+        import numpy as np
+        m = self.tensors[name]
+        if m.quant_type != 0:
+            raise ValueError(f"{name}: quant type {m.quant_type}, not f32")
+        raw = self.image[m.data_offset + 12:m.data_offset + 12 + 4 * m.total_values]
+        t = torch.from_numpy(np.frombuffer(raw.tobytes(), dtype=np.float32).copy())
+        return t if device is None else t.to(device)
 
 
 @dataclass

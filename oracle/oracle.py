@@ -250,6 +250,39 @@ def q8_dequantize(stream, n: int) -> np.ndarray:
     return out[:n]
 
 
+def oom_scan(image):
+    """OomLoader::load's metadata scan (src/quant.rs:320-367): [(name, quant_type, num_blocks, total_values,
+    data_offset, data_bytes)] in file order.  The reference's loop stops at a truncated header or block; here
+    that raises ValueError, matching the library's stricter scan."""
+    b = bytes(image)
+    if len(b) < 12 or b[:4] != b"OOML":
+        raise ValueError("not an .oom file")
+    count = int.from_bytes(b[8:12], "little")
+    off, out = 12, []
+    for _ in range(count):
+        if off + 4 > len(b):
+            raise ValueError("truncated header")
+        nl = int.from_bytes(b[off:off + 4], "little")
+        if off + 4 + nl + 9 > len(b):
+            raise ValueError("truncated header")
+        name = b[off + 4:off + 4 + nl].decode()
+        off += 4 + nl
+        qt = b[off]
+        nb = int.from_bytes(b[off + 1:off + 5], "little")
+        n = int.from_bytes(b[off + 5:off + 9], "little")
+        off += 9
+        start = off
+        for _ in range(nb):  # skip the blocks by their length fields
+            if off + 12 > len(b):
+                raise ValueError("truncated block")
+            ln = int.from_bytes(b[off + 8:off + 12], "little")
+            if off + 12 + ln > len(b):
+                raise ValueError("truncated block")
+            off += 12 + ln
+        out.append((name, qt, nb, n, start, off - start))
+    return out
+
+
 def linear(x, w, b=None):
     """x [T, cols] @ w[rows, cols]^T (+ b): the reference's matvec per token (oom_inference.rs:168-180)."""
     x, w = _c(x), _c(w)
