@@ -496,7 +496,7 @@ class OomFile:
         import numpy as np
         raw = self.blocks(name)
         dev = torch.empty((raw.size + 3) // 4 * 4, dtype=torch.uint8, device=engine.device)
-        dev[:raw.size].copy_(torch.from_numpy(np.ascontiguousarray(raw)))
+        dev[:raw.size].copy_(torch.from_numpy(np.array(raw)))  # a writable host copy of the (read-only) image
         return engine.q8_repack(dev[:raw.size], rows * cols, rows, cols)
 
     def f32_tensor(self, name: str, device=None) -> torch.Tensor:
