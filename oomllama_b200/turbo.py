@@ -584,6 +584,32 @@ class Q8Model:
     final_norm: torch.Tensor
     eps: float
 
+    @classmethod
+    def from_oom(cls, oom: "OomFile", engine: "TurboEngine", n_layers: int, inter: int, vocab: int,
+                 eps: float = 1e-6) -> "Q8Model":
+        """A model's resident weights from an .oom file, by the converter's tensor names
+        (map_tensor_name, src/gguf2oom.rs:936-979): Q8 projections, embedding and LM head; f32 norms and
+        biases (src/gguf2oom.rs:1027-1037).  Shapes come from the engine's configuration.  A file without
+        lm_head.weight (tied embeddings) uses the embedding table as the LM head."""
+        c = engine.config
+        H, nq, nkv = c.hidden_size, c.n_heads * HEAD_DIM, c.n_kv_heads * HEAD_DIM
+        dev = engine.device
+        f32 = lambda name: oom.f32_tensor(name, dev) if name in oom.tensors else None  # noqa: E731
+        layers = []
+        for i in range(n_layers):
+            p = f"model.layers.{i}."
+            m = lambda n, r, k: oom.q8_matrix(engine, p + n, r, k)  # noqa: E731
+            layers.append(Q8DecoderLayer(
+                q=m("self_attn.q_proj.weight", nq, H), k=m("self_attn.k_proj.weight", nkv, H),
+                v=m("self_attn.v_proj.weight", nkv, H), o=m("self_attn.o_proj.weight", H, nq),
+                gate=m("mlp.gate_proj.weight", inter, H), up=m("mlp.up_proj.weight", inter, H),
+                down=m("mlp.down_proj.weight", H, inter), input_norm=f32(p + "input_layernorm.weight"),
+                post_norm=f32(p + "post_attention_layernorm.weight"), eps=eps, bq=f32(p + "self_attn.q_proj.bias"),
+                bk=f32(p + "self_attn.k_proj.bias"), bv=f32(p + "self_attn.v_proj.bias")))
+        embed = oom.q8_matrix(engine, "model.embed_tokens.weight", vocab, H)
+        head = oom.q8_matrix(engine, "lm_head.weight", vocab, H) if "lm_head.weight" in oom.tensors else embed
+        return cls(layers=layers, embed=embed, lm_head=head, final_norm=f32("model.norm.weight"), eps=eps)
+
     def c_struct(self) -> _lib.Q8Model:
         arr = (_lib.Q8Layer * len(self.layers))(*[l.c_struct() for l in self.layers])
         m = _lib.Q8Model(len(self.layers), ctypes.cast(arr, ctypes.POINTER(_lib.Q8Layer)), self.embed.c_struct(),

@@ -250,6 +250,22 @@ def q8_dequantize(stream, n: int) -> np.ndarray:
     return out[:n]
 
 
+def oom_image(tensors) -> bytes:
+    """An .oom file image as the reference's writer produces it (src/gguf2oom.rs:708-716 header, :782-829 Q8
+    tensors via q8_quantize, :835-861 raw f32 tensors): tensors = [(name, "q8" | "f32", values)]."""
+    import struct
+    out = bytearray(b"OOML" + struct.pack("<II", 1, len(tensors)))
+    for name, kind, values in tensors:
+        v = _c(values).ravel()
+        nm = name.encode()
+        out += struct.pack("<I", len(nm)) + nm
+        if kind == "q8":
+            out += struct.pack("<BII", 8, (v.size + 255) // 256, v.size) + q8_quantize(v).tobytes()
+        else:
+            out += struct.pack("<BII", 0, 1, v.size) + struct.pack("<ffI", 0.0, 0.0, 4 * v.size) + v.tobytes()
+    return bytes(out)
+
+
 def oom_scan(image):
     """OomLoader::load's metadata scan (src/quant.rs:320-367): [(name, quant_type, num_blocks, total_values,
     data_offset, data_bytes)] in file order.  The reference's loop stops at a truncated header or block; here

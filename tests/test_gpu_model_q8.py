@@ -191,3 +191,67 @@ def test_decode_step_q8_rejects_mismatched_models(oracle):
         eng.decode_step_q8(bad, [0], tok)
     assert e.value.code == 1
     eng.close()
+
+
+def test_decode_step_q8_from_an_oom_file(oracle):
+    # a 2-layer model written as an .oom file by the oracle's restatement of the converter
+    # (Q8 projections, f32 norms and biases, the converter's tensor names), loaded by OomFile +
+    # Q8Model.from_oom through the device repack, then greedy steps against the oracle
+    from oomllama_b200 import OomFile, Q8Model
+    n_layers, hq, hkv, inter, vocab, D, eps = 2, 2, 1, 512, 1024, 128, 1e-6
+    H = hq * D
+    rng = np.random.default_rng(21)
+    w = lambda r, c, s=0.05: (rng.standard_normal((r, c)) * s).astype(np.float32)  # noqa: E731
+    tensors, ref_layers = [], []
+    for i in range(n_layers):
+        p = f"model.layers.{i}."
+        mats = {"q": w(hq * D, H), "k": w(hkv * D, H), "v": w(hkv * D, H), "o": w(H, hq * D),
+                "gate": w(inter, H), "up": w(inter, H), "down": w(H, inter)}
+        names = {"q": "self_attn.q_proj.weight", "k": "self_attn.k_proj.weight", "v": "self_attn.v_proj.weight",
+                 "o": "self_attn.o_proj.weight", "gate": "mlp.gate_proj.weight", "up": "mlp.up_proj.weight",
+                 "down": "mlp.down_proj.weight"}
+        bq, bk, bv = [(rng.standard_normal(n) * 0.1).astype(np.float32) for n in (hq * D, hkv * D, hkv * D)]
+        n1, n2 = (1 + 0.1 * rng.standard_normal((2, H))).astype(np.float32)
+        for key, nm in names.items():
+            tensors.append((p + nm, "q8", mats[key]))
+        tensors += [(p + "self_attn.q_proj.bias", "f32", bq), (p + "self_attn.k_proj.bias", "f32", bk),
+                    (p + "self_attn.v_proj.bias", "f32", bv), (p + "input_layernorm.weight", "f32", n1),
+                    (p + "post_attention_layernorm.weight", "f32", n2)]
+        deq = {k: oracle.q8_dequantize(oracle.q8_quantize(v), v.size).reshape(v.shape) for k, v in mats.items()}
+        ref_layers.append(dict(deq, bq=bq, bk=bk, bv=bv, n1=n1, n2=n2, eps=eps))
+    emb, head = w(vocab, H, 1.0), w(vocab, H, 0.2)
+    fn = (1 + 0.1 * rng.standard_normal(H)).astype(np.float32)
+    tensors += [("model.embed_tokens.weight", "q8", emb), ("model.norm.weight", "f32", fn),
+                ("lm_head.weight", "q8", head)]
+    image = oracle.oom_image(tensors)
+    lens = [9, 40]
+    B, steps = len(lens), 4
+    eng = make_engine(hq, hkv, [L + steps for L in lens], kv_dtype="f32", variant="interleaved", theta=1e6,
+                      hidden=H, n_layers=n_layers, shuffle_seed=2)
+    model = Q8Model.from_oom(OomFile(image), eng, n_layers, inter, vocab, eps)
+    caches = []
+    for l in range(n_layers):
+        kc = [rng.standard_normal((L, hkv, D)).astype(np.float32) for L in lens]
+        vc = [rng.standard_normal((L, hkv, D)).astype(np.float32) for L in lens]
+        for b in range(B):
+            eng.kv_write(l, b, torch.from_numpy(kc[b]).cuda(), torch.from_numpy(vc[b]).cuda())
+        caches.append((kc, vc))
+    cos_t, sin_t = oracle.rope_table(1e6, D, max(lens) + steps)
+    ref_emb = oracle.q8_dequantize(oracle.q8_quantize(emb), emb.size).reshape(emb.shape)
+    ref_head = oracle.q8_dequantize(oracle.q8_quantize(head), head.size).reshape(head.shape)
+    rl = list(lens)
+    tokens = torch.tensor([5, 1000], dtype=torch.int32, device="cuda")
+    logits = torch.empty(B, vocab, device="cuda")
+    for step in range(steps):
+        tok_in = tokens.cpu().numpy()
+        eng.decode_step_q8(model, list(range(B)), tokens, next_tokens=tokens, logits=logits)
+        eng.sync()
+        got, lg = tokens.cpu().numpy(), logits.cpu().numpy()
+        want, ref_lg = oracle.model_decode_step(tok_in, ref_emb, ref_layers, fn, ref_head, eps, caches, rl, hq, hkv,
+                                                cos_t, sin_t, oracle.ROPE_INTERLEAVED)
+        tol = F32_ATOL * max(1.0, np.abs(ref_lg).max())
+        assert_close(lg, ref_lg, tol, what=f"logits step {step}")
+        top2 = np.sort(ref_lg, axis=1)[:, -2:]
+        clear = (top2[:, 1] - top2[:, 0]) > 2 * tol
+        assert (got[clear] == want[clear]).all()
+    eng.close()
