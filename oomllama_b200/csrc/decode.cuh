@@ -151,6 +151,28 @@ __device__ __forceinline__ DecodeItem decode_item(const DecodeSched& s, const Se
   return it;
 }
 
+// The kernel is launched as a programmatic dependent of the one before it
+// (the RoPE + append): while that one finishes, pull the first pages of this
+// item's K/V into L2, then wait for it before reading q or the cache.
+constexpr int kDecPrefetchPages = 8;
+__device__ __forceinline__ void prefetch_then_wait(const KVPool& pool, const DecodeArgs& a, int seq, int g, int pb,
+                                                   int pe, int elem_bytes) {
+  const int np = min(pe - pb, kDecPrefetchPages);
+  if (np > 0) {
+    const int lines = kPageSize * kHeadDim * elem_bytes / 128;  // 128-byte lines per (page, kv head) chunk
+    const int* bt = pool.block_table + (size_t)seq * pool.max_pages_per_seq;
+    for (int i = threadIdx.x; i < np * 2 * lines; i += blockDim.x) {
+      const int pi = pb + i / (2 * lines), r = i % (2 * lines);
+      const int page = __ldg(bt + pi);
+      if ((unsigned)page >= (unsigned)pool.n_pool_pages) continue;  // reported by the main loop
+      const size_t chunk = ((size_t)(a.layer * pool.n_pool_pages + page) * pool.n_kv + g) * kPageSize * kHeadDim;
+      const char* base = static_cast<const char*>(r < lines ? pool.k : pool.v) + chunk * elem_bytes;
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(base + (size_t)(r % lines) * 128));
+    }
+  }
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
 __device__ __forceinline__ void write_empty_row(const DecodeArgs& a, int z, int g) {
   for (int i = threadIdx.x; i < a.group * kHeadDim; i += blockDim.x) {
     const int h = g * a.group + i / kHeadDim;
@@ -174,6 +196,7 @@ __global__ void __launch_bounds__((kDecWarps + 1) * 32, 2)
   const int seq = sb.seq[z];
   const int L = sb.len[z];
   const int pb = item.pb, pe = item.pe;
+  prefetch_then_wait(pool, a, seq, g, pb, pe, 2);
   if (pb >= pe) {
     if (L <= 0 && split == 0) write_empty_row(a, z, g);
     return;
@@ -337,6 +360,7 @@ __global__ void __launch_bounds__(kDecWarps * 32)
   const int seq = sb.seq[z];
   const int L = sb.len[z];
   const int pb = item.pb, pe = item.pe;
+  prefetch_then_wait(pool, a, seq, g, pb, pe, 4);
   if (pb >= pe) {
     if (L <= 0 && split == 0) write_empty_row(a, z, g);
     return;

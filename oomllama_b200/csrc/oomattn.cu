@@ -489,12 +489,25 @@ int launch_decode_rows(oomattn_ctx* ctx, int layer, const SeqBatch& sb, const fl
   a.status = ctx->d_status;
   a.timeout_ns = ctx->timeout_ns;
   KVPool pool = make_pool(ctx);
+  // a programmatic dependent of the append before it (see prefetch_then_wait)
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(n_items);
+  cfg.stream = ctx->stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t le;
   if (ctx->cfg.kv_dtype == OOMATTN_DTYPE_BF16) {
-    decode_bf16_kernel<<<n_items, (kDecWarps + 1) * 32, kDecSmemBytes, ctx->stream>>>(ctx->kmap, ctx->vmap, pool, a,
-                                                                                      sb, sched);
+    cfg.blockDim = dim3((kDecWarps + 1) * 32);
+    cfg.dynamicSmemBytes = kDecSmemBytes;
+    le = cudaLaunchKernelEx(&cfg, decode_bf16_kernel, ctx->kmap, ctx->vmap, pool, a, sb, sched);
   } else {
-    decode_f32_kernel<<<n_items, kDecWarps * 32, 0, ctx->stream>>>(pool, a, sb, sched);
+    cfg.blockDim = dim3(kDecWarps * 32);
+    le = cudaLaunchKernelEx(&cfg, decode_f32_kernel, pool, a, sb, sched);
   }
+  if (le != cudaSuccess) return fail(ctx, OOMATTN_ERR_CUDA, "decode launch: %s", cudaGetErrorString(le));
   CKLAUNCH();
   return OOMATTN_OK;
 }

@@ -135,6 +135,8 @@ __device__ __forceinline__ void add_bias8(float* x, const float* b) {
 template <bool IN_BF16, bool Q_BF16, bool KV_BF16>
 __global__ void __launch_bounds__(256)
     rope_append_kernel(const AppendArgs ap, const KVPool pool, const __grid_constant__ SeqBatch sb, int T) {
+  // the decode that follows may launch now: it waits for this grid before reading
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int hq = ap.n_heads, hkv = pool.n_kv;
   const int units_tok = (hq + 2 * hkv) * 8;
   const int first = ap.q ? 0 : hq * 8;  // no q: K/V rows only
@@ -219,6 +221,8 @@ __global__ void f32_to_bf16_kernel(const float* __restrict__ x, uint16_t* __rest
 template <int T, bool WBF16>
 __global__ void __launch_bounds__(256)
     qkv_gemv_rope_append_kernel(const GemvArgs ga, const KVPool pool, const __grid_constant__ SeqBatch sb) {
+  // the decode that follows may launch now: it waits for this grid before reading
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   __shared__ float y[16][T];
   const AppendArgs& ap = ga.ap;
   const int grp = blockIdx.x;
