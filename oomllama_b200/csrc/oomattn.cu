@@ -360,7 +360,7 @@ int launch_rope_append(oomattn_ctx* ctx, const AppendArgs& ap, const SeqBatch& s
 // are ordered by range size, longest first, so that the block scheduler's
 // in-order hand-out of CTAs to free slots is a longest-processing-time list
 // schedule.  t is the best of three candidates -- the smallest t that gives at
-// most 1, 2 or 3 waves of CTAs on the resident slots -- judged by simulating
+// most 1, 2 or 3 waves of CTAs on the resident slots -- scored by simulating
 // that list schedule with kDecodeFillPages pages of fixed cost per CTA
 // (pipeline fill and merge).  Returns the number of items (the grid size).
 constexpr int kDecodeFillPages = 12;     // bf16 cache
