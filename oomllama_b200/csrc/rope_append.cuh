@@ -272,8 +272,8 @@ __global__ void __launch_bounds__(256)
   } else {
     const float* wp0 = reinterpret_cast<const float*>(W) + wrow[0];
     const float* wp1 = reinterpret_cast<const float*>(W) + wrow[1];
-#pragma unroll 4
-    for (int j = lane * 4; j < H; j += 128) {
+#pragma unroll 8
+    for (int j = lane * 4; j < H; j += 128) {  // 16 loads of 16 bytes in flight per lane
       const float4 wa = __ldcs(reinterpret_cast<const float4*>(wp0 + j));
       const float4 wb = __ldcs(reinterpret_cast<const float4*>(wp1 + j));
 #pragma unroll
