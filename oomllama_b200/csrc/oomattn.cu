@@ -1396,8 +1396,9 @@ int q8_run(oomattn_ctx* ctx, const Q8Job* jobs, int n_jobs, const float* x, cons
   for (int t0 = 0; t0 < n_tokens; t0 += group) {
     const int nt = std::min(group, n_tokens - t0);
     if (norm_w) {
-      rmsnorm_prep_x_kernel<<<nt, kNormThreads, 0, ctx->stream>>>(x + (size_t)t0 * cols, norm_w, eps, cols, xh, xl,
-                                                                  xsum, ctx->d_status);
+      const dim3 ngrid(nt, (nchunks + kNormThreads / 32 - 1) / (kNormThreads / 32));
+      rmsnorm_prep_x_kernel<<<ngrid, kNormThreads, 0, ctx->stream>>>(x + (size_t)t0 * cols, norm_w, eps, cols, xh,
+                                                                     xl, xsum, ctx->d_status);
     } else {
       const long long prep_warps = (long long)nt * nchunks;
       q8_prep_x_kernel<<<(unsigned)((prep_warps + 7) / 8), 256, 0, ctx->stream>>>(

@@ -445,10 +445,10 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(const float* __re
   }
 }
 
-// RMSNorm fused into the x split of the linear that reads it: one CTA per
-// token forms the row's sum of squares exactly as rmsnorm_kernel does, then
-// its warps split the normalised row x / sqrt(mean(x^2) + eps) * w chunk by
-// chunk exactly as q8_prep_x_kernel does.  The normalised row itself is not
+// RMSNorm fused into the x split of the linear that reads it: CTAs (token,
+// group of 8 chunks) each form the row's sum of squares exactly as
+// rmsnorm_kernel does, then their warps split the normalised row
+// x / sqrt(mean(x^2) + eps) * w chunk by chunk exactly as q8_prep_x_kernel does.  The normalised row itself is not
 // stored: only the linears read it (src/oomllama.rs:389, :395, :549).
 __global__ void __launch_bounds__(kNormThreads) rmsnorm_prep_x_kernel(const float* __restrict__ x,
                                                                       const float* __restrict__ w, float eps,
@@ -473,7 +473,10 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_prep_x_kernel(const floa
   const float denom = sqrtf(tot / (float)cols + eps);
   const int lane = threadIdx.x & 31;
   const int nchunks = cols / kQ8Chunk;
-  for (int ch = threadIdx.x >> 5; ch < nchunks; ch += kNormThreads / 32) {
+  // blockIdx.y picks this CTA's 8 chunks: every CTA of a token forms the same
+  // sum of squares (read from L2), so a token's split is spread over several SMs
+  for (int ch = blockIdx.y * (kNormThreads / 32) + (threadIdx.x >> 5); ch < nchunks;
+       ch += gridDim.y * (kNormThreads / 32)) {
     const int c = ch * kQ8Chunk + 2 * lane;
     const float2 xv = *reinterpret_cast<const float2*>(xr + c);
     const float2 g = *reinterpret_cast<const float2*>(w + c);
