@@ -1293,7 +1293,7 @@ int ensure_q8_scratch(oomattn_ctx* ctx, size_t bytes, int row_tiles) {
 template <int NT, int MT, int S, bool XA>
 cudaError_t launch_q8_linear(const Q8Args& a, int row_blocks, cudaStream_t st) {
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(a.splits * a.tgroups, row_blocks);
+  cfg.gridDim = dim3(a.splits, row_blocks);
   cfg.blockDim = dim3(kQ8Warps * 32);
   cfg.dynamicSmemBytes = 0;
   cfg.stream = st;
@@ -1340,10 +1340,11 @@ struct Q8Plan {
 Q8Plan plan_q8(const oomattn_ctx* ctx, int rows, int cols, int nt) {
   Q8Plan p;
   const int nchunks = cols / kQ8Chunk;
-  // two row tiles per warp for tall matrices and for large short ones (the down
-  // projection: 25.1 against 26.9 us at one token); a 16-token pass has no
-  // registers left for the second
-  p.mt = (nt == 1 && (rows >= 64 * ctx->num_sms || (long long)rows * cols >= (32ll << 20))) ? 2 : 1;
+  // two row tiles per warp for tall matrices (gate+up at 16 tokens: 57.6
+  // against 66.6 us for two 8-token CTAs per weight tile) and, at one token
+  // tile, for large short ones (the down projection: 25.1 against 26.9 us at
+  // one token; at 16 tokens it halves the CTAs for no gain)
+  p.mt = (rows >= 64 * ctx->num_sms || (nt == 1 && (long long)rows * cols >= (32ll << 20))) ? 2 : 1;
   p.row_blocks = (rows + 16 * p.mt - 1) / (16 * p.mt);
   const int want = std::max(1, (ctx->num_sms + p.row_blocks - 1) / p.row_blocks);
   p.splits = std::max(1, std::min(want, nchunks / kQ8Warps));
@@ -1376,11 +1377,11 @@ int q8_run(oomattn_ctx* ctx, const Q8Job* jobs, int n_jobs, const float* x, cons
   size_t part_floats = 0;
   int max_blocks = 1;
   for (int nt = 1; nt <= 2; ++nt) {
-    const Q8Plan p = plan_q8(ctx, total_rows, cols, (nt == 2 && total_rows >= 64 * ctx->num_sms) ? 1 : nt);
+    const Q8Plan p = plan_q8(ctx, total_rows, cols, nt);
     int blocks = 0;
     for (int j = 0; j < n_jobs; ++j) blocks += (jobs[j].w->rows + 16 * p.mt - 1) / (16 * p.mt);
     part_floats = std::max(part_floats, (size_t)p.splits * 8 * nt * total_rows);
-    max_blocks = std::max(max_blocks, blocks * nt);
+    max_blocks = std::max(max_blocks, blocks);
   }
   if (n_tokens == 0) return OOMATTN_OK;
   const int group = 16;
@@ -1406,12 +1407,7 @@ int q8_run(oomattn_ctx* ctx, const Q8Job* jobs, int n_jobs, const float* x, cons
     }
     CKLAUNCH();
     const int ntiles = nt > 8 ? 2 : 1;
-    // 16 tokens: for tall matrices (gate+up: 67.2 against 72.2 us) two 8-token CTAs per weight tile,
-    // adjacent in launch order so the second read of each weight byte hits L2; otherwise one CTA
-    // with two token tiles (faster for the shorter matrices)
-    const int tgroups = (ntiles == 2 && total_rows >= 64 * ctx->num_sms) ? 2 : 1;
-    const int nt_kernel = tgroups == 2 ? 1 : ntiles;
-    const Q8Plan p = plan_q8(ctx, total_rows, cols, nt_kernel);
+    const Q8Plan p = plan_q8(ctx, total_rows, cols, ntiles);
     Q8Args a;
     memset(&a, 0, sizeof(a));
     a.n_mats = n_jobs;
@@ -1423,7 +1419,6 @@ int q8_run(oomattn_ctx* ctx, const Q8Job* jobs, int n_jobs, const float* x, cons
     a.counters = ctx->d_q8_counters;
     a.splits = p.splits;
     a.chunks_per_split = p.cps;
-    a.tgroups = tgroups;
     a.status = ctx->d_status;
     int blocks = 0;
     size_t row_prefix = 0;
@@ -1438,12 +1433,14 @@ int q8_run(oomattn_ctx* ctx, const Q8Job* jobs, int n_jobs, const float* x, cons
       m.bias = jobs[j].bias;
       m.residual = jobs[j].residual ? jobs[j].residual + (size_t)t0 * w->rows : nullptr;
       m.y = jobs[j].y + (size_t)t0 * w->rows;
-      m.part = part + (size_t)p.splits * 8 * ntiles * row_prefix;  // [splits][token groups][8 NT][rows]
+      m.part = part + (size_t)p.splits * 8 * ntiles * row_prefix;  // [splits][8 NT][rows]
       blocks += (w->rows + 16 * p.mt - 1) / (16 * p.mt);
       row_prefix += w->rows;
     }
-    // one token tile: x read a chunk ahead; two: a 3-deep weight ring, x read at use
-    const cudaError_t le = nt_kernel == 2 ? launch_q8_linear<2, 1, 3, false>(a, blocks, ctx->stream)
+    // one token tile: x read a chunk ahead; two: x read at use, with a 3-deep
+    // weight ring for one row tile and a 2-deep one for two
+    const cudaError_t le = ntiles == 2 ? (p.mt == 2 ? launch_q8_linear<2, 2, 2, false>(a, blocks, ctx->stream)
+                                                    : launch_q8_linear<2, 1, 3, false>(a, blocks, ctx->stream))
                            : p.mt == 2 ? launch_q8_linear<1, 2, 2, true>(a, blocks, ctx->stream)
                                        : launch_q8_linear<1, 1, 2, true>(a, blocks, ctx->stream);
     if (le != cudaSuccess) return fail(ctx, OOMATTN_ERR_CUDA, "q8_linear launch: %s", cudaGetErrorString(le));

@@ -63,10 +63,9 @@ struct Q8Args {
   const uint32_t* xl;   // [n_tokens][cols / 2] fp16 pairs: x - hi rounded to fp16
   const float* xsum;    // [n_tokens][cols / 64]
   int n_tokens;
-  unsigned* counters;   // [row blocks][tgroups]: arrivals, zero between launches
+  unsigned* counters;   // [row blocks]: arrivals, zero between launches
   int splits;
   int chunks_per_split;
-  int tgroups;          // 8-token groups of the pass, each its own CTA over the same weights
   int* status;
 };
 
@@ -251,6 +250,7 @@ __device__ __forceinline__ void q8_load_x(const Q8Base<NT, MT>& b, int ch, Q8X<N
 
 template <int NT, int MT>
 __device__ __forceinline__ void q8_compute_chunk(const Q8W<MT>& w, const Q8X<NT>& d, float (&acc)[MT][NT][4]) {
+  constexpr bool kOneChain = NT * MT >= 4;
 #pragma unroll
   for (int m = 0; m < MT; ++m) {
     // A fragments of the 4 k-steps: step s takes bytes 4s..4s+3 of the thread's 16
@@ -267,12 +267,15 @@ __device__ __forceinline__ void q8_compute_chunk(const Q8W<MT>& w, const Q8X<NT>
     const float ka = w.ma[m] - 1024.f * w.sa[m], kb = w.mb[m] - 1024.f * w.sb[m];
 #pragma unroll
     for (int n = 0; n < NT; ++n) {
-      // hi and lo products accumulate in two independent chains
+      // hi and lo products accumulate in two independent chains, or, with four
+      // or more (row tile, token tile) pairs, in one: the pairs already give
+      // independent MMAs, and the registers go to the weight ring
       float dh[4] = {0.f, 0.f, 0.f, 0.f}, dl[4] = {0.f, 0.f, 0.f, 0.f};
+      float(&dlo)[4] = kOneChain ? dh : dl;
 #pragma unroll
       for (int s = 0; s < 4; ++s) {
         mma_f16_16816(dh, af[s][0], af[s][1], af[s][2], af[s][3], d.bh[n][2 * s], d.bh[n][2 * s + 1]);
-        mma_f16_16816(dl, af[s][0], af[s][1], af[s][2], af[s][3], d.bl[n][2 * s], d.bl[n][2 * s + 1]);
+        mma_f16_16816(dlo, af[s][0], af[s][1], af[s][2], af[s][3], d.bl[n][2 * s], d.bl[n][2 * s + 1]);
       }
       // rows g, g + 8 x tokens 8n + 2c, 8n + 2c + 1
       acc[m][n][0] = fmaf(w.sa[m], dh[0] + dl[0], fmaf(ka, d.x0[n], acc[m][n][0]));
@@ -297,17 +300,8 @@ __global__ void __launch_bounds__(kQ8Warps * 32, 2) q8_linear_kernel(const Q8Arg
   __shared__ int s_last;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, c = lane & 3;
-  Q8View a = q8_view(args, blockIdx.y);
-  // token group tg of the pass: the groups of a weight tile are adjacent CTAs,
-  // so the second read of each weight byte is an L2 hit
-  const int tg = blockIdx.x % args.tgroups, sp = blockIdx.x / args.tgroups;
-  const int tok0 = 8 * NT * tg;
-  a.n_tokens = min(8 * NT, a.n_tokens - tok0);
-  a.y += (size_t)tok0 * a.rows;
-  if (a.residual) a.residual += (size_t)tok0 * a.rows;
-  const uint32_t* xh0 = args.xh + (size_t)tok0 * (a.cols / 2);
-  const float* xsum0 = args.xsum + (size_t)tok0 * (a.cols / kQ8Chunk);
-  const unsigned cidx = blockIdx.y * args.tgroups + tg;
+  const Q8View a = q8_view(args, blockIdx.y);
+  const int sp = blockIdx.x;
   const int rb = a.rb;
   const int row0 = rb * 16 * MT;
   const int nchunks = a.cols / kQ8Chunk;
@@ -325,8 +319,8 @@ __global__ void __launch_bounds__(kQ8Warps * 32, 2) q8_linear_kernel(const Q8Arg
 #pragma unroll
   for (int n = 0; n < NT; ++n) {
     const int tok = 8 * n + g, t0 = 8 * n + 2 * c;
-    b.xh[n] = tok < a.n_tokens ? xh0 + (size_t)tok * (a.cols / 2) + 8 * c : nullptr;
-    b.xs0[n] = xsum0 + (size_t)t0 * nchunks;
+    b.xh[n] = tok < a.n_tokens ? args.xh + (size_t)tok * (a.cols / 2) + 8 * c : nullptr;
+    b.xs0[n] = args.xsum + (size_t)t0 * nchunks;
     b.has0[n] = t0 < a.n_tokens;
     b.has1[n] = t0 + 1 < a.n_tokens;
   }
@@ -376,7 +370,7 @@ __global__ void __launch_bounds__(kQ8Warps * 32, 2) q8_linear_kernel(const Q8Arg
   __syncthreads();
   const int tp = 8 * NT;
   const int rows_cta = 16 * MT;
-  float* part = a.part + ((size_t)sp * args.tgroups + tg) * tp * a.rows;
+  float* part = a.part + (size_t)sp * tp * a.rows;
   for (int i = threadIdx.x; i < MT * NT * 128; i += blockDim.x) {
     const int m = i / (NT * 128), n = (i / 128) % NT, e = (i / 32) & 3, l = i & 31;
     float v = 0.f;
@@ -395,7 +389,7 @@ __global__ void __launch_bounds__(kQ8Warps * 32, 2) q8_linear_kernel(const Q8Arg
   __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) {
-    const unsigned prev = atomicAdd(&args.counters[cidx], 1u);
+    const unsigned prev = atomicAdd(&args.counters[blockIdx.y], 1u);
     s_last = (prev == (unsigned)a.splits - 1);
   }
   __syncthreads();
@@ -406,10 +400,10 @@ __global__ void __launch_bounds__(kQ8Warps * 32, 2) q8_linear_kernel(const Q8Arg
     if (row >= a.rows) continue;
     float v = 0.f;
     for (int s = 0; s < a.splits; ++s)
-      v += __ldcg(a.part + (((size_t)s * args.tgroups + tg) * tp + tok) * a.rows + row);
+      v += __ldcg(a.part + ((size_t)s * tp + tok) * a.rows + row);
     a.y[(size_t)tok * a.rows + row] = q8_epilogue(a, tok, row, v);
   }
-  if (threadIdx.x == 0) args.counters[cidx] = 0;
+  if (threadIdx.x == 0) args.counters[blockIdx.y] = 0;
 }
 
 // ------------------------------------------------------------------ RMSNorm

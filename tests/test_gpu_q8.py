@@ -55,8 +55,9 @@ def test_q8_linear_golden(eng):
 
 
 @pytest.mark.parametrize("rows,cols,T", [(16, 64, 1), (64, 256, 3), (128, 320, 8), (48, 704, 9), (96, 512, 17),
-                                         (32, 128, 70)])
+                                         (32, 128, 70), (9488, 128, 13)])
 def test_q8_linear_small(oracle, eng, rows, cols, T):
+    # 9488 rows: a tall matrix (two row tiles per warp) whose last 32-row block is half outside it
     out, ref = _case(oracle, eng, rows, cols, T, seed=rows * 1000 + cols + T)
     assert_close(out, ref, F32_ATOL, what=f"q8 {rows}x{cols} T={T}")
 
