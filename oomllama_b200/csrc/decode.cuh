@@ -101,15 +101,26 @@ __device__ __forceinline__ void combine_and_store(const MergeSmem& ms, const Dec
   consumer_bar();
   if (!*s_last) return;
   __threadfence();
+  // every (q head, split) lse in one round of loads, staged over the per-warp
+  // O area (its last reader passed the barriers above); then each thread's
+  // partial O loads run several splits ahead
+  float* lse_s = const_cast<float*>(&ms.o[0][0][0]);  // [kMaxGroup][nsplit]
+  for (int i = tid; i < a.group * nsplit; i += kDecWarps * 32) {
+    const int jj = i / nsplit, s = i - jj * nsplit;
+    lse_s[i] = __ldcg(a.part_lse + ((size_t)z * a.n_heads + g * a.group + jj) * a.max_splits + s);
+  }
+  consumer_bar();
   if (active) {
     const size_t prow0 = ((size_t)z * a.n_heads + h) * a.max_splits;
+    const float* ls_j = lse_s + j * nsplit;
     float M = -INFINITY;
-    for (int s = 0; s < nsplit; ++s) M = fmaxf(M, __ldcg(a.part_lse + prow0 + s));
+    for (int s = 0; s < nsplit; ++s) M = fmaxf(M, ls_j[s]);
     float wsum = 0.f;
 #pragma unroll
     for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+#pragma unroll 4
     for (int s = 0; s < nsplit; ++s) {
-      const float ls = __ldcg(a.part_lse + prow0 + s);
+      const float ls = ls_j[s];
       const float wt = (ls == -INFINITY) ? 0.f : exp2f(ls - M);
       wsum += wt;
       const float4* pp = reinterpret_cast<const float4*>(a.part_o + (prow0 + s) * kHeadDim + d0);

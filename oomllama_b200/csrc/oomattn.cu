@@ -28,7 +28,15 @@ using namespace oomattn;
 
 namespace {
 
-constexpr int kMaxSplits = 32;                        // split-KV partials per (row, q head)
+// Split-KV partials per (row, q head).  f32 caches: up to 64, a one-page split
+// per CTA up to 1024 cached tokens (C1 f32 decode: 10.9 us at 33 splits, 12.3
+// at 17).  bf16 caches keep 32: one row of 2048 tokens ran 2.8 us slower per
+// layer step at 43 splits than at 26.
+constexpr int kMaxSplits = 64;
+constexpr int kMaxSplitsBf16 = 32;
+int split_cap(int kv_dtype) { return kv_dtype == OOMATTN_DTYPE_BF16 ? kMaxSplitsBf16 : kMaxSplits; }
+static_assert(kMaxGroup * kMaxSplits <= kDecWarps * kMaxGroup * kMergeStride,
+              "the decode merge stages [group][splits] lse values over the per-warp O area");
 constexpr unsigned long long kDefaultTimeoutNs = 2000000000ull;  // bounded device waits: 2 s
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -469,7 +477,7 @@ int launch_decode_rows(oomattn_ctx* ctx, int layer, const SeqBatch& sb, const fl
   key[0] = sb.n;
   for (int z = 0; z < sb.n; ++z) key[z + 1] = sb.len[z] > 0 ? (sb.len[z] + kPageSize - 1) / kPageSize : 0;
   if (ctx->sched_key.size() != (size_t)sb.n + 1 || !std::equal(key, key + sb.n + 1, ctx->sched_key.begin())) {
-    ctx->sched_items = plan_decode(sb, n_kv, slots, kMaxSplits,
+    ctx->sched_items = plan_decode(sb, n_kv, slots, split_cap(ctx->cfg.kv_dtype),
                                    ctx->cfg.kv_dtype == OOMATTN_DTYPE_BF16 ? kDecodeFillPages : kDecodeFillPagesF32,
                                    ctx->sched);
     ctx->sched_key.assign(key, key + sb.n + 1);
@@ -484,7 +492,7 @@ int launch_decode_rows(oomattn_ctx* ctx, int layer, const SeqBatch& sb, const fl
   a.layer = layer;
   a.n_heads = ctx->cfg.n_heads;
   a.group = ctx->group;
-  a.max_splits = kMaxSplits;
+  a.max_splits = split_cap(ctx->cfg.kv_dtype);
   a.qscale = ctx->scale * 1.4426950408889634f;
   a.part_o = ctx->d_part_o;
   a.part_lse = ctx->d_part_lse;
@@ -572,7 +580,7 @@ int oomattn_create(const oomattn_config* cfg, int device, void* stream, oomattn_
   if (cudaMemcpy(ctx->d_cos, ctx->h_cos.data(), tab, cudaMemcpyHostToDevice) != cudaSuccess ||
       cudaMemcpy(ctx->d_sin, ctx->h_sin.data(), tab, cudaMemcpyHostToDevice) != cudaSuccess)
     return bail(OOMATTN_ERR_CUDA);
-  const size_t parts = (size_t)kMaxBatch * c.n_heads * kMaxSplits;
+  const size_t parts = (size_t)kMaxBatch * c.n_heads * split_cap(c.kv_dtype);
   if (cudaMalloc(&ctx->d_part_o, parts * kHeadDim * sizeof(float)) != cudaSuccess ||
       cudaMalloc(&ctx->d_part_lse, parts * sizeof(float)) != cudaSuccess ||
       cudaMalloc(&ctx->d_counters, (size_t)kMaxBatch * c.n_kv_heads * sizeof(unsigned)) != cudaSuccess ||
@@ -1163,7 +1171,7 @@ extern "C" int oomattn_decode_static_scratch(int device, void* stream, int32_t k
 
   // Split plan as in oomattn_decode, capped so that every (row, q head, split)
   // partial fits the static array: nsplit <= slots / (rows * heads).
-  const int cap_splits = std::max(1, std::min(kMaxSplits, kStaticPartSlots / (n_rows * n_heads)));
+  const int cap_splits = std::max(1, std::min(split_cap(kv_dtype), kStaticPartSlots / (n_rows * n_heads)));
   DecodeSched sched;
   const int n_items = plan_decode(sb, n_kv_heads, num_sms * (kv_dtype == OOMATTN_DTYPE_BF16 ? 2 : 3), cap_splits,
                                   kv_dtype == OOMATTN_DTYPE_BF16 ? kDecodeFillPages : kDecodeFillPagesF32, sched);
