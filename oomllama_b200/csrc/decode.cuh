@@ -103,7 +103,7 @@ __device__ __forceinline__ void combine_and_store(const MergeSmem& ms, const Dec
   __threadfence();
   // every (q head, split) lse in one round of loads, staged over the per-warp
   // O area (its last reader passed the barriers above); then each thread's
-  // partial O loads run several splits ahead
+  // partial O loads run eight splits ahead
   float* lse_s = const_cast<float*>(&ms.o[0][0][0]);  // [kMaxGroup][nsplit]
   for (int i = tid; i < a.group * nsplit; i += kDecWarps * 32) {
     const int jj = i / nsplit, s = i - jj * nsplit;
@@ -118,7 +118,7 @@ __device__ __forceinline__ void combine_and_store(const MergeSmem& ms, const Dec
     float wsum = 0.f;
 #pragma unroll
     for (int i = 0; i < 8; ++i) acc[i] = 0.f;
-#pragma unroll 4
+#pragma unroll 8
     for (int s = 0; s < nsplit; ++s) {
       const float ls = ls_j[s];
       const float wt = (ls == -INFINITY) ? 0.f : exp2f(ls - M);
@@ -196,6 +196,9 @@ __global__ void __launch_bounds__((kDecWarps + 1) * 32, 2)
     decode_bf16_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
                        const KVPool pool, const DecodeArgs a, const __grid_constant__ SeqBatch sb,
                        const __grid_constant__ DecodeSched sched) {
+  // a programmatic dependent (the next layer's QKV GEMV) may launch now; it
+  // waits for this grid before it reads or writes anything
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kDecStages * kDecStageBytes);
@@ -364,6 +367,7 @@ __global__ void __launch_bounds__((kDecWarps + 1) * 32, 2)
 __global__ void __launch_bounds__(kDecWarps * 32)
     decode_f32_kernel(const KVPool pool, const DecodeArgs a, const __grid_constant__ SeqBatch sb,
                       const __grid_constant__ DecodeSched sched) {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");  // as in decode_bf16_kernel
   __shared__ MergeSmem ms;
   __shared__ int s_last;
   const DecodeItem item = decode_item(sched, sb, blockIdx.x);

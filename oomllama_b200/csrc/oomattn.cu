@@ -525,6 +525,24 @@ int launch_decode_rows(oomattn_ctx* ctx, int layer, const SeqBatch& sb, const fl
 
 }  // namespace
 
+namespace {
+// The GEMV is a programmatic dependent of the kernel before it: it launches
+// during that kernel's tail and waits (griddepcontrol.wait) before reading x.
+template <int T, bool WBF16>
+cudaError_t launch_gemv(const GemvArgs& ga, const KVPool& pool, const SeqBatch& sb, int grid, cudaStream_t st) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(256);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, qkv_gemv_rope_append_kernel<T, WBF16>, ga, pool, sb);
+}
+}  // namespace
+
 extern "C" {
 
 const char* oomattn_version(void) { return "oomattn 0.1 (sm_100a)"; }
@@ -851,11 +869,10 @@ int oomattn_qkv_rope_append(oomattn_ctx* ctx, int32_t layer, int32_t n_seqs, con
     KVPool pool = make_pool(ctx);
 #define OOMATTN_GEMV_CASE(TT)                                                                          \
   case TT:                                                                                             \
-    if (ga.w_bf16)                                                                                     \
-      qkv_gemv_rope_append_kernel<TT, true><<<grid, 256, 0, ctx->stream>>>(ga, pool, sb);              \
-    else                                                                                               \
-      qkv_gemv_rope_append_kernel<TT, false><<<grid, 256, 0, ctx->stream>>>(ga, pool, sb);             \
+    le = ga.w_bf16 ? launch_gemv<TT, true>(ga, pool, sb, grid, ctx->stream)                            \
+                   : launch_gemv<TT, false>(ga, pool, sb, grid, ctx->stream);                          \
     break;
+    cudaError_t le = cudaSuccess;
     switch ((int)T) {
       OOMATTN_GEMV_CASE(1)
       OOMATTN_GEMV_CASE(2)
@@ -875,7 +892,7 @@ int oomattn_qkv_rope_append(oomattn_ctx* ctx, int32_t layer, int32_t n_seqs, con
       OOMATTN_GEMV_CASE(16)
     }
 #undef OOMATTN_GEMV_CASE
-    CKLAUNCH();
+    if (le != cudaSuccess) return fail(ctx, OOMATTN_ERR_CUDA, "qkv gemv launch: %s", cudaGetErrorString(le));
     commit_append(ctx, layer, sb, n_new);
     return OOMATTN_OK;
   }
