@@ -615,7 +615,11 @@ int oomattn_create(const oomattn_config* cfg, int device, void* stream, oomattn_
   if (cudaFuncSetAttribute(decode_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kDecSmemBytes) !=
           cudaSuccess ||
       cudaFuncSetAttribute(prefill_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kPfSmemBytes) !=
-          cudaSuccess)
+          cudaSuccess ||
+      cudaFuncSetAttribute(q8_linear_xs_kernel<2, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)q8_xs_smem_bytes(kQ8XsMaxChunks)) != cudaSuccess ||
+      cudaFuncSetAttribute(q8_linear_xs_kernel<1, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)q8_xs_smem_bytes(kQ8XsMaxChunks)) != cudaSuccess)
     return bail(OOMATTN_ERR_CUDA);
   cudaFuncAttributes fa;
   if (cudaFuncGetAttributes(&fa, prefill_bf16_kernel) != cudaSuccess) return bail(OOMATTN_ERR_CUDA);
@@ -1378,6 +1382,57 @@ Q8Plan plan_q8(const oomattn_ctx* ctx, int rows, int cols, int nt) {
   return p;
 }
 
+// 16-token form with x staged in shared memory (q8_linear_xs_kernel): for
+// matrices of at least 32 M weights, one CTA per SM over a row group of 256 * MT
+// rows and a column range of 8 to kQ8XsMaxChunks chunks.  MT = 2 (2-deep
+// weight ring) or MT = 1 (4-deep ring), and the ranges, minimise
+// waves x (MT x chunks per range + kQ8XsFixed), a fixed cost for staging x,
+// filling the ring and the merge in units of 256 rows x one chunk; ties go to
+// fewer ranges, then to MT = 1.  Measured at 16 tokens (Qwen2.5-7B shapes,
+// us): gate+up MT 2: 51.2 (MT 1: 57.0), gate MT 1: 29.2 (33.6), down MT 1: 35.6
+// (43.6), LM head MT 2: 206 (213); deeper rings for MT = 2 spill and lose.
+constexpr int kQ8XsFixed = 8;
+struct Q8XsPlan {
+  int mt, groups, splits, cps;
+};
+bool use_q8_xs(int ntiles, int total_rows, int cols) {
+  return ntiles == 2 && (long long)total_rows * cols >= (32ll << 20) && cols / kQ8Chunk >= 8;
+}
+Q8XsPlan plan_q8_xs(const oomattn_ctx* ctx, const Q8Job* jobs, int n_jobs, int nchunks) {
+  Q8XsPlan best{1, 0, 1, nchunks};
+  long long best_cost = -1;
+  for (int mt = 2; mt >= 1; --mt) {
+    int groups = 0;
+    for (int j = 0; j < n_jobs; ++j) groups += (jobs[j].w->rows + 256 * mt - 1) / (256 * mt);
+    for (int s = (nchunks + kQ8XsMaxChunks - 1) / kQ8XsMaxChunks; s <= std::max(1, nchunks / 8); ++s) {
+      const int cps = (nchunks + s - 1) / s;
+      const int splits = (nchunks + cps - 1) / cps;
+      const long long waves = ((long long)groups * splits + ctx->num_sms - 1) / ctx->num_sms;
+      const long long cost = waves * (mt * cps + kQ8XsFixed);
+      if (best_cost < 0 || cost < best_cost || (cost == best_cost && mt < best.mt)) {
+        best_cost = cost;
+        best = {mt, groups, splits, cps};
+      }
+    }
+  }
+  return best;
+}
+
+template <int MT, int S>
+cudaError_t launch_q8_linear_xs(const Q8Args& a, int groups, cudaStream_t st) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(a.splits, groups);
+  cfg.blockDim = dim3(kQ8XsWarps * 32);
+  cfg.dynamicSmemBytes = q8_xs_smem_bytes(a.chunks_per_split);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, q8_linear_xs_kernel<MT, S>, a);
+}
+
 // Runs every job (up to kQ8MaxMats, all of the same width) on the same input:
 // x, or silu(x) * up when `up` is given.  Tokens run in passes of up to 16
 // (two MMA token tiles; each weight byte is read once per pass): one x split
@@ -1407,6 +1462,11 @@ int q8_run(oomattn_ctx* ctx, const Q8Job* jobs, int n_jobs, const float* x, cons
     for (int j = 0; j < n_jobs; ++j) blocks += (jobs[j].w->rows + 16 * p.mt - 1) / (16 * p.mt);
     part_floats = std::max(part_floats, (size_t)p.splits * 8 * nt * total_rows);
     max_blocks = std::max(max_blocks, blocks);
+    if (use_q8_xs(nt, total_rows, cols)) {
+      const Q8XsPlan xp = plan_q8_xs(ctx, jobs, n_jobs, cols / kQ8Chunk);
+      part_floats = std::max(part_floats, (size_t)xp.splits * 8 * nt * total_rows);
+      max_blocks = std::max(max_blocks, xp.groups);
+    }
   }
   if (n_tokens == 0) return OOMATTN_OK;
   const int group = 16;
@@ -1432,7 +1492,10 @@ int q8_run(oomattn_ctx* ctx, const Q8Job* jobs, int n_jobs, const float* x, cons
     }
     CKLAUNCH();
     const int ntiles = nt > 8 ? 2 : 1;
+    const bool xs = use_q8_xs(ntiles, total_rows, cols);
     const Q8Plan p = plan_q8(ctx, total_rows, cols, ntiles);
+    const Q8XsPlan xp = xs ? plan_q8_xs(ctx, jobs, n_jobs, nchunks) : Q8XsPlan{p.mt, 0, p.splits, p.cps};
+    const int rows_per_block = xs ? 256 * xp.mt : 16 * p.mt;
     Q8Args a;
     memset(&a, 0, sizeof(a));
     a.n_mats = n_jobs;
@@ -1442,8 +1505,8 @@ int q8_run(oomattn_ctx* ctx, const Q8Job* jobs, int n_jobs, const float* x, cons
     a.xsum = xsum;
     a.n_tokens = nt;
     a.counters = ctx->d_q8_counters;
-    a.splits = p.splits;
-    a.chunks_per_split = p.cps;
+    a.splits = xp.splits;
+    a.chunks_per_split = xp.cps;
     a.status = ctx->d_status;
     int blocks = 0;
     size_t row_prefix = 0;
@@ -1458,13 +1521,15 @@ int q8_run(oomattn_ctx* ctx, const Q8Job* jobs, int n_jobs, const float* x, cons
       m.bias = jobs[j].bias;
       m.residual = jobs[j].residual ? jobs[j].residual + (size_t)t0 * w->rows : nullptr;
       m.y = jobs[j].y + (size_t)t0 * w->rows;
-      m.part = part + (size_t)p.splits * 8 * ntiles * row_prefix;  // [splits][8 NT][rows]
-      blocks += (w->rows + 16 * p.mt - 1) / (16 * p.mt);
+      m.part = part + (size_t)xp.splits * 8 * ntiles * row_prefix;  // [splits][8 NT][rows]
+      blocks += (w->rows + rows_per_block - 1) / rows_per_block;
       row_prefix += w->rows;
     }
     // one token tile: x read a chunk ahead; two: x read at use, with a 3-deep
     // weight ring for one row tile and a 2-deep one for two
-    const cudaError_t le = ntiles == 2 ? (p.mt == 2 ? launch_q8_linear<2, 2, 2, false>(a, blocks, ctx->stream)
+    const cudaError_t le = xs ? (xp.mt == 2 ? launch_q8_linear_xs<2, 2>(a, blocks, ctx->stream)
+                                            : launch_q8_linear_xs<1, 4>(a, blocks, ctx->stream))
+                           : ntiles == 2 ? (p.mt == 2 ? launch_q8_linear<2, 2, 2, false>(a, blocks, ctx->stream)
                                                     : launch_q8_linear<2, 1, 3, false>(a, blocks, ctx->stream))
                            : p.mt == 2 ? launch_q8_linear<1, 2, 2, true>(a, blocks, ctx->stream)
                                        : launch_q8_linear<1, 1, 2, true>(a, blocks, ctx->stream);

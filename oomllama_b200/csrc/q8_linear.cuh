@@ -406,6 +406,154 @@ __global__ void __launch_bounds__(kQ8Warps * 32, 2) q8_linear_kernel(const Q8Arg
   if (threadIdx.x == 0) args.counters[blockIdx.y] = 0;
 }
 
+// ------------------------------------------------- 16 tokens, x in shared memory
+// Form for 9..16 tokens on large matrices.  At 16 tokens the x fragments of a
+// chunk (16 tokens x 64 columns as fp16 hi + lo: 4 KB) outweigh the chunk's
+// weight bytes per warp (1-2 KB), and in the form above every CTA re-reads its
+// whole column range of x from L2.  Here a CTA of 16 warps (one per SM, all
+// 64K registers) owns 16 * 16 * MT rows and one column range: it stages the
+// range's x hi / lo words and chunk sums in shared memory once, then each warp
+// streams its own 16 * MT rows across the range with an S-deep weight ring,
+// reading x fragments from shared memory.  Token rows are padded to 4 words
+// past a multiple of 32 so that the 16-byte fragment loads of a warp's 8
+// tokens fall in distinct banks.  Each warp owns its rows, so there is no
+// reduction across warps; CTAs of other column ranges merge through the
+// split-K partial buffer in split order, as above.
+constexpr int kQ8XsWarps = 16;
+constexpr int kQ8XsMaxChunks = 48;  // columns per range: 48 x 64 (x staging: 48 x 64 x 16 tokens x 4 B = 192 KB)
+
+__host__ __device__ constexpr int q8_xs_stride(int cps) { return cps * 32 + 4; }  // words per token row
+__host__ __device__ constexpr size_t q8_xs_smem_bytes(int cps) {
+  return ((size_t)32 * q8_xs_stride(cps) + (size_t)16 * (cps + 1)) * 4;
+}
+
+template <int MT, int S>
+__global__ void __launch_bounds__(kQ8XsWarps * 32, 1) q8_linear_xs_kernel(const Q8Args args) {
+  constexpr int NT = 2;
+  extern __shared__ __align__(16) uint32_t xs[];
+  __shared__ int s_last;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, c = lane & 3;
+  const Q8View a = q8_view(args, blockIdx.y);
+  const int nchunks = a.cols / kQ8Chunk;
+  const int cps = args.chunks_per_split;
+  const int sp = blockIdx.x;
+  const int c0 = sp * cps, c1 = min(nchunks, c0 + cps);
+  const int stride = q8_xs_stride(cps);
+  uint32_t* xs_h = xs;
+  uint32_t* xs_l = xs + 16 * stride;
+  float* xs_s = reinterpret_cast<float*>(xs + 32 * stride);  // [16][cps + 1]
+  const int rows_cta = kQ8XsWarps * 16 * MT;
+  const int row0 = a.rb * rows_cta + warp * 16 * MT;
+
+  Q8Base<NT, MT> b;
+  b.row8 = 8LL * a.cols;
+#pragma unroll
+  for (int m = 0; m < MT; ++m) {
+    b.live[m] = row0 + 16 * m < a.rows;
+    b.fa[m] = (long long)(row0 + 16 * m + g) * a.cols + 16 * c;
+  }
+  Q8W<MT> w[S];
+  int ch = c0;
+  // the first S - 1 chunks' weights do not depend on the x split
+#pragma unroll
+  for (int s = 0; s < S - 1; ++s)
+    if (ch + s < c1) q8_load_w<NT, MT>(a, b, ch + s, w[s]);
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  // stage the range's x: 16 token rows of hi and lo words (zero past n_tokens)
+  // and their chunk sums
+  {
+    const int q4 = (c1 - c0) * 8;  // 16-byte words per token row
+    const size_t xrow = (size_t)a.cols / 2;
+    for (int i = threadIdx.x; i < 16 * q4; i += blockDim.x) {
+      const int t = i / q4, k = (i - t * q4) * 4;
+      uint4 h = make_uint4(0, 0, 0, 0), l = make_uint4(0, 0, 0, 0);
+      if (t < a.n_tokens) {
+        h = __ldg(reinterpret_cast<const uint4*>(args.xh + t * xrow + (size_t)c0 * 32 + k));
+        l = __ldg(reinterpret_cast<const uint4*>(args.xl + t * xrow + (size_t)c0 * 32 + k));
+      }
+      *reinterpret_cast<uint4*>(xs_h + t * stride + k) = h;
+      *reinterpret_cast<uint4*>(xs_l + t * stride + k) = l;
+    }
+    for (int i = threadIdx.x; i < 16 * (c1 - c0); i += blockDim.x) {
+      const int t = i / (c1 - c0), k = i - t * (c1 - c0);
+      xs_s[t * (cps + 1) + k] = t < a.n_tokens ? __ldg(args.xsum + (size_t)t * nchunks + c0 + k) : 0.f;
+    }
+  }
+  __syncthreads();
+
+  float acc[MT][NT][4];
+#pragma unroll
+  for (int m = 0; m < MT; ++m)
+#pragma unroll
+    for (int n = 0; n < NT; ++n)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[m][n][e] = 0.f;
+  while (ch < c1) {
+#pragma unroll
+    for (int s = 0; s < S; ++s) {
+      if (ch >= c1) break;
+      const int nx = ch + S - 1;
+      if (nx < c1) q8_load_w<NT, MT>(a, b, nx, w[(s + S - 1) % S]);
+      const int cl = ch - c0;
+      Q8X<NT> xf;
+#pragma unroll
+      for (int n = 0; n < NT; ++n) {
+        const uint32_t* ph = xs_h + (8 * n + g) * stride + cl * 32 + 8 * c;
+        const uint32_t* pl = xs_l + (8 * n + g) * stride + cl * 32 + 8 * c;
+        const uint4 h0 = *reinterpret_cast<const uint4*>(ph), h1 = *reinterpret_cast<const uint4*>(ph + 4);
+        const uint4 l0 = *reinterpret_cast<const uint4*>(pl), l1 = *reinterpret_cast<const uint4*>(pl + 4);
+        xf.bh[n][0] = h0.x; xf.bh[n][1] = h0.y; xf.bh[n][2] = h0.z; xf.bh[n][3] = h0.w;
+        xf.bh[n][4] = h1.x; xf.bh[n][5] = h1.y; xf.bh[n][6] = h1.z; xf.bh[n][7] = h1.w;
+        xf.bl[n][0] = l0.x; xf.bl[n][1] = l0.y; xf.bl[n][2] = l0.z; xf.bl[n][3] = l0.w;
+        xf.bl[n][4] = l1.x; xf.bl[n][5] = l1.y; xf.bl[n][6] = l1.z; xf.bl[n][7] = l1.w;
+        xf.x0[n] = xs_s[(8 * n + 2 * c) * (cps + 1) + cl];
+        xf.x1[n] = xs_s[(8 * n + 2 * c + 1) * (cps + 1) + cl];
+      }
+      q8_compute_chunk<NT, MT>(w[s], xf, acc);
+      ++ch;
+    }
+  }
+
+  // each warp owns its rows: write y, or this range's partial sums
+  const int tp = 8 * NT;
+  float* part = a.part + (size_t)sp * tp * a.rows;
+#pragma unroll
+  for (int m = 0; m < MT; ++m)
+#pragma unroll
+    for (int n = 0; n < NT; ++n)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int row = row0 + 16 * m + g + ((e & 2) ? 8 : 0);
+        const int tok = 8 * n + 2 * c + (e & 1);
+        if (row >= a.rows || tok >= a.n_tokens) continue;
+        if (a.splits == 1)
+          a.y[(size_t)tok * a.rows + row] = q8_epilogue(a, tok, row, acc[m][n][e]);
+        else
+          part[(size_t)tok * a.rows + row] = acc[m][n][e];
+      }
+  if (a.splits == 1) return;
+  // the last CTA of this row group sums the ranges in order
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const unsigned prev = atomicAdd(&args.counters[blockIdx.y], 1u);
+    s_last = (prev == (unsigned)a.splits - 1);
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  const int rg0 = a.rb * rows_cta;
+  for (int i = threadIdx.x; i < rows_cta * a.n_tokens; i += blockDim.x) {
+    const int tok = i / rows_cta, row = rg0 + i % rows_cta;
+    if (row >= a.rows) continue;
+    float v = 0.f;
+    for (int s = 0; s < a.splits; ++s) v += __ldcg(a.part + ((size_t)s * tp + tok) * a.rows + row);
+    a.y[(size_t)tok * a.rows + row] = q8_epilogue(a, tok, row, v);
+  }
+  if (threadIdx.x == 0) args.counters[blockIdx.y] = 0;
+}
+
 // ------------------------------------------------------------------ RMSNorm
 // out[t] = x[t] / sqrt(mean(x[t]^2) + eps) * w  (GhostRMSNorm::forward,
 // src/oomllama.rs:200-211), f32.  One CTA per token: the sum of squares is a

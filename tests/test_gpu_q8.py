@@ -62,9 +62,12 @@ def test_q8_linear_small(oracle, eng, rows, cols, T):
     assert_close(out, ref, F32_ATOL, what=f"q8 {rows}x{cols} T={T}")
 
 
-@pytest.mark.parametrize("rows,cols,T", [(3584, 3584, 1), (512, 3584, 4), (3584, 18944, 2), (18944, 3584, 16)])
+@pytest.mark.parametrize("rows,cols,T", [(3584, 3584, 1), (512, 3584, 4), (3584, 18944, 2), (18944, 3584, 16),
+                                         (3584, 18944, 11), (9488, 3584, 13)])
 def test_q8_linear_qwen7b_shapes(oracle, eng, rows, cols, T):
-    # Qwen2.5-7B projections: q/o 3584x3584, k/v 512x3584, down 3584x18944, gate/up 18944x3584
+    # Qwen2.5-7B projections: q/o 3584x3584, k/v 512x3584, down 3584x18944, gate/up 18944x3584.
+    # 9..16 tokens on >= 32 M weights stage x in shared memory: down at T=11 runs 20 column
+    # ranges merged in order; 9488 rows leave the last 512-row group partly outside the matrix
     out, ref = _case(oracle, eng, rows, cols, T, seed=rows + cols + T, bias=(rows != 18944))
     assert_close(out, ref, F32_ATOL, what=f"q8 {rows}x{cols} T={T}")
 
