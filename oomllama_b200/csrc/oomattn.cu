@@ -616,10 +616,14 @@ int oomattn_create(const oomattn_config* cfg, int device, void* stream, oomattn_
           cudaSuccess ||
       cudaFuncSetAttribute(prefill_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kPfSmemBytes) !=
           cudaSuccess ||
-      cudaFuncSetAttribute(q8_linear_xs_kernel<2, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           (int)q8_xs_smem_bytes(kQ8XsMaxChunks)) != cudaSuccess ||
-      cudaFuncSetAttribute(q8_linear_xs_kernel<1, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           (int)q8_xs_smem_bytes(kQ8XsMaxChunks)) != cudaSuccess)
+      cudaFuncSetAttribute(q8_linear_xs_kernel<2, 2, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)q8_xs_smem_bytes(2, q8_xs_max_chunks(2))) != cudaSuccess ||
+      cudaFuncSetAttribute(q8_linear_xs_kernel<2, 1, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)q8_xs_smem_bytes(2, q8_xs_max_chunks(2))) != cudaSuccess ||
+      cudaFuncSetAttribute(q8_linear_xs_kernel<1, 2, kQ8Xs1S2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)q8_xs_smem_bytes(1, q8_xs_max_chunks(1))) != cudaSuccess ||
+      cudaFuncSetAttribute(q8_linear_xs_kernel<1, 1, kQ8Xs1S1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)q8_xs_smem_bytes(1, q8_xs_max_chunks(1))) != cudaSuccess)
     return bail(OOMATTN_ERR_CUDA);
   cudaFuncAttributes fa;
   if (cudaFuncGetAttributes(&fa, prefill_bf16_kernel) != cudaSuccess) return bail(OOMATTN_ERR_CUDA);
@@ -1382,29 +1386,37 @@ Q8Plan plan_q8(const oomattn_ctx* ctx, int rows, int cols, int nt) {
   return p;
 }
 
-// 16-token form with x staged in shared memory (q8_linear_xs_kernel): for
-// matrices of at least 32 M weights, one CTA per SM over a row group of 256 * MT
-// rows and a column range of 8 to kQ8XsMaxChunks chunks.  MT = 2 (2-deep
-// weight ring) or MT = 1 (4-deep ring), and the ranges, minimise
+// The form with x staged in shared memory (q8_linear_xs_kernel): for matrices
+// of at least 32 M weights, one CTA per SM over a row group of 256 * MT rows
+// and a column range of 8 to 96 / NT chunks.  MT and the ranges minimise
 // waves x (MT x chunks per range + kQ8XsFixed), a fixed cost for staging x,
 // filling the ring and the merge in units of 256 rows x one chunk; ties go to
-// fewer ranges, then to MT = 1.  Measured at 16 tokens (Qwen2.5-7B shapes,
-// us): gate+up MT 2: 51.2 (MT 1: 57.0), gate MT 1: 29.2 (33.6), down MT 1: 35.6
-// (43.6), LM head MT 2: 206 (213); deeper rings for MT = 2 spill and lose.
+// fewer ranges, then to MT = 1.
+//  - Two token tiles (9..16 tokens): always.  Measured at 16 tokens
+//    (Qwen2.5-7B shapes, us, against the register-x form): gate+up MT 2: 51.2
+//    (57.7), gate MT 1: 29.2 (30.6), down MT 1: 35.6 (41.9), LM head MT 2: 206
+//    (226); MT 2 with 3- or 4-deep rings spills and loses.
+//  - One token tile: only when the plan fits in one wave and gives each warp
+//    at least 30 chunks, where staging x and filling the 8-deep ring are
+//    amortised: gate+up 30.8 (35.7) at 1 token, 32.0 (37.4) at 8; down 20.7
+//    (25.0) at 1 token.  Shorter runs lose: gate (two 28-chunk ranges) 19.3
+//    against 19.4 at 1 token and 22.0 against 20.7 at 8; the LM head (4.01
+//    waves) 137 against 132.
 constexpr int kQ8XsFixed = 8;
 struct Q8XsPlan {
   int mt, groups, splits, cps;
 };
-bool use_q8_xs(int ntiles, int total_rows, int cols) {
-  return ntiles == 2 && (long long)total_rows * cols >= (32ll << 20) && cols / kQ8Chunk >= 8;
+bool q8_xs_size_ok(int total_rows, int cols) {
+  return (long long)total_rows * cols >= (32ll << 20) && cols / kQ8Chunk >= 8;
 }
-Q8XsPlan plan_q8_xs(const oomattn_ctx* ctx, const Q8Job* jobs, int n_jobs, int nchunks) {
+Q8XsPlan plan_q8_xs(const oomattn_ctx* ctx, const Q8Job* jobs, int n_jobs, int nchunks, int nt) {
   Q8XsPlan best{1, 0, 1, nchunks};
   long long best_cost = -1;
   for (int mt = 2; mt >= 1; --mt) {
     int groups = 0;
     for (int j = 0; j < n_jobs; ++j) groups += (jobs[j].w->rows + 256 * mt - 1) / (256 * mt);
-    for (int s = (nchunks + kQ8XsMaxChunks - 1) / kQ8XsMaxChunks; s <= std::max(1, nchunks / 8); ++s) {
+    const int mx = q8_xs_max_chunks(nt);
+    for (int s = (nchunks + mx - 1) / mx; s <= std::max(1, nchunks / 8); ++s) {
       const int cps = (nchunks + s - 1) / s;
       const int splits = (nchunks + cps - 1) / cps;
       const long long waves = ((long long)groups * splits + ctx->num_sms - 1) / ctx->num_sms;
@@ -1418,19 +1430,19 @@ Q8XsPlan plan_q8_xs(const oomattn_ctx* ctx, const Q8Job* jobs, int n_jobs, int n
   return best;
 }
 
-template <int MT, int S>
+template <int NT, int MT, int S>
 cudaError_t launch_q8_linear_xs(const Q8Args& a, int groups, cudaStream_t st) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(a.splits, groups);
   cfg.blockDim = dim3(kQ8XsWarps * 32);
-  cfg.dynamicSmemBytes = q8_xs_smem_bytes(a.chunks_per_split);
+  cfg.dynamicSmemBytes = q8_xs_smem_bytes(NT, a.chunks_per_split);
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, q8_linear_xs_kernel<MT, S>, a);
+  return cudaLaunchKernelEx(&cfg, q8_linear_xs_kernel<NT, MT, S>, a);
 }
 
 // Runs every job (up to kQ8MaxMats, all of the same width) on the same input:
@@ -1462,8 +1474,8 @@ int q8_run(oomattn_ctx* ctx, const Q8Job* jobs, int n_jobs, const float* x, cons
     for (int j = 0; j < n_jobs; ++j) blocks += (jobs[j].w->rows + 16 * p.mt - 1) / (16 * p.mt);
     part_floats = std::max(part_floats, (size_t)p.splits * 8 * nt * total_rows);
     max_blocks = std::max(max_blocks, blocks);
-    if (use_q8_xs(nt, total_rows, cols)) {
-      const Q8XsPlan xp = plan_q8_xs(ctx, jobs, n_jobs, cols / kQ8Chunk);
+    if (q8_xs_size_ok(total_rows, cols)) {
+      const Q8XsPlan xp = plan_q8_xs(ctx, jobs, n_jobs, cols / kQ8Chunk, nt);
       part_floats = std::max(part_floats, (size_t)xp.splits * 8 * nt * total_rows);
       max_blocks = std::max(max_blocks, xp.groups);
     }
@@ -1492,9 +1504,14 @@ int q8_run(oomattn_ctx* ctx, const Q8Job* jobs, int n_jobs, const float* x, cons
     }
     CKLAUNCH();
     const int ntiles = nt > 8 ? 2 : 1;
-    const bool xs = use_q8_xs(ntiles, total_rows, cols);
     const Q8Plan p = plan_q8(ctx, total_rows, cols, ntiles);
-    const Q8XsPlan xp = xs ? plan_q8_xs(ctx, jobs, n_jobs, nchunks) : Q8XsPlan{p.mt, 0, p.splits, p.cps};
+    Q8XsPlan xp{p.mt, 0, p.splits, p.cps};
+    bool xs = false;
+    if (q8_xs_size_ok(total_rows, cols)) {
+      const Q8XsPlan t = plan_q8_xs(ctx, jobs, n_jobs, nchunks, ntiles);
+      xs = ntiles == 2 || ((long long)t.groups * t.splits <= ctx->num_sms && t.cps >= 30);
+      if (xs) xp = t;
+    }
     const int rows_per_block = xs ? 256 * xp.mt : 16 * p.mt;
     Q8Args a;
     memset(&a, 0, sizeof(a));
@@ -1527,8 +1544,11 @@ int q8_run(oomattn_ctx* ctx, const Q8Job* jobs, int n_jobs, const float* x, cons
     }
     // one token tile: x read a chunk ahead; two: x read at use, with a 3-deep
     // weight ring for one row tile and a 2-deep one for two
-    const cudaError_t le = xs ? (xp.mt == 2 ? launch_q8_linear_xs<2, 2>(a, blocks, ctx->stream)
-                                            : launch_q8_linear_xs<1, 4>(a, blocks, ctx->stream))
+    const cudaError_t le =
+        xs ? (ntiles == 2 ? (xp.mt == 2 ? launch_q8_linear_xs<2, 2, 2>(a, blocks, ctx->stream)
+                                        : launch_q8_linear_xs<2, 1, 4>(a, blocks, ctx->stream))
+                          : (xp.mt == 2 ? launch_q8_linear_xs<1, 2, kQ8Xs1S2>(a, blocks, ctx->stream)
+                                        : launch_q8_linear_xs<1, 1, kQ8Xs1S1>(a, blocks, ctx->stream)))
                            : ntiles == 2 ? (p.mt == 2 ? launch_q8_linear<2, 2, 2, false>(a, blocks, ctx->stream)
                                                     : launch_q8_linear<2, 1, 3, false>(a, blocks, ctx->stream))
                            : p.mt == 2 ? launch_q8_linear<1, 2, 2, true>(a, blocks, ctx->stream)

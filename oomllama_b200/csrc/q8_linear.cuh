@@ -420,16 +420,18 @@ __global__ void __launch_bounds__(kQ8Warps * 32, 2) q8_linear_kernel(const Q8Arg
 // reduction across warps; CTAs of other column ranges merge through the
 // split-K partial buffer in split order, as above.
 constexpr int kQ8XsWarps = 16;
-constexpr int kQ8XsMaxChunks = 48;  // columns per range: 48 x 64 (x staging: 48 x 64 x 16 tokens x 4 B = 192 KB)
+// chunks per range: 96 / NT (x staging: 96 x 64 columns x 8 tokens x 4 B = 192 KB)
+__host__ __device__ constexpr int q8_xs_max_chunks(int nt) { return 96 / nt; }
+constexpr int kQ8Xs1S2 = 3, kQ8Xs1S1 = 8;  // one token tile: ring depth for MT = 2 and MT = 1
 
 __host__ __device__ constexpr int q8_xs_stride(int cps) { return cps * 32 + 4; }  // words per token row
-__host__ __device__ constexpr size_t q8_xs_smem_bytes(int cps) {
-  return ((size_t)32 * q8_xs_stride(cps) + (size_t)16 * (cps + 1)) * 4;
+__host__ __device__ constexpr size_t q8_xs_smem_bytes(int nt, int cps) {
+  return ((size_t)16 * nt * q8_xs_stride(cps) + (size_t)8 * nt * (cps + 1)) * 4;
 }
 
-template <int MT, int S>
+template <int NT, int MT, int S>
 __global__ void __launch_bounds__(kQ8XsWarps * 32, 1) q8_linear_xs_kernel(const Q8Args args) {
-  constexpr int NT = 2;
+  constexpr int TR = 8 * NT;  // staged token rows
   extern __shared__ __align__(16) uint32_t xs[];
   __shared__ int s_last;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -441,8 +443,8 @@ __global__ void __launch_bounds__(kQ8XsWarps * 32, 1) q8_linear_xs_kernel(const 
   const int c0 = sp * cps, c1 = min(nchunks, c0 + cps);
   const int stride = q8_xs_stride(cps);
   uint32_t* xs_h = xs;
-  uint32_t* xs_l = xs + 16 * stride;
-  float* xs_s = reinterpret_cast<float*>(xs + 32 * stride);  // [16][cps + 1]
+  uint32_t* xs_l = xs + TR * stride;
+  float* xs_s = reinterpret_cast<float*>(xs + 2 * TR * stride);  // [TR][cps + 1]
   const int rows_cta = kQ8XsWarps * 16 * MT;
   const int row0 = a.rb * rows_cta + warp * 16 * MT;
 
@@ -460,12 +462,12 @@ __global__ void __launch_bounds__(kQ8XsWarps * 32, 1) q8_linear_xs_kernel(const 
   for (int s = 0; s < S - 1; ++s)
     if (ch + s < c1) q8_load_w<NT, MT>(a, b, ch + s, w[s]);
   asm volatile("griddepcontrol.wait;" ::: "memory");
-  // stage the range's x: 16 token rows of hi and lo words (zero past n_tokens)
+  // stage the range's x: TR token rows of hi and lo words (zero past n_tokens)
   // and their chunk sums
   {
     const int q4 = (c1 - c0) * 8;  // 16-byte words per token row
     const size_t xrow = (size_t)a.cols / 2;
-    for (int i = threadIdx.x; i < 16 * q4; i += blockDim.x) {
+    for (int i = threadIdx.x; i < TR * q4; i += blockDim.x) {
       const int t = i / q4, k = (i - t * q4) * 4;
       uint4 h = make_uint4(0, 0, 0, 0), l = make_uint4(0, 0, 0, 0);
       if (t < a.n_tokens) {
@@ -475,7 +477,7 @@ __global__ void __launch_bounds__(kQ8XsWarps * 32, 1) q8_linear_xs_kernel(const 
       *reinterpret_cast<uint4*>(xs_h + t * stride + k) = h;
       *reinterpret_cast<uint4*>(xs_l + t * stride + k) = l;
     }
-    for (int i = threadIdx.x; i < 16 * (c1 - c0); i += blockDim.x) {
+    for (int i = threadIdx.x; i < TR * (c1 - c0); i += blockDim.x) {
       const int t = i / (c1 - c0), k = i - t * (c1 - c0);
       xs_s[t * (cps + 1) + k] = t < a.n_tokens ? __ldg(args.xsum + (size_t)t * nchunks + c0 + k) : 0.f;
     }

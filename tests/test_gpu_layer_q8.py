@@ -35,11 +35,11 @@ def test_rmsnorm(oracle):
 
 
 @pytest.mark.parametrize("T,H,inter", [(1, 256, 512), (3, 512, 1408), (9, 256, 640), (12, 2048, 8192),
-                                         (10, 1024, 20480)])
+                                         (10, 1024, 20480), (5, 2048, 8192)])
 def test_q8_mlp_with_residual(oracle, T, H, inter):
-    # (12, 2048, 8192) and (10, 1024, 20480): gate+up runs as one launch of the
-    # shared-memory-x form over both matrices' row groups, with one and with two
-    # row tiles per warp
+    # (12, 2048, 8192), (10, 1024, 20480) and (5, 2048, 8192): gate+up runs as
+    # one launch of the shared-memory-x form over both matrices' row groups,
+    # with one and with two row tiles per warp, and with one token tile
     eng = make_engine(2, 1, [16])
     rng = np.random.default_rng(T + H)
     gate, gd = _q8(oracle, inter, H, rng)
