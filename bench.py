@@ -42,8 +42,8 @@ PREFILL_FLOPS = 4 * D * HQ * S_PREFILL * (S_PREFILL + 1) // 2   # 120,288,444,41
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 SPEC_PEAKS = {"hbm_gbs": 7700.0, "bf16_tflops": 2250.0}  # nominal B200 (HGX HBM3e; dense bf16), for context
 # dram__bytes_read.sum + dram__bytes_write.sum per launch from one ncu capture
-# of each kernel on these workloads (profiles/prefill_bf16_kernel_qwen7b_s4096.md,
-# profiles/decode_bf16_kernel_llama8b_ctx32k.md).
+# of each kernel on these workloads: the 4096-token causal prefill and the
+# 8 x 32768-token Llama-3 decode.
 NCU_TRAFFIC_BYTES = {"prefill_bf16_kernel": 37_828_096 + 6_703_360, "decode_bf16_kernel": 1_074_328_000 + 5_611_008}
 
 
