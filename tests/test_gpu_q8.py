@@ -72,10 +72,13 @@ def test_q8_linear_qwen7b_shapes(oracle, eng, rows, cols, T):
     assert_close(out, ref, F32_ATOL, what=f"q8 {rows}x{cols} T={T}")
 
 
-def test_q8_linear_repeatable(oracle, eng):
-    # split-K partials are merged in split order by the last CTA: identical bits on every call
-    wq, _ = _matrix(oracle, 512, 3584, seed=3)
-    x = torch.randn(3, 3584, generator=torch.Generator().manual_seed(4)).cuda()
+@pytest.mark.parametrize("rows,cols,T", [(512, 3584, 3), (3584, 18944, 11)])
+def test_q8_linear_repeatable(oracle, eng, rows, cols, T):
+    # split-K partials (and, for the 16-token form with x in shared memory, the
+    # 10 column ranges of 3584x18944) are merged in split order by the last
+    # CTA: identical bits on every call
+    wq, _ = _matrix(oracle, rows, cols, seed=3)
+    x = torch.randn(T, cols, generator=torch.Generator().manual_seed(4)).cuda()
     y1 = eng.q8_linear(wq, x).clone()
     y2 = eng.q8_linear(wq, x)
     eng.sync()
