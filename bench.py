@@ -47,15 +47,37 @@ SPEC_PEAKS = {"hbm_gbs": 7700.0, "bf16_tflops": 2250.0}  # nominal B200 (HGX HBM
 NCU_TRAFFIC_BYTES = {"prefill_bf16_kernel": 37_828_096 + 6_703_360, "decode_bf16_kernel": 1_074_328_000 + 5_611_008}
 
 
+SECTIONS = ("prefill", "decode-llama", "decode-qwen", "c1", "q8", "layer", "repack", "model")
+
+
 def parse():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
     p.add_argument("--steps", type=int, default=20)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--no-secondary", action="store_true")
+    p.add_argument("--only", default="", help="comma-separated subset of: " + ", ".join(SECTIONS) +
+                   " (\"decode\" = both decode configurations); default all")
+    p.add_argument("--no-secondary", action="store_true", help="the headline prefill only")
     p.add_argument("--no-cpu-baseline", action="store_true")
     return p.parse_args()
+
+
+def sections(args):
+    if args.no_secondary:
+        return {"prefill"}
+    if not args.only:
+        return set(SECTIONS)
+    out = set()
+    for name in args.only.split(","):
+        name = name.strip()
+        if name == "decode":
+            out |= {"decode-llama", "decode-qwen"}
+        elif name in SECTIONS:
+            out.add(name)
+        elif name:
+            raise SystemExit(f"--only: unknown section {name!r}")
+    return out
 
 
 def load_peaks():
@@ -99,6 +121,15 @@ class Dist:
         import torch.distributed as dist
         t = torch.tensor([x], dtype=torch.float64, device=f"cuda:{self.local}")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def sum(self, x: float) -> float:
+        if not self.pg:
+            return x
+        import torch
+        import torch.distributed as dist
+        t = torch.tensor([x], dtype=torch.float64, device=f"cuda:{self.local}")
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
         return float(t.item())
 
     def close(self):
@@ -161,30 +192,48 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------- prefill (headline)
-def bench_prefill(args, dist_, torch):
+def block_flops(blocks, n_heads, s=S_PREFILL):
+    """Algorithmic causal FLOPs of the 256-row query blocks `blocks` ([lo, hi) ranges) for n_heads
+    q heads: query row i sees i + 1 keys, 4 * d FLOPs per (row, key)."""
+    f = 0
+    for lo, hi in blocks:
+        r0, r1 = 256 * lo, min(s, 256 * hi)
+        f += (r1 * (r1 + 1) - r0 * (r0 + 1)) // 2
+    return 4 * D * n_heads * f
+
+
+def bench_prefill(args, dist_, torch, strong):
+    """One C2 prefill step per GPU.  strong: the ranks share ONE sequence (PrefillShardPlan: kv-head
+    groups, then zig-zag query blocks); otherwise every rank runs its own whole sequence."""
     from oomllama_b200 import TurboConfig, TurboEngine
+    from oomllama_b200.shard import PrefillShardPlan
     dev = torch.cuda.current_device()
-    cfg = TurboConfig(n_layers=1, hidden_size=HQ * D, n_heads=HQ, n_kv_heads=HKV, max_seq_len=S_PREFILL,
+    W, r = dist_.world, dist_.rank
+    plan = PrefillShardPlan(HQ, HKV, W if strong else 1, r if strong else 0)
+    hq, hkv = len(plan.q_heads), len(plan.kv_heads)
+    blocks = plan.blocks(S_PREFILL)
+    rank_flops = block_flops(blocks, hq)
+    cfg = TurboConfig(n_layers=1, hidden_size=hq * D, n_heads=hq, n_kv_heads=hkv, max_seq_len=S_PREFILL,
                       max_seqs=1, kv_dtype="bf16", rope_variant="interleaved", rope_theta=1e6)
     eng = TurboEngine(cfg, device=dev)
-    n_sets = 4  # 4 x 37.7 MB of Q/K/V inputs > 126 MB L2, rotated between steps
-    g = torch.Generator(device="cuda").manual_seed(1 + dist_.rank)
+    n_sets = 4  # 4 x 37.7 MB of Q/K/V inputs (whole heads) > 126 MB L2, rotated between steps
+    g = torch.Generator(device="cuda").manual_seed(1 + (plan.group if strong else r))
     sets = []
     for _ in range(n_sets):
-        q = torch.randn(S_PREFILL, HQ * D, generator=g, device="cuda").to(torch.bfloat16)
-        k = torch.randn(S_PREFILL, HKV * D, generator=g, device="cuda").to(torch.bfloat16)
-        v = torch.randn(S_PREFILL, HKV * D, generator=g, device="cuda").to(torch.bfloat16)
+        q = torch.randn(S_PREFILL, hq * D, generator=g, device="cuda").to(torch.bfloat16)
+        k = torch.randn(S_PREFILL, hkv * D, generator=g, device="cuda").to(torch.bfloat16)
+        v = torch.randn(S_PREFILL, hkv * D, generator=g, device="cuda").to(torch.bfloat16)
         sets.append((q, k, v))
-    q_rot = torch.empty(S_PREFILL, HQ, D, dtype=torch.bfloat16, device="cuda")
-    out = torch.empty(S_PREFILL, HQ, D, dtype=torch.float32, device="cuda")
+    out = torch.empty(S_PREFILL, hq, D, dtype=torch.float32, device="cuda")
+    pf_stream = torch.cuda.current_stream()
 
-    def step(i, ev=None):
-        q, k, v = sets[i % n_sets]
+    def step(i, ev=None, qkv=None, o=None):
+        q, k, v = sets[i % n_sets] if qkv is None else qkv
         eng.reset()
         qr = eng.rope_append(0, [0], q, k, v, q_out_dtype=torch.bfloat16)
         if ev is not None:
             ev[0].record()
-        eng.prefill(0, 0, qr, out=out)
+        eng.prefill(0, 0, qr, out=out if o is None else o, blocks=blocks)
         if ev is not None:
             ev[1].record()
 
@@ -230,7 +279,8 @@ def bench_prefill(args, dist_, torch):
         t1.record()
         torch.cuda.synchronize()
         dist_.barrier()
-        # the prefill kernel alone: CUDA events around each launch of eager steps
+        # the prefill kernel alone: CUDA events around each launch of eager steps (on the stream the
+        # kernel is launched on)
         for i in range(args.steps):
             step(i, evs[i])
         torch.cuda.synchronize()
@@ -242,18 +292,18 @@ def bench_prefill(args, dist_, torch):
     ms_max = dist_.max(ms)
     kern_max = dist_.max(kern_ms)
 
-    # e2e through the public API with pinned host buffers.  Every step copies
-    # its Q/K/V host->device, runs RoPE/append + prefill, and copies the f32
-    # attention output device->host.  Like a serving loop, the copies run on
-    # their own streams and overlap the neighbouring steps' compute (inputs
-    # and outputs double-buffered on both sides).
-    hq = [tuple(t.cpu().pin_memory() for t in s) for s in sets[:2]]
-    ho = [torch.empty(S_PREFILL, HQ, D, dtype=torch.float32).pin_memory() for _ in range(2)]
+    # e2e through the public API with pinned host buffers.  Every step copies this rank's Q/K/V
+    # host->device, runs RoPE/append + prefill, and copies the f32 attention rows of its query
+    # blocks device->host.  Like a serving loop, the copies run on their own streams and overlap the
+    # neighbouring steps' compute (inputs and outputs double-buffered on both sides).
+    rows = [(256 * lo, min(S_PREFILL, 256 * hi)) for lo, hi in blocks]
+    hq_ = [tuple(t.cpu().pin_memory() for t in s_) for s_ in sets[:2]]
+    ho = [torch.empty(S_PREFILL, hq, D, dtype=torch.float32).pin_memory() for _ in range(2)]
     dq = [[torch.empty_like(t) for t in sets[0]] for _ in range(2)]
-    dout = [torch.empty(S_PREFILL, HQ, D, dtype=torch.float32, device="cuda") for _ in range(2)]
+    dout = [torch.empty(S_PREFILL, hq, D, dtype=torch.float32, device="cuda") for _ in range(2)]
     s_in, s_out = torch.cuda.Stream(), torch.cuda.Stream()
-    s_comp = torch.cuda.current_stream()
-    ev = lambda: torch.cuda.Event()
+    s_comp = pf_stream
+    ev = lambda: torch.cuda.Event()  # noqa: E731
     in_ready, in_free = [ev(), ev()], [ev(), ev()]
     out_ready, out_free = [ev(), ev()], [ev(), ev()]
     for e_ in in_free + out_free:
@@ -263,19 +313,18 @@ def bench_prefill(args, dist_, torch):
         b = i % 2
         with torch.cuda.stream(s_in):
             s_in.wait_event(in_free[b])
-            for d_, h_ in zip(dq[b], hq[i % 2]):
+            for d_, h_ in zip(dq[b], hq_[i % 2]):
                 d_.copy_(h_, non_blocking=True)
             in_ready[b].record(s_in)
         s_comp.wait_event(in_ready[b])
         s_comp.wait_event(out_free[b])
-        eng.reset()
-        qr = eng.rope_append(0, [0], dq[b][0], dq[b][1], dq[b][2], q_out_dtype=torch.bfloat16)
-        eng.prefill(0, 0, qr, out=dout[b])
+        step(i, qkv=dq[b], o=dout[b])
         in_free[b].record(s_comp)
         out_ready[b].record(s_comp)
         with torch.cuda.stream(s_out):
             s_out.wait_event(out_ready[b])
-            ho[b].copy_(dout[b], non_blocking=True)
+            for a_, z_ in rows:
+                ho[b][a_:z_].copy_(dout[b][a_:z_], non_blocking=True)
             out_free[b].record(s_out)
 
     for i in range(3):
@@ -291,22 +340,40 @@ def bench_prefill(args, dist_, torch):
     torch.cuda.synchronize()
     dist_.barrier()
     e2e_ms = dist_.max(a.elapsed_time(b) / e_steps)
-    h2d = sum(t.numel() * t.element_size() for t in hq[0])
-    d2h = ho[0].numel() * ho[0].element_size()
+    h2d = sum(t.numel() * t.element_size() for t in hq_[0])
+    d2h = sum((z_ - a_) * hq * D * 4 for a_, z_ in rows)
     eng.close()
     return {
-        "ms": ms_max, "kernel_ms": kern_max, "clocks": clk.summary(), "e2e_ms": e2e_ms, "h2d": h2d, "d2h": d2h,
-        "launches_per_step": 2,
+        "ms": ms_max, "kernel_ms": kern_max, "kernel_ms_local": kern_ms, "clocks": clk.summary(), "e2e_ms": e2e_ms,
+        "h2d": dist_.sum(h2d), "d2h": dist_.sum(d2h), "launches_per_step": 2, "rank_flops": rank_flops,
+        "heads": hq, "blocks": blocks,
     }
 
 
 # ---------------------------------------------------------------- decode (secondary)
+def f64_attention(q, k, v, scale):
+    """Float64 restatement of one decode row for the in-bench parity check: q [hq, d], k, v
+    [hkv, L, d]; q head h reads kv head h // (hq / hkv); softmax(scale * K q) V per head."""
+    hq, hkv = q.shape[0], k.shape[0]
+    grp = hq // hkv
+    out = np.empty_like(q, dtype=np.float64)
+    for h in range(hq):
+        kk, vv = k[h // grp].astype(np.float64), v[h // grp].astype(np.float64)
+        s_ = kk @ q[h].astype(np.float64) * scale
+        p = np.exp(s_ - s_.max())
+        out[h] = p @ vv / p.sum()
+    return out
+
+
 def bench_decode(args, dist_, torch, name):
-    """Split-KV decode.  llama: 32q/8kv, batch 8, 32768 context, split-half
-    theta=5e5, sharded by kv-head group.  qwen-batched: 28q/4kv, batch 64,
-    context U[1024,8192], shuffled pages; beyond 4 GPUs the context is split
-    in world/4 slices and partials are merged after an NCCL all-gather."""
+    """Split-KV decode.  llama: 32q/8kv, batch 8, 32768 context, split-half theta=5e5, sharded by
+    kv-head group (strong scaling: the same 8 x 32768 work at every N).  qwen-batched: 28q/4kv, batch
+    64, context U[1024,8192], shuffled pages; beyond 4 GPUs each context is split in world/4 slices,
+    and one step is the packed decode, ONE all-gather of the group's (O, lse) partials over NCCL and
+    the merge.  After timing, rank-local parity of sampled rows (every local q head) against a
+    float64 restatement over the whole context (slices gathered from the group)."""
     from oomllama_b200 import TurboConfig, TurboEngine
+    from oomllama_b200.shard import DecodeShardPlan, SplitContextDecoder, new_group_comms
     dev = torch.cuda.current_device()
     W, r = dist_.world, dist_.rank
     if name == "llama-32k":
@@ -316,22 +383,21 @@ def bench_decode(args, dist_, torch, name):
         hq, hkv, B, variant, theta = 28, 4, 64, "interleaved", 1e6
         lens = np.random.default_rng(2).integers(1024, 8193, size=B).tolist()
         lens = [L + 1 for L in lens]  # cached tokens + the new one
-    from oomllama_b200.shard import DecodeShardPlan, gather_partials, new_group_comms
     plan = DecodeShardPlan(hq, hkv, W, r)
     ctx_split = plan.ctx_split
     l_hkv, l_hq = len(plan.kv_heads), len(plan.q_heads)
-    # this rank's slice of every sequence: whole pages
-    slices = [plan.context_slice(L) for L in lens]
+    slices = [plan.context_slice(L) for L in lens]  # this rank's slice of every sequence: whole pages
     local = [b - a for a, b in slices]
     n_pages = sum(-(-x // 16) for x in local)
     cfg = TurboConfig(n_layers=1, hidden_size=0, n_heads=l_hq, n_kv_heads=l_hkv, max_seq_len=max(lens) + 16,
                       max_seqs=B, n_pages=max(1, n_pages), kv_dtype="bf16", rope_variant=variant, rope_theta=theta)
     eng = TurboEngine(cfg, device=dev, assign_pages=False)
     perm = np.random.default_rng(3 + r).permutation(max(1, n_pages))
-    o = 0
+    tables, o = [], 0
     for s in range(B):
         np_s = -(-local[s] // 16)
-        eng.set_block_table(s, perm[o:o + np_s].tolist())
+        tables.append(perm[o:o + np_s])
+        eng.set_block_table(s, tables[s].tolist())
         o += np_s
         eng.set_seq_len(0, s, local[s])
     kp, vp = eng.kv_pool()
@@ -340,49 +406,102 @@ def bench_decode(args, dist_, torch, name):
     vp.normal_(generator=g)
     kp[:, -1].zero_()
     vp[:, -1].zero_()  # the null page stays zero
-    q = torch.randn(B, l_hq, D, generator=g, device="cuda")
-    outb = torch.empty(B, l_hq, D, device="cuda")
-    lse = torch.empty(B, l_hq, device="cuda")
-    merge = ctx_split > 1
+    # the query is the same on every rank of a group (its heads, seeded by the group)
+    gq = torch.Generator(device="cuda").manual_seed(101 + plan.group)
+    q = torch.randn(B, l_hq, D, generator=gq, device="cuda")
     comm = None
     if dist_.pg:
         import torch.distributed as tdist
         comm = new_group_comms(plan, tdist)[plan.group]  # every rank creates every group, in order
+    dec = SplitContextDecoder(eng, plan, tdist if dist_.pg else None, comm)
+    seqs = list(range(B))
+    merge = ctx_split > 1
+    stream = torch.cuda.current_stream()
 
     def step(ev=None):
         if ev is not None:
-            ev[0].record()
-        eng.decode(0, list(range(B)), q, with_lse=merge, out=outb, lse=lse)
+            ev[0].record(stream)
+        if not merge:
+            out = eng.decode(0, seqs, q)
+            if ev is not None:
+                ev[1].record(stream)
+            return out
+        packed, gathered, out = dec.buffers(B, l_hq, q.device)
+        eng.decode_packed(0, seqs, q, out=packed)
         if ev is not None:
-            ev[1].record()
-        if merge:
-            # K-D: all-gather the group's (O, lse) partials over NCCL, then the K-B2 merge
-            import torch.distributed as tdist
-            parts, lses = gather_partials(outb, lse, plan, tdist, comm)
-            eng.merge_partials(parts, lses)
+            ev[1].record(stream)
+        from oomllama_b200.shard import gather_packed
+        gather_packed(packed, plan, tdist, comm, out=gathered)
+        if ev is not None:
+            ev[2].record(stream)
+        eng.merge_packed(gathered, ctx_split, out=out.view(B * l_hq, D))
+        if ev is not None:
+            ev[3].record(stream)
+        return out
 
     steps = max(5, args.steps)
     for _ in range(args.warmup):
         step()
     eng.sync()
-    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
-    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    mk = lambda: torch.cuda.Event(enable_timing=True)  # noqa: E731
+    evs = [(mk(), mk(), mk(), mk()) if merge else (mk(), mk()) for _ in range(steps)]
+    t0, t1 = mk(), mk()
     dist_.barrier()
-    t0.record()
+    t0.record(stream)
+    for i in range(steps):
+        step()
+    t1.record(stream)
+    torch.cuda.synchronize()
+    dist_.barrier()
+    ms = dist_.max(t0.elapsed_time(t1) / steps)
+    # the stages, from CUDA events around each (eager steps, after the timed region)
+    dist_.barrier()
     for i in range(steps):
         step(evs[i])
-    t1.record()
     torch.cuda.synchronize()
     dist_.barrier()
     eng.sync()
-    ms = dist_.max(t0.elapsed_time(t1) / steps)
-    kern_ms = sum(a.elapsed_time(b) for a, b in evs) / steps
-    kern_max = dist_.max(kern_ms)
+    kern_local = sum(e[0].elapsed_time(e[1]) for e in evs) / steps
+    coll_ms = sum(e[1].elapsed_time(e[2]) for e in evs) / steps if merge else 0.0
+    merge_ms = sum(e[2].elapsed_time(e[3]) for e in evs) / steps if merge else 0.0
+    kern_max = dist_.max(kern_local)
     local_bytes = sum(local) * l_hkv * D * 2 * 2
     total_bytes = sum(lens) * hkv * D * 2 * 2
+
+    # parity: sampled rows, every local q head, over the whole context
+    out = step()
+    torch.cuda.synchronize()
+    scale = 1.0 / math.sqrt(D)
+    rows = np.random.default_rng(17).choice(B, size=min(3, B), replace=False)
+    worst, worst_rel = 0.0, 0.0
+    for z in rows:
+        pg = torch.from_numpy(tables[z].astype(np.int64)).cuda()
+        kr = kp[0].index_select(0, pg).permute(1, 0, 2, 3).reshape(l_hkv, -1, D)[:, :local[z]]
+        vr = vp[0].index_select(0, pg).permute(1, 0, 2, 3).reshape(l_hkv, -1, D)[:, :local[z]]
+        if merge:  # the group's slices of this row, in slice order
+            import torch.distributed as tdist
+            cap = max(plan.slice_of(lens[z], s_)[1] - plan.slice_of(lens[z], s_)[0] for s_ in range(ctx_split))
+            pad_k = torch.zeros(l_hkv, cap, D, dtype=kr.dtype, device="cuda")
+            pad_v = torch.zeros_like(pad_k)
+            pad_k[:, :local[z]] = kr
+            pad_v[:, :local[z]] = vr
+            gk = [torch.empty_like(pad_k) for _ in range(ctx_split)]
+            gv = [torch.empty_like(pad_v) for _ in range(ctx_split)]
+            tdist.all_gather(gk, pad_k, group=comm)
+            tdist.all_gather(gv, pad_v, group=comm)
+            n_s = [plan.slice_of(lens[z], s_)[1] - plan.slice_of(lens[z], s_)[0] for s_ in range(ctx_split)]
+            kr = torch.cat([gk[s_][:, :n_s[s_]] for s_ in range(ctx_split)], dim=1)
+            vr = torch.cat([gv[s_][:, :n_s[s_]] for s_ in range(ctx_split)], dim=1)
+        ref = f64_attention(q[z].cpu().numpy(), kr.float().cpu().numpy(), vr.float().cpu().numpy(), scale)
+        got = out[z].double().cpu().numpy()
+        worst = max(worst, float(np.abs(got - ref).max()))
+        worst_rel = max(worst_rel, float(np.linalg.norm(got - ref) / np.linalg.norm(ref)))
+    worst, worst_rel = dist_.max(worst), dist_.max(worst_rel)
     eng.close()
-    return {"ms": ms, "kernel_ms": kern_max, "local_bytes": local_bytes, "total_bytes": total_bytes, "batch": B,
-            "merge": merge, "lens_sum": sum(lens), "kern_local_ms": kern_ms}
+    return {"ms": ms, "kernel_ms": kern_max, "kern_local_ms": kern_local, "coll_ms": dist_.max(coll_ms),
+            "merge_ms": dist_.max(merge_ms), "local_bytes": local_bytes, "total_bytes": total_bytes, "batch": B,
+            "merge": merge, "lens_sum": sum(lens), "parity_max_abs": worst, "parity_rel": worst_rel,
+            "parity_ok": bool(worst <= 2e-3 and worst_rel <= 1e-2)}
 
 
 # ---------------------------------------------------------------- Q8 linear (K-E, secondary)
@@ -837,7 +956,7 @@ def reference_arm(args):
     line = {
         "impl": "reference", "metric": "prefill-attn TFLOPS (causal GQA 28q/4kv d128, S=4096)",
         "value": value, "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic ~N(0,1), seeded", "config": workload_config(args.gpus),
         "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": nt, "kind": "port",
                          "sample": f"{n_pairs} random (query row, head) pairs per step of the 4096-token causal "
@@ -849,9 +968,11 @@ def reference_arm(args):
 
 
 def workload_config(n):
-    return {"workload": "causal prefill, Qwen2.5-7B GQA 28q/4kv d128, 4096 tokens/seq, bf16 Q/K/V ~N(0,1), "
-                        "interleaved RoPE theta=1e6, paged bf16 KV cache (16-token pages)",
-            "sequences": n, "seq_len": S_PREFILL, "parallelism": f"sequence-sharded x{n} (one sequence per GPU)",
+    return {"workload": "causal prefill, Qwen2.5-7B GQA 28q/4kv d128, one sequence of 4096 tokens, bf16 Q/K/V "
+                        "~N(0,1), interleaved RoPE theta=1e6, paged bf16 KV cache (16-token pages)",
+            "sequences": 1, "seq_len": S_PREFILL,
+            "parallelism": "1 GPU" if n == 1 else
+            f"one sequence over {n} GPUs: kv-head groups" + (", zig-zag 256-row query blocks" if n > HKV else ""),
             "l2": "inputs rotated over 4 sets of 37.7 MB (> 126 MB L2)"}
 
 
@@ -865,46 +986,73 @@ def main():
     torch.cuda.set_device(dist_.local)
     from oomllama_b200 import _lib
     _lib.load()  # fail loudly when the library is missing
+    only = sections(args)
     peaks, peak_src = load_peaks()
-    pf = bench_prefill(args, dist_, torch)
     W = dist_.world
-    value = W * PREFILL_FLOPS / (pf["ms"] * 1e-3) / 1e12
-    achieved = PREFILL_FLOPS / (pf["kernel_ms"] * 1e-3) / 1e12
-    timed_s = pf["ms"] * args.steps * 1e-3
-    peak_key = "bf16_tflops_sustained" if timed_s > 1.0 else "bf16_tflops"
-    line = {
-        "metric": "prefill-attn TFLOPS (causal GQA 28q/4kv d128, S=4096)", "value": value, "unit": "TFLOP/s",
-        "n_gpus": W, "steps": args.steps, "warmup": args.warmup, "ms_per_step": pf["ms"], "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic ~N(0,1), seeded",
-        "config": workload_config(W),
-        "roofline": {"bound": "tensor", "kernel": "prefill_bf16_kernel", "achieved": achieved,
-                     "peak": peaks[peak_key], "unit": "TFLOP/s", "frac": achieved / peaks[peak_key],
-                     "frac_of_spec": achieved / SPEC_PEAKS["bf16_tflops"],
-                     "peak_source": f"{peak_src} {peak_key}",
-                     "traffic": NCU_TRAFFIC_BYTES["prefill_bf16_kernel"],
-                     "algorithmic_flops_per_launch": PREFILL_FLOPS},
-        "e2e": {"value": W * PREFILL_FLOPS / (pf["e2e_ms"] * 1e-3) / 1e12, "unit": "TFLOP/s",
-                "h2d_bytes_per_step": pf["h2d"], "d2h_bytes_per_step": pf["d2h"],
-                "api": "TurboEngine.rope_append + TurboEngine.prefill (C ABI) from pinned host buffers"},
-        "gpu_launches": pf["launches_per_step"] * args.steps,
-        "clocks": pf["clocks"],
-    }
-    if not args.no_secondary:
-        dec = {}
-        for name in ("llama-32k", "qwen-batched"):
-            r = bench_decode(args, dist_, torch, name)
-            gbs = r["total_bytes"] / (r["ms"] * 1e-3) / 1e9
-            kern_gbs = r["local_bytes"] / (r["kernel_ms"] * 1e-3) / 1e9
-            dec[name] = {
-                "hbm_gbs": gbs, "tok_s": r["batch"] / (r["ms"] * 1e-3), "ms_per_step": r["ms"],
-                "bytes_per_step": r["total_bytes"], "split_context_merge": r["merge"],
-                "roofline": {"bound": "hbm", "kernel": "decode_bf16_kernel", "achieved": kern_gbs,
-                             "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": kern_gbs / peaks["hbm_gbs"],
-                             "frac_of_spec": kern_gbs / SPEC_PEAKS["hbm_gbs"],
-                             "traffic": NCU_TRAFFIC_BYTES["decode_bf16_kernel"] if name == "llama-32k" and W == 1
-                             else None},
-            }
+    line = {"metric": "prefill-attn TFLOPS (causal GQA 28q/4kv d128, S=4096)", "value": None, "unit": "TFLOP/s",
+            "n_gpus": W, "steps": args.steps, "warmup": args.warmup, "ms_per_step": None, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic ~N(0,1), seeded",
+            "config": workload_config(W)}
+    summary = {}
+    if "prefill" in only:
+        pf = bench_prefill(args, dist_, torch, strong=True)
+        achieved = pf["rank_flops"] / (pf["kernel_ms"] * 1e-3) / 1e12
+        timed_s = pf["ms"] * args.steps * 1e-3
+        peak_key = "bf16_tflops_sustained" if timed_s > 1.0 else "bf16_tflops"
+        line.update({
+            "value": PREFILL_FLOPS / (pf["ms"] * 1e-3) / 1e12, "ms_per_step": pf["ms"],
+            "roofline": {"bound": "tensor", "kernel": "prefill_bf16_kernel", "achieved": achieved,
+                         "peak": peaks[peak_key], "unit": "TFLOP/s", "frac": achieved / peaks[peak_key],
+                         "frac_of_spec": achieved / SPEC_PEAKS["bf16_tflops"],
+                         "peak_source": f"{peak_src} {peak_key}",
+                         "traffic": NCU_TRAFFIC_BYTES["prefill_bf16_kernel"] if W == 1 else None,
+                         "algorithmic_flops_per_launch": pf["rank_flops"], "heads_per_gpu": pf["heads"],
+                         "query_blocks_per_gpu": pf["blocks"]},
+            "e2e": {"value": PREFILL_FLOPS / (pf["e2e_ms"] * 1e-3) / 1e12, "unit": "TFLOP/s",
+                    "h2d_bytes_per_step": pf["h2d"], "d2h_bytes_per_step": pf["d2h"],
+                    "api": "TurboEngine.rope_append + TurboEngine.prefill (C ABI) from pinned host buffers"},
+            "gpu_launches": pf["launches_per_step"] * args.steps,
+            "clocks": pf["clocks"],
+        })
+        summary["prefill"] = {"tflops": round(line["value"], 1), "kernel_us": round(pf["kernel_ms"] * 1e3, 1),
+                              "frac": round(line["roofline"]["frac"], 4)}
+        if W > 1:
+            wk = bench_prefill(args, dist_, torch, strong=False)
+            line["weak_scaling"] = {
+                "value": W * PREFILL_FLOPS / (wk["ms"] * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": wk["ms"],
+                "kernel_ms": wk["kernel_ms"], "sequences": W, "parallelism": f"one whole sequence per GPU x{W}"}
+            summary["prefill"]["weak_tflops"] = round(line["weak_scaling"]["value"], 1)
+    dec = {}
+    for name in ("llama-32k", "qwen-batched"):
+        if ("decode-llama" if name == "llama-32k" else "decode-qwen") not in only:
+            continue
+        r = bench_decode(args, dist_, torch, name)
+        gbs = r["total_bytes"] / (r["ms"] * 1e-3) / 1e9
+        kern_gbs = r["local_bytes"] / (r["kernel_ms"] * 1e-3) / 1e9
+        dec[name] = {
+            "hbm_gbs": gbs, "tok_s": r["batch"] / (r["ms"] * 1e-3), "ms_per_step": r["ms"],
+            "bytes_per_step": r["total_bytes"], "split_context_merge": r["merge"], "scaling": "strong",
+            "stages_ms": {"decode_kernel": r["kernel_ms"], "all_gather": r["coll_ms"], "merge": r["merge_ms"]},
+            "roofline": {"bound": "hbm", "kernel": "decode_bf16_kernel", "achieved": kern_gbs,
+                         "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": kern_gbs / peaks["hbm_gbs"],
+                         "frac_of_spec": kern_gbs / SPEC_PEAKS["hbm_gbs"],
+                         "traffic": NCU_TRAFFIC_BYTES["decode_bf16_kernel"] if name == "llama-32k" and W == 1
+                         else None},
+            "parity": {"ok": r["parity_ok"], "max_abs": r["parity_max_abs"], "rel": r["parity_rel"],
+                       "against": "float64 restatement, 3 sampled rows x every q head, whole context"},
+        }
+        summary["decode_" + ("c4" if name == "llama-32k" else "c3")] = {
+            "gbs": round(gbs, 1), "tok_s": round(dec[name]["tok_s"], 1), "step_us": round(r["ms"] * 1e3, 1),
+            "kern_us": round(r["kernel_ms"] * 1e3, 1), "coll_us": round(r["coll_ms"] * 1e3, 1),
+            "merge_us": round(r["merge_ms"] * 1e3, 1), "frac_gpu": round(dec[name]["roofline"]["frac"], 4),
+            "parity_ok": r["parity_ok"]}
+    if dec:
         line["decode"] = dec
+        if line["value"] is None:  # a decode-only run: its first configuration is the line's metric
+            first = next(iter(dec.values()))
+            line.update({"metric": "decode-attn HBM GB/s", "value": first["hbm_gbs"], "unit": "GB/s",
+                         "ms_per_step": first["ms_per_step"], "roofline": first["roofline"]})
+    if "c1" in only:
         ms, byts = bench_c1(args, dist_, torch)
         gbs = byts / (ms * 1e-3) / 1e9
         line["c1_decode_f32"] = {
@@ -916,18 +1064,20 @@ def main():
                          "frac_of_spec": gbs / SPEC_PEAKS["hbm_gbs"], "traffic": None},
             "l2": "4 layers' weights and caches rotate (4 x 68 MB > 126 MB L2)",
         }
+        summary["c1"] = {"step_us": round(ms * 1e3, 1), "frac": round(gbs / peaks["hbm_gbs"], 4)}
         if dist_.rank == 0 and W == 1 and not args.no_cpu_baseline:
             v, nt = cpu_c1_sample()
             line["c1_decode_f32"]["cpu_baseline"] = {
                 "value": v, "unit": "tok/s", "cores": nt, "kind": "port",
                 "sample": "the whole C1 step: oracle QKV matvec + RoPE + append + GQA attention, best of 5"}
+    if "q8" in only:
         q8 = {}
         for T in (1, 8, 16):
             ms, byts = bench_q8(args, dist_, torch, T)
             gbs = W * byts / (ms * 1e-3) / 1e9
             q8[f"qwen7b-layer-T{T}"] = {
                 "hbm_gbs": gbs, "ms_per_step": ms, "bytes_per_step": byts, "tokens": T,
-                "linears": [f"{n} {r}x{c}" for n, r, c in Q8_LAYER],
+                "linears": [f"{n} {r_}x{c}" for n, r_, c in Q8_LAYER],
                 "roofline": {"bound": "hbm", "kernel": "q8_linear_kernel (with q8_prep_x_kernel)",
                              "achieved": gbs / W, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                              "frac": gbs / W / peaks["hbm_gbs"], "traffic": None},
@@ -938,6 +1088,8 @@ def main():
                     "value": v, "unit": "GB/s", "cores": nt, "kind": "port",
                     "sample": "64 rows of each linear: oracle Q8 dequantise + matvec"}
         line["q8_linear"] = q8
+        summary["q8_frac"] = {k.split("-")[-1]: round(v["roofline"]["frac"], 3) for k, v in q8.items()}
+    if "layer" in only:
         lay = {}
         for B in (1, 16):
             ms, byts = bench_layer_q8(args, dist_, torch, B)
@@ -951,6 +1103,7 @@ def main():
                              "frac": byts / (ms * 1e-3) / 1e9 / peaks["hbm_gbs"], "traffic": None},
             }
         line["decoder_layer_q8"] = lay
+    if "repack" in only:
         ms, e2e_ms, sb, moved = bench_oom_repack(args, dist_, torch)
         rp = {
             "workload": "device repack of a Qwen2.5-7B gate matrix's .oom Q8 block stream (18944 x 3584, 70.5 MB)",
@@ -968,6 +1121,7 @@ def main():
                                   "sample": "2048 x 3584 of the same stream: the oracle's block walk to f32",
                                   "host_unpack_gbs": unp}
         line["oom_repack"] = rp
+    if "model" in only:
         B, P, G = 16, 2048, 256
         r = bench_model_q8(args, dist_, torch, B, P, G)
         step_ms = r["ms"] / G
@@ -983,11 +1137,16 @@ def main():
             "cpu_baseline": None,
             "cpu_baseline_note": "not run: the full-size CPU reference model is infeasible on the host",
         }
-    if dist_.rank == 0 and W == 1 and not args.no_cpu_baseline:
+        summary["model_q8"] = {"tok_s": round(line["model_q8"]["tok_s"], 1),
+                               "frac": round(line["model_q8"]["frac_of_hbm"], 4)}
+    if "prefill" in only and dist_.rank == 0 and W == 1 and not args.no_cpu_baseline:
         v, nt, desc = cpu_prefill_sample()
         v1, _, desc1 = cpu_prefill_sample(seconds_budget=3.0, threads=1)
         line["cpu_baseline"] = {"value": v, "unit": "TFLOP/s", "cores": nt, "kind": "port", "sample": desc,
                                 "single_thread": {"value": v1, "cores": 1, "sample": desc1}}
+    # the compact summary goes last: a reader that keeps only the end of the line still sees the
+    # decode half of the metric and the per-stage split
+    line["summary"] = summary
     if dist_.rank == 0:
         print(json.dumps(line))
     dist_.close()

@@ -54,6 +54,11 @@ typedef enum oomattn_status {
 } oomattn_status;
 
 enum { OOMATTN_DTYPE_F32 = 0, OOMATTN_DTYPE_BF16 = 1 };
+/* Floats per (row, q head) in the packed decode output: O in [0, 128), the
+ * natural-log LSE at 128, 3 floats of padding (16-byte aligned rows). */
+#define OOMATTN_PACKED_STRIDE 132
+/* Test-only flags (oomattn_set_test_flags). */
+enum { OOMATTN_TEST_DROP_DECODE_COPIES = 1 };
 /* RoPE pairing: split-half pairs (x[i], x[i+64]) -- apply_rope_llama,
  * src/oomllama_turbo.rs:443-467, and TurboEngine::apply_rope :737-786;
  * interleaved pairs (x[2i], x[2i+1]) -- apply_rope, :402-438. */
@@ -94,6 +99,17 @@ int oomattn_set_stream(oomattn_ctx* ctx, void* stream);
 /* Waits for the context's stream and reports device-side check failures
  * (OOMATTN_ERR_TIMEOUT / OOMATTN_ERR_DEVICE_CHECK), clearing them. */
 int oomattn_sync(oomattn_ctx* ctx);
+
+/* Limit of every bounded device-side wait of this context's kernels (default
+ * 2 s).  A wait that runs out records OOMATTN_ERR_TIMEOUT for oomattn_sync and
+ * ends its kernel.  No counterpart in the reference (it has no device waits). */
+int oomattn_set_wait_limit(oomattn_ctx* ctx, uint64_t timeout_ns);
+
+/* Test-only launch flags, 0 in normal use.  OOMATTN_TEST_DROP_DECODE_COPIES
+ * makes the bf16 decode's copy producer issue nothing, so that its consumers'
+ * bounded waits run out: a test of the timeout path that faults nothing.  No
+ * counterpart in the reference. */
+int oomattn_set_test_flags(oomattn_ctx* ctx, int32_t flags);
 
 /* TurboEngine::reset / ModelKVCache::clear (src/oomllama_turbo.rs:95-99,
  * 726-728): every layer's length of every sequence becomes 0.  Page
@@ -158,6 +174,15 @@ int oomattn_rope_append(oomattn_ctx* ctx, int32_t layer, int32_t n_seqs, const i
                         int32_t n_new, const void* q, const void* k, const void* v, int32_t in_dtype,
                         const float* bq, const float* bk, const float* bv, void* q_out, int32_t q_out_dtype);
 
+/* The q half of the RoPE step (TurboEngine::apply_rope, src/oomllama_turbo.rs:
+ * 737-786, and apply_rope :402-438, by the context's variant) at explicit
+ * positions, with nothing appended: q rows [n_rows][n_heads][128] in in_dtype
+ * (+ bq f32 or NULL) -> q_out in q_out_dtype; positions (host) < max_seq_len.
+ * Used by the ranks of a split context that do not hold the new token's slot:
+ * they attend with the same rotated query as the rank that appends it. */
+int oomattn_rope_q(oomattn_ctx* ctx, int32_t n_rows, const int32_t* positions /* host */, const void* q,
+                   int32_t in_dtype, const float* bq, void* q_out, int32_t q_out_dtype);
+
 /* Fused QKV projection + bias + RoPE + append (src/oomllama_turbo.rs:638-681).
  *   x: f32 [T][hidden]; wq [n_heads*128][hidden], wk/wv [n_kv*128][hidden] in
  *   w_dtype; bq/bk/bv f32 or NULL; q_out as in oomattn_rope_append.
@@ -178,11 +203,23 @@ int oomattn_qkv_rope_append(oomattn_ctx* ctx, int32_t layer, int32_t n_seqs, con
 int oomattn_decode(oomattn_ctx* ctx, int32_t layer, int32_t n_rows, const int32_t* seq_ids /* host */,
                    const int32_t* lens /* host, may be NULL */, const float* q, float* out, float* lse);
 
+/* oomattn_decode with the outputs packed for the split-context exchange
+ * (flash_attention_forward's decode rows, src/oomllama_turbo.rs:304-369):
+ * packed [n_rows][n_heads][OOMATTN_PACKED_STRIDE] f32 (16-byte aligned), O
+ * at [0, 128) and the natural-log LSE at 128, so one collective moves both. */
+int oomattn_decode_packed(oomattn_ctx* ctx, int32_t layer, int32_t n_rows, const int32_t* seq_ids /* host */,
+                          const int32_t* lens /* host, may be NULL */, const float* q, float* packed);
+
 /* K-B2 / K-D merge: combine n_parts split-context results of n_rows rows:
  * parts [n_parts][n_rows][128] (each normalised), lses [n_parts][n_rows]
  * (natural log); out [n_rows][128], lse_out [n_rows] or NULL. */
 int oomattn_merge_partials(oomattn_ctx* ctx, int32_t n_parts, int32_t n_rows, const float* parts, const float* lses,
                            float* out, float* lse_out);
+
+/* The same merge over packed partials [n_parts][n_rows][OOMATTN_PACKED_STRIDE]
+ * (the all-gathered outputs of oomattn_decode_packed, n_rows = rows x heads). */
+int oomattn_merge_packed(oomattn_ctx* ctx, int32_t n_parts, int32_t n_rows, const float* packed, float* out,
+                         float* lse_out);
 
 /* Decode for callers that cannot allocate device memory.  No counterpart in
  * the reference.  Some hosts cannot call cudaMalloc while decoding: their
@@ -196,23 +233,40 @@ int oomattn_merge_partials(oomattn_ctx* ctx, int32_t n_parts, int32_t n_rows, co
  *   device, stream: the GPU and cudaStream_t to run on
  *   kv_dtype: OOMATTN_DTYPE_BF16 or OOMATTN_DTYPE_F32
  *   k_pool, v_pool: [n_pool_pages][n_kv_heads][16][128] in kv_dtype, 16-byte aligned
- *   block_table: device int32 [*][max_pages_per_seq]; every page id a row
- *     reaches must be < n_pool_pages (ids are not validated on the host)
+ *   block_table: device int32 [n_block_rows][max_pages_per_seq]
  *   q, out: f32 [n_rows][n_heads][128]; lse: f32 [n_rows][n_heads] or NULL
  *   seq_ids, lens (host): row z attends to the first lens[z] slots of block-table row seq_ids[z]
  *   errbuf (host, optional): receives a message when the call fails
+ * The caller keeps these rules, which only the device can check:
+ *   - every seq_ids[z] is below the block table's row count n_block_rows (the
+ *     kernels read row seq_ids[z] without knowing how many rows there are);
+ *   - every page id a row reaches is below n_pool_pages.  A larger id is read as
+ *     the pool's last page and reported by oomattn_decode_static_scratch_status,
+ *     so the pool should end with a zeroed page that no sequence uses;
+ *   - slots past lens[z] in a row's last page hold finite values (they are
+ *     weighted by zero, and 0 x inf or 0 x NaN would reach the output).
  * Limits: n_rows <= 128, n_kv_heads <= 64, n_heads / n_kv_heads <= 8; larger
  * requests return OOMATTN_ERR_OUT_OF_RANGE.  The split count is capped so
  * that n_rows * n_heads * splits <= 16384.  The first call on a device looks
  * up the array's address and must come before any stream capture on that
  * device.  All calls on a device share the array: calls whose GPU work
  * overlaps (different streams, other host threads) race and must be ordered
- * by the caller. */
+ * by the caller.  Device-side errors (an out-of-range page id, a wait that
+ * gave up) accumulate in a status word inside the same array until
+ * oomattn_decode_static_scratch_status reads them. */
 int oomattn_decode_static_scratch(int device, void* stream, int32_t kv_dtype, const void* k_pool, const void* v_pool,
                                   int32_t n_pool_pages, const int32_t* block_table, int32_t max_pages_per_seq,
                                   int32_t n_heads, int32_t n_kv_heads, float softmax_scale, int32_t n_rows,
                                   const int32_t* seq_ids /* host */, const int32_t* lens /* host */, const float* q,
                                   float* out, float* lse, char* errbuf /* host, may be NULL */, int32_t errbuf_len);
+
+/* The device-side error bits that oomattn_decode_static_scratch calls on
+ * `device` have recorded since the last read, and clears them: waits for
+ * `stream`, writes the bits to *flags_out (host) and returns OOMATTN_OK (none),
+ * OOMATTN_ERR_TIMEOUT or OOMATTN_ERR_DEVICE_CHECK.  Allocates nothing.  No
+ * counterpart in the reference. */
+int oomattn_decode_static_scratch_status(int device, void* stream, int32_t* flags_out /* host */,
+                                         char* errbuf /* host, may be NULL */, int32_t errbuf_len);
 
 /* ---------------------------------------------------------------- K-C */
 
@@ -222,6 +276,16 @@ int oomattn_decode_static_scratch(int device, void* stream, int32_t kv_dtype, co
  *   out_dtype; lse: f32 [n_new][n_heads] or NULL. */
 int oomattn_prefill(oomattn_ctx* ctx, int32_t layer, int32_t seq, int32_t n_new, const void* q, void* out,
                     int32_t out_dtype, float* lse);
+
+/* oomattn_prefill for some of the 256-row query blocks only: block b is query
+ * rows [256 b, 256 b + 256) of the n_new; the launch computes the blocks of the
+ * n_ranges ranges [ranges[2i], ranges[2i+1]) (host, at most 4, disjoint, inside
+ * [0, ceil(n_new / 256))) and writes only their rows of out and lse.  A rank of
+ * a prefill sharded beyond the kv-head count takes a zig-zag share of the
+ * blocks (flash_attention_forward's causal path, src/oomllama_turbo.rs:344-368,
+ * split over GPUs; the reference has no multi-GPU attention). */
+int oomattn_prefill_blocks(oomattn_ctx* ctx, int32_t layer, int32_t seq, int32_t n_new, const void* q, void* out,
+                           int32_t out_dtype, float* lse, int32_t n_ranges, const int32_t* ranges /* host */);
 
 /* ------------------------------------------------------- the layer step */
 

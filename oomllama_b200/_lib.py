@@ -17,6 +17,8 @@ STATUS_NAMES = {
     7: "NO_MEMORY", 8: "UNSUPPORTED", 9: "DEVICE_CHECK",
 }
 DTYPE_F32, DTYPE_BF16 = 0, 1
+PACKED_STRIDE = 132                 # floats per (row, q head) of a packed decode output: O[128], lse, pad
+TEST_DROP_DECODE_COPIES = 1         # oomattn_set_test_flags: the bf16 decode's producer issues no copies
 ROPE_SPLIT_HALF, ROPE_INTERLEAVED = 0, 1
 
 # Every exported symbol of include/oomattn.h.
@@ -28,6 +30,8 @@ EXPORTS = (
     "oomattn_prefill", "oomattn_attention_forward_with_bias", "oomattn_decode_static_scratch",
     "oomattn_q8_unpack", "oomattn_q8_linear", "oomattn_rmsnorm", "oomattn_q8_mlp", "oomattn_decoder_layer_q8",
     "oomattn_embed_q8", "oomattn_argmax", "oomattn_decode_step_q8", "oomattn_oom_scan", "oomattn_q8_repack",
+    "oomattn_set_wait_limit", "oomattn_set_test_flags", "oomattn_rope_q", "oomattn_decode_packed",
+    "oomattn_merge_packed", "oomattn_decode_static_scratch_status", "oomattn_prefill_blocks",
 )
 
 
@@ -126,6 +130,13 @@ def load():
         "oomattn_oom_scan": ([P, ctypes.c_uint64, ctypes.POINTER(OomTensor), I, ctypes.POINTER(ctypes.c_int32),
                               ctypes.c_char_p, I], ctypes.c_int),
         "oomattn_q8_repack": ([P, P, ctypes.c_uint64, ctypes.c_int64, P, P, P], ctypes.c_int),
+        "oomattn_set_wait_limit": ([P, ctypes.c_uint64], ctypes.c_int),
+        "oomattn_set_test_flags": ([P, I], ctypes.c_int),
+        "oomattn_rope_q": ([P, I, IP, P, I, P, P, I], ctypes.c_int),
+        "oomattn_decode_packed": ([P, I, I, IP, IP, P, P], ctypes.c_int),
+        "oomattn_merge_packed": ([P, I, I, P, P, P], ctypes.c_int),
+        "oomattn_decode_static_scratch_status": ([ctypes.c_int, P, IP, ctypes.c_char_p, I], ctypes.c_int),
+        "oomattn_prefill_blocks": ([P, I, I, I, P, P, I, P, I, IP], ctypes.c_int),
     }
     for name, (args, res) in sig.items():
         fn = getattr(L, name)

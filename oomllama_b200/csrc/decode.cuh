@@ -79,10 +79,11 @@ __device__ __forceinline__ void combine_and_store(const MergeSmem& ms, const Dec
     for (int i = 0; i < 8; ++i) acc[i] *= inv;
     lse2 = M + log2f(lsum);
     if (nsplit == 1) {
-      float4* op = reinterpret_cast<float4*>(a.out + ((size_t)z * a.n_heads + h) * kHeadDim + d0);
+      float4* op = reinterpret_cast<float4*>(a.out + ((size_t)z * a.n_heads + h) * a.o_stride + d0);
       op[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
       op[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
-      if (a.lse && (tid & 15) == 0) a.lse[(size_t)z * a.n_heads + h] = lse2 * 0.69314718055994531f;
+      if (a.lse && (tid & 15) == 0)
+        a.lse[((size_t)z * a.n_heads + h) * a.lse_stride] = lse2 * 0.69314718055994531f;
     } else {
       const size_t prow = ((size_t)z * a.n_heads + h) * a.max_splits + split;
       float4* pp = reinterpret_cast<float4*>(a.part_o + prow * kHeadDim + d0);
@@ -129,10 +130,11 @@ __device__ __forceinline__ void combine_and_store(const MergeSmem& ms, const Dec
       acc[4] += wt * v.x; acc[5] += wt * v.y; acc[6] += wt * v.z; acc[7] += wt * v.w;
     }
     const float inv = 1.f / wsum;
-    float4* op = reinterpret_cast<float4*>(a.out + ((size_t)z * a.n_heads + h) * kHeadDim + d0);
+    float4* op = reinterpret_cast<float4*>(a.out + ((size_t)z * a.n_heads + h) * a.o_stride + d0);
     op[0] = make_float4(acc[0] * inv, acc[1] * inv, acc[2] * inv, acc[3] * inv);
     op[1] = make_float4(acc[4] * inv, acc[5] * inv, acc[6] * inv, acc[7] * inv);
-    if (a.lse && (tid & 15) == 0) a.lse[(size_t)z * a.n_heads + h] = (M + log2f(wsum)) * 0.69314718055994531f;
+    if (a.lse && (tid & 15) == 0)
+      a.lse[((size_t)z * a.n_heads + h) * a.lse_stride] = (M + log2f(wsum)) * 0.69314718055994531f;
   }
   if (tid == 0) a.counters[(size_t)z * n_kv + g] = 0u;
 }
@@ -187,8 +189,8 @@ __device__ __forceinline__ void prefetch_then_wait(const KVPool& pool, const Dec
 __device__ __forceinline__ void write_empty_row(const DecodeArgs& a, int z, int g) {
   for (int i = threadIdx.x; i < a.group * kHeadDim; i += blockDim.x) {
     const int h = g * a.group + i / kHeadDim;
-    a.out[((size_t)z * a.n_heads + h) * kHeadDim + (i % kHeadDim)] = 0.f;
-    if (a.lse && (i % kHeadDim) == 0) a.lse[(size_t)z * a.n_heads + h] = -INFINITY;
+    a.out[((size_t)z * a.n_heads + h) * a.o_stride + (i % kHeadDim)] = 0.f;
+    if (a.lse && (i % kHeadDim) == 0) a.lse[((size_t)z * a.n_heads + h) * a.lse_stride] = -INFINITY;
   }
 }
 
@@ -230,7 +232,9 @@ __global__ void __launch_bounds__((kDecWarps + 1) * 32, 2)
 
   if (warp == kDecWarps) {
     // ---------------- producer: one elected lane issues the TMA loads
-    if (lane == 0) {
+    // (kTestDropDecodeCopies: a test makes the consumers' bounded waits run
+    // out by issuing nothing; they record kDevErrTimeout and the CTA ends.)
+    if (lane == 0 && !(a.test_flags & kTestDropDecodeCopies)) {
       prefetch_tensormap(&kmap);
       prefetch_tensormap(&vmap);
       const int* bt = pool.block_table + (size_t)seq * pool.max_pages_per_seq;
@@ -474,14 +478,18 @@ __global__ void __launch_bounds__(kDecWarps * 32)
 }
 
 // K-B2 standalone: merge P split-context partials (from P GPUs or P launches)
-// given as normalised O_p [P][rows][128] and natural-log lse_p [P][rows].
-__global__ void merge_partials_kernel(const float* __restrict__ parts, const float* __restrict__ lses, int n_parts,
-                                      int n_rows, float* __restrict__ out, float* __restrict__ lse_out) {
+// given as normalised O_p and natural-log lse_p; partial (p, r) has its O at
+// parts + (p * n_rows + r) * part_stride and its lse at lses[(p * n_rows + r) *
+// lse_stride] (128 / 1 for separate [P][rows][128] and [P][rows] arrays, 132 /
+// 132 for the packed (O, lse) rows that one collective moves).
+__global__ void merge_partials_kernel(const float* __restrict__ parts, const float* __restrict__ lses,
+                                      int part_stride, int lse_stride, int n_parts, int n_rows,
+                                      float* __restrict__ out, float* __restrict__ lse_out) {
   const int r = blockIdx.x;
   const int d = threadIdx.x;  // 128 threads
   if (r >= n_rows) return;
   float M = -INFINITY;
-  for (int p = 0; p < n_parts; ++p) M = fmaxf(M, lses[(size_t)p * n_rows + r]);
+  for (int p = 0; p < n_parts; ++p) M = fmaxf(M, lses[((size_t)p * n_rows + r) * lse_stride]);
   if (M == -INFINITY) {
     out[(size_t)r * kHeadDim + d] = 0.f;
     if (lse_out && d == 0) lse_out[r] = -INFINITY;
@@ -489,10 +497,10 @@ __global__ void merge_partials_kernel(const float* __restrict__ parts, const flo
   }
   float acc = 0.f, wsum = 0.f;
   for (int p = 0; p < n_parts; ++p) {
-    const float lp = lses[(size_t)p * n_rows + r];
+    const float lp = lses[((size_t)p * n_rows + r) * lse_stride];
     const float wt = (lp == -INFINITY) ? 0.f : expf(lp - M);
     wsum += wt;
-    acc += wt * parts[((size_t)p * n_rows + r) * kHeadDim + d];
+    acc += wt * parts[((size_t)p * n_rows + r) * part_stride + d];
   }
   out[(size_t)r * kHeadDim + d] = acc / wsum;
   if (lse_out && d == 0) lse_out[r] = M + logf(wsum);

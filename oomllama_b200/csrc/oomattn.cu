@@ -69,6 +69,7 @@ struct oomattn_ctx {
   size_t esize = 4;
   float scale = 0.f;
   unsigned long long timeout_ns = kDefaultTimeoutNs;
+  int test_flags = 0;  // OOMATTN_TEST_* launch flags (tests only)
   // device state
   void* kpool = nullptr;
   void* vpool = nullptr;
@@ -200,6 +201,24 @@ int encode_q_map(oomattn_ctx* ctx, const void* q, int n_new, CUtensorMap* map) {
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(ctx, OOMATTN_ERR_CUDA, "cuTensorMapEncodeTiled(q) failed: %d", (int)r);
+  return OOMATTN_OK;
+}
+
+// The prefill output [n_new][n_heads][128] (f32 or bf16) as the target of
+// the epilogue's TMA stores: boxes of 128 rows x 128 bytes (32 f32 or 64 bf16
+// columns) of one head, 128-byte swizzled; rows past n_new are clipped.
+int encode_out_map(oomattn_ctx* ctx, void* out, int n_new, bool bf16, CUtensorMap* map) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) return fail(ctx, OOMATTN_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  const uint64_t es = bf16 ? 2 : 4;
+  cuuint64_t dims[3] = {(cuuint64_t)kHeadDim, (cuuint64_t)ctx->cfg.n_heads, (cuuint64_t)n_new};
+  cuuint64_t strides[2] = {(cuuint64_t)kHeadDim * es, (cuuint64_t)ctx->cfg.n_heads * kHeadDim * es};
+  cuuint32_t box[3] = {(cuuint32_t)(128 / es), 1, 128};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, out, dims,
+                   strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(ctx, OOMATTN_ERR_CUDA, "cuTensorMapEncodeTiled(out) failed: %d", (int)r);
   return OOMATTN_OK;
 }
 
@@ -340,7 +359,7 @@ int launch_rope_append(oomattn_ctx* ctx, const AppendArgs& ap, const SeqBatch& s
   for (const void* p : ptrs)
     if (p && !aligned16(p)) return fail(ctx, OOMATTN_ERR_INVALID_ARG, "tensors and biases must be 16-byte aligned");
   const int hq = ctx->cfg.n_heads, hkv = ctx->cfg.n_kv_heads;
-  const long long units = (long long)T * ((hq + 2 * hkv) * 8 - (ap.q ? 0 : hq * 8));
+  const long long units = (long long)T * ((ap.k ? (hq + 2 * hkv) * 8 : hq * 8) - (ap.q ? 0 : hq * 8));
   if (units >= (1ll << 31)) return fail(ctx, OOMATTN_ERR_OUT_OF_RANGE, "%d tokens in one append call", T);
   // four CTAs per SM, each thread looping over several 16-element units (measured: 16.1 us for a
   // 4096-token bf16 prefill against 18.1 us with one unit per thread)
@@ -470,7 +489,8 @@ int plan_decode(const SeqBatch& sb, int n_kv, int slots, int max_splits, int fil
   return items;
 }
 
-int launch_decode_rows(oomattn_ctx* ctx, int layer, const SeqBatch& sb, const float* q, float* out, float* lse) {
+int launch_decode_rows(oomattn_ctx* ctx, int layer, const SeqBatch& sb, const float* q, float* out, float* lse,
+                       int o_stride, int lse_stride) {
   const int n_kv = ctx->cfg.n_kv_heads;
   const int slots = ctx->num_sms * (ctx->cfg.kv_dtype == OOMATTN_DTYPE_BF16 ? 2 : 3);
   int key[kMaxBatch + 1];
@@ -489,6 +509,9 @@ int launch_decode_rows(oomattn_ctx* ctx, int layer, const SeqBatch& sb, const fl
   a.q = q;
   a.out = out;
   a.lse = lse;
+  a.o_stride = o_stride;
+  a.lse_stride = lse_stride;
+  a.test_flags = ctx->test_flags;
   a.layer = layer;
   a.n_heads = ctx->cfg.n_heads;
   a.group = ctx->group;
@@ -526,6 +549,37 @@ int launch_decode_rows(oomattn_ctx* ctx, int layer, const SeqBatch& sb, const fl
 }  // namespace
 
 namespace {
+// Decode rows in launches of at most kMaxBatch rows; (row, head) outputs at
+// out + (row * n_heads + head) * o_stride and lse + (row * n_heads + head) * lse_stride.
+int decode_rows_impl(oomattn_ctx* ctx, int layer, int n_rows, const int32_t* seq_ids, const int32_t* lens,
+                     const float* q, float* out, float* lse, int o_stride, int lse_stride) {
+  int rc = check_layer(ctx, layer);
+  if (rc) return rc;
+  DeviceGuard dg(ctx->device);
+  const int hq = ctx->cfg.n_heads;
+  for (int r0 = 0; r0 < n_rows; r0 += kMaxBatch) {
+    const int n = std::min(kMaxBatch, n_rows - r0);
+    SeqBatch sb;
+    sb.n = n;
+    for (int z = 0; z < n; ++z) {
+      const int seq = seq_ids[r0 + z];
+      rc = check_seq(ctx, seq);
+      if (rc) return rc;
+      const int cur = ctx->h_len[(size_t)layer * ctx->cfg.max_seqs + seq];
+      const int len = lens ? lens[r0 + z] : cur;
+      if (len < 0 || len > cur)
+        return fail(ctx, OOMATTN_ERR_OUT_OF_RANGE, "row %d: length %d outside [0, %d]", r0 + z, len, cur);
+      sb.seq[z] = seq;
+      sb.len[z] = len;
+      sb.pos[z] = 0;
+    }
+    rc = launch_decode_rows(ctx, layer, sb, q + (size_t)r0 * hq * kHeadDim, out + (size_t)r0 * hq * o_stride,
+                            lse ? lse + (size_t)r0 * hq * lse_stride : nullptr, o_stride, lse_stride);
+    if (rc) return rc;
+  }
+  return OOMATTN_OK;
+}
+
 // The GEMV is a programmatic dependent of the kernel before it: it launches
 // during that kernel's tail and waits (griddepcontrol.wait) before reading x.
 template <int T, bool WBF16>
@@ -840,6 +894,42 @@ int oomattn_rope_append(oomattn_ctx* ctx, int32_t layer, int32_t n_seqs, const i
   return OOMATTN_OK;
 }
 
+int oomattn_rope_q(oomattn_ctx* ctx, int32_t n_rows, const int32_t* positions, const void* q, int32_t in_dtype,
+                   const float* bq, void* q_out, int32_t q_out_dtype) {
+  if (!ctx) return OOMATTN_ERR_INVALID_ARG;
+  if (!positions || !q || !q_out || n_rows <= 0) return fail(ctx, OOMATTN_ERR_INVALID_ARG, "bad rope_q arguments");
+  int rc = validate_dtype(ctx, in_dtype, "rope_q input");
+  if (!rc) rc = validate_dtype(ctx, q_out_dtype, "rope_q q_out");
+  if (rc) return rc;
+  DeviceGuard dg(ctx->device);
+  const int in_es = in_dtype == OOMATTN_DTYPE_BF16 ? 2 : 4, out_es = q_out_dtype == OOMATTN_DTYPE_BF16 ? 2 : 4;
+  for (int r0 = 0; r0 < n_rows; r0 += kMaxBatch) {
+    const int n = std::min(kMaxBatch, n_rows - r0);
+    SeqBatch sb;
+    sb.n = n;
+    for (int z = 0; z < n; ++z) {
+      const int pos = positions[r0 + z];
+      if (pos < 0 || pos >= ctx->cfg.max_seq_len)
+        return fail(ctx, OOMATTN_ERR_OUT_OF_RANGE, "row %d: position %d outside [0, %d)", r0 + z, pos,
+                    ctx->cfg.max_seq_len);
+      sb.seq[z] = 0;
+      sb.len[z] = 0;
+      sb.pos[z] = pos;
+    }
+    AppendArgs ap = base_append_args(ctx, 0, 1);
+    ap.q = (const uint8_t*)q + (size_t)r0 * ctx->cfg.n_heads * kHeadDim * in_es;
+    ap.k = nullptr;  // q rows only: nothing is appended
+    ap.v = nullptr;
+    ap.in_bf16 = in_dtype == OOMATTN_DTYPE_BF16;
+    ap.q_out = (uint8_t*)q_out + (size_t)r0 * ctx->cfg.n_heads * kHeadDim * out_es;
+    ap.q_out_bf16 = q_out_dtype == OOMATTN_DTYPE_BF16;
+    ap.bq = bq;
+    rc = launch_rope_append(ctx, ap, sb, n);
+    if (rc) return rc;
+  }
+  return OOMATTN_OK;
+}
+
 int oomattn_qkv_rope_append(oomattn_ctx* ctx, int32_t layer, int32_t n_seqs, const int32_t* seq_ids, int32_t n_new,
                             const float* x, const void* wq, const void* wk, const void* wv, int32_t w_dtype,
                             const float* bq, const float* bk, const float* bv, void* q_out, int32_t q_out_dtype) {
@@ -930,31 +1020,18 @@ int oomattn_decode(oomattn_ctx* ctx, int32_t layer, int32_t n_rows, const int32_
                    const float* q, float* out, float* lse) {
   if (!ctx) return OOMATTN_ERR_INVALID_ARG;
   if (!seq_ids || !q || !out || n_rows <= 0) return fail(ctx, OOMATTN_ERR_INVALID_ARG, "bad decode arguments");
-  int rc = check_layer(ctx, layer);
-  if (rc) return rc;
-  DeviceGuard dg(ctx->device);
-  const int hq = ctx->cfg.n_heads;
-  for (int r0 = 0; r0 < n_rows; r0 += kMaxBatch) {
-    const int n = std::min(kMaxBatch, n_rows - r0);
-    SeqBatch sb;
-    sb.n = n;
-    for (int z = 0; z < n; ++z) {
-      const int seq = seq_ids[r0 + z];
-      rc = check_seq(ctx, seq);
-      if (rc) return rc;
-      const int cur = ctx->h_len[(size_t)layer * ctx->cfg.max_seqs + seq];
-      const int len = lens ? lens[r0 + z] : cur;
-      if (len < 0 || len > cur)
-        return fail(ctx, OOMATTN_ERR_OUT_OF_RANGE, "row %d: length %d outside [0, %d]", r0 + z, len, cur);
-      sb.seq[z] = seq;
-      sb.len[z] = len;
-      sb.pos[z] = 0;
-    }
-    rc = launch_decode_rows(ctx, layer, sb, q + (size_t)r0 * hq * kHeadDim, out + (size_t)r0 * hq * kHeadDim,
-                            lse ? lse + (size_t)r0 * hq : nullptr);
-    if (rc) return rc;
-  }
-  return OOMATTN_OK;
+  return decode_rows_impl(ctx, layer, n_rows, seq_ids, lens, q, out, lse, kHeadDim, 1);
+}
+
+int oomattn_decode_packed(oomattn_ctx* ctx, int32_t layer, int32_t n_rows, const int32_t* seq_ids,
+                          const int32_t* lens, const float* q, float* packed) {
+  if (!ctx) return OOMATTN_ERR_INVALID_ARG;
+  if (!seq_ids || !q || !packed || n_rows <= 0)
+    return fail(ctx, OOMATTN_ERR_INVALID_ARG, "bad decode_packed arguments");
+  if (reinterpret_cast<uintptr_t>(packed) % 16 != 0)
+    return fail(ctx, OOMATTN_ERR_INVALID_ARG, "packed must be 16-byte aligned");
+  return decode_rows_impl(ctx, layer, n_rows, seq_ids, lens, q, packed, packed + kHeadDim, OOMATTN_PACKED_STRIDE,
+                          OOMATTN_PACKED_STRIDE);
 }
 
 int oomattn_merge_partials(oomattn_ctx* ctx, int32_t n_parts, int32_t n_rows, const float* parts, const float* lses,
@@ -964,15 +1041,51 @@ int oomattn_merge_partials(oomattn_ctx* ctx, int32_t n_parts, int32_t n_rows, co
     return fail(ctx, OOMATTN_ERR_INVALID_ARG, "bad merge arguments");
   if (n_rows == 0) return OOMATTN_OK;
   DeviceGuard dg(ctx->device);
-  merge_partials_kernel<<<n_rows, kHeadDim, 0, ctx->stream>>>(parts, lses, n_parts, n_rows, out, lse_out);
+  merge_partials_kernel<<<n_rows, kHeadDim, 0, ctx->stream>>>(parts, lses, kHeadDim, 1, n_parts, n_rows, out,
+                                                               lse_out);
   CKLAUNCH();
+  return OOMATTN_OK;
+}
+
+int oomattn_merge_packed(oomattn_ctx* ctx, int32_t n_parts, int32_t n_rows, const float* packed, float* out,
+                         float* lse_out) {
+  if (!ctx) return OOMATTN_ERR_INVALID_ARG;
+  if (!packed || !out || n_parts <= 0 || n_rows < 0)
+    return fail(ctx, OOMATTN_ERR_INVALID_ARG, "bad merge_packed arguments");
+  if (n_rows == 0) return OOMATTN_OK;
+  DeviceGuard dg(ctx->device);
+  merge_partials_kernel<<<n_rows, kHeadDim, 0, ctx->stream>>>(packed, packed + kHeadDim, OOMATTN_PACKED_STRIDE,
+                                                               OOMATTN_PACKED_STRIDE, n_parts, n_rows, out, lse_out);
+  CKLAUNCH();
+  return OOMATTN_OK;
+}
+
+int oomattn_set_wait_limit(oomattn_ctx* ctx, uint64_t timeout_ns) {
+  if (!ctx || timeout_ns == 0) return fail(ctx, OOMATTN_ERR_INVALID_ARG, "the wait limit must be positive");
+  ctx->timeout_ns = timeout_ns;
+  return OOMATTN_OK;
+}
+
+int oomattn_set_test_flags(oomattn_ctx* ctx, int32_t flags) {
+  if (!ctx || (flags & ~OOMATTN_TEST_DROP_DECODE_COPIES))
+    return fail(ctx, OOMATTN_ERR_INVALID_ARG, "unknown test flags %d", flags);
+  ctx->test_flags = flags;
   return OOMATTN_OK;
 }
 
 int oomattn_prefill(oomattn_ctx* ctx, int32_t layer, int32_t seq, int32_t n_new, const void* q, void* out,
                     int32_t out_dtype, float* lse) {
   if (!ctx) return OOMATTN_ERR_INVALID_ARG;
-  if (!q || !out || n_new <= 0) return fail(ctx, OOMATTN_ERR_INVALID_ARG, "bad prefill arguments");
+  if (n_new <= 0) return fail(ctx, OOMATTN_ERR_INVALID_ARG, "bad prefill arguments");
+  const int32_t all[2] = {0, (n_new + 255) / 256};
+  return oomattn_prefill_blocks(ctx, layer, seq, n_new, q, out, out_dtype, lse, 1, all);
+}
+
+int oomattn_prefill_blocks(oomattn_ctx* ctx, int32_t layer, int32_t seq, int32_t n_new, const void* q, void* out,
+                           int32_t out_dtype, float* lse, int32_t n_ranges, const int32_t* ranges) {
+  if (!ctx) return OOMATTN_ERR_INVALID_ARG;
+  if (!q || !out || n_new <= 0 || !ranges || n_ranges <= 0)
+    return fail(ctx, OOMATTN_ERR_INVALID_ARG, "bad prefill arguments");
   int rc = check_layer(ctx, layer);
   if (!rc) rc = check_seq(ctx, seq);
   if (!rc) rc = validate_dtype(ctx, out_dtype, "prefill out");
@@ -983,14 +1096,36 @@ int oomattn_prefill(oomattn_ctx* ctx, int32_t layer, int32_t seq, int32_t n_new,
   if (ctx->prefill_regs != kPfLaunchRegs)
     return fail(ctx, OOMATTN_ERR_UNSUPPORTED, "prefill kernel compiled with %d registers per thread, expected %d",
                 ctx->prefill_regs, kPfLaunchRegs);
-  if (reinterpret_cast<uintptr_t>(q) % 16 != 0) return fail(ctx, OOMATTN_ERR_INVALID_ARG, "q must be 16-byte aligned");
+  if (reinterpret_cast<uintptr_t>(q) % 16 != 0 || reinterpret_cast<uintptr_t>(out) % 16 != 0)
+    return fail(ctx, OOMATTN_ERR_INVALID_ARG, "q and out must be 16-byte aligned");
   const int L = ctx->h_len[(size_t)layer * ctx->cfg.max_seqs + seq];
   if (n_new > L) return fail(ctx, OOMATTN_ERR_OUT_OF_RANGE, "n_new %d exceeds the cached length %d", n_new, L);
-  DeviceGuard dg(ctx->device);
-  CUtensorMap qmap;
-  rc = encode_q_map(ctx, q, n_new, &qmap);
-  if (rc) return rc;
+  const int n_pairs = (n_new + 255) / 256;
+  if (n_ranges > kPfMaxRanges)
+    return fail(ctx, OOMATTN_ERR_INVALID_ARG, "%d block ranges (at most %d)", n_ranges, kPfMaxRanges);
   PrefillArgs a;
+  memset(&a, 0, sizeof(a));
+  // ranges sorted by descending start; they must lie in [0, n_pairs) and not overlap
+  int order[kPfMaxRanges];
+  for (int r = 0; r < n_ranges; ++r) order[r] = r;
+  std::sort(order, order + n_ranges, [&](int x, int y) { return ranges[2 * x] > ranges[2 * y]; });
+  long long blocks = 0;
+  for (int i = 0; i < n_ranges; ++i) {
+    const int lo = ranges[2 * order[i]], hi = ranges[2 * order[i] + 1];
+    if (lo < 0 || hi > n_pairs || lo >= hi)
+      return fail(ctx, OOMATTN_ERR_OUT_OF_RANGE, "block range [%d, %d) outside [0, %d) or empty", lo, hi, n_pairs);
+    if (i > 0 && hi > a.range_lo[i - 1])
+      return fail(ctx, OOMATTN_ERR_INVALID_ARG, "block ranges overlap");
+    a.range_lo[i] = lo;
+    a.range_hi[i] = hi;
+    blocks += hi - lo;
+  }
+  a.n_ranges = n_ranges;
+  DeviceGuard dg(ctx->device);
+  CUtensorMap qmap, omap;
+  rc = encode_q_map(ctx, q, n_new, &qmap);
+  if (!rc) rc = encode_out_map(ctx, out, n_new, out_dtype == OOMATTN_DTYPE_BF16, &omap);
+  if (rc) return rc;
   a.out = out;
   a.out_bf16 = out_dtype == OOMATTN_DTYPE_BF16;
   a.lse = lse;
@@ -1000,12 +1135,12 @@ int oomattn_prefill(oomattn_ctx* ctx, int32_t layer, int32_t seq, int32_t n_new,
   a.layer = layer;
   a.n_heads = ctx->cfg.n_heads;
   a.group = ctx->group;
-  a.n_pairs = (n_new + 255) / 256;
+  a.n_pairs = n_pairs;
   a.qscale = ctx->scale * 1.4426950408889634f;
   a.status = ctx->d_status;
   a.timeout_ns = ctx->timeout_ns;
-  prefill_bf16_kernel<<<a.n_pairs * a.n_heads, kPfThreads, kPfSmemBytes, ctx->stream>>>(qmap, ctx->kmap, ctx->vmap,
-                                                                                        make_pool(ctx), a);
+  prefill_bf16_kernel<<<(unsigned)(blocks * a.n_heads), kPfThreads, kPfSmemBytes, ctx->stream>>>(
+      qmap, ctx->kmap, ctx->vmap, omap, make_pool(ctx), a);
   CKLAUNCH();
   return OOMATTN_OK;
 }
@@ -1103,11 +1238,16 @@ constexpr int kStaticMaxKv = 64;         // kv heads per launch covered by the c
 constexpr size_t kStaticPartOBytes = (size_t)kStaticPartSlots * kHeadDim * sizeof(float);  // 8 MiB
 constexpr size_t kStaticPartLseBytes = (size_t)kStaticPartSlots * sizeof(float);          // 64 KiB
 constexpr size_t kStaticCounterBytes = (size_t)kMaxBatch * kStaticMaxKv * sizeof(unsigned);  // 32 KiB
-constexpr size_t kStaticScratchBytes = kStaticPartOBytes + kStaticPartLseBytes + kStaticCounterBytes;
+constexpr size_t kStaticStatusBytes = 256;  // one int: the kernels' error bits, kept until read
+constexpr size_t kStaticScratchBytes = kStaticPartOBytes + kStaticPartLseBytes + kStaticCounterBytes +
+                                       kStaticStatusBytes;
 constexpr int kStaticMaxDevices = 64;
 
 // The scratch: every GPU that loads this library holds one copy until the
-// process exits.  All calls on a device share it.
+// process exits.  All calls on a device share it.  Its last 256 bytes hold
+// the status word the kernels OR their error bits into; it starts at zero
+// (static device memory is zero-initialised) and is cleared only when
+// oomattn_decode_static_scratch_status reads it.
 static __device__ __align__(256) unsigned char g_decode_scratch[kStaticScratchBytes];
 
 std::mutex g_static_mu;
@@ -1192,6 +1332,8 @@ extern "C" int oomattn_decode_static_scratch(int device, void* stream, int32_t k
   float* part_lse = reinterpret_cast<float*>(static_cast<unsigned char*>(scratch) + kStaticPartOBytes);
   unsigned* counters =
       reinterpret_cast<unsigned*>(static_cast<unsigned char*>(scratch) + kStaticPartOBytes + kStaticPartLseBytes);
+  int* status = reinterpret_cast<int*>(static_cast<unsigned char*>(scratch) + kStaticPartOBytes +
+                                       kStaticPartLseBytes + kStaticCounterBytes);
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
 
   // Split plan as in oomattn_decode, capped so that every (row, q head, split)
@@ -1220,6 +1362,9 @@ extern "C" int oomattn_decode_static_scratch(int device, void* stream, int32_t k
   a.q = q;
   a.out = out;
   a.lse = lse;
+  a.o_stride = kHeadDim;
+  a.lse_stride = 1;
+  a.test_flags = 0;
   a.layer = 0;
   a.n_heads = n_heads;
   a.group = n_heads / n_kv_heads;
@@ -1228,7 +1373,7 @@ extern "C" int oomattn_decode_static_scratch(int device, void* stream, int32_t k
   a.part_o = part_o;
   a.part_lse = part_lse;
   a.counters = counters;
-  a.status = nullptr;
+  a.status = status;  // read and cleared by oomattn_decode_static_scratch_status
   a.timeout_ns = kDefaultTimeoutNs;
   if (pool.kv_bf16) {
     // Tensor maps are encoded on the host into kernel parameters: no allocation.
@@ -1255,6 +1400,43 @@ extern "C" int oomattn_decode_static_scratch(int device, void* stream, int32_t k
   e = cudaGetLastError();
   if (e != cudaSuccess)
     return static_fail(errbuf, errbuf_len, OOMATTN_ERR_CUDA, "kernel launch: %s", cudaGetErrorString(e));
+  return OOMATTN_OK;
+}
+
+extern "C" int oomattn_decode_static_scratch_status(int device, void* stream, int32_t* flags_out, char* errbuf,
+                                                    int32_t errbuf_len) {
+  if (errbuf && errbuf_len > 0) errbuf[0] = '\0';
+  if (flags_out) *flags_out = 0;
+  if (device < 0 || device >= kStaticMaxDevices)
+    return static_fail(errbuf, errbuf_len, OOMATTN_ERR_OUT_OF_RANGE, "device %d outside [0, %d)", device,
+                       kStaticMaxDevices);
+  void* scratch = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(g_static_mu);
+    scratch = g_static_scratch[device];
+  }
+  if (!scratch) return OOMATTN_OK;  // no call has run on this device
+  DeviceGuard dg(device);
+  int* status = reinterpret_cast<int*>(static_cast<unsigned char*>(scratch) + kStaticPartOBytes +
+                                       kStaticPartLseBytes + kStaticCounterBytes);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  int h = 0;
+  cudaError_t e = cudaMemcpyAsync(&h, status, sizeof(int), cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e == cudaSuccess && h) {
+    e = cudaMemsetAsync(status, 0, sizeof(int), st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  }
+  if (e != cudaSuccess)
+    return static_fail(errbuf, errbuf_len, OOMATTN_ERR_CUDA, "reading the status word: %s", cudaGetErrorString(e));
+  if (flags_out) *flags_out = h;
+  if (h & kDevErrTimeout)
+    return static_fail(errbuf, errbuf_len, OOMATTN_ERR_TIMEOUT, "a decode wait gave up (status %d)", h);
+  if (h & kDevErrBounds)
+    return static_fail(errbuf, errbuf_len, OOMATTN_ERR_DEVICE_CHECK,
+                       "a block-table page id was outside [0, n_pool_pages) and read as the last pool page (status %d)",
+                       h);
+  if (h) return static_fail(errbuf, errbuf_len, OOMATTN_ERR_DEVICE_CHECK, "device check failed (status %d)", h);
   return OOMATTN_OK;
 }
 

@@ -36,10 +36,18 @@ struct KVPool {
   int kv_bf16;
 };
 
+// Test-only launch flags of the decode kernel (DecodeArgs::test_flags).
+enum : int {
+  kTestDropDecodeCopies = 1,  // the bf16 producer issues no copies: every consumer wait runs out its limit
+};
+
 struct DecodeArgs {
   const float* q;       // [rows][n_heads][128], rotated
-  float* out;           // [rows][n_heads][128]
-  float* lse;           // [rows][n_heads], natural log; may be null
+  float* out;           // (row, q head) output at out + ((row * n_heads) + head) * o_stride, 128 floats
+  float* lse;           // natural log at lse[((row * n_heads) + head) * lse_stride]; may be null
+  int o_stride;         // 128 for [rows][n_heads][128]; 132 for the packed (O, lse) layout
+  int lse_stride;       // 1 for [rows][n_heads]; 132 for the packed layout
+  int test_flags;       // 0 outside tests
   int layer;
   int n_heads;
   int group;            // n_heads / n_kv

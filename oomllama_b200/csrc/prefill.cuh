@@ -19,7 +19,8 @@
 //               row per thread, read from TMEM, online softmax with a lazily
 //               rescaled O (only when the running max grows by > 2^8), P
 //               written back into TMEM over the S columns as fp16, then the
-//               final O / l epilogue
+//               final O / l epilogue, staged in shared memory (over the
+//               tile's Q buffer) and written by TMA stores
 // The two softmax groups ping-pong: while one computes exponentials the tensor
 // core runs the other tile's MMAs.
 // TMEM (512 columns): S0 [0,128) S1 [128,256) O0 [256,384) O1 [384,512);
@@ -46,6 +47,8 @@ constexpr int kPfSoftmaxRegs = 208;
 static_assert(128 * kPfProducerRegs + 256 * kPfSoftmaxRegs <= kPfThreads * kPfLaunchRegs,
               "register split exceeds the launch allocation");
 
+constexpr int kPfMaxRanges = 4;
+
 struct PrefillArgs {
   void* out;           // [n_new][n_heads][128]
   int out_bf16;
@@ -57,6 +60,13 @@ struct PrefillArgs {
   int n_heads;
   int group;
   int n_pairs;         // ceil(n_new / 256)
+  // The 256-row query blocks ("pairs") this launch computes: ranges [lo, hi)
+  // ordered by descending lo, so that taking each range from its top gives
+  // the whole grid in descending causal work (one range [0, n_pairs) by
+  // default; a rank of a sharded prefill takes its zig-zag share).
+  int n_ranges;
+  int range_lo[kPfMaxRanges];
+  int range_hi[kPfMaxRanges];
   float qscale;        // softmax scale * log2(e)
   int* status;
   unsigned long long timeout_ns;
@@ -145,6 +155,38 @@ __device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_
       : "memory")
 
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// ------------------------------------------------------------ epilogue helpers
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t x, uint32_t y, uint32_t z, uint32_t w) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(x), "r"(y), "r"(z), "r"(w) : "memory");
+}
+// Named barrier over the 128 threads (4 warps) of one softmax tile.
+__device__ __forceinline__ void tile_bar(int id) { asm volatile("bar.sync %0, 128;" ::"r"(id) : "memory"); }
+// The same barrier, returning whether `pred` holds in all 128 threads.
+__device__ __forceinline__ bool tile_bar_and(int id, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.b32 p, %2, 0;\n\t"
+      "bar.red.and.pred q, %1, 128, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"(id), "r"((uint32_t)pred)
+      : "memory");
+  return r != 0;
+}
+// 3D tiled bulk-tensor store from this CTA's shared memory (innermost x a multiple of 16 bytes).
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void* src, int x, int y, int z) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Waits until every committed bulk store has finished reading its shared memory.
+__device__ __forceinline__ void bulk_wait_group_read0() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // Shared-memory matrix descriptor (sm_100 format): start address, leading /
@@ -171,7 +213,8 @@ __host__ __device__ constexpr uint32_t make_idesc_bf16(bool b_mn_major) { return
 // ------------------------------------------------------------ the kernel
 __global__ void __launch_bounds__(kPfThreads, 1)
     prefill_bf16_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
-                        const __grid_constant__ CUtensorMap vmap, const KVPool pool, const PrefillArgs a) {
+                        const __grid_constant__ CUtensorMap vmap, const __grid_constant__ CUtensorMap omap,
+                        const KVPool pool, const PrefillArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;                                // [2 tiles][2 halves][128][128 B]
@@ -191,9 +234,28 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // heaviest work first: block b -> pair (n_pairs - 1 - b / n_heads), head b % n_heads
+  // heaviest work first: block b -> the (b / n_heads)-th pair of the ranges
+  // taken top down, head b % n_heads
   const int h = blockIdx.x % a.n_heads;
-  const int pair = a.n_pairs - 1 - (int)(blockIdx.x / a.n_heads);
+  int pair = 0;
+  {
+    // unrolled with constant indices, so the ranges are read from the
+    // parameter space rather than copied to a local array
+    int k = (int)(blockIdx.x / a.n_heads);
+    bool found = false;
+#pragma unroll
+    for (int r = 0; r < kPfMaxRanges; ++r) {
+      const int n = a.range_hi[r] - a.range_lo[r];
+      if (!found && r < a.n_ranges) {
+        if (k < n) {
+          pair = a.range_hi[r] - 1 - k;
+          found = true;
+        } else {
+          k -= n;
+        }
+      }
+    }
+  }
   const int g = h / a.group;
   const int q0 = pair * 256;
   int rows_valid[2], ntile[2];
@@ -248,6 +310,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       prefetch_tensormap(&qmap);
       prefetch_tensormap(&kmap);
       prefetch_tensormap(&vmap);
+      prefetch_tensormap(&omap);
       mbar_arrive_expect_tx(q_full, 2 * kTileBytes);
       for (int i = 0; i < 2; ++i)
         for (int c = 0; c < 2; ++c)
@@ -527,39 +590,76 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       const uint64_t acc2 = f2_add(f2_add(acc[0], acc[1]), f2_add(acc[2], acc[3]));
       l += f2_lo(acc2) + f2_hi(acc2);
     }
-    if (ok && (i ? ntile[1] : ntile[0]) > 0) {
-      ok = mbar_wait(&o_full[i], 0, a.status, a.timeout_ns);
+    // Epilogue: O / l staged in shared memory and written by TMA stores.
+    // The staging area is this tile's Q buffer (every MMA that read it has
+    // completed once o_full fires), 32 KB: f32 output goes out in two rounds
+    // of 64 columns, bf16 in one.  Each round is two boxes of [128 rows][128 B]
+    // in the 128-byte-swizzled layout, so a warp's 16-byte shared stores hit
+    // distinct banks; one thread of the tile issues the stores, which clip the
+    // rows past n_new.  The tile's 128 threads agree on the outcome of the
+    // bounded o_full wait before any of them enters a named barrier.
+    if ((i ? ntile[1] : ntile[0]) > 0) {
+      bool okw = ok && mbar_wait(&o_full[i], 0, a.status, a.timeout_ns);
       tc_fence_after();
-      if (ok) {
-        const bool valid = r < (i ? rows_valid[1] : rows_valid[0]);
+      okw = tile_bar_and(1 + i, okw);
+      if (okw) {
         const float inv = 1.f / l;
-        const size_t orow = ((size_t)row_in_chunk * a.n_heads + h) * kHeadDim;
+        uint8_t* stage = sQ + i * kTileBytes;
+        const uint32_t st0 = smem_u32(stage) + (uint32_t)r * 128u;
+        const uint32_t rsw = (uint32_t)(r & 7);
+        const bool issuer = quarter == 0 && lane == 0;
+        const int qrow0 = q0 + 128 * i;
+        if (a.out_bf16) {
 #pragma unroll
-        for (int ch = 0; ch < 4; ++ch) {
-          uint32_t orr[32];
-          OOMATTN_TMEM_LD32((tmem + 256 + i * 128) + lane_off + ch * 32, orr);
-          tmem_wait_ld();
-          if (valid) {
-            if (a.out_bf16) {
-              uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(a.out) + orow + ch * 32);
+          for (int b = 0; b < 2; ++b) {  // box b: columns [64 b, 64 b + 64)
+            uint32_t orr[64];
+            OOMATTN_TMEM_LD32((tmem + 256 + i * 128) + lane_off + b * 64, orr);
+            OOMATTN_TMEM_LD32((tmem + 256 + i * 128) + lane_off + b * 64 + 32, (orr + 32));
+            tmem_wait_ld();
 #pragma unroll
-              for (int v = 0; v < 4; ++v) {
-                uint4 w;
-                w.x = pack_bf16(__uint_as_float(orr[8 * v + 0]) * inv, __uint_as_float(orr[8 * v + 1]) * inv);
-                w.y = pack_bf16(__uint_as_float(orr[8 * v + 2]) * inv, __uint_as_float(orr[8 * v + 3]) * inv);
-                w.z = pack_bf16(__uint_as_float(orr[8 * v + 4]) * inv, __uint_as_float(orr[8 * v + 5]) * inv);
-                w.w = pack_bf16(__uint_as_float(orr[8 * v + 6]) * inv, __uint_as_float(orr[8 * v + 7]) * inv);
-                dst[v] = w;
-              }
-            } else {
-              float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(a.out) + orow + ch * 32);
+            for (int c = 0; c < 8; ++c)
+              st_shared_v4(st0 + b * kHalfTileBytes + (((uint32_t)c ^ rsw) << 4),
+                           pack_bf16(__uint_as_float(orr[8 * c + 0]) * inv, __uint_as_float(orr[8 * c + 1]) * inv),
+                           pack_bf16(__uint_as_float(orr[8 * c + 2]) * inv, __uint_as_float(orr[8 * c + 3]) * inv),
+                           pack_bf16(__uint_as_float(orr[8 * c + 4]) * inv, __uint_as_float(orr[8 * c + 5]) * inv),
+                           pack_bf16(__uint_as_float(orr[8 * c + 6]) * inv, __uint_as_float(orr[8 * c + 7]) * inv));
+          }
+          fence_proxy_async_smem();
+          tile_bar(1 + i);
+          if (issuer) {
+            tma_store_3d(&omap, stage, 0, h, qrow0);
+            tma_store_3d(&omap, stage + kHalfTileBytes, 64, h, qrow0);
+            bulk_commit_group();
+            bulk_wait_group_read0();
+          }
+        } else {
 #pragma unroll
-              for (int v = 0; v < 8; ++v)
-                dst[v] = make_float4(__uint_as_float(orr[4 * v + 0]) * inv, __uint_as_float(orr[4 * v + 1]) * inv,
-                                     __uint_as_float(orr[4 * v + 2]) * inv, __uint_as_float(orr[4 * v + 3]) * inv);
+          for (int c2 = 0; c2 < 2; ++c2) {  // round c2: columns [64 c2, 64 c2 + 64)
+            if (c2 == 1) tile_bar(1 + i);  // the issuer has seen round 0's reads of the staging area end
+#pragma unroll
+            for (int b = 0; b < 2; ++b) {  // box b: 32 columns
+              uint32_t orr[32];
+              OOMATTN_TMEM_LD32((tmem + 256 + i * 128) + lane_off + (2 * c2 + b) * 32, orr);
+              tmem_wait_ld();
+#pragma unroll
+              for (int c = 0; c < 8; ++c)
+                st_shared_v4(st0 + b * kHalfTileBytes + (((uint32_t)c ^ rsw) << 4),
+                             __float_as_uint(__uint_as_float(orr[4 * c + 0]) * inv),
+                             __float_as_uint(__uint_as_float(orr[4 * c + 1]) * inv),
+                             __float_as_uint(__uint_as_float(orr[4 * c + 2]) * inv),
+                             __float_as_uint(__uint_as_float(orr[4 * c + 3]) * inv));
+            }
+            fence_proxy_async_smem();
+            tile_bar(1 + i);
+            if (issuer) {
+              tma_store_3d(&omap, stage, 64 * c2, h, qrow0);
+              tma_store_3d(&omap, stage + kHalfTileBytes, 64 * c2 + 32, h, qrow0);
+              bulk_commit_group();
+              bulk_wait_group_read0();
             }
           }
         }
+        const bool valid = r < (i ? rows_valid[1] : rows_valid[0]);
         if (valid && a.lse) a.lse[(size_t)row_in_chunk * a.n_heads + h] = (m_used + log2f(l)) * 0.69314718055994531f;
       }
     }

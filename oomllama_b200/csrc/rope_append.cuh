@@ -139,8 +139,9 @@ __global__ void __launch_bounds__(256)
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int hq = ap.n_heads, hkv = pool.n_kv;
   const int units_tok = (hq + 2 * hkv) * 8;
-  const int first = ap.q ? 0 : hq * 8;  // no q: K/V rows only
-  const int per_tok = units_tok - first;
+  const int first = ap.q ? 0 : hq * 8;         // no q: K/V rows only
+  const int last = ap.k ? units_tok : hq * 8;  // no k/v: q rows only (nothing is appended)
+  const int per_tok = last - first;
   const int total = T * per_tok;  // < 2^31 (checked on the host): 32-bit index arithmetic
   for (int w = blockIdx.x * blockDim.x + threadIdx.x; w < total; w += gridDim.x * blockDim.x) {
     const int t = w / per_tok;

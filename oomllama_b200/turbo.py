@@ -157,6 +157,14 @@ class TurboEngine:
         self._bind_stream()
         check(self._ctx, self._L.oomattn_sync(self._ctx))
 
+    def set_wait_limit(self, timeout_ns: int):
+        """Limit of the kernels' bounded device waits (default 2 s)."""
+        check(self._ctx, self._L.oomattn_set_wait_limit(self._ctx, int(timeout_ns)))
+
+    def set_test_flags(self, flags: int):
+        """Test-only launch flags (_lib.TEST_DROP_DECODE_COPIES); 0 in normal use."""
+        check(self._ctx, self._L.oomattn_set_test_flags(self._ctx, int(flags)))
+
     def reset(self):
         """TurboEngine::reset (src/oomllama_turbo.rs:726-728)."""
         check(self._ctx, self._L.oomattn_reset(self._ctx))
@@ -229,6 +237,22 @@ class TurboEngine:
             _ptr(bq), _ptr(bk), _ptr(bv), _ptr(q_out), _DT[q_out_dtype]))
         return q_out
 
+    def rope_q(self, positions, q, bq=None, q_out_dtype=torch.float32, out=None):
+        """RoPE of q rows [R, Hq*128] at explicit positions, nothing appended (the q half of
+        TurboEngine::apply_rope, src/oomllama_turbo.rs:737-786).  Returns [R, Hq, 128]."""
+        positions = list(positions)
+        R = len(positions)
+        c = self.config
+        _dev(q, "q", self.device, numel=R * c.n_heads * HEAD_DIM)
+        if bq is not None:
+            _dev(bq, "bq", self.device, dtype=torch.float32, numel=c.n_heads * HEAD_DIM)
+        if out is None:
+            out = torch.empty(R, c.n_heads, HEAD_DIM, dtype=q_out_dtype, device=q.device)
+        self._bind_stream()
+        check(self._ctx, self._L.oomattn_rope_q(self._ctx, R, int_array(positions), _ptr(q), _dtype_code(q), _ptr(bq),
+                                                _ptr(out), _DT[out.dtype]))
+        return out
+
     def qkv_rope_append(self, layer: int, seq_ids, x, wq, wk, wv, bq=None, bk=None, bv=None,
                         q_out_dtype=torch.float32):
         """QKV projection + bias + RoPE + append (src/oomllama_turbo.rs:638-681).
@@ -267,9 +291,38 @@ class TurboEngine:
             _ptr(out), _ptr(lse) if with_lse else None))
         return (out, lse) if with_lse else out
 
-    def prefill(self, layer: int, seq: int, q, out_dtype=torch.float32, with_lse: bool = False, out=None):
+    def decode_packed(self, layer: int, seq_ids, q, lens=None, out=None):
+        """decode() with (O, lse) packed per (row, q head) for one collective:
+        -> [rows, Hq, PACKED_STRIDE] f32, O in [..., :128], natural-log lse in [..., 128]."""
+        seq_ids = list(seq_ids)
+        c = self.config
+        rows = len(seq_ids)
+        _dev(q, "q", self.device, dtype=torch.float32, numel=rows * c.n_heads * HEAD_DIM)
+        if out is None:
+            out = torch.empty(rows, c.n_heads, _lib.PACKED_STRIDE, dtype=torch.float32, device=q.device)
+        else:
+            _dev(out, "out", self.device, dtype=torch.float32, numel=rows * c.n_heads * _lib.PACKED_STRIDE)
+        self._bind_stream()
+        check(self._ctx, self._L.oomattn_decode_packed(
+            self._ctx, layer, rows, int_array(seq_ids), None if lens is None else int_array(lens), _ptr(q),
+            _ptr(out)))
+        return out
+
+    def merge_packed(self, packed: torch.Tensor, n_parts: int, out=None, lse=None):
+        """LSE merge of packed partials [P, R, PACKED_STRIDE] -> (out [R, 128], lse [R])."""
+        R = packed.numel() // (n_parts * _lib.PACKED_STRIDE)
+        _dev(packed, "packed", self.device, dtype=torch.float32, numel=n_parts * R * _lib.PACKED_STRIDE)
+        out = torch.empty(R, HEAD_DIM, dtype=torch.float32, device=packed.device) if out is None else out
+        _dev(out, "out", self.device, dtype=torch.float32, numel=R * HEAD_DIM)
+        self._bind_stream()
+        check(self._ctx, self._L.oomattn_merge_packed(self._ctx, n_parts, R, _ptr(packed), _ptr(out), _ptr(lse)))
+        return out, lse
+
+    def prefill(self, layer: int, seq: int, q, out_dtype=torch.float32, with_lse: bool = False, out=None,
+                blocks=None):
         """Causal attention of the n_new newest tokens of `seq` (bf16 cache).
-        q [n_new, Hq, 128] bf16 (rotated) -> out [n_new, Hq, 128]."""
+        q [n_new, Hq, 128] bf16 (rotated) -> out [n_new, Hq, 128].  `blocks`: optional list of
+        (lo, hi) ranges of 256-row query blocks to compute (the others' rows are not written)."""
         c = self.config
         n_new = q.shape[0]
         _dev(q, "q", self.device, dtype=torch.bfloat16, numel=n_new * c.n_heads * HEAD_DIM)
@@ -277,8 +330,14 @@ class TurboEngine:
             out = torch.empty(n_new, c.n_heads, HEAD_DIM, dtype=out_dtype, device=q.device)
         lse = torch.empty(n_new, c.n_heads, dtype=torch.float32, device=q.device) if with_lse else None
         self._bind_stream()
-        check(self._ctx, self._L.oomattn_prefill(self._ctx, layer, seq, n_new, _ptr(q), _ptr(out),
-                                                 _DT[out.dtype], _ptr(lse)))
+        if blocks is None:
+            check(self._ctx, self._L.oomattn_prefill(self._ctx, layer, seq, n_new, _ptr(q), _ptr(out),
+                                                     _DT[out.dtype], _ptr(lse)))
+        else:
+            flat = [int(x) for lo_hi in blocks for x in lo_hi]
+            check(self._ctx, self._L.oomattn_prefill_blocks(self._ctx, layer, seq, n_new, _ptr(q), _ptr(out),
+                                                            _DT[out.dtype], _ptr(lse), len(blocks),
+                                                            int_array(flat)))
         return (out, lse) if with_lse else out
 
     def merge_partials(self, parts: torch.Tensor, lses: torch.Tensor):

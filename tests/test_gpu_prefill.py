@@ -110,3 +110,39 @@ def test_prefill_growing_scores_rescales_o(oracle, prefix, n_new):
     eng.close()
     assert_close(as_f32_np(out), ref, BF16_ATOL, BF16_RTOL, what=f"growing-score prefill P={prefix} n={n_new}")
     assert_close(lse.cpu().numpy(), ref_lse, 2e-3 * 24, BF16_RTOL, what="growing-score prefill lse")
+
+
+def test_prefill_query_block_ranges_match_whole_launch():
+    # the sharded prefill's per-rank launch: only the blocks of its ranges are written, and each
+    # equals the whole launch's rows bit for bit (the same CTA work unit computes them)
+    from oomllama_b200.shard import PrefillShardPlan
+    n_new = 2000  # 8 blocks, the last one ragged
+    eng = make_engine(28, 4, [n_new], kv_dtype="bf16", shuffle_seed=3)
+    k = randn((n_new, 4, 128), 31, torch.bfloat16)
+    v = randn((n_new, 4, 128), 32, torch.bfloat16)
+    eng.kv_write(0, 0, k.cuda(), v.cuda())
+    q = randn((n_new, 28, 128), 33, torch.bfloat16).cuda()
+    full, full_lse = eng.prefill(0, 0, q, with_lse=True)
+    for plan in (PrefillShardPlan(28, 4, 8, 0), PrefillShardPlan(28, 4, 8, 1), PrefillShardPlan(28, 4, 4, 0)):
+        blocks = plan.blocks(n_new)
+        part = torch.full_like(full, float("nan"))
+        part, lse = eng.prefill(0, 0, q, out=part, with_lse=True, blocks=blocks)
+        eng.sync()
+        rows = torch.zeros(n_new, dtype=torch.bool)
+        for lo, hi in blocks:
+            rows[256 * lo:min(n_new, 256 * hi)] = True
+        rows = rows.cuda()
+        assert torch.equal(part[rows], full[rows]) and torch.equal(lse[rows], full_lse[rows])
+        assert torch.isnan(part[~rows]).all()
+    # every block covered once by the two zig-zag ranks of a kv head
+    cover = np.zeros(8, int)
+    for r in range(2):
+        for lo, hi in PrefillShardPlan(28, 4, 8, r).blocks(n_new):
+            cover[lo:hi] += 1
+    assert (cover == 1).all()
+    from oomllama_b200._lib import OomAttnError
+    with pytest.raises(OomAttnError):
+        eng.prefill(0, 0, q, blocks=[(0, 9)])  # past the last block
+    with pytest.raises(OomAttnError):
+        eng.prefill(0, 0, q, blocks=[(0, 4), (3, 6)])  # overlapping
+    eng.close()
