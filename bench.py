@@ -40,6 +40,10 @@ sys.path.insert(0, ROOT)
 S_PREFILL, HQ, HKV, D = 4096, 28, 4, 128
 PREFILL_FLOPS = 4 * D * HQ * S_PREFILL * (S_PREFILL + 1) // 2   # 120,288,444,416 per sequence
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+# a device-side sleep (about 25 us) queued before a start event: the host enqueues the launches
+# meanwhile, so the event pairs bracket device work, not host launch latency (used for the per-stage
+# split of a split-context decode step; a kernel's own time comes from a CUDA graph of its launches)
+GPU_SLEEP_CYCLES = 50_000
 SPEC_PEAKS = {"hbm_gbs": 7700.0, "bf16_tflops": 2250.0}  # nominal B200 (HGX HBM3e; dense bf16), for context
 # dram__bytes_read.sum + dram__bytes_write.sum per launch from one ncu capture
 # of each kernel on these workloads: the 4096-token causal prefill and the
@@ -231,16 +235,12 @@ def bench_prefill(args, dist_, torch, strong):
         q, k, v = sets[i % n_sets] if qkv is None else qkv
         eng.reset()
         qr = eng.rope_append(0, [0], q, k, v, q_out_dtype=torch.bfloat16)
-        if ev is not None:
-            ev[0].record()
         eng.prefill(0, 0, qr, out=out if o is None else o, blocks=blocks)
-        if ev is not None:
-            ev[1].record()
+        return qr
 
     for i in range(args.warmup):
         step(i)
     eng.sync()
-    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
 
     def load_for(seconds):
@@ -279,16 +279,27 @@ def bench_prefill(args, dist_, torch, strong):
         t1.record()
         torch.cuda.synchronize()
         dist_.barrier()
-        # the prefill kernel alone: CUDA events around each launch of eager steps (on the stream the
-        # kernel is launched on)
-        for i in range(args.steps):
-            step(i, evs[i])
+        # the prefill kernel alone: a CUDA graph of back-to-back launches over each set's rotated q (the
+        # cache holds the last set's K/V; every launch does the step's work), CUDA events on its stream
+        qrs = [step(i).clone() for i in range(n_sets)]
+        with torch.cuda.stream(side):
+            kg = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(kg, stream=side):
+                for i in range(n_sets):
+                    eng.prefill(0, 0, qrs[i], out=out, blocks=blocks)
+        torch.cuda.synchronize()
+        kg.replay()
+        ka, kb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ka.record()
+        for _ in range(args.steps):
+            kg.replay()
+        kb.record()
         torch.cuda.synchronize()
         load_for(0.5)
     eng.sync()
-    del graphs
+    del graphs, kg
     ms = t0.elapsed_time(t1) / args.steps
-    kern_ms = sum(a.elapsed_time(b) for a, b in evs) / args.steps
+    kern_ms = ka.elapsed_time(kb) / (args.steps * n_sets)
     ms_max = dist_.max(ms)
     kern_max = dist_.max(kern_ms)
 
@@ -420,6 +431,8 @@ def bench_decode(args, dist_, torch, name):
 
     def step(ev=None):
         if ev is not None:
+            # the GPU sleeps while the host enqueues the step, so the events bracket device work only
+            torch.cuda._sleep(GPU_SLEEP_CYCLES)
             ev[0].record(stream)
         if not merge:
             out = eng.decode(0, seqs, q)
@@ -454,16 +467,37 @@ def bench_decode(args, dist_, torch, name):
     torch.cuda.synchronize()
     dist_.barrier()
     ms = dist_.max(t0.elapsed_time(t1) / steps)
-    # the stages, from CUDA events around each (eager steps, after the timed region)
-    dist_.barrier()
-    for i in range(steps):
-        step(evs[i])
+    # the decode kernel alone: a CUDA graph of back-to-back launches on this rank
+    side = torch.cuda.Stream()
+    packed = dec.buffers(B, l_hq, q.device)[0] if merge else None
+    with torch.cuda.stream(side):
+        for _ in range(2):
+            eng.decode_packed(0, seqs, q, out=packed) if merge else eng.decode(0, seqs, q)
+        kg = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(kg, stream=side):
+            for _ in range(4):
+                eng.decode_packed(0, seqs, q, out=packed) if merge else eng.decode(0, seqs, q)
     torch.cuda.synchronize()
+    kg.replay()
+    ka, kb = mk(), mk()
+    ka.record(stream)
+    for _ in range(steps):
+        kg.replay()
+    kb.record(stream)
+    torch.cuda.synchronize()
+    kern_local = ka.elapsed_time(kb) / (4 * steps)
+    del kg
+    # the all-gather and merge stages of a split-context step: CUDA events around each (eager steps)
+    coll_ms = merge_ms = 0.0
+    if merge:
+        dist_.barrier()
+        for i in range(steps):
+            step(evs[i])
+        torch.cuda.synchronize()
+        coll_ms = sum(e[1].elapsed_time(e[2]) for e in evs) / steps
+        merge_ms = sum(e[2].elapsed_time(e[3]) for e in evs) / steps
     dist_.barrier()
     eng.sync()
-    kern_local = sum(e[0].elapsed_time(e[1]) for e in evs) / steps
-    coll_ms = sum(e[1].elapsed_time(e[2]) for e in evs) / steps if merge else 0.0
-    merge_ms = sum(e[2].elapsed_time(e[3]) for e in evs) / steps if merge else 0.0
     kern_max = dist_.max(kern_local)
     local_bytes = sum(local) * l_hkv * D * 2 * 2
     total_bytes = sum(lens) * hkv * D * 2 * 2
@@ -738,10 +772,11 @@ def q8_random_matrix(torch, rows, cols, g, std=0.02, chunk=1 << 26):
 
 
 def bench_model_q8(args, dist_, torch, B=16, prompt=2048, gen=256, n_layers=28):
-    """Greedy decode of the whole Qwen2.5-7B-shaped model on resident Q8 weights (oomattn_decode_step_q8:
-    embedding, 28 decoder layers, final RMSNorm, LM head 152064 x 3584, argmax; each step's ids feed the
-    next on the device and are copied to pinned host memory) for B sequences: gen steps after a prompt of
-    `prompt` tokens whose KV entries are synthetic ~N(0, 1) bf16 (the prompt's prefill is not run)."""
+    """The whole Qwen2.5-7B-shaped model on resident Q8 weights: the prompt of B sequences x `prompt` random
+    token ids through oomattn_prefill_step_q8 (every layer's projections on the tensor cores, K-A append,
+    K-C causal attention; timed separately), then `gen` greedy steps of oomattn_decode_step_q8 (embedding, 28
+    decoder layers, final RMSNorm, LM head 152064 x 3584, argmax; each step's ids feed the next on the device
+    and are copied to pinned host memory) over the cache the prefill wrote."""
     from oomllama_b200 import Q8DecoderLayer, Q8Model, TurboConfig, TurboEngine
     dev = torch.cuda.current_device()
     H, hq, hkv, inter, vocab = 3584, 28, 4, 18944, 152064
@@ -754,9 +789,6 @@ def bench_model_q8(args, dist_, torch, B=16, prompt=2048, gen=256, n_layers=28):
     for b in range(B):
         eng.set_block_table(b, perm[b * pages_per:(b + 1) * pages_per].tolist())
     g = torch.Generator(device="cuda").manual_seed(4 + dist_.rank)
-    kp, vp = eng.kv_pool()
-    kp.normal_(generator=g)
-    vp.normal_(generator=g)
     bias = lambda n: torch.randn(n, device="cuda", generator=g) * 0.02  # noqa: E731
     layers = [Q8DecoderLayer(q=q8_random_matrix(torch, hq * D, H, g), k=q8_random_matrix(torch, hkv * D, H, g),
                              v=q8_random_matrix(torch, hkv * D, H, g), o=q8_random_matrix(torch, H, hq * D, g),
@@ -767,23 +799,36 @@ def bench_model_q8(args, dist_, torch, B=16, prompt=2048, gen=256, n_layers=28):
     model = Q8Model(layers=layers, embed=q8_random_matrix(torch, vocab, H, g),
                     lm_head=q8_random_matrix(torch, vocab, H, g), final_norm=torch.ones(H, device="cuda"), eps=1e-6)
     seqs = list(range(B))
-    first = torch.randint(0, vocab, (B,), dtype=torch.int32, device="cuda", generator=g)
-    tokens = first.clone()
+    prompt_ids = torch.randint(0, vocab, (B, prompt), dtype=torch.int32, device="cuda", generator=g)
+    tokens = torch.empty(B, dtype=torch.int32, device="cuda")
     out_host = torch.empty(gen, B, dtype=torch.int32).pin_memory()
+    stream = torch.cuda.current_stream()
+    mk = lambda: torch.cuda.Event(enable_timing=True)  # noqa: E731
 
-    def reset():
-        for l in range(n_layers):
-            for b in range(B):
-                eng.set_seq_len(l, b, prompt)
-        tokens.copy_(first)
+    def run_prefill():
+        eng.reset()
+        eng.prefill_step_q8(model, seqs, prompt_ids, next_tokens=tokens)
 
-    reset()
+    run_prefill()  # warm-up: grows the scratch
+    eng.sync()
+    dist_.barrier()
+    p0, p1 = mk(), mk()
+    p0.record(stream)
+    run_prefill()
+    p1.record(stream)
+    torch.cuda.synchronize()
+    eng.sync()
+    prefill_ms = dist_.max(p0.elapsed_time(p1))
+    first = tokens.clone()
+    # decode warm-up, then the timed chain from the prefill's state
     for _ in range(max(3, args.warmup)):
         eng.decode_step_q8(model, seqs, tokens, next_tokens=tokens)
     eng.sync()
-    reset()
-    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    stream = torch.cuda.current_stream()
+    for l in range(n_layers):
+        for b in range(B):
+            eng.set_seq_len(l, b, prompt)
+    tokens.copy_(first)
+    t0, t1 = mk(), mk()
     dist_.barrier()
     torch.cuda.synchronize()
     with ClockSampler(dev) as clk:
@@ -803,9 +848,13 @@ def bench_model_q8(args, dist_, torch, B=16, prompt=2048, gen=256, n_layers=28):
                  for m in (lay.q, lay.k, lay.v, lay.o, lay.gate, lay.up, lay.down))
     wbytes += vocab * H + 8 * (vocab * H // 256)  # LM head (the embedding reads B rows)
     kv_per_step = sum(B * (prompt + i + 1) * hkv * D * 2 * 2 * n_layers for i in range(gen)) / gen
+    layer_params = sum(m.rows * m.cols for m in (layers[0].q, layers[0].k, layers[0].v, layers[0].o, layers[0].gate,
+                                                 layers[0].up, layers[0].down))
+    prefill_flops = 2.0 * B * prompt * layer_params * n_layers + \
+        n_layers * B * 4.0 * D * hq * prompt * (prompt + 1) / 2 + 2.0 * B * vocab * H
     eng.close()
     return {"ms": ms, "ids": ids, "lens_ok": lens_ok, "weight_bytes": wbytes, "kv_bytes_per_step": kv_per_step,
-            "clocks": clocks}
+            "clocks": clocks, "prefill_ms": prefill_ms, "prefill_flops": prefill_flops}
 
 
 def synthetic_q8_stream(rows, cols, seed=6):
@@ -1131,14 +1180,20 @@ def main():
             "tok_s": W * B * G / (r["ms"] * 1e-3), "decode_ms": r["ms"], "ms_per_step": step_ms,
             "bytes_per_step": step_bytes, "hbm_gbs": step_bytes / (step_ms * 1e-3) / 1e9,
             "frac_of_hbm": step_bytes / (step_ms * 1e-3) / 1e9 / peaks["hbm_gbs"],
-            "prompt": "KV of the prompt synthetic ~N(0,1) bf16; its prefill is not run",
+            "prefill": {"tok_s": W * B * P / (r["prefill_ms"] * 1e-3), "ms": r["prefill_ms"],
+                        "tflops": r["prefill_flops"] / (r["prefill_ms"] * 1e-3) / 1e12,
+                        "frac_of_bf16_peak": r["prefill_flops"] / (r["prefill_ms"] * 1e-3) / 1e12 /
+                        peaks["bf16_tflops_sustained"],
+                        "api": "TurboEngine.prefill_step_q8: 16 x 2048 random prompt ids, all 28 layers"},
+            "prompt": "random token ids run through the model's prefill; decode attends over the KV it wrote",
             "api": "TurboEngine.decode_step_q8 per step, ids copied to pinned host memory each step",
             "distinct_ids": int(len(np.unique(r["ids"]))), "lens_ok": r["lens_ok"], "clocks": r["clocks"],
             "cpu_baseline": None,
             "cpu_baseline_note": "not run: the full-size CPU reference model is infeasible on the host",
         }
         summary["model_q8"] = {"tok_s": round(line["model_q8"]["tok_s"], 1),
-                               "frac": round(line["model_q8"]["frac_of_hbm"], 4)}
+                               "frac": round(line["model_q8"]["frac_of_hbm"], 4),
+                               "prefill_tok_s": round(line["model_q8"]["prefill"]["tok_s"], 1)}
     if "prefill" in only and dist_.rank == 0 and W == 1 and not args.no_cpu_baseline:
         v, nt, desc = cpu_prefill_sample()
         v1, _, desc1 = cpu_prefill_sample(seconds_budget=3.0, threads=1)

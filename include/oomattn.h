@@ -186,8 +186,8 @@ int oomattn_rope_q(oomattn_ctx* ctx, int32_t n_rows, const int32_t* positions /*
 /* Fused QKV projection + bias + RoPE + append (src/oomllama_turbo.rs:638-681).
  *   x: f32 [T][hidden]; wq [n_heads*128][hidden], wk/wv [n_kv*128][hidden] in
  *   w_dtype; bq/bk/bv f32 or NULL; q_out as in oomattn_rope_append.
- * T <= 8 runs one fused GEMV kernel (weights read once); larger T runs a
- * cuBLAS GEMM followed by the K-A epilogue kernel. */
+ * T <= 16 runs one fused GEMV kernel (weights read once); larger T runs the
+ * tensor-core linear (as oomattn_linear) followed by the K-A epilogue kernel. */
 int oomattn_qkv_rope_append(oomattn_ctx* ctx, int32_t layer, int32_t n_seqs, const int32_t* seq_ids /* host */,
                             int32_t n_new, const float* x, const void* wq, const void* wk, const void* wv,
                             int32_t w_dtype, const float* bq, const float* bk, const float* bv, void* q_out,
@@ -287,6 +287,20 @@ int oomattn_prefill(oomattn_ctx* ctx, int32_t layer, int32_t seq, int32_t n_new,
 int oomattn_prefill_blocks(oomattn_ctx* ctx, int32_t layer, int32_t seq, int32_t n_new, const void* q, void* out,
                            int32_t out_dtype, float* lse, int32_t n_ranges, const int32_t* ranges /* host */);
 
+/* ------------------------------------------------------- linear projections */
+
+/* y[t][r] = sum_c x[t][c] * w[r][c] (+ bias[r]): candle's x @ W^T of the
+ * projections (src/oomllama_turbo.rs:643-645) and of o_proj (:715-720).
+ *   x f32 [n_tokens][cols], w [rows][cols] in w_dtype, bias f32 [rows] or
+ *   NULL, y f32 [n_tokens][rows]; device pointers, 16-byte aligned.
+ * Up to 16 tokens with f32 weights: a GEMV that streams W once.  Otherwise
+ * the tcgen05 tensor-core linear: x (and f32 W) split into bf16 hi + lo
+ * planes, three products per tile (two for bf16 W), f32 accumulation --
+ * within 1e-4 of the f32 product at unit-scale activations.  Needs
+ * cols % 8 == 0 and rows % 4 == 0. */
+int oomattn_linear(oomattn_ctx* ctx, const float* x, const void* w, int32_t w_dtype, int32_t n_tokens, int32_t rows,
+                   int32_t cols, const float* bias, float* y);
+
 /* ------------------------------------------------------- the layer step */
 
 /* TurboEngine::attention_forward_with_bias (src/oomllama_turbo.rs:618-723) for
@@ -340,7 +354,10 @@ int oomattn_q8_unpack(const uint8_t* stream /* host */, uint64_t stream_bytes, i
  * y [n_tokens][rows], bias [rows] -- all device pointers.  rows must be a
  * multiple of 16 and cols of 64; |x| < 65504 (x enters the tensor cores as an
  * fp16 hi/lo pair; larger values are reported by oomattn_sync as
- * OOMATTN_ERR_DEVICE_CHECK). */
+ * OOMATTN_ERR_DEVICE_CHECK).  Up to 64 tokens the weights stream through
+ * 16-token passes; more tokens (a prefill chunk), with cols % 256 == 0, run
+ * the tcgen05 tensor-core linear: W converted to fp16 q values once per call,
+ * each 256-value block's dot products promoted with its scale and min. */
 int oomattn_q8_linear(oomattn_ctx* ctx, const oomattn_q8_matrix* w /* host struct */, const float* x,
                       int32_t n_tokens, const float* bias, float* y);
 
@@ -454,6 +471,20 @@ typedef struct oomattn_q8_model {
  * one. */
 int oomattn_decode_step_q8(oomattn_ctx* ctx, const oomattn_q8_model* m /* host struct */, int32_t n_seqs,
                            const int32_t* seq_ids /* host */, const int32_t* tokens, int32_t* next, float* logits);
+
+/* The prompt of n_seqs sequences through the whole model
+ * (OomLlamaModel::forward_turbo over all prompt tokens, src/oomllama.rs:504-553,
+ * as GhostLlamaModel's generate calls it, :969-970), then the first greedy pick:
+ * tokens [n_seqs][n_new] int32 (device) are embedded, every decoder layer
+ * appends their K/V to its cache (K-A), attends causally over each sequence
+ * (K-C) and runs its projections and MLP on the tensor cores (Q8 weights); the
+ * final RMSNorm, LM head and argmax of each sequence's last prompt token give
+ * next[b] (device; logits [n_seqs][vocab] or NULL).  Needs a bf16 cache; the
+ * sequences' lengths grow by n_new in every layer. */
+int oomattn_prefill_step_q8(oomattn_ctx* ctx, const oomattn_q8_model* m /* host struct */, int32_t n_seqs,
+                            const int32_t* seq_ids /* host */, int32_t n_new, const int32_t* tokens, int32_t* next,
+                            float* logits);
+
 
 #ifdef __cplusplus
 }

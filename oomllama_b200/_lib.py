@@ -32,6 +32,7 @@ EXPORTS = (
     "oomattn_embed_q8", "oomattn_argmax", "oomattn_decode_step_q8", "oomattn_oom_scan", "oomattn_q8_repack",
     "oomattn_set_wait_limit", "oomattn_set_test_flags", "oomattn_rope_q", "oomattn_decode_packed",
     "oomattn_merge_packed", "oomattn_decode_static_scratch_status", "oomattn_prefill_blocks",
+    "oomattn_linear", "oomattn_prefill_step_q8",
 )
 
 
@@ -137,6 +138,8 @@ def load():
         "oomattn_merge_packed": ([P, I, I, P, P, P], ctypes.c_int),
         "oomattn_decode_static_scratch_status": ([ctypes.c_int, P, IP, ctypes.c_char_p, I], ctypes.c_int),
         "oomattn_prefill_blocks": ([P, I, I, I, P, P, I, P, I, IP], ctypes.c_int),
+        "oomattn_linear": ([P, P, P, I, I, I, I, P, P], ctypes.c_int),
+        "oomattn_prefill_step_q8": ([P, ctypes.POINTER(Q8Model), I, IP, I, P, P, P], ctypes.c_int),
     }
     for name, (args, res) in sig.items():
         fn = getattr(L, name)

@@ -43,7 +43,7 @@ def build(force: bool = False, verbose: bool = False) -> str:
     if not force and not needs_build():
         return LIB
     tmp = LIB + ".tmp"
-    cmd = [nvcc(), *NVCC_FLAGS, "-o", tmp, *SOURCES, "-lcublas"]
+    cmd = [nvcc(), *NVCC_FLAGS, "-o", tmp, *SOURCES]
     if verbose:
         print(" ".join(cmd), file=sys.stderr)
     subprocess.run(cmd, check=True, cwd=ROOT)

@@ -2,9 +2,8 @@
 // validation, the paged-cache bookkeeping that mirrors LayerKVCache /
 // ModelKVCache (src/oomllama_turbo.rs:26-104), tensor maps, split planning and
 // kernel launches.  Everything here is plain host C++ over the CUDA runtime;
-// the only library calls are cuBLAS GEMMs for projections of more than 8
-// tokens and for o_proj.
-#include <cublas_v2.h>
+// every kernel it launches is this library's own (no cuBLAS or other compute
+// library).
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <math.h>
@@ -19,6 +18,7 @@
 #include "../../include/oomattn.h"
 #include "common.cuh"
 #include "decode.cuh"
+#include "gemm.cuh"
 #include "params.cuh"
 #include "prefill.cuh"
 #include "q8_linear.cuh"
@@ -83,15 +83,18 @@ struct oomattn_ctx {
   CUtensorMap kmap{}, vmap{};
   bool have_maps = false;
   int prefill_regs = 0;  // compiled register count of the prefill kernel
+  int kf_q8_regs = 0;    // and of the Q8 tensor-core linear (its register split needs kKfLaunchRegs)
   // host mirrors (authoritative for lengths; updated at enqueue time)
   std::vector<int> h_block_table;  // [max_seqs][max_pages_per_seq]
   std::vector<int> h_len;          // [n_layers][max_seqs]
   std::vector<int> h_pos_off;      // [max_seqs]
   std::vector<float> h_cos, h_sin; // [max_seq_len][64]
   // lazily grown scratch for the layer step
-  cublasHandle_t cublas = nullptr;
   float* d_scratch = nullptr;
   size_t scratch_bytes = 0;
+  // K-F (tensor-core linear): the split / converted operand planes
+  uint8_t* d_kf = nullptr;
+  size_t kf_bytes = 0;
   // Q8 linear: activation splits and split-K partials, and per-row-tile
   // arrival counters (zero between launches)
   uint8_t* d_q8_scratch = nullptr;
@@ -279,32 +282,150 @@ int ensure_scratch(oomattn_ctx* ctx, size_t bytes) {
   return OOMATTN_OK;
 }
 
-int ensure_cublas(oomattn_ctx* ctx) {
-  if (!ctx->cublas) {
-    if (cublasCreate(&ctx->cublas) != CUBLAS_STATUS_SUCCESS)
-      return fail(ctx, OOMATTN_ERR_CUDA, "cublasCreate failed");
-    cublasSetMathMode(ctx->cublas, CUBLAS_PEDANTIC_MATH);  // true f32, no TF32
-  }
-  cublasSetStream(ctx->cublas, ctx->stream);
+// ------------------------------------------------------------------ K-F host side
+// A 2D row-major tensor [outer][inner] of 16-bit or f32 elements as a TMA map
+// with 128-byte-swizzled boxes [box_outer][box_inner]; reads past the edges
+// fill zeros and stores past them are dropped.
+int encode_2d(oomattn_ctx* ctx, const void* base, CUtensorMapDataType dt, int es, uint64_t inner, uint64_t outer,
+              uint32_t box_inner, uint32_t box_outer, CUtensorMap* map) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) return fail(ctx, OOMATTN_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)outer};
+  cuuint64_t strides[1] = {(cuuint64_t)inner * es};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(ctx, OOMATTN_ERR_CUDA, "cuTensorMapEncodeTiled(linear operand) failed: %d", (int)r);
   return OOMATTN_OK;
 }
 
-// C[T][N] = A[T][K] . W[N][K]^T in f32 (row-major); with a bf16 W the
-// activations arrive already converted to bf16 (A16) and the GEMM accumulates
-// in f32.
-int gemm_xwT(oomattn_ctx* ctx, const float* A, const void* W, int w_bf16, float* C, int T, int N, int K,
-             const void* A16 = nullptr) {
-  int rc = ensure_cublas(ctx);
-  if (rc) return rc;
-  const float one = 1.f, zero = 0.f;
-  cublasStatus_t st;
-  if (!w_bf16) {
-    st = cublasSgemm(ctx->cublas, CUBLAS_OP_T, CUBLAS_OP_N, N, T, K, &one, (const float*)W, K, A, K, &zero, C, N);
-  } else {
-    st = cublasGemmEx(ctx->cublas, CUBLAS_OP_T, CUBLAS_OP_N, N, T, K, &one, W, CUDA_R_16BF, K, A16, CUDA_R_16BF, K,
-                      &zero, C, CUDA_R_32F, N, CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
+uint8_t* kf_scratch(oomattn_ctx* ctx, size_t bytes, int* rc) {
+  *rc = OOMATTN_OK;
+  if (bytes > ctx->kf_bytes) {
+    if (ctx->d_kf) {
+      cudaStreamSynchronize(ctx->stream);
+      cudaFree(ctx->d_kf);
+      ctx->d_kf = nullptr;
+      ctx->kf_bytes = 0;
+    }
+    if (cudaMalloc(&ctx->d_kf, bytes) != cudaSuccess) {
+      *rc = fail(ctx, OOMATTN_ERR_NO_MEMORY, "linear operand scratch of %zu bytes failed", bytes);
+      return nullptr;
+    }
+    ctx->kf_bytes = bytes;
   }
-  if (st != CUBLAS_STATUS_SUCCESS) return fail(ctx, OOMATTN_ERR_CUDA, "cuBLAS GEMM failed: %d", (int)st);
+  return ctx->d_kf;
+}
+
+size_t align256(size_t b) { return (b + 255) & ~size_t(255); }
+
+// One tensor-core linear launch: out [M][N] = A [M][K] . B [N][K]^T over the
+// given 16-bit planes (bf16, or fp16 for Q8 with the promotion operands).
+template <bool Q8, int BPLANES>
+int kf_launch(oomattn_ctx* ctx, int M, int N, int K, const void* a_hi, const void* a_lo, const void* b_hi,
+              const void* b_lo, const float* bias, const float* residual, float* out, const float* scale_t = nullptr,
+              const float* min_t = nullptr, const float* xsum = nullptr) {
+  const CUtensorMapDataType dt16 = Q8 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  CUtensorMap am_hi, am_lo, bm_hi, bm_lo, om, rm;
+  int rc = encode_2d(ctx, a_hi, dt16, 2, K, M, kKfBK, kKfBM, &am_hi);
+  if (!rc) rc = encode_2d(ctx, a_lo, dt16, 2, K, M, kKfBK, kKfBM, &am_lo);
+  if (!rc) rc = encode_2d(ctx, b_hi, dt16, 2, K, N, kKfBK, kKfBN, &bm_hi);
+  if (!rc) rc = encode_2d(ctx, BPLANES == 2 ? b_lo : b_hi, dt16, 2, K, N, kKfBK, kKfBN, &bm_lo);
+  if (!rc) rc = encode_2d(ctx, out, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, N, M, 32, kKfBM, &om);
+  if (!rc) rc = encode_2d(ctx, residual ? residual : out, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, N, M, 32, kKfBM, &rm);
+  if (rc) return rc;
+  KfArgs a;
+  a.M = M;
+  a.N = N;
+  a.K = K;
+  a.m_tiles = (M + kKfBM - 1) / kKfBM;
+  a.n_tiles = (N + kKfBN - 1) / kKfBN;
+  a.bias = bias;
+  a.scale_t = scale_t;
+  a.min_t = min_t;
+  a.xsum = xsum;
+  a.has_residual = residual != nullptr;
+  a.status = ctx->d_status;
+  a.timeout_ns = ctx->timeout_ns;
+  const long long grid = (long long)a.m_tiles * a.n_tiles;
+  if (grid >= (1ll << 31)) return fail(ctx, OOMATTN_ERR_OUT_OF_RANGE, "linear of %d x %d too large", M, N);
+  kf_gemm_kernel<Q8, BPLANES><<<(unsigned)grid, kKfThreads, kKfSmemBytes, ctx->stream>>>(am_hi, am_lo, bm_hi, bm_lo,
+                                                                                         om, rm, a);
+  CKLAUNCH();
+  return OOMATTN_OK;
+}
+
+// One output of an f32 (or bf16-weight) linear: out = x W^T (+ bias) (+ residual).
+struct KfJob {
+  const void* w;  // [n][k], f32 or bf16
+  int w_bf16;
+  int n;
+  const float* bias;
+  const float* residual;  // [m][n] or null (may alias out)
+  float* out;             // [m][n]
+};
+
+// x [m][k] f32 times several weight matrices of the same width on the tensor
+// cores: x is split into bf16 hi/lo planes once, each f32 W into its planes.
+int kf_linear_f32(oomattn_ctx* ctx, const float* x, int m, int k, const KfJob* jobs, int n_jobs) {
+  if (m <= 0) return OOMATTN_OK;
+  if (k % 8 || (reinterpret_cast<uintptr_t>(x) & 15))
+    return fail(ctx, OOMATTN_ERR_UNSUPPORTED, "the tensor-core linear needs k %% 8 == 0 and 16-byte aligned x");
+  size_t wmax = 0;
+  for (int j = 0; j < n_jobs; ++j) {
+    const KfJob& jb = jobs[j];
+    if (jb.n % 4 || !jb.w || !jb.out || (reinterpret_cast<uintptr_t>(jb.w) & 15) ||
+        (reinterpret_cast<uintptr_t>(jb.out) & 15) || (jb.bias && (reinterpret_cast<uintptr_t>(jb.bias) & 15)) ||
+        (jb.residual && (reinterpret_cast<uintptr_t>(jb.residual) & 15)))
+      return fail(ctx, OOMATTN_ERR_UNSUPPORTED,
+                  "the tensor-core linear needs rows %% 4 == 0 and 16-byte aligned weights, bias and outputs");
+    if (!jb.w_bf16) wmax = std::max(wmax, (size_t)jb.n * k);
+  }
+  const size_t xb = align256((size_t)m * k * 2), wb = align256(wmax * 2);
+  int rc;
+  uint8_t* sc = kf_scratch(ctx, 2 * xb + 2 * wb, &rc);
+  if (rc) return rc;
+  uint16_t* xh = reinterpret_cast<uint16_t*>(sc);
+  uint16_t* xl = reinterpret_cast<uint16_t*>(sc + xb);
+  uint16_t* wh = reinterpret_cast<uint16_t*>(sc + 2 * xb);
+  uint16_t* wl = reinterpret_cast<uint16_t*>(sc + 2 * xb + wb);
+  const size_t xn4 = (size_t)m * k / 4;
+  kf_split_bf16_kernel<<<(unsigned)std::min<size_t>((xn4 + 255) / 256, (size_t)ctx->num_sms * 8), 256, 0,
+                         ctx->stream>>>(x, xh, xl, xn4);
+  CKLAUNCH();
+  for (int j = 0; j < n_jobs; ++j) {
+    const KfJob& jb = jobs[j];
+    if (jb.w_bf16) {
+      rc = kf_launch<false, 1>(ctx, m, jb.n, k, xh, xl, jb.w, nullptr, jb.bias, jb.residual, jb.out);
+    } else {
+      const size_t wn4 = (size_t)jb.n * k / 4;
+      kf_split_bf16_kernel<<<(unsigned)std::min<size_t>((wn4 + 255) / 256, (size_t)ctx->num_sms * 8), 256, 0,
+                             ctx->stream>>>(static_cast<const float*>(jb.w), wh, wl, wn4);
+      CKLAUNCH();
+      rc = kf_launch<false, 2>(ctx, m, jb.n, k, xh, xl, wh, wl, jb.bias, jb.residual, jb.out);
+    }
+    if (rc) return rc;
+  }
+  return OOMATTN_OK;
+}
+
+// f32 GEMV for T <= 16 tokens (f32 weights): y = x W^T (+ bias) (+ residual).
+int f32_gemv(oomattn_ctx* ctx, const float* x, const float* w, int T, int n, int k, const float* bias,
+             const float* residual, float* y) {
+  if (k % 4 || ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w)) & 15))
+    return fail(ctx, OOMATTN_ERR_UNSUPPORTED, "the f32 GEMV needs k %% 4 == 0 and 16-byte aligned x and W");
+  const int grid = (int)(((long long)(n + 1) / 2 * 32 + 255) / 256);
+#define OOMATTN_GEMV_T(TT) \
+  case TT: f32_gemv_kernel<TT><<<grid, 256, 0, ctx->stream>>>(x, w, bias, residual, y, n, k); break;
+  switch (T) {
+    OOMATTN_GEMV_T(1) OOMATTN_GEMV_T(2) OOMATTN_GEMV_T(3) OOMATTN_GEMV_T(4) OOMATTN_GEMV_T(5) OOMATTN_GEMV_T(6)
+    OOMATTN_GEMV_T(7) OOMATTN_GEMV_T(8) OOMATTN_GEMV_T(9) OOMATTN_GEMV_T(10) OOMATTN_GEMV_T(11)
+    OOMATTN_GEMV_T(12) OOMATTN_GEMV_T(13) OOMATTN_GEMV_T(14) OOMATTN_GEMV_T(15) OOMATTN_GEMV_T(16)
+    default: return fail(ctx, OOMATTN_ERR_INVALID_ARG, "f32 GEMV of %d tokens", T);
+  }
+#undef OOMATTN_GEMV_T
+  CKLAUNCH();
   return OOMATTN_OK;
 }
 
@@ -677,11 +798,19 @@ int oomattn_create(const oomattn_config* cfg, int device, void* stream, oomattn_
       cudaFuncSetAttribute(q8_linear_xs_kernel<1, 2, kQ8Xs1S2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            (int)q8_xs_smem_bytes(1, q8_xs_max_chunks(1))) != cudaSuccess ||
       cudaFuncSetAttribute(q8_linear_xs_kernel<1, 1, kQ8Xs1S1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           (int)q8_xs_smem_bytes(1, q8_xs_max_chunks(1))) != cudaSuccess)
+                           (int)q8_xs_smem_bytes(1, q8_xs_max_chunks(1))) != cudaSuccess ||
+      cudaFuncSetAttribute(kf_gemm_kernel<false, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, kKfSmemBytes) !=
+          cudaSuccess ||
+      cudaFuncSetAttribute(kf_gemm_kernel<false, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kKfSmemBytes) !=
+          cudaSuccess ||
+      cudaFuncSetAttribute(kf_gemm_kernel<true, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kKfSmemBytes) !=
+          cudaSuccess)
     return bail(OOMATTN_ERR_CUDA);
   cudaFuncAttributes fa;
   if (cudaFuncGetAttributes(&fa, prefill_bf16_kernel) != cudaSuccess) return bail(OOMATTN_ERR_CUDA);
   ctx->prefill_regs = fa.numRegs;
+  if (cudaFuncGetAttributes(&fa, kf_gemm_kernel<true, 1>) != cudaSuccess) return bail(OOMATTN_ERR_CUDA);
+  ctx->kf_q8_regs = fa.numRegs;
   if (cudaDeviceSynchronize() != cudaSuccess) return bail(OOMATTN_ERR_CUDA);
   *out = ctx;
   return OOMATTN_OK;
@@ -691,11 +820,10 @@ int oomattn_destroy(oomattn_ctx* ctx) {
   if (!ctx) return OOMATTN_ERR_INVALID_ARG;
   DeviceGuard dg(ctx->device);
   if (ctx->stream) cudaStreamSynchronize(ctx->stream);
-  if (ctx->cublas) cublasDestroy(ctx->cublas);
   void* ptrs[] = {ctx->kpool,     ctx->vpool,      ctx->d_block_table, ctx->d_cos,    ctx->d_sin,
                   ctx->d_part_o,  ctx->d_part_lse, ctx->d_counters,    ctx->d_status, ctx->d_scratch,
                   ctx->d_q8_scratch, ctx->d_q8_counters, ctx->d_layer_scratch, ctx->d_model_scratch,
-                  ctx->d_argmax_part};
+                  ctx->d_argmax_part, ctx->d_kf};
   for (void* p : ptrs)
     if (p) cudaFree(p);
   delete ctx;
@@ -994,26 +1122,35 @@ int oomattn_qkv_rope_append(oomattn_ctx* ctx, int32_t layer, int32_t n_seqs, con
     commit_append(ctx, layer, sb, n_new);
     return OOMATTN_OK;
   }
-  // Larger T: cuBLAS projections into scratch, then the K-A epilogue kernel.
+  // Larger T: tensor-core projections (K-F) into scratch, then the K-A epilogue kernel.
   const int wb = w_dtype == OOMATTN_DTYPE_BF16;
   const size_t proj_bytes = (size_t)T * (nq + 2 * nk) * sizeof(float);
-  rc = ensure_scratch(ctx, proj_bytes + (wb ? (size_t)T * H * 2 : 0));
+  rc = ensure_scratch(ctx, proj_bytes);
   if (rc) return rc;
   float* sq = ctx->d_scratch;
   float* sk = sq + (size_t)T * nq;
   float* sv = sk + (size_t)T * nk;
-  void* x16 = nullptr;
-  if (wb) {
-    x16 = (uint8_t*)ctx->d_scratch + proj_bytes;
-    f32_to_bf16_kernel<<<std::min<long long>(4096, (T * H + 255) / 256), 256, 0, ctx->stream>>>(
-        x, (uint16_t*)x16, (size_t)T * H);
-    CKLAUNCH();
-  }
-  if ((rc = gemm_xwT(ctx, x, wq, wb, sq, (int)T, nq, H, x16)) ||
-      (rc = gemm_xwT(ctx, x, wk, wb, sk, (int)T, nk, H, x16)) || (rc = gemm_xwT(ctx, x, wv, wb, sv, (int)T, nk, H, x16)))
-    return rc;
+  const KfJob jobs[3] = {{wq, wb, nq, nullptr, nullptr, sq}, {wk, wb, nk, nullptr, nullptr, sk},
+                         {wv, wb, nk, nullptr, nullptr, sv}};
+  rc = kf_linear_f32(ctx, x, (int)T, H, jobs, 3);
+  if (rc) return rc;
   return oomattn_rope_append(ctx, layer, n_seqs, seq_ids, n_new, sq, sk, sv, OOMATTN_DTYPE_F32, bq, bk, bv, q_out,
                              q_out_dtype);
+}
+
+int oomattn_linear(oomattn_ctx* ctx, const float* x, const void* w, int32_t w_dtype, int32_t n_tokens, int32_t rows,
+                   int32_t cols, const float* bias, float* y) {
+  if (!ctx) return OOMATTN_ERR_INVALID_ARG;
+  if (!x || !w || !y || n_tokens < 0 || rows <= 0 || cols <= 0)
+    return fail(ctx, OOMATTN_ERR_INVALID_ARG, "bad linear arguments");
+  int rc = validate_dtype(ctx, w_dtype, "linear weights");
+  if (rc) return rc;
+  if (n_tokens == 0) return OOMATTN_OK;
+  DeviceGuard dg(ctx->device);
+  if (n_tokens <= kGemvMaxT && w_dtype == OOMATTN_DTYPE_F32)
+    return f32_gemv(ctx, x, static_cast<const float*>(w), n_tokens, rows, cols, bias, nullptr, y);
+  const KfJob job{w, w_dtype == OOMATTN_DTYPE_BF16, rows, bias, nullptr, y};
+  return kf_linear_f32(ctx, x, n_tokens, cols, &job, 1);
 }
 
 int oomattn_decode(oomattn_ctx* ctx, int32_t layer, int32_t n_rows, const int32_t* seq_ids, const int32_t* lens,
@@ -1185,9 +1322,10 @@ int oomattn_attention_forward_with_bias(oomattn_ctx* ctx, int32_t layer, int32_t
     float* sv = sk + (size_t)T * ctx->cfg.n_kv_heads * kHeadDim;
     const int nk = ctx->cfg.n_kv_heads * kHeadDim;
     const int H = ctx->cfg.hidden_size;
-    if ((rc = gemm_xwT(ctx, x, wq, 0, sq, (int)T, qo, H)) || (rc = gemm_xwT(ctx, x, wk, 0, sk, (int)T, nk, H)) ||
-        (rc = gemm_xwT(ctx, x, wv, 0, sv, (int)T, nk, H)))
-      return rc;
+    const KfJob jobs[3] = {{wq, 0, qo, nullptr, nullptr, sq}, {wk, 0, nk, nullptr, nullptr, sk},
+                           {wv, 0, nk, nullptr, nullptr, sv}};
+    rc = kf_linear_f32(ctx, x, (int)T, H, jobs, 3);
+    if (rc) return rc;
     rc = oomattn_rope_append(ctx, layer, batch, seqs.data(), seq_len, sq, sk, sv, OOMATTN_DTYPE_F32, bq, bk, bv,
                              use_prefill ? qb16 : (void*)qbuf, use_prefill ? OOMATTN_DTYPE_BF16 : OOMATTN_DTYPE_F32);
   }
@@ -1210,8 +1348,11 @@ int oomattn_attention_forward_with_bias(oomattn_ctx* ctx, int32_t layer, int32_t
     rc = oomattn_decode(ctx, layer, (int)T, rs.data(), rl.data(), qbuf, abuf, nullptr);
     if (rc) return rc;
   }
-  // o_proj: out = attn . Wo^T   (src/oomllama_turbo.rs:715-720)
-  return gemm_xwT(ctx, abuf, wo, 0, out, (int)T, o_out, qo);
+  // o_proj: out = attn . Wo^T   (src/oomllama_turbo.rs:715-720): a GEMV for decode-sized
+  // token counts, the tensor-core linear above that
+  if (T <= kGemvMaxT) return f32_gemv(ctx, abuf, wo, (int)T, o_out, qo, nullptr, nullptr, out);
+  const KfJob oj{wo, 0, o_out, nullptr, nullptr, out};
+  return kf_linear_f32(ctx, abuf, (int)T, qo, &oj, 1);
 }
 
 }  // extern "C"
@@ -1632,6 +1773,63 @@ cudaError_t launch_q8_linear_xs(const Q8Args& a, int groups, cudaStream_t st) {
 // (two MMA token tiles; each weight byte is read once per pass): one x split
 // per pass, then one linear launch over all jobs' row blocks, a programmatic
 // dependent of the split.
+// Prefill-sized Q8 linears on the tensor cores (K-F): the input is normalised
+// (rmsnorm_kernel) when norm_w is given and split into fp16 hi/lo planes with
+// its block sums once; each matrix is converted to fp16 with its scales and
+// minima transposed, then multiplied with the block promotion.  Above this
+// many tokens the weight conversion costs less than re-reading the weights
+// once per 16-token pass of K-E.
+constexpr int kKfQ8MinTokens = 64;
+
+bool kf_q8_fits(const Q8Job* jobs, int n_jobs) {
+  for (int j = 0; j < n_jobs; ++j) {
+    const Q8Job& jb = jobs[j];
+    if (jb.w->cols % kKfQ8Block || jb.w->rows % 4) return false;
+    const uintptr_t al = reinterpret_cast<uintptr_t>(jb.y) | reinterpret_cast<uintptr_t>(jb.bias) |
+                         reinterpret_cast<uintptr_t>(jb.residual);
+    if (al & 15) return false;
+  }
+  return true;
+}
+
+int kf_linear_q8(oomattn_ctx* ctx, const Q8Job* jobs, int n_jobs, const float* x, const float* up, int m,
+                 const float* norm_w, float eps) {
+  const int k = jobs[0].w->cols;
+  size_t wmax = 0;
+  for (int j = 0; j < n_jobs; ++j) wmax = std::max(wmax, (size_t)jobs[j].w->rows * k);
+  const size_t xnb = norm_w ? align256((size_t)m * k * 4) : 0, xb = align256((size_t)m * k * 2);
+  const size_t sb = align256((size_t)m * (k / kKfQ8Block) * 4), wb = align256(wmax * 2);
+  const size_t tb = align256(wmax / kKfQ8Block * 4);
+  int rc;
+  uint8_t* sc = kf_scratch(ctx, xnb + 2 * xb + sb + wb + 2 * tb, &rc);
+  if (rc) return rc;
+  float* xn = reinterpret_cast<float*>(sc);
+  uint16_t* xh = reinterpret_cast<uint16_t*>(sc + xnb);
+  uint16_t* xl = reinterpret_cast<uint16_t*>(sc + xnb + xb);
+  float* xsum = reinterpret_cast<float*>(sc + xnb + 2 * xb);
+  uint16_t* w16 = reinterpret_cast<uint16_t*>(sc + xnb + 2 * xb + sb);
+  float* st = reinterpret_cast<float*>(sc + xnb + 2 * xb + sb + wb);
+  float* mt = reinterpret_cast<float*>(sc + xnb + 2 * xb + sb + wb + tb);
+  if (norm_w) {
+    rmsnorm_kernel<<<m, kNormThreads, 0, ctx->stream>>>(x, norm_w, eps, k, xn);
+    CKLAUNCH();
+    x = xn;
+  }
+  const long long warps = (long long)m * (k / kKfQ8Block);
+  kf_prep_x16_kernel<<<(unsigned)std::min<long long>((warps + 7) / 8, (long long)ctx->num_sms * 16), 256, 0,
+                       ctx->stream>>>(x, up, xh, xl, xsum, m, k, ctx->d_status);
+  CKLAUNCH();
+  for (int j = 0; j < n_jobs; ++j) {
+    const oomattn_q8_matrix* w = jobs[j].w;
+    kf_prep_w8_kernel<<<ctx->num_sms * 8, 256, 0, ctx->stream>>>(w->q, w->scale, w->min, w16, st, mt, w->rows, k);
+    CKLAUNCH();
+    rc = kf_launch<true, 1>(ctx, m, w->rows, k, xh, xl, w16, nullptr, jobs[j].bias, jobs[j].residual, jobs[j].y, st,
+                            mt, xsum);
+    if (rc) return rc;
+  }
+  return OOMATTN_OK;
+}
+
 int q8_run(oomattn_ctx* ctx, const Q8Job* jobs, int n_jobs, const float* x, const float* up, int n_tokens,
            const float* norm_w = nullptr, float eps = 0.f) {
   if (!x || n_tokens < 0) return fail(ctx, OOMATTN_ERR_INVALID_ARG, "bad Q8 input");
@@ -1663,6 +1861,8 @@ int q8_run(oomattn_ctx* ctx, const Q8Job* jobs, int n_jobs, const float* x, cons
     }
   }
   if (n_tokens == 0) return OOMATTN_OK;
+  if (n_tokens > kKfQ8MinTokens && ctx->kf_q8_regs == kKfLaunchRegs && kf_q8_fits(jobs, n_jobs))
+    return kf_linear_q8(ctx, jobs, n_jobs, x, up, n_tokens, norm_w, eps);
   const int group = 16;
   const int nchunks = cols / kQ8Chunk;
   const size_t xw = (size_t)group * (cols / 2);
@@ -1946,6 +2146,105 @@ extern "C" int oomattn_decode_step_q8(oomattn_ctx* ctx, const oomattn_q8_model* 
   }
   const Q8Job head{&m->lm_head, nullptr, nullptr, lg};
   rc = q8_run(ctx, &head, 1, xa, nullptr, n_seqs, m->final_norm, m->eps);
+  if (rc) return rc;
+  return oomattn_argmax(ctx, lg, n_seqs, (int)vocab, next);
+}
+
+extern "C" int oomattn_prefill_step_q8(oomattn_ctx* ctx, const oomattn_q8_model* m, int32_t n_seqs,
+                                       const int32_t* seq_ids, int32_t n_new, const int32_t* tokens, int32_t* next,
+                                       float* logits) {
+  if (!ctx) return OOMATTN_ERR_INVALID_ARG;
+  if (!m || !m->layers || !seq_ids || !tokens || !next || n_seqs <= 0 || n_new <= 0)
+    return fail(ctx, OOMATTN_ERR_INVALID_ARG, "bad prefill_step_q8 arguments");
+  if (m->n_layers <= 0 || m->n_layers > ctx->cfg.n_layers)
+    return fail(ctx, OOMATTN_ERR_OUT_OF_RANGE, "model has %d layers, the context %d", m->n_layers, ctx->cfg.n_layers);
+  if (ctx->cfg.kv_dtype != OOMATTN_DTYPE_BF16)
+    return fail(ctx, OOMATTN_ERR_UNSUPPORTED, "the model prefill runs the tensor-core attention: bf16 cache needed");
+  const int H = ctx->cfg.hidden_size, hq = ctx->cfg.n_heads, hkv = ctx->cfg.n_kv_heads;
+  const int nq = hq * kHeadDim, nkv = hkv * kHeadDim;
+  if (m->embed.cols != H || m->lm_head.cols != H || !m->final_norm)
+    return fail(ctx, OOMATTN_ERR_INVALID_ARG, "embedding / LM head width or final norm does not match hidden %d", H);
+  for (int l = 0; l < m->n_layers; ++l) {
+    const oomattn_q8_layer* w = &m->layers[l];
+    if (w->q.rows != nq || w->k.rows != nkv || w->v.rows != nkv || w->q.cols != H || w->k.cols != H ||
+        w->v.cols != H || w->o.rows != H || w->o.cols != nq || w->gate.cols != H || w->up.cols != H ||
+        w->up.rows != w->gate.rows || w->down.rows != H || w->down.cols != w->gate.rows || !w->input_norm ||
+        !w->post_norm)
+      return fail(ctx, OOMATTN_ERR_INVALID_ARG, "layer %d: weight shapes do not match the configuration", l);
+  }
+  DeviceGuard dg(ctx->device);
+  const size_t T = (size_t)n_seqs * n_new, B = (size_t)n_seqs, vocab = (size_t)m->lm_head.rows;
+  const size_t inter = (size_t)m->layers[0].gate.rows;
+  auto up32 = [](size_t n) { return (n + 31) / 32 * 32; };  // 128-byte aligned pieces
+  // model scratch: the residual stream (two buffers), the last token of each sequence, the logits
+  const size_t need_m = (2 * up32(T * H) + up32(B * H) + (logits ? 0 : up32(B * vocab)) + 64) * 4;
+  if (need_m > ctx->model_scratch_bytes) {
+    if (ctx->d_model_scratch) {
+      cudaStreamSynchronize(ctx->stream);
+      cudaFree(ctx->d_model_scratch);
+      ctx->d_model_scratch = nullptr;
+      ctx->model_scratch_bytes = 0;
+    }
+    if (cudaMalloc(&ctx->d_model_scratch, need_m) != cudaSuccess)
+      return fail(ctx, OOMATTN_ERR_NO_MEMORY, "model scratch allocation of %zu bytes failed", need_m);
+    ctx->model_scratch_bytes = need_m;
+  }
+  float* xa = ctx->d_model_scratch;
+  float* xb = xa + up32(T * H);
+  float* xlast = xb + up32(T * H);
+  float* lg = logits ? logits : xlast + up32(B * H);
+  // layer scratch: q, k, v, rotated q (bf16), attention output, h, gate, up
+  int rc;
+  float* sb = layer_scratch(ctx, up32(T * nq) * 3 + up32(T * nkv) * 2 + up32(T * nq / 2) + up32(T * H) +
+                                     2 * up32(T * inter) + 64, &rc);
+  if (rc) return rc;
+  auto carve = [&](size_t n) {
+    float* p = sb;
+    sb += up32(n);
+    return p;
+  };
+  float* q = carve(T * nq);
+  float* k = carve(T * nkv);
+  float* v = carve(T * nkv);
+  uint16_t* qr = reinterpret_cast<uint16_t*>(carve(T * nq / 2 + 1));
+  float* att = carve(T * nq);
+  float* h = carve(T * H);
+  float* g = carve(T * inter);
+  float* u = carve(T * inter);
+  // OomLlamaModel::forward_turbo (src/oomllama.rs:504-553) over a prompt of n_new tokens per sequence:
+  // every token's K/V enters each layer's cache, attention is causal over the sequence (K-C), and the
+  // last token's logits give the first greedy pick (src/oomllama.rs:969-976)
+  rc = oomattn_embed_q8(ctx, &m->embed, tokens, (int32_t)T, xa);
+  if (rc) return rc;
+  for (int l = 0; l < m->n_layers; ++l) {
+    const oomattn_q8_layer* w = &m->layers[l];
+    const Q8Job qkv[3] = {{&w->q, w->bq, nullptr, q}, {&w->k, w->bk, nullptr, k}, {&w->v, w->bv, nullptr, v}};
+    rc = q8_run(ctx, qkv, 3, xa, nullptr, (int)T, w->input_norm, w->eps);
+    if (rc) return rc;
+    rc = oomattn_rope_append(ctx, l, n_seqs, seq_ids, n_new, q, k, v, OOMATTN_DTYPE_F32, nullptr, nullptr, nullptr,
+                             qr, OOMATTN_DTYPE_BF16);
+    if (rc) return rc;
+    for (int b = 0; b < n_seqs; ++b) {
+      rc = oomattn_prefill(ctx, l, seq_ids[b], n_new, qr + (size_t)b * n_new * nq, att + (size_t)b * n_new * nq,
+                           OOMATTN_DTYPE_F32, nullptr);
+      if (rc) return rc;
+    }
+    const Q8Job o{&w->o, nullptr, xa, h};
+    rc = q8_run(ctx, &o, 1, att, nullptr, (int)T);
+    if (rc) return rc;
+    const Q8Job gu[2] = {{&w->gate, nullptr, nullptr, g}, {&w->up, nullptr, nullptr, u}};
+    rc = q8_run(ctx, gu, 2, h, nullptr, (int)T, w->post_norm, w->eps);
+    if (rc) return rc;
+    const Q8Job dn{&w->down, nullptr, h, xb};
+    rc = q8_run(ctx, &dn, 1, g, u, (int)T);
+    if (rc) return rc;
+    std::swap(xa, xb);
+  }
+  // the last prompt token of each sequence
+  CK(cudaMemcpy2DAsync(xlast, (size_t)H * 4, xa + (size_t)(n_new - 1) * H, (size_t)n_new * H * 4, (size_t)H * 4, B,
+                       cudaMemcpyDeviceToDevice, ctx->stream));
+  const Q8Job head{&m->lm_head, nullptr, nullptr, lg};
+  rc = q8_run(ctx, &head, 1, xlast, nullptr, n_seqs, m->final_norm, m->eps);
   if (rc) return rc;
   return oomattn_argmax(ctx, lg, n_seqs, (int)vocab, next);
 }

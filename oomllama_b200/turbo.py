@@ -376,6 +376,23 @@ class TurboEngine:
         return out
 
 
+    def linear(self, x: torch.Tensor, w: torch.Tensor, bias=None, out=None):
+        """x @ W^T (+ bias) for f32 activations and f32 or bf16 weights [out, in] (candle's matmul with the
+        transposed weight, src/oomllama_turbo.rs:643-645, :715-720): x [T, in] -> [T, out] f32."""
+        if x.dim() != 2 or w.dim() != 2 or x.shape[1] != w.shape[1]:
+            raise ValueError(f"x {tuple(x.shape)} and w {tuple(w.shape)} do not match")
+        _dev(x, "x", self.device, dtype=torch.float32)
+        _dev(w, "w", self.device)
+        T, (rows, cols) = x.shape[0], w.shape
+        if bias is not None:
+            _dev(bias, "bias", self.device, dtype=torch.float32, numel=rows)
+        out = (torch.empty(T, rows, dtype=torch.float32, device=x.device) if out is None
+               else _dev(out, "out", self.device, dtype=torch.float32, numel=T * rows))
+        self._bind_stream()
+        check(self._ctx, self._L.oomattn_linear(self._ctx, _ptr(x), _ptr(w), _dtype_code(w), T, rows, cols,
+                                                _ptr(bias), _ptr(out)))
+        return out
+
     # ------------------------------------------------------------ Q8 weights (K-E)
     def q8_linear(self, w: "Q8Matrix", x: torch.Tensor, bias=None, out=None):
         """x @ W^T (+ bias) for a resident Q8 matrix: x [T, cols] f32 -> [T, rows] f32.
@@ -482,6 +499,22 @@ class TurboEngine:
         check(self._ctx, self._L.oomattn_decode_step_q8(self._ctx, ctypes.byref(model.c_struct()), B, ids,
                                                         _ptr(tokens), _ptr(nxt),
                                                         None if logits is None else _ptr(logits)))
+        return nxt
+
+    def prefill_step_q8(self, model: "Q8Model", seq_ids, tokens: torch.Tensor, next_tokens=None, logits=None):
+        """The prompt through the whole model (OomLlamaModel::forward_turbo over every prompt token,
+        src/oomllama.rs:504-553, 969-970): int32 tokens [B, n_new] -> int32 next [B], the greedy pick after each
+        sequence's last prompt token.  Every layer's cache grows by n_new tokens per sequence (bf16 cache)."""
+        B, n_new = tokens.shape
+        _dev(tokens, "tokens", self.device, dtype=torch.int32)
+        nxt = (torch.empty(B, dtype=torch.int32, device=self.device) if next_tokens is None
+               else _dev(next_tokens, "next_tokens", self.device, dtype=torch.int32, numel=B))
+        if logits is not None:
+            _dev(logits, "logits", self.device, dtype=torch.float32, numel=B * model.lm_head.rows)
+        self._bind_stream()
+        check(self._ctx, self._L.oomattn_prefill_step_q8(self._ctx, ctypes.byref(model.c_struct()), B,
+                                                         int_array(seq_ids), n_new, _ptr(tokens), _ptr(nxt),
+                                                         None if logits is None else _ptr(logits)))
         return nxt
 
 

@@ -255,3 +255,52 @@ def test_decode_step_q8_from_an_oom_file(oracle):
         clear = (top2[:, 1] - top2[:, 0]) > 2 * tol
         assert (got[clear] == want[clear]).all()
     eng.close()
+
+
+def test_prefill_step_q8_then_greedy_decode(oracle):
+    # C5's order on a reduced two-layer model: a prompt of 80 tokens per sequence through the whole
+    # model (tensor-core Q8 projections above 64 tokens, K-A append, K-C causal attention), the first
+    # greedy pick from the last prompt token, then greedy decode steps over the bf16 cache the prefill
+    # wrote.  The oracle runs the prompt token by token (one decode step per position), which is the
+    # same causal computation; bf16 KV tolerance on the logits (max-abs <= 2e-3 x max(1, |logit|),
+    # norm-relative <= 1e-2), picks equal wherever the oracle's top-two margin is clear.
+    n_layers, hq, hkv, inter, vocab, D, n_new, steps = 2, 2, 1, 512, 1024, 128, 80, 4
+    model, ref = _model(oracle, n_layers, hq, hkv, inter, vocab, seed=77)
+    B = 2
+    eng = make_engine(hq, hkv, [n_new + steps] * B, kv_dtype="bf16", variant="interleaved", theta=1e6,
+                      hidden=hq * D, n_layers=n_layers, shuffle_seed=8)
+    rng = np.random.default_rng(78)
+    prompt = rng.integers(0, vocab, (B, n_new)).astype(np.int32)
+    cos_t, sin_t = oracle.rope_table(1e6, D, n_new + steps)
+    caches = [([np.zeros((0, hkv, D), np.float32) for _ in range(B)],
+               [np.zeros((0, hkv, D), np.float32) for _ in range(B)]) for _ in range(n_layers)]
+    rl = [0] * B
+    for i in range(n_new):
+        want, ref_lg = oracle.model_decode_step(prompt[:, i], ref["embed"], ref["layers"], ref["final_norm"],
+                                                ref["lm_head"], 1e-6, caches, rl, hq, hkv, cos_t, sin_t,
+                                                oracle.ROPE_INTERLEAVED, kv_bf16=True)
+    logits = torch.empty(B, vocab, device="cuda")
+    tokens = eng.prefill_step_q8(model, list(range(B)), torch.from_numpy(prompt).cuda(), logits=logits)
+    eng.sync()
+    assert [eng.seq_len(l, b) for l in range(n_layers) for b in range(B)] == [n_new] * (n_layers * B)
+    for step in range(steps + 1):
+        got, lg = tokens.cpu().numpy(), logits.cpu().numpy()
+        tol = 2e-3 * max(1.0, np.abs(ref_lg).max())
+        assert_close(lg, ref_lg, tol, 1e-2, what=f"logits after {n_new + step} tokens")
+        assert got.tolist() == oracle.argmax(lg).tolist()
+        top2 = np.sort(ref_lg, axis=1)[:, -2:]
+        clear = (top2[:, 1] - top2[:, 0]) > 2 * tol
+        assert (got[clear] == want[clear]).all(), f"picks {got} vs oracle {want}"
+        if step == steps:
+            break
+        tok_in = got.copy()  # both follow the library's pick
+        eng.decode_step_q8(model, list(range(B)), tokens, next_tokens=tokens, logits=logits)
+        eng.sync()
+        want, ref_lg = oracle.model_decode_step(tok_in, ref["embed"], ref["layers"], ref["final_norm"],
+                                                ref["lm_head"], 1e-6, caches, rl, hq, hkv, cos_t, sin_t,
+                                                oracle.ROPE_INTERLEAVED, kv_bf16=True)
+    # the prefill's cache holds the oracle's rotated, bf16-rounded keys of the prompt
+    k_gpu, _ = eng.kv_read(0, 1)
+    kc = caches[0][0][1]  # [L, hkv, D]
+    np.testing.assert_allclose(k_gpu.float().numpy()[:, :n_new], kc[:n_new].transpose(1, 0, 2), atol=0.02, rtol=0.01)
+    eng.close()

@@ -102,8 +102,8 @@ def test_qkv_gemv_rope_append(oracle, T, variant):
 
 @pytest.mark.parametrize("T", [12, 40])
 def test_qkv_bf16_weights(oracle, T):
-    # 12 tokens: fused GEMV with bf16 weights (f32 x); 40 tokens: cuBLAS projection
-    # (x rounded to bf16 for the bf16 GEMM) + the K-A epilogue kernel
+    # 12 tokens: fused GEMV with bf16 weights (f32 x); 40 tokens: the tensor-core linear (x split into
+    # bf16 hi + lo, so x keeps about 16 significant bits) + the K-A epilogue kernel
     H, n_heads, n_kv = 512, 8, 2
     eng = make_engine(n_heads, n_kv, [64], kv_dtype="bf16", hidden=H)
     x = randn((T, H), 30)
@@ -113,8 +113,7 @@ def test_qkv_bf16_weights(oracle, T):
     q_out = eng.qkv_rope_append(0, [0], x.cuda(), wq.cuda(), wk.cuda(), wv.cuda())
     eng.sync()
     c, s_ = oracle.rope_table(1e6, 128, 64)
-    xr = x if T <= 16 else x.to(torch.bfloat16)
-    xq = (xr.double() @ wq.double().T).float().numpy().reshape(T, n_heads, 128)
+    xq = (x.double() @ wq.double().T).float().numpy().reshape(T, n_heads, 128)
     qr = oracle.rope_tokens(xq, np.arange(T), c, s_, oracle.ROPE_INTERLEAVED)
     np.testing.assert_allclose(q_out.cpu().numpy(), qr, atol=1e-4, rtol=1e-4)
     eng.close()
