@@ -48,7 +48,7 @@ SPEC_PEAKS = {"hbm_gbs": 7700.0, "bf16_tflops": 2250.0}  # nominal B200 (HGX HBM
 # dram__bytes_read.sum + dram__bytes_write.sum per launch from one ncu capture
 # of each kernel on these workloads: the 4096-token causal prefill and the
 # 8 x 32768-token Llama-3 decode.
-NCU_TRAFFIC_BYTES = {"prefill_bf16_kernel": 37_828_096 + 6_703_360, "decode_bf16_kernel": 1_074_328_000 + 5_611_008}
+NCU_TRAFFIC_BYTES = {"prefill_bf16_kernel": 37_828_608 + 7_362_048, "decode_bf16_kernel": 1_074_328_000 + 5_611_008}
 
 
 SECTIONS = ("prefill", "decode-llama", "decode-qwen", "c1", "q8", "layer", "repack", "model")
