@@ -22,6 +22,7 @@
 #include "params.cuh"
 #include "prefill.cuh"
 #include "q8_linear.cuh"
+#include "q8_tc.cuh"
 #include "rope_append.cuh"
 
 using namespace oomattn;
@@ -38,6 +39,7 @@ int split_cap(int kv_dtype) { return kv_dtype == OOMATTN_DTYPE_BF16 ? kMaxSplits
 static_assert(kMaxGroup * kMaxSplits <= kDecWarps * kMaxGroup * kMergeStride,
               "the decode merge stages [group][splits] lse values over the per-warp O area");
 constexpr unsigned long long kDefaultTimeoutNs = 2000000000ull;  // bounded device waits: 2 s
+constexpr int kPfMinKeyChunk = 4;  // key tiles per unit of a key-split prefill, at least
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -95,6 +97,9 @@ struct oomattn_ctx {
   // K-F (tensor-core linear): the split / converted operand planes
   uint8_t* d_kf = nullptr;
   size_t kf_bytes = 0;
+  // key-split prefill: the chunks' partial O and lse
+  uint8_t* d_pf_part = nullptr;
+  size_t pf_part_bytes = 0;
   // Q8 linear: activation splits and split-K partials, and per-row-tile
   // arrival counters (zero between launches)
   uint8_t* d_q8_scratch = nullptr;
@@ -804,7 +809,8 @@ int oomattn_create(const oomattn_config* cfg, int device, void* stream, oomattn_
       cudaFuncSetAttribute(kf_gemm_kernel<false, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kKfSmemBytes) !=
           cudaSuccess ||
       cudaFuncSetAttribute(kf_gemm_kernel<true, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kKfSmemBytes) !=
-          cudaSuccess)
+          cudaSuccess ||
+      cudaFuncSetAttribute(q8_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmemBytes) != cudaSuccess)
     return bail(OOMATTN_ERR_CUDA);
   cudaFuncAttributes fa;
   if (cudaFuncGetAttributes(&fa, prefill_bf16_kernel) != cudaSuccess) return bail(OOMATTN_ERR_CUDA);
@@ -823,7 +829,7 @@ int oomattn_destroy(oomattn_ctx* ctx) {
   void* ptrs[] = {ctx->kpool,     ctx->vpool,      ctx->d_block_table, ctx->d_cos,    ctx->d_sin,
                   ctx->d_part_o,  ctx->d_part_lse, ctx->d_counters,    ctx->d_status, ctx->d_scratch,
                   ctx->d_q8_scratch, ctx->d_q8_counters, ctx->d_layer_scratch, ctx->d_model_scratch,
-                  ctx->d_argmax_part, ctx->d_kf};
+                  ctx->d_argmax_part, ctx->d_kf, ctx->d_pf_part};
   for (void* p : ptrs)
     if (p) cudaFree(p);
   delete ctx;
@@ -1259,10 +1265,52 @@ int oomattn_prefill_blocks(oomattn_ctx* ctx, int32_t layer, int32_t seq, int32_t
   }
   a.n_ranges = n_ranges;
   DeviceGuard dg(ctx->device);
-  CUtensorMap qmap, omap;
+  // Key split: when one work unit (the pair with the most key tiles) would run
+  // much longer than the launch's work per SM -- a sharded rank's few heads --
+  // the units are cut into chunks of about that per-SM share of key tiles, so
+  // the heaviest block no longer sets the launch time; their partials are
+  // merged by one more kernel.  A whole 28-head 4096-token launch is not split.
+  const int prefix = L - n_new;
+  auto pair_tiles = [&](int p) { return (prefix + std::min(n_new, 256 * p + 256) + 127) / 128; };
+  long long work = 0;
+  int max_tiles = 1;
+  for (int i = 0; i < n_ranges; ++i)
+    for (int p = a.range_lo[i]; p < a.range_hi[i]; ++p) {
+      work += (long long)pair_tiles(p) * ctx->cfg.n_heads;
+      max_tiles = std::max(max_tiles, pair_tiles(p));
+    }
+  const int per_sm = (int)((work + ctx->num_sms - 1) / ctx->num_sms);
+  int key_chunk = max_tiles;
+  if (2 * max_tiles > 3 * per_sm) key_chunk = std::max(kPfMinKeyChunk, per_sm);
+  const int n_chunks = (max_tiles + key_chunk - 1) / key_chunk;
+  a.key_chunk = key_chunk;
+  a.n_pad = (n_new + 127) / 128 * 128;
+  a.part_lse = nullptr;
+  float* part_o = nullptr;
+  CUtensorMap qmap, omap, pmap;
   rc = encode_q_map(ctx, q, n_new, &qmap);
   if (!rc) rc = encode_out_map(ctx, out, n_new, out_dtype == OOMATTN_DTYPE_BF16, &omap);
   if (rc) return rc;
+  pmap = omap;
+  if (n_chunks > 1) {
+    const size_t rows_all = (size_t)n_chunks * a.n_pad;
+    const size_t ob = rows_all * ctx->cfg.n_heads * kHeadDim * 4, lb = rows_all * ctx->cfg.n_heads * 4;
+    if (ob + lb > ctx->pf_part_bytes) {
+      if (ctx->d_pf_part) {
+        cudaStreamSynchronize(ctx->stream);
+        cudaFree(ctx->d_pf_part);
+        ctx->d_pf_part = nullptr;
+        ctx->pf_part_bytes = 0;
+      }
+      if (cudaMalloc(&ctx->d_pf_part, ob + lb) != cudaSuccess)
+        return fail(ctx, OOMATTN_ERR_NO_MEMORY, "prefill partial scratch of %zu bytes failed", ob + lb);
+      ctx->pf_part_bytes = ob + lb;
+    }
+    part_o = reinterpret_cast<float*>(ctx->d_pf_part);
+    a.part_lse = reinterpret_cast<float*>(ctx->d_pf_part + ob);
+    rc = encode_out_map(ctx, part_o, (int)rows_all, false, &pmap);
+    if (rc) return rc;
+  }
   a.out = out;
   a.out_bf16 = out_dtype == OOMATTN_DTYPE_BF16;
   a.lse = lse;
@@ -1276,9 +1324,14 @@ int oomattn_prefill_blocks(oomattn_ctx* ctx, int32_t layer, int32_t seq, int32_t
   a.qscale = ctx->scale * 1.4426950408889634f;
   a.status = ctx->d_status;
   a.timeout_ns = ctx->timeout_ns;
-  prefill_bf16_kernel<<<(unsigned)(blocks * a.n_heads), kPfThreads, kPfSmemBytes, ctx->stream>>>(
-      qmap, ctx->kmap, ctx->vmap, omap, make_pool(ctx), a);
+  prefill_bf16_kernel<<<dim3((unsigned)(blocks * a.n_heads), n_chunks), kPfThreads, kPfSmemBytes, ctx->stream>>>(
+      qmap, ctx->kmap, ctx->vmap, omap, pmap, make_pool(ctx), a);
   CKLAUNCH();
+  if (n_chunks > 1) {
+    const long long warps = (long long)n_new * a.n_heads;
+    prefill_chunk_merge_kernel<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, ctx->stream>>>(part_o, a);
+    CKLAUNCH();
+  }
   return OOMATTN_OK;
 }
 
@@ -1773,6 +1826,87 @@ cudaError_t launch_q8_linear_xs(const Q8Args& a, int groups, cudaStream_t st) {
 // (two MMA token tiles; each weight byte is read once per pass): one x split
 // per pass, then one linear launch over all jobs' row blocks, a programmatic
 // dependent of the split.
+// The tensor-core form of a decode-sized pass (q8_tc_kernel) for large
+// matrices: rows in tiles of 128, all of a launch's matrices' tiles in one
+// grid; a grid of less than a wave of tiles is also split along the columns
+// into ranges of whole 256-column blocks.
+#ifndef OOMATTN_Q8_TC_MIN_TOKENS
+#define OOMATTN_Q8_TC_MIN_TOKENS 9
+#endif
+constexpr int kQ8TcMinTokens = OOMATTN_Q8_TC_MIN_TOKENS;
+struct Q8TcPlan {
+  int row_tiles, splits, sps;
+};
+bool q8_tc_fits(const Q8Job* jobs, int n_jobs, int total_rows, int cols) {
+  if (!q8_xs_size_ok(total_rows, cols) || cols % 256) return false;
+  for (int j = 0; j < n_jobs; ++j)
+    if (jobs[j].w->rows % kTcRows) return false;
+  return true;
+}
+Q8TcPlan plan_q8_tc(const oomattn_ctx* ctx, int total_rows, int cols) {
+  Q8TcPlan p;
+  p.row_tiles = total_rows / kTcRows;
+  const int n_st = cols / kTcCols;
+  int splits = std::max(1, std::min(ctx->num_sms / std::max(1, p.row_tiles), n_st / 8));
+  int sps = (n_st + splits - 1) / splits;
+  sps += sps & 1;  // whole 256-column blocks
+  p.sps = sps;
+  p.splits = (n_st + sps - 1) / sps;
+  return p;
+}
+
+int launch_q8_tc(oomattn_ctx* ctx, const Q8Job* jobs, int n_jobs, int cols, int t0, int nt, const uint32_t* xh,
+                 const uint32_t* xl, const float* xsum, float* part, int total_rows) {
+  const Q8TcPlan p = plan_q8_tc(ctx, total_rows, cols);
+  CUtensorMap wm[kTcMaxMats], xhm, xlm;
+  int rc = encode_2d(ctx, xh, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, cols, nt, 64, 16, &xhm);
+  if (!rc) rc = encode_2d(ctx, xl, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, cols, nt, 64, 16, &xlm);
+  if (rc) return rc;
+  Q8TcArgs a;
+  memset(&a, 0, sizeof(a));
+  a.n_mats = n_jobs;
+  a.cols = cols;
+  a.xsum = xsum;
+  a.n_tokens = nt;
+  a.splits = p.splits;
+  a.stages_per_split = p.sps;
+  a.counters = ctx->d_q8_counters;
+  a.status = ctx->d_status;
+  a.timeout_ns = ctx->timeout_ns;
+  int tiles = 0;
+  size_t row_prefix = 0;
+  for (int j = 0; j < n_jobs; ++j) {
+    const oomattn_q8_matrix* w = jobs[j].w;
+    rc = encode_2d(ctx, w->q, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, cols, w->rows, kTcCols, kTcRows, &wm[j]);
+    if (rc) return rc;
+    Q8TcMat& m = a.m[j];
+    m.scale = w->scale;
+    m.min = w->min;
+    m.rows = w->rows;
+    m.rb_begin = tiles;
+    m.bias = jobs[j].bias;
+    m.residual = jobs[j].residual ? jobs[j].residual + (size_t)t0 * w->rows : nullptr;
+    m.y = jobs[j].y + (size_t)t0 * w->rows;
+    m.part = part + (size_t)p.splits * 16 * row_prefix;
+    tiles += w->rows / kTcRows;
+    row_prefix += w->rows;
+  }
+  for (int j = n_jobs; j < kTcMaxMats; ++j) wm[j] = wm[0];
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(tiles, p.splits);
+  cfg.blockDim = dim3(kTcThreads);
+  cfg.dynamicSmemBytes = kTcSmemBytes;
+  cfg.stream = ctx->stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t le = cudaLaunchKernelEx(&cfg, q8_tc_kernel, wm[0], wm[1], wm[2], xhm, xlm, a);
+  if (le != cudaSuccess) return fail(ctx, OOMATTN_ERR_CUDA, "q8 tensor-core pass launch: %s", cudaGetErrorString(le));
+  return OOMATTN_OK;
+}
+
 // Prefill-sized Q8 linears on the tensor cores (K-F): the input is normalised
 // (rmsnorm_kernel) when norm_w is given and split into fp16 hi/lo planes with
 // its block sums once; each matrix is converted to fp16 with its scales and
@@ -1860,6 +1994,12 @@ int q8_run(oomattn_ctx* ctx, const Q8Job* jobs, int n_jobs, const float* x, cons
       max_blocks = std::max(max_blocks, xp.groups);
     }
   }
+  const bool tc_fits = q8_tc_fits(jobs, n_jobs, total_rows, cols);
+  if (tc_fits) {
+    const Q8TcPlan tp = plan_q8_tc(ctx, total_rows, cols);
+    part_floats = std::max(part_floats, (size_t)tp.splits * 16 * total_rows);
+    max_blocks = std::max(max_blocks, tp.row_tiles);
+  }
   if (n_tokens == 0) return OOMATTN_OK;
   if (n_tokens > kKfQ8MinTokens && ctx->kf_q8_regs == kKfLaunchRegs && kf_q8_fits(jobs, n_jobs))
     return kf_linear_q8(ctx, jobs, n_jobs, x, up, n_tokens, norm_w, eps);
@@ -1885,6 +2025,11 @@ int q8_run(oomattn_ctx* ctx, const Q8Job* jobs, int n_jobs, const float* x, cons
           x + (size_t)t0 * cols, up ? up + (size_t)t0 * cols : nullptr, nt, cols, xh, xl, xsum, ctx->d_status);
     }
     CKLAUNCH();
+    if (tc_fits && nt >= kQ8TcMinTokens) {
+      rc = launch_q8_tc(ctx, jobs, n_jobs, cols, t0, nt, xh, xl, xsum, part, total_rows);
+      if (rc) return rc;
+      continue;
+    }
     const int ntiles = nt > 8 ? 2 : 1;
     const Q8Plan p = plan_q8(ctx, total_rows, cols, ntiles);
     Q8XsPlan xp{p.mt, 0, p.splits, p.cps};

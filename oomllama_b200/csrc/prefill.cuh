@@ -67,6 +67,14 @@ struct PrefillArgs {
   int n_ranges;
   int range_lo[kPfMaxRanges];
   int range_hi[kPfMaxRanges];
+  // Key split: grid.y indexes chunks of key_chunk 128-key tiles; a unit
+  // (pair, head, chunk) covers key tiles [chunk * key_chunk, + key_chunk).
+  // A pair whose last tile needs more than key_chunk key tiles writes each
+  // chunk's normalised O and lse as partials (rows padded to n_pad per chunk)
+  // for prefill_chunk_merge_kernel; other pairs write out directly.
+  int key_chunk;
+  int n_pad;           // n_new rounded up to 128
+  float* part_lse;     // [chunks][n_pad][n_heads] natural log
   float qscale;        // softmax scale * log2(e)
   int* status;
   unsigned long long timeout_ns;
@@ -214,7 +222,7 @@ __host__ __device__ constexpr uint32_t make_idesc_bf16(bool b_mn_major) { return
 __global__ void __launch_bounds__(kPfThreads, 1)
     prefill_bf16_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
                         const __grid_constant__ CUtensorMap vmap, const __grid_constant__ CUtensorMap omap,
-                        const KVPool pool, const PrefillArgs a) {
+                        const __grid_constant__ CUtensorMap pmap, const KVPool pool, const PrefillArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;                                // [2 tiles][2 halves][128][128 B]
@@ -265,7 +273,14 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     // KV tiles needed by the last valid row (slot P + q0 + 128 i + rows - 1)
     ntile[i] = rows_valid[i] > 0 ? (a.prefix + q0 + 128 * i + rows_valid[i] + 127) / 128 : 0;
   }
-  const int n_kv_tiles = max(ntile[0], ntile[1]);
+  // this unit's chunk of key tiles: absolute tiles jb + j for local j < ntl[i]
+  const int jb = (int)blockIdx.y * a.key_chunk;
+  int ntl[2];
+#pragma unroll
+  for (int i = 0; i < 2; ++i) ntl[i] = max(0, min(ntile[i], jb + a.key_chunk) - jb);
+  const int n_kv_tiles = max(ntl[0], ntl[1]);
+  if (n_kv_tiles == 0) return;  // a chunk past this pair's keys: the whole CTA leaves
+  const bool split_pair = max(ntile[0], ntile[1]) > a.key_chunk;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -311,6 +326,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       prefetch_tensormap(&kmap);
       prefetch_tensormap(&vmap);
       prefetch_tensormap(&omap);
+      prefetch_tensormap(&pmap);
       mbar_arrive_expect_tx(q_full, 2 * kTileBytes);
       for (int i = 0; i < 2; ++i)
         for (int c = 0; c < 2; ++c)
@@ -348,13 +364,13 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       };
       bool ok = true;
       int rows[8], next_rows[8];
-      if (n_kv_tiles > 0) tile_rows(0, rows);
+      if (n_kv_tiles > 0) tile_rows(jb, rows);
       for (int j = 0; j < n_kv_tiles && ok; ++j) {
         const int sk = j % kPfKStages, sv = j % kPfVStages;
         if (j >= kPfKStages) ok = mbar_wait(&k_empty[sk], ((j / kPfKStages) - 1) & 1, a.status, a.timeout_ns);
         if (!ok) break;
         load_tile(sK + sk * kTileBytes, &kmap, &k_full[sk], rows);
-        if (j + 1 < n_kv_tiles) tile_rows(j + 1, next_rows);
+        if (j + 1 < n_kv_tiles) tile_rows(jb + j + 1, next_rows);
         if (j >= kPfVStages) ok = mbar_wait(&v_empty[sv], ((j / kPfVStages) - 1) & 1, a.status, a.timeout_ns);
         if (!ok) break;
         load_tile(sV + sv * kTileBytes, &vmap, &v_full[sv], rows);
@@ -427,14 +443,14 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       };
       // tile i uses K/V tile j when j < ntile[i]; ntile[1] >= ntile[0] unless Q1 is empty,
       // so the last user of a tile in issue order is Q1 when Q1 uses it, else Q0
-      auto last_user = [&](int j) { return j < ntile[1] ? 1 : 0; };
+      auto last_user = [&](int j) { return j < ntl[1] ? 1 : 0; };
       // Each commit tracks every MMA issued before it, so committing a ring's
       // "empty" barrier right after the last MMA that reads the stage frees it
       // as soon as those MMAs finish.
       if (ok && n_kv_tiles > 0) {
         wait_k(0);
         for (int i = 0; i < 2 && ok; ++i)
-          if ((i ? ntile[1] : ntile[0]) > 0) {
+          if ((i ? ntl[1] : ntl[0]) > 0) {
             issue_s(i, 0);
             tc_commit(&s_full[i]);
           }
@@ -442,7 +458,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       }
       for (int j = 0; j < n_kv_tiles && ok; ++j) {
         for (int i = 0; i < 2 && ok; ++i) {
-          if (j >= (i ? ntile[1] : ntile[0])) continue;
+          if (j >= (i ? ntl[1] : ntl[0])) continue;
           wait_v(j);
           if (!ok) break;
           ok = mbar_wait(&p_full[2 * i], j & 1, a.status, a.timeout_ns);
@@ -454,7 +470,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
           tc_fence_after();
           issue_pv_half(i, j, 1);
           if (i == last_user(j)) tc_commit(&v_empty[j % kPfVStages]);
-          if (j + 1 < (i ? ntile[1] : ntile[0])) {
+          if (j + 1 < (i ? ntl[1] : ntl[0])) {
             wait_k(j + 1);
             if (!ok) break;
             issue_s(i, j + 1);
@@ -510,7 +526,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     float m_used = -INFINITY, l = 0.f;
     bool ok = true;
     const float cl = a.qscale;
-    for (int j = 0; j < (i ? ntile[1] : ntile[0]) && ok; ++j) {
+    for (int j = 0; j < (i ? ntl[1] : ntl[0]) && ok; ++j) {
       ok = mbar_wait(&s_full[i], j & 1, a.status, a.timeout_ns);
       if (!ok) break;
       tc_fence_after();
@@ -520,7 +536,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       OOMATTN_TMEM_LD32((tmem + i * 128) + lane_off + 64, (sr + 64));
       OOMATTN_TMEM_LD32((tmem + i * 128) + lane_off + 96, (sr + 96));
       tmem_wait_ld();
-      const int lim = qslot - j * 128;  // columns c <= lim are visible
+      const int lim = qslot - (jb + j) * 128;  // columns c <= lim are visible
       if (__any_sync(0xffffffffu, lim < 127)) {
 #pragma unroll
         for (int c = 0; c < 128; ++c)
@@ -569,7 +585,10 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       // warp arrives (barrier count 4).  The scale-and-shift and the row sum
       // run as packed f32x2 FMA-pipe instructions, the exponential on MUFU.
       const uint64_t cl2 = f2_pack(cl, cl);
-      const uint64_t nm2 = f2_pack(-m_used, -m_used);
+      // a row with no visible key yet (possible only in a key-split chunk past
+      // its own slot) keeps m = -inf: shift by 0 so its masked scores give p = 0
+      const float m_eff = m_used == -INFINITY ? 0.f : m_used;
+      const uint64_t nm2 = f2_pack(-m_eff, -m_eff);
       uint64_t acc[4] = {0, 0, 0, 0};
 #pragma unroll
       for (int half = 0; half < 2; ++half) {
@@ -598,18 +617,20 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     // distinct banks; one thread of the tile issues the stores, which clip the
     // rows past n_new.  The tile's 128 threads agree on the outcome of the
     // bounded o_full wait before any of them enters a named barrier.
-    if ((i ? ntile[1] : ntile[0]) > 0) {
+    if ((i ? ntl[1] : ntl[0]) > 0) {
       bool okw = ok && mbar_wait(&o_full[i], 0, a.status, a.timeout_ns);
       tc_fence_after();
       okw = tile_bar_and(1 + i, okw);
       if (okw) {
-        const float inv = 1.f / l;
+        const float inv = l > 0.f ? 1.f / l : 0.f;  // l = 0: no visible key in this chunk
         uint8_t* stage = sQ + i * kTileBytes;
         const uint32_t st0 = smem_u32(stage) + (uint32_t)r * 128u;
         const uint32_t rsw = (uint32_t)(r & 7);
         const bool issuer = quarter == 0 && lane == 0;
-        const int qrow0 = q0 + 128 * i;
-        if (a.out_bf16) {
+        // a split pair's chunk goes to its partial rows: chunk y at rows [y * n_pad, ...)
+        const CUtensorMap* tmap = split_pair ? &pmap : &omap;
+        const int qrow0 = (split_pair ? (int)blockIdx.y * a.n_pad : 0) + q0 + 128 * i;
+        if (a.out_bf16 && !split_pair) {  // partials stay f32
 #pragma unroll
           for (int b = 0; b < 2; ++b) {  // box b: columns [64 b, 64 b + 64)
             uint32_t orr[64];
@@ -627,8 +648,8 @@ __global__ void __launch_bounds__(kPfThreads, 1)
           fence_proxy_async_smem();
           tile_bar(1 + i);
           if (issuer) {
-            tma_store_3d(&omap, stage, 0, h, qrow0);
-            tma_store_3d(&omap, stage + kHalfTileBytes, 64, h, qrow0);
+            tma_store_3d(tmap, stage, 0, h, qrow0);
+            tma_store_3d(tmap, stage + kHalfTileBytes, 64, h, qrow0);
             bulk_commit_group();
             bulk_wait_group_read0();
           }
@@ -652,15 +673,19 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             fence_proxy_async_smem();
             tile_bar(1 + i);
             if (issuer) {
-              tma_store_3d(&omap, stage, 64 * c2, h, qrow0);
-              tma_store_3d(&omap, stage + kHalfTileBytes, 64 * c2 + 32, h, qrow0);
+              tma_store_3d(tmap, stage, 64 * c2, h, qrow0);
+              tma_store_3d(tmap, stage + kHalfTileBytes, 64 * c2 + 32, h, qrow0);
               bulk_commit_group();
               bulk_wait_group_read0();
             }
           }
         }
         const bool valid = r < (i ? rows_valid[1] : rows_valid[0]);
-        if (valid && a.lse) a.lse[(size_t)row_in_chunk * a.n_heads + h] = (m_used + log2f(l)) * 0.69314718055994531f;
+        if (valid && split_pair)
+          a.part_lse[((size_t)blockIdx.y * a.n_pad + row_in_chunk) * a.n_heads + h] =
+              (l > 0.f ? (m_used + log2f(l)) * 0.69314718055994531f : -INFINITY);
+        else if (valid && a.lse)
+          a.lse[(size_t)row_in_chunk * a.n_heads + h] = (l > 0.f ? (m_used + log2f(l)) * 0.69314718055994531f : -INFINITY);
       }
     }
   }
@@ -670,6 +695,56 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
+}
+
+// The rows of key-split pairs: out[row][h] = sum_c w_c O_c / sum_c w_c with
+// w_c = e^(lse_c - max lse) over the chunks that hold work for the row's tile
+// (chunk c does when c * key_chunk < the tile's key-tile count; a row that
+// sees no key of such a chunk has its lse at -inf there, and chunk 0, which
+// holds key 0, is never empty).  One warp per (row,
+// head), 4 dimensions per lane; rows of unsplit pairs, or outside the
+// launch's block ranges, were written by the prefill kernel itself.
+__global__ void prefill_chunk_merge_kernel(const float* __restrict__ part_o, const PrefillArgs a) {
+  const long long item = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (item >= (long long)a.n_new * a.n_heads) return;
+  const int row = (int)(item / a.n_heads), h = (int)(item - (long long)row * a.n_heads);
+  const int pair = row >> 8;
+  bool mine = false;
+#pragma unroll
+  for (int r = 0; r < kPfMaxRanges; ++r)
+    if (r < a.n_ranges && pair >= a.range_lo[r] && pair < a.range_hi[r]) mine = true;
+  const int pair_end = min(a.n_new, 256 * pair + 256);
+  if (!mine || (a.prefix + pair_end + 127) / 128 <= a.key_chunk) return;
+  const int tile_end = min(a.n_new, (row / 128) * 128 + 128);
+  const int nt = (a.prefix + tile_end + 127) / 128;
+  const int nc = (nt + a.key_chunk - 1) / a.key_chunk;
+  float M = -INFINITY;
+  for (int c = 0; c < nc; ++c) M = fmaxf(M, a.part_lse[((size_t)c * a.n_pad + row) * a.n_heads + h]);
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  float wsum = 0.f;
+  for (int c = 0; c < nc; ++c) {
+    const float w = expf(a.part_lse[((size_t)c * a.n_pad + row) * a.n_heads + h] - M);
+    const float4 o = __ldg(reinterpret_cast<const float4*>(part_o + (((size_t)c * a.n_pad + row) * a.n_heads + h) *
+                                                           kHeadDim) + lane);
+    wsum += w;
+    acc.x += w * o.x;
+    acc.y += w * o.y;
+    acc.z += w * o.z;
+    acc.w += w * o.w;
+  }
+  const float inv = 1.f / wsum;
+  const size_t o_off = ((size_t)row * a.n_heads + h) * kHeadDim + lane * 4;
+  if (a.out_bf16) {
+    uint2 v;
+    v.x = pack_bf16(acc.x * inv, acc.y * inv);
+    v.y = pack_bf16(acc.z * inv, acc.w * inv);
+    *reinterpret_cast<uint2*>(reinterpret_cast<uint16_t*>(a.out) + o_off) = v;
+  } else {
+    *reinterpret_cast<float4*>(reinterpret_cast<float*>(a.out) + o_off) =
+        make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+  }
+  if (a.lse && lane == 0) a.lse[(size_t)row * a.n_heads + h] = M + logf(wsum);
 }
 
 }  // namespace oomattn

@@ -91,3 +91,21 @@ def test_q8_mlp_tensor_core_form(oracle, eng):
     eng.sync()
     ref = oracle.linear(oracle.swiglu(oracle.linear(x, gd), oracle.linear(x, ud)), dd) + res
     assert_close(y.cpu().numpy(), ref, F32_ATOL, what="q8 mlp T=100")
+
+
+@pytest.mark.parametrize("T,rows,cols", [(16, 8192, 4096), (9, 8192, 4096), (12, 512, 65536)])
+def test_q8_linear_tensor_core_decode_form(oracle, eng, T, rows, cols):
+    # 9-16 tokens on a matrix of at least 32 M weights: the tcgen05 pass (weights converted into TMEM,
+    # x hi/lo as a 32-row B operand); 512 x 65536 has 4 row tiles, so its columns split into ranges
+    # whose partial sums the last CTA of a row tile adds in order; bias and residual in the epilogue
+    wq, wd = _q8(oracle, rows, cols, seed=T + rows)
+    rng = np.random.default_rng(T + 7)
+    x = rng.standard_normal((T, cols)).astype(np.float32)
+    b = (rng.standard_normal(rows) * 0.1).astype(np.float32)
+    y1 = eng.q8_linear(wq, torch.from_numpy(x).cuda(), torch.from_numpy(b).cuda())
+    y2 = eng.q8_linear(wq, torch.from_numpy(x).cuda(), torch.from_numpy(b).cuda())
+    eng.sync()
+    ref = _f64_linear(x, wd, b)
+    assert_close(y1.cpu().numpy(), ref, F32_ATOL * max(1.0, float(np.abs(ref).max()) / 4),
+                 what=f"q8 tensor-core pass T={T} {rows}x{cols}")
+    assert torch.equal(y1, y2), "the split merge is not repeatable"

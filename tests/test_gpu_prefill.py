@@ -113,8 +113,9 @@ def test_prefill_growing_scores_rescales_o(oracle, prefix, n_new):
 
 
 def test_prefill_query_block_ranges_match_whole_launch():
-    # the sharded prefill's per-rank launch: only the blocks of its ranges are written, and each
-    # equals the whole launch's rows bit for bit (the same CTA work unit computes them)
+    # the sharded prefill's per-rank launch: only the blocks of its ranges are written, and they match
+    # the whole launch's rows (a launch of few blocks may cut the heaviest blocks' keys into chunks
+    # merged by their lse, so the match is to the bf16 tolerance rather than bit for bit)
     from oomllama_b200.shard import PrefillShardPlan
     n_new = 2000  # 8 blocks, the last one ragged
     eng = make_engine(28, 4, [n_new], kv_dtype="bf16", shuffle_seed=3)
@@ -132,7 +133,8 @@ def test_prefill_query_block_ranges_match_whole_launch():
         for lo, hi in blocks:
             rows[256 * lo:min(n_new, 256 * hi)] = True
         rows = rows.cuda()
-        assert torch.equal(part[rows], full[rows]) and torch.equal(lse[rows], full_lse[rows])
+        assert_close(part[rows].cpu().numpy(), full[rows].cpu().numpy(), BF16_ATOL, BF16_RTOL, what=f"{blocks}")
+        assert_close(lse[rows].cpu().numpy(), full_lse[rows].cpu().numpy(), 1e-3, what=f"lse {blocks}")
         assert torch.isnan(part[~rows]).all()
     # every block covered once by the two zig-zag ranks of a kv head
     cover = np.zeros(8, int)
@@ -145,4 +147,37 @@ def test_prefill_query_block_ranges_match_whole_launch():
         eng.prefill(0, 0, q, blocks=[(0, 9)])  # past the last block
     with pytest.raises(OomAttnError):
         eng.prefill(0, 0, q, blocks=[(0, 4), (3, 6)])  # overlapping
+    eng.close()
+
+
+@pytest.mark.parametrize("prefix,n_new,out_dtype", [(0, 4096, torch.float32), (700, 3000, torch.float32),
+                                                    (0, 2500, torch.bfloat16)])
+def test_prefill_key_split_few_heads(oracle, prefix, n_new, out_dtype):
+    # a launch with few heads (a sharded rank's share): the heaviest query blocks would set the launch
+    # time, so their key range is cut into chunks whose partials are merged; rows of blocks with few
+    # keys are written directly -- every row checked against the oracle on sampled (row, head) pairs
+    n_heads, n_kv = 4, 1
+    L = prefix + n_new
+    eng = make_engine(n_heads, n_kv, [L], kv_dtype="bf16", shuffle_seed=21)
+    k = randn((L, n_kv, 128), 41, torch.bfloat16)
+    v = randn((L, n_kv, 128), 42, torch.bfloat16)
+    eng.kv_write(0, 0, k.cuda(), v.cuda())
+    q = randn((n_new, n_heads, 128), 43, torch.bfloat16)
+    out, lse = eng.prefill(0, 0, q.cuda(), out_dtype=out_dtype, with_lse=True)
+    eng.sync()
+    kf, vf = as_f32_np(k).transpose(1, 0, 2).copy(), as_f32_np(v).transpose(1, 0, 2).copy()
+    qf = as_f32_np(q)
+    rng = np.random.default_rng(n_new)
+    rows = np.concatenate([rng.integers(0, n_new, 200), [0, n_new - 1, n_new - 129]]).astype(np.int32)
+    heads = rng.integers(0, n_heads, rows.size).astype(np.int32)
+    # the oracle's rows are positions prefix + row of a causal prefill over the whole cache
+    qfull = np.zeros((L, n_heads, 128), np.float32)
+    qfull[prefix:] = qf
+    ref = oracle.gqa_attention_rows(qfull, kf, vf, rows + prefix, heads, causal=True)
+    got = as_f32_np(out)[rows, heads]
+    if out_dtype == torch.bfloat16:
+        assert np.abs(got - ref).max() <= BF16_ATOL + 2.0 ** -8 * np.abs(ref).max()
+    else:
+        assert_close(got, ref, BF16_ATOL, BF16_RTOL, what=f"key-split prefill P={prefix} n={n_new}")
+    assert np.isfinite(lse.cpu().numpy()).all()
     eng.close()
