@@ -1855,18 +1855,18 @@ Q8TcPlan plan_q8_tc(const oomattn_ctx* ctx, int total_rows, int cols) {
   return p;
 }
 
-int launch_q8_tc(oomattn_ctx* ctx, const Q8Job* jobs, int n_jobs, int cols, int t0, int nt, const uint32_t* xh,
-                 const uint32_t* xl, const float* xsum, float* part, int total_rows) {
+int launch_q8_tc(oomattn_ctx* ctx, const Q8Job* jobs, int n_jobs, int cols, int t0, int nt, const uint8_t* digits,
+                 const float* xsum, const float* sx, float* part, int total_rows) {
   const Q8TcPlan p = plan_q8_tc(ctx, total_rows, cols);
-  CUtensorMap wm[kTcMaxMats], xhm, xlm;
-  int rc = encode_2d(ctx, xh, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, cols, nt, 64, 16, &xhm);
-  if (!rc) rc = encode_2d(ctx, xl, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, cols, nt, 64, 16, &xlm);
+  CUtensorMap wm[kTcMaxMats], dm;
+  int rc = encode_2d(ctx, digits, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, cols, kTcDigitRows, kTcCols, kTcDigitRows, &dm);
   if (rc) return rc;
   Q8TcArgs a;
   memset(&a, 0, sizeof(a));
   a.n_mats = n_jobs;
   a.cols = cols;
   a.xsum = xsum;
+  a.sx = sx;
   a.n_tokens = nt;
   a.splits = p.splits;
   a.stages_per_split = p.sps;
@@ -1902,7 +1902,7 @@ int launch_q8_tc(oomattn_ctx* ctx, const Q8Job* jobs, int n_jobs, int cols, int 
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  const cudaError_t le = cudaLaunchKernelEx(&cfg, q8_tc_kernel, wm[0], wm[1], wm[2], xhm, xlm, a);
+  const cudaError_t le = cudaLaunchKernelEx(&cfg, q8_tc_kernel, wm[0], wm[1], wm[2], dm, a);
   if (le != cudaSuccess) return fail(ctx, OOMATTN_ERR_CUDA, "q8 tensor-core pass launch: %s", cudaGetErrorString(le));
   return OOMATTN_OK;
 }
@@ -2006,15 +2006,28 @@ int q8_run(oomattn_ctx* ctx, const Q8Job* jobs, int n_jobs, const float* x, cons
   const int group = 16;
   const int nchunks = cols / kQ8Chunk;
   const size_t xw = (size_t)group * (cols / 2);
-  const size_t bytes = 2 * xw * 4 + (size_t)group * nchunks * 4 + part_floats * 4 + 256;
+  const size_t bytes = 2 * xw * 4 + (size_t)group * nchunks * 4 + (size_t)group * (cols / 256) * 4 +
+                       part_floats * 4 + 256;
   int rc = ensure_q8_scratch(ctx, bytes, max_blocks);
   if (rc) return rc;
   uint32_t* xh = reinterpret_cast<uint32_t*>(ctx->d_q8_scratch);
   uint32_t* xl = xh + xw;
   float* xsum = reinterpret_cast<float*>(xl + xw);
-  float* part = xsum + (size_t)group * nchunks;
+  float* sx = xsum + (size_t)group * nchunks;  // [16][cols / 256], the integer form's digit scales
+  float* part = sx + (size_t)group * (cols / 256);
   for (int t0 = 0; t0 < n_tokens; t0 += group) {
     const int nt = std::min(group, n_tokens - t0);
+    if (tc_fits && nt >= kQ8TcMinTokens) {
+      // the integer tensor-core pass: x as digits (the 64 x cols bytes over the xh/xl area)
+      uint8_t* digits = reinterpret_cast<uint8_t*>(xh);
+      const dim3 dgrid(16, (cols / 256 + kDigitBlocksPerCta - 1) / kDigitBlocksPerCta);
+      q8_digits_kernel<<<dgrid, 256, 0, ctx->stream>>>(x + (size_t)t0 * cols, up ? up + (size_t)t0 * cols : nullptr,
+                                                      norm_w, eps, nt, cols, digits, xsum, sx, ctx->d_status);
+      CKLAUNCH();
+      rc = launch_q8_tc(ctx, jobs, n_jobs, cols, t0, nt, digits, xsum, sx, part, total_rows);
+      if (rc) return rc;
+      continue;
+    }
     if (norm_w) {
       const dim3 ngrid(nt, (nchunks + kNormThreads / 32 - 1) / (kNormThreads / 32));
       rmsnorm_prep_x_kernel<<<ngrid, kNormThreads, 0, ctx->stream>>>(x + (size_t)t0 * cols, norm_w, eps, cols, xh,
@@ -2025,11 +2038,6 @@ int q8_run(oomattn_ctx* ctx, const Q8Job* jobs, int n_jobs, const float* x, cons
           x + (size_t)t0 * cols, up ? up + (size_t)t0 * cols : nullptr, nt, cols, xh, xl, xsum, ctx->d_status);
     }
     CKLAUNCH();
-    if (tc_fits && nt >= kQ8TcMinTokens) {
-      rc = launch_q8_tc(ctx, jobs, n_jobs, cols, t0, nt, xh, xl, xsum, part, total_rows);
-      if (rc) return rc;
-      continue;
-    }
     const int ntiles = nt > 8 ? 2 : 1;
     const Q8Plan p = plan_q8(ctx, total_rows, cols, ntiles);
     Q8XsPlan xp{p.mt, 0, p.splits, p.cps};

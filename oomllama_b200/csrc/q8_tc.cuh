@@ -1,39 +1,37 @@
 // K-E, tensor-core form for decode-sized token counts on large matrices:
 // y[t][r] = sum_c x[t][c] W[r][c] (+ bias) (+ residual) for up to 16 tokens,
-// W resident as Q8 (BlockQ8View::dequantize_fast, src/quant.rs:201-224), with
-// the arithmetic of q8_linear_kernel: A = 1024 + q as fp16 (exact), x split
-// into fp16 hi + lo, and per 256-value block of a row
-//   sum_k x_k (min + q_k s) = s * D + (min - 1024 s) * X,   D = sum_k (1024 + q_k) x_k.
+// W resident as Q8 (BlockQ8View::dequantize_fast, src/quant.rs:201-224), on the
+// integer tensor cores (tcgen05.mma kind::i8, u8 x u8 -> s32, exact).
 //
-// The pass is HBM-bound: every weight byte is read once, so what matters is
-// how many bytes are in flight and how little each byte costs on the SM.
-//   warp 12      TMA producer (one lane): per stage a [128 rows][128 columns]
-//                Q8 weight box (16 KB, 128-byte swizzled) and the stage's x
-//                hi/lo boxes ([16 tokens][64 columns] fp16, 4 x 2 KB), into an
-//                8-stage ring (192 KB in flight per SM).  A token past n_tokens
-//                reads as zero (the x maps end there).
-//   warps 0-7    converters in two groups of four (one warp per TMEM lane
-//                quarter each) taking alternate stages: thread r reads weight
-//                row r's 128 bytes of the stage from shared memory
-//                (conflict-free under the swizzle), forms 1024 + q as fp16
-//                pairs with one byte permute per pair, and writes them straight
-//                into TMEM as the MMA's A operand (tcgen05.st; four 64-column
-//                slots), so the fp16 weights never touch shared memory.
-//   warps 8-11   promoters: thread r holds row r's accumulators and adds each
-//                finished 256-column block, acc[t] += s (D_hi[t] + D_lo[t]) +
-//                c X[t], with the block's scale, min and x sums loaded before
-//                it waits for the block (their L2 latency kept off the
-//                converters' path), then writes the result.
-//   warp 13      MMA issuer (one lane): tcgen05.mma kind::f16, M = 128 weight
-//                rows, N = 32 (16 tokens x {hi, lo}), K = 16, A from TMEM, B (x)
-//                from shared memory; D of a block in one of two TMEM buffers.
+// The weight bytes enter the MMA as they are stored: A = q (u8), straight from
+// the TMA-loaded shared-memory tile, with no conversion.  x is written by
+// q8_digits_kernel as three base-128 digits per value relative to the largest
+// magnitude sx of its 256-column block (per token):
+//   x = sx / 127 * (e0 + e1 / 128 + e2 / 16384),  e0 in [-127, 127], e1, e2 in [-64, 64]
+// (about 21 significant bits of sx), each digit stored as e + 128 (u8).  B
+// has 64 rows: digit d of token t in row 16 d + t, and row 48 all ones, so the
+// MMA also forms S = sum q, and every 256-column block's contribution is
+//   sum_k q_k x_k = sx / 127 * ((D0 - 128 S) + (D1 - 128 S) / 128 + (D2 - 128 S) / 16384)
+//   block: scale * that + min * X_t,   X_t = sum of x over the block,
+// the block's affine map applied after its dot product (src/quant.rs:201-224).
+// Every D stays below 2^24 (255 * 255 * 256), so the integer sums are exact
+// and convert to f32 exactly.
+//
+//   warp 4       TMA producer (one lane): per stage a [128 rows][128 columns]
+//                weight box (16 KB) and the stage's [64 rows][128 columns]
+//                digit box (8 KB), 128-byte swizzled, into an 8-stage ring
+//                (192 KB in flight per SM)
+//   warp 5       MMA issuer (one lane): M = 128 weight rows, N = 64, K = 32:
+//                4 MMAs per stage; the D of a 256-column block in one of two
+//                TMEM buffers
+//   warps 0-3    promoters: thread r holds row r's 16 accumulators; each
+//                block's scale, min and the tokens' block sums and sx are
+//                loaded before the thread waits for the block's D
 // Matrices of a launch (q/k/v, gate/up) split the grid's row tiles; a matrix
 // with few row tiles is also split along its columns (grid.y), and the last
 // CTA of a row tile to finish adds the splits' partial sums in split order,
 // so results do not depend on CTA timing.
 #pragma once
-#include <cuda_fp16.h>
-
 #include "common.cuh"
 #include "prefill.cuh"
 #include "q8_linear.cuh"
@@ -44,12 +42,12 @@ constexpr int kTcRows = 128;                       // weight rows per CTA (TMEM 
 constexpr int kTcCols = 128;                       // columns per stage
 constexpr int kTcStages = 8;
 constexpr int kTcWBytes = kTcRows * kTcCols;       // 16 KB of Q8 weights per stage
-constexpr int kTcXBytes = 32 * kTcCols * 2;        // 8 KB: 16 tokens x {hi, lo} x 128 columns fp16
+constexpr int kTcXBytes = 64 * kTcCols;            // 8 KB: 64 digit rows x 128 columns
 constexpr int kTcStageBytes = kTcWBytes + kTcXBytes;
 constexpr int kTcSmemBytes = kTcStages * kTcStageBytes + 1024 + 256;
-constexpr int kTcThreads = 448;
-constexpr int kTcSlots = 4;                        // TMEM A slots of 64 columns
+constexpr int kTcThreads = 192;
 constexpr int kTcMaxMats = 3;
+constexpr int kTcDigitRows = 64;                   // B rows: 3 digits x 16 tokens, the ones row, zeros
 
 struct Q8TcMat {
   const float* scale;
@@ -67,6 +65,7 @@ struct Q8TcArgs {
   int n_mats;
   int cols;
   const float* xsum;      // [16][cols / 64] sums of x per 64-column chunk
+  const float* sx;        // [16][cols / 256] each token's largest |x| per 256-column block
   int n_tokens;           // <= 16
   int splits;             // column ranges per row tile
   int stages_per_split;   // even: a range holds whole 256-column blocks
@@ -75,36 +74,38 @@ struct Q8TcArgs {
   unsigned long long timeout_ns;
 };
 
-// M = 128, N = 32, fp16 x fp16 -> f32, A from TMEM (K-major), B K-major.
-__host__ __device__ constexpr uint32_t tc_idesc() {
-  return (1u << 4) | ((32u >> 3) << 17) | ((128u >> 4) << 24);
+// kind::i8 instruction descriptor: s32 accumulate, A and B unsigned 8-bit,
+// both K-major, M = 128, N = 64.
+__host__ __device__ constexpr uint32_t tc_i8_idesc() {
+  return (2u << 4) | ((64u >> 3) << 17) | ((128u >> 4) << 24);
 }
 
-#define OOMATTN_TMEM_LD16(taddr, r)                                                                              \
-  asm volatile("tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, " \
-               "[%16];"                                                                                          \
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),  \
-                 "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),         \
-                 "=r"(r[15])                                                                                     \
-               : "r"(taddr))
+__device__ __forceinline__ void mma_i8_ss(uint32_t d_tmem, uint32_t a_lo, uint32_t a_hi, uint32_t b_lo,
+                                          uint32_t b_hi, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t.reg .b64 da, db;\n\t"
+      "setp.ne.b32 p, %6, 0;\n\t"
+      "mov.b64 da, {%1, %2};\n\t"
+      "mov.b64 db, {%3, %4};\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], da, db, %5, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_lo), "r"(a_hi), "r"(b_lo), "r"(b_hi), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
 
 __global__ void __launch_bounds__(kTcThreads, 1)
     q8_tc_kernel(const __grid_constant__ CUtensorMap wmap0, const __grid_constant__ CUtensorMap wmap1,
-                 const __grid_constant__ CUtensorMap wmap2, const __grid_constant__ CUtensorMap xhmap,
-                 const __grid_constant__ CUtensorMap xlmap, const Q8TcArgs a) {
+                 const __grid_constant__ CUtensorMap wmap2, const __grid_constant__ CUtensorMap dmap,
+                 const Q8TcArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kTcStages * kTcStageBytes);
-  uint64_t* full = bars;                   // [kTcStages]: weights + x of a stage landed
-  uint64_t* empty = full + kTcStages;      // [kTcStages]: 4 converter warps + the MMA commit
-  uint64_t* a_full = empty + kTcStages;    // [kTcSlots]: a TMEM A slot written (4 converter warps)
-  uint64_t* a_empty = a_full + kTcSlots;   // [kTcSlots]: the MMAs reading the slot completed
-  uint64_t* d_full = a_empty + kTcSlots;   // [2]: a block's D complete
-  uint64_t* d_empty = d_full + 2;          // [2]: the converters have read D
+  uint64_t* full = bars;                   // [kTcStages]: weights + digits of a stage landed
+  uint64_t* empty = full + kTcStages;      // [kTcStages]: the stage's MMAs completed
+  uint64_t* d_full = empty + kTcStages;    // [2]: a block's D complete
+  uint64_t* d_empty = d_full + 2;          // [2]: the promoters have read D
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(d_empty + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // this CTA's matrix and row tile
   const int rb = blockIdx.x;
   int mi = 0;
 #pragma unroll
@@ -123,11 +124,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < kTcStages; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 5);
-    }
-    for (int b = 0; b < kTcSlots; ++b) {
-      mbar_init(&a_full[b], 4);
-      mbar_init(&a_empty[b], 1);
+      mbar_init(&empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&d_full[b], 1);
@@ -135,31 +132,21 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
     fence_mbar_init();
   }
-  if (warp == 13) {
-    tmem_alloc(tmem_slot, 512);
+  if (warp == 5) {
+    tmem_alloc(tmem_slot, 128);
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem = *tmem_slot;  // A slots at columns 0, 64, 128, 192; D buffers at 256 and 288
-  constexpr uint32_t kDCol = 64 * kTcSlots;
+  const uint32_t tmem = *tmem_slot;  // D buffers at columns 0 and 64
 
-  if (warp == 12) {
+  if (warp == 4) {
     // ------------------------------------------------ TMA producer
     if (lane == 0) {
       prefetch_tensormap(wmap);
-      prefetch_tensormap(&xhmap);
-      prefetch_tensormap(&xlmap);
-      auto load_x = [&](int i) {
-        uint8_t* xs = smem + (i % kTcStages) * kTcStageBytes + kTcWBytes;
-        const int c = (s_begin + i) * kTcCols;
-        tma_load_2d(xs, &xhmap, &full[i % kTcStages], c, 0);
-        tma_load_2d(xs + 2048, &xlmap, &full[i % kTcStages], c, 0);
-        tma_load_2d(xs + 4096, &xhmap, &full[i % kTcStages], c + 64, 0);
-        tma_load_2d(xs + 6144, &xlmap, &full[i % kTcStages], c + 64, 0);
-      };
-      // the first stages' weights go out before the x split this kernel
+      prefetch_tensormap(&dmap);
+      // the first stages' weights go out before the digit split this kernel
       // depends on has finished (programmatic dependent launch)
       const int pre = min(n_st, kTcStages);
       for (int i = 0; i < pre; ++i) {
@@ -167,134 +154,95 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         tma_load_2d(smem + i * kTcStageBytes, wmap, &full[i], (s_begin + i) * kTcCols, r0);
       }
       asm volatile("griddepcontrol.wait;" ::: "memory");
-      for (int i = 0; i < pre; ++i) load_x(i);
+      for (int i = 0; i < pre; ++i)
+        tma_load_2d(smem + i * kTcStageBytes + kTcWBytes, &dmap, &full[i], (s_begin + i) * kTcCols, 0);
       int issued = pre;
       for (int i = pre; i < n_st; ++i) {
         const int s = i % kTcStages;
         if (!mbar_wait(&empty[s], ((i / kTcStages) - 1) & 1, a.status, a.timeout_ns)) break;
         mbar_arrive_expect_tx(&full[s], kTcStageBytes);
         tma_load_2d(smem + s * kTcStageBytes, wmap, &full[s], (s_begin + i) * kTcCols, r0);
-        load_x(i);
+        tma_load_2d(smem + s * kTcStageBytes + kTcWBytes, &dmap, &full[s], (s_begin + i) * kTcCols, 0);
         issued = i + 1;
       }
+      // drain: the last copies this lane issued land before the CTA can exit
       for (int i = max(0, issued - kTcStages); i < issued; ++i)
         mbar_wait(&full[i % kTcStages], (i / kTcStages) & 1, a.status, a.timeout_ns);
     }
-  } else if (warp == 13) {
+  } else if (warp == 5) {
     // ------------------------------------------------ MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc = tc_idesc();
+      constexpr uint32_t idesc = tc_i8_idesc();
       const uint64_t d0 = make_sdesc(smem_u32(smem), 16, 1024);
       const uint32_t dlo = (uint32_t)d0, dhi = (uint32_t)(d0 >> 32);
       bool ok = true;
       for (int i = 0; i < n_st && ok; ++i) {
-        const int s = i % kTcStages, slot = i % kTcSlots, b = i >> 1, first = (i & 1) == 0;
-        ok = mbar_wait(&full[s], (i / kTcStages) & 1, a.status, a.timeout_ns) &&
-             mbar_wait(&a_full[slot], (i / kTcSlots) & 1, a.status, a.timeout_ns);
+        const int s = i % kTcStages, b = i >> 1, first = (i & 1) == 0;
+        ok = mbar_wait(&full[s], (i / kTcStages) & 1, a.status, a.timeout_ns);
         if (ok && first && b >= 2) ok = mbar_wait(&d_empty[b & 1], ((b >> 1) - 1) & 1, a.status, a.timeout_ns);
         if (!ok) break;
         tc_fence_after();
-        const uint32_t d = tmem + kDCol + 32 * (b & 1);
-        const uint32_t xs = dlo + (uint32_t)((s * kTcStageBytes + kTcWBytes) >> 4);
+        const uint32_t d = tmem + 64 * (b & 1);
+        const uint32_t wa = dlo + (uint32_t)((s * kTcStageBytes) >> 4);
+        const uint32_t xb = wa + (uint32_t)(kTcWBytes >> 4);
 #pragma unroll
-        for (int kk = 0; kk < kTcCols / 16; ++kk) {
-          // B: k-step kk of the [32 rows][64 columns] half (kk / 4), 32 bytes per step
-          const uint32_t bd = xs + (uint32_t)((kk >> 2) * (4096 >> 4) + (kk & 3) * 2);
-          mma_ts_lh(d, tmem + slot * 64 + kk * 8, bd, dhi, idesc, (first && kk == 0) ? 0u : 1u);
-        }
-        tc_commit(&a_empty[slot]);
+        for (int kk = 0; kk < kTcCols / 32; ++kk)  // 32 columns (bytes) per k-step of the 128-byte row
+          mma_i8_ss(d, wa + kk * 2, dhi, xb + kk * 2, dhi, idesc, (first && kk == 0) ? 0u : 1u);
         tc_commit(&empty[s]);
         if (!first) tc_commit(&d_full[b & 1]);
       }
     }
-  } else if (warp < 8) {
-    // ------------------------------------------------ converters (warps 0-7)
-    const int grp = warp >> 2;             // converts the stages i with i % 2 == grp
-    const int r = (warp & 3) * 32 + lane;  // weight row within the tile = TMEM lane
-    const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
-    const uint32_t rsw = (uint32_t)(r & 7);
-    bool ok = true;
-    for (int i = grp; i < n_st && ok; i += 2) {
-      const int s = i % kTcStages, slot = i % kTcSlots;
-      ok = mbar_wait(&full[s], (i / kTcStages) & 1, a.status, a.timeout_ns);
-      if (ok && i >= kTcSlots) ok = mbar_wait(&a_empty[slot], ((i / kTcSlots) - 1) & 1, a.status, a.timeout_ns);
-      ok = __all_sync(0xffffffffu, ok);
-      if (!ok) break;
-      tc_fence_after();
-      // row r's 128 weight bytes: 8 chunks of 16, chunk j at position j ^ (r % 8);
-      // each half (64 columns) converted and stored to TMEM in turn
-      const uint32_t row = smem_u32(smem + s * kTcStageBytes) + (uint32_t)r * 128u;
-#pragma unroll
-      for (int hf = 0; hf < 2; ++hf) {
-        uint32_t w[32];
-#pragma unroll
-        for (int jj = 0; jj < 4; ++jj) {
-          const int j = hf * 4 + jj;
-          uint32_t q0, q1, q2, q3;
-          asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
-                       : "=r"(q0), "=r"(q1), "=r"(q2), "=r"(q3)
-                       : "r"(row + ((((uint32_t)j) ^ rsw) << 4)));
-          const uint32_t qs[4] = {q0, q1, q2, q3};
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            w[8 * jj + 2 * u] = __byte_perm(qs[u], 0x64646464u, 0x4140);      // bytes 0, 1 -> 1024 + q
-            w[8 * jj + 2 * u + 1] = __byte_perm(qs[u], 0x64646464u, 0x4342);  // bytes 2, 3
-          }
-        }
-        OOMATTN_TMEM_ST32(tmem + lane_off + slot * 64 + hf * 32, w);
-      }
-      tmem_wait_st();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&a_full[slot]);
-        mbar_arrive(&empty[s]);  // the weights of the stage are read
-      }
-    }
-  } else if (warp < 12) {
-    // ------------------------------------------------ promoters (warps 8-11)
-    const int r = (warp & 3) * 32 + lane;
+  } else {
+    // ------------------------------------------------ promoters (warps 0-3)
+    const int r = warp * 32 + lane;  // weight row within the tile = TMEM lane
     const int R = r0 + r;
-    const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
+    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
     float acc[16];
 #pragma unroll
     for (int t = 0; t < 16; ++t) acc[t] = 0.f;
-    asm volatile("griddepcontrol.wait;" ::: "memory");  // xsum comes from the x split
+    asm volatile("griddepcontrol.wait;" ::: "memory");  // sx and xsum come from the digit split
     bool ok = true;
     for (int b = 0; b < n_blocks && ok; ++b) {
       // this block's operands first: their latency overlaps the wait for D
-      const int kb = s_begin / 2 + b;  // 256-column block within the row
-      float sc = 0.f, c = 0.f;
+      const int kb = s_begin / 2 + b;
+      float sc = 0.f, mn = 0.f;
       if (R < M.rows) {
         const size_t blk = (size_t)R * kb_total + kb;
         sc = __ldg(M.scale + blk);
-        c = __ldg(M.min + blk) - 1024.f * sc;
+        mn = __ldg(M.min + blk);
       }
-      float X[16];
+      float X[16], unit[16];  // block sums, sx / 127
       const float* xs = a.xsum + 4 * kb;
 #pragma unroll
       for (int t = 0; t < 16; ++t) {
         if (t < a.n_tokens) {
           const float4 x4 = __ldg(reinterpret_cast<const float4*>(xs + (size_t)t * (a.cols / 64)));
           X[t] = (x4.x + x4.y) + (x4.z + x4.w);
+          unit[t] = __ldg(a.sx + (size_t)t * kb_total + kb) * (1.f / 127.f);
         } else {
           X[t] = 0.f;
+          unit[t] = 0.f;
         }
       }
       ok = mbar_wait(&d_full[b & 1], (b >> 1) & 1, a.status, a.timeout_ns);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc_fence_after();
-      uint32_t dr[32];
-      OOMATTN_TMEM_LD16(tmem + lane_off + kDCol + 32 * (b & 1), dr);
-      OOMATTN_TMEM_LD16(tmem + lane_off + kDCol + 32 * (b & 1) + 16, (dr + 16));
+      uint32_t dr[64];
+      OOMATTN_TMEM_LD32(tmem + lane_off + 64 * (b & 1), dr);
+      OOMATTN_TMEM_LD32(tmem + lane_off + 64 * (b & 1) + 32, (dr + 32));
       tmem_wait_ld();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&d_empty[b & 1]);
+      const int s128 = 128 * (int)dr[48];  // 128 x the sum of the block's q of this row
 #pragma unroll
-      for (int t = 0; t < 16; ++t)
-        acc[t] = fmaf(sc, __uint_as_float(dr[t]) + __uint_as_float(dr[16 + t]), fmaf(c, X[t], acc[t]));
+      for (int t = 0; t < 16; ++t) {
+        const float e0 = (float)((int)dr[t] - s128), e1 = (float)((int)dr[16 + t] - s128);
+        const float e2 = (float)((int)dr[32 + t] - s128);
+        const float dot = unit[t] * (e0 + (e1 * (1.f / 128.f) + e2 * (1.f / 16384.f)));
+        acc[t] = fmaf(sc, dot, fmaf(mn, X[t], acc[t]));
+      }
     }
     ok = __all_sync(0xffffffffu, ok);
     // ------------------------------------------------ epilogue
@@ -339,10 +287,119 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 13) {
+  if (warp == 5) {
     tc_fence_after();
-    tmem_dealloc(tmem, 512);
+    tmem_dealloc(tmem, 128);
   }
+}
+
+// The x split of the integer form, for up to 16 tokens: CTAs (token slot,
+// group of 8 256-column blocks), one warp per block.  The row the linear reads
+// -- x, x RMS-normalised with weight w (the row's sum of squares formed by
+// every CTA exactly as rmsnorm_kernel forms it), or the gated activation
+// silu(x) * up (as q8_prep_x_kernel forms it) -- gives per block its largest
+// magnitude sx, three base-128 digits per value (+128, u8) into rows t, 16 + t
+// and 32 + t of digits [64][cols], and its sums over each 64-column chunk (a
+// fixed shuffle tree).  A slot past n_tokens writes zero digits (128).  The
+// CTAs of slot 0 also write the ones row (48) and the zero rows (49-63) of
+// their columns.  A non-finite value is reported through the status word.
+constexpr int kDigitBlocksPerCta = 8;
+__global__ void __launch_bounds__(256) q8_digits_kernel(const float* __restrict__ x, const float* __restrict__ up,
+                                                        const float* __restrict__ norm_w, float eps, int n_tokens,
+                                                        int cols, uint8_t* __restrict__ digits,
+                                                        float* __restrict__ xsum, float* __restrict__ sx,
+                                                        int* status) {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  __shared__ float red[8];
+  const int t = blockIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, wp = tid >> 5;
+  const int kb_total = cols / 256;
+  const int kb = blockIdx.y * kDigitBlocksPerCta + wp;  // this warp's 256-column block
+  const bool has_block = kb < kb_total;
+  const int c0 = kb * 256 + lane * 8;  // this lane's 8 columns
+  if (t == 0 && has_block) {
+#pragma unroll
+    for (int rr = 48; rr < 64; ++rr)
+      *reinterpret_cast<uint2*>(digits + (size_t)rr * cols + c0) =
+          rr == 48 ? make_uint2(0x01010101u, 0x01010101u) : make_uint2(0u, 0u);
+  }
+  if (t >= n_tokens) {
+    if (has_block)
+#pragma unroll
+      for (int d = 0; d < 3; ++d)
+        *reinterpret_cast<uint2*>(digits + (size_t)(16 * d + t) * cols + c0) = make_uint2(0x80808080u, 0x80808080u);
+    return;
+  }
+  const float* xr = x + (size_t)t * cols;
+  float denom = 1.f;
+  if (norm_w) {
+    // the sum of squares exactly as rmsnorm_kernel forms it (every CTA of the token forms it)
+    float s = 0.f;
+    for (int i = tid * 4; i < cols; i += 256 * 4) {
+      const float4 v = *reinterpret_cast<const float4*>(xr + i);
+      s += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+    }
+#pragma unroll
+    for (int d = 16; d > 0; d >>= 1) s += __shfl_xor_sync(0xffffffffu, s, d);
+    if (lane == 0) red[wp] = s;
+    __syncthreads();
+    float tot = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) tot += red[k];
+    denom = sqrtf(tot / (float)cols + eps);
+  }
+  if (!has_block) return;
+  float v[8];
+  {
+    const float4 p = *reinterpret_cast<const float4*>(xr + c0), q = *reinterpret_cast<const float4*>(xr + c0 + 4);
+    v[0] = p.x; v[1] = p.y; v[2] = p.z; v[3] = p.w; v[4] = q.x; v[5] = q.y; v[6] = q.z; v[7] = q.w;
+  }
+  if (norm_w) {
+    const float4 p = *reinterpret_cast<const float4*>(norm_w + c0), q = *reinterpret_cast<const float4*>(norm_w + c0 + 4);
+    const float w8[8] = {p.x, p.y, p.z, p.w, q.x, q.y, q.z, q.w};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = v[i] / denom * w8[i];
+  }
+  if (up) {
+    const float* ur = up + (size_t)t * cols + c0;
+    const float4 p = *reinterpret_cast<const float4*>(ur), q = *reinterpret_cast<const float4*>(ur + 4);
+    const float u8[8] = {p.x, p.y, p.z, p.w, q.x, q.y, q.z, q.w};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = v[i] * (1.f / (1.f + expf(-v[i]))) * u8[i];
+  }
+  float mx = 0.f;
+  bool bad = false;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    bad |= !(fabsf(v[i]) <= 3.0e38f);
+    mx = fmaxf(mx, fabsf(v[i]));
+  }
+#pragma unroll
+  for (int d = 16; d > 0; d >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, d));
+  if (bad) report_error(status, kDevErrX16);
+  if (lane == 0) sx[(size_t)t * kb_total + kb] = mx;
+  const float k127 = mx > 0.f ? 127.f / mx : 0.f;
+  uint32_t e[3][2] = {{0u, 0u}, {0u, 0u}, {0u, 0u}};
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float z = v[i] * k127;
+    const float d0 = fminf(127.f, fmaxf(-127.f, rintf(z)));
+    const float r1 = (z - d0) * 128.f;
+    const float d1 = fminf(64.f, fmaxf(-64.f, rintf(r1)));
+    const float r2 = (r1 - d1) * 128.f;
+    const float d2 = fminf(64.f, fmaxf(-64.f, rintf(r2)));
+    e[0][i >> 2] |= (uint32_t)((int)d0 + 128) << (8 * (i & 3));
+    e[1][i >> 2] |= (uint32_t)((int)d1 + 128) << (8 * (i & 3));
+    e[2][i >> 2] |= (uint32_t)((int)d2 + 128) << (8 * (i & 3));
+  }
+#pragma unroll
+  for (int d = 0; d < 3; ++d)
+    *reinterpret_cast<uint2*>(digits + (size_t)(16 * d + t) * cols + c0) = make_uint2(e[d][0], e[d][1]);
+  // the 64-column chunk sums: lanes 8j..8j+7 hold chunk j of the block
+  float s = ((v[0] + v[1]) + (v[2] + v[3])) + ((v[4] + v[5]) + (v[6] + v[7]));
+#pragma unroll
+  for (int d = 4; d > 0; d >>= 1) s += __shfl_xor_sync(0xffffffffu, s, d);
+  if ((lane & 7) == 0) xsum[(size_t)t * (cols / 64) + kb * 4 + (lane >> 3)] = s;
 }
 
 }  // namespace oomattn

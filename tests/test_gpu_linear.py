@@ -109,3 +109,71 @@ def test_q8_linear_tensor_core_decode_form(oracle, eng, T, rows, cols):
     assert_close(y1.cpu().numpy(), ref, F32_ATOL * max(1.0, float(np.abs(ref).max()) / 4),
                  what=f"q8 tensor-core pass T={T} {rows}x{cols}")
     assert torch.equal(y1, y2), "the split merge is not repeatable"
+
+
+def _gpu_q8(rows, cols, g):
+    from oomllama_b200 import Q8Matrix
+    nb = rows * cols // 256
+    return Q8Matrix(torch.randint(0, 256, (rows * cols,), dtype=torch.uint8, device="cuda", generator=g),
+                    torch.rand(nb, device="cuda", generator=g) * 2e-4, -torch.rand(nb, device="cuda", generator=g) * 0.02,
+                    rows, cols)
+
+
+def _f64_q8(w):
+    q = w.q.view(w.rows, w.cols).double()
+    s = w.scale.double().repeat_interleave(256).view(w.rows, w.cols)
+    m = w.min.double().repeat_interleave(256).view(w.rows, w.cols)
+    return m + q * s
+
+
+def test_q8_mlp_integer_form_with_gated_input(eng):
+    # 16 tokens through gate/up (9472 x 3584 each, one launch) and down (3584 x 9472) on the integer
+    # tensor-core form, the gated activation formed in down's digit split and the residual added in
+    # its epilogue; against float64 on the device, and against the 16-token-pass form on 8 tokens
+    g = torch.Generator(device="cuda").manual_seed(5)
+    H, inter, T = 3584, 9472, 16
+    gate, up, down = _gpu_q8(inter, H, g), _gpu_q8(inter, H, g), _gpu_q8(H, inter, g)
+    x = torch.randn(T, H, device="cuda", generator=g)
+    res = torch.randn(T, H, device="cuda", generator=g)
+    y16 = eng.q8_mlp(gate, up, down, x, residual=res)
+    y8 = torch.cat([eng.q8_mlp(gate, up, down, x[:8].contiguous(), residual=res[:8].contiguous()),
+                    eng.q8_mlp(gate, up, down, x[8:].contiguous(), residual=res[8:].contiguous())])
+    eng.sync()
+    xd = x.double()
+    hg, hu = xd @ _f64_q8(gate).T, xd @ _f64_q8(up).T
+    ref = (hg * torch.sigmoid(hg) * hu) @ _f64_q8(down).T + res.double()
+    tol = F32_ATOL * max(1.0, float(ref.abs().max()))
+    assert_close(y16.cpu().numpy(), ref.cpu().numpy(), tol, what="q8 mlp, integer form")
+    assert_close(y16.cpu().numpy(), y8.cpu().numpy(), tol, what="integer form vs 16-token passes")
+
+
+def test_decoder_layer_integer_form_with_normalised_input(oracle):
+    # one decoder layer's step for 16 sequences whose gate/up (2 x 8192 x 2048) run on the integer
+    # tensor-core form with the RMSNorm folded into their digit split, against the same layer run as
+    # two 8-sequence steps (the register form) on an identical second context
+    from oomllama_b200 import Q8DecoderLayer, TurboConfig, TurboEngine
+    H, hq, hkv, inter, B, ctx = 2048, 16, 2, 8192, 16, 300
+    g = torch.Generator(device="cuda").manual_seed(9)
+    w = Q8DecoderLayer(q=_gpu_q8(hq * 128, H, g), k=_gpu_q8(hkv * 128, H, g), v=_gpu_q8(hkv * 128, H, g),
+                       o=_gpu_q8(H, hq * 128, g), gate=_gpu_q8(inter, H, g), up=_gpu_q8(inter, H, g),
+                       down=_gpu_q8(H, inter, g), input_norm=1 + 0.1 * torch.randn(H, device="cuda", generator=g),
+                       post_norm=1 + 0.1 * torch.randn(H, device="cuda", generator=g), eps=1e-6)
+    x = torch.randn(B, H, device="cuda", generator=g)
+    kv_k = torch.randn(B, ctx, hkv, 128, device="cuda", generator=g)
+    kv_v = torch.randn(B, ctx, hkv, 128, device="cuda", generator=g)
+    outs = []
+    for split in (False, True):
+        eng = TurboEngine(TurboConfig(n_layers=1, hidden_size=H, n_heads=hq, n_kv_heads=hkv, max_seq_len=ctx + 16,
+                                      max_seqs=B, kv_dtype="f32", rope_variant="interleaved", rope_theta=1e6))
+        for b in range(B):
+            eng.kv_write(0, b, kv_k[b].contiguous(), kv_v[b].contiguous())
+        if split:
+            o = torch.cat([eng.decoder_layer_q8(0, range(8), x[:8].contiguous(), w),
+                           eng.decoder_layer_q8(0, range(8, 16), x[8:].contiguous(), w)])
+        else:
+            o = eng.decoder_layer_q8(0, range(B), x, w)
+        eng.sync()
+        outs.append(o.cpu().numpy())
+        eng.close()
+    tol = F32_ATOL * max(1.0, float(np.abs(outs[1]).max()))
+    assert_close(outs[0], outs[1], tol, what="decoder layer, integer form vs register form")
