@@ -478,6 +478,25 @@ AppendArgs base_append_args(oomattn_ctx* ctx, int layer, int n_new) {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// A launch as a programmatic dependent of the kernel before it on the stream:
+// it may start while that kernel runs; the kernel waits (griddepcontrol.wait)
+// before it touches anything the earlier kernel reads or writes.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                       Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
 // Vectorised K-A epilogue over T tokens (one template instance per input /
 // q-output / cache dtype combination).
 int launch_rope_append(oomattn_ctx* ctx, const AppendArgs& ap, const SeqBatch& sb, int T) {
@@ -492,7 +511,8 @@ int launch_rope_append(oomattn_ctx* ctx, const AppendArgs& ap, const SeqBatch& s
   const int grid = (int)std::max<long long>(1, std::min<long long>((units + 255) / 256, (long long)ctx->num_sms * 4));
   const KVPool pool = make_pool(ctx);
   const int combo = (ap.in_bf16 ? 4 : 0) | (ap.q_out_bf16 ? 2 : 0) | (pool.kv_bf16 ? 1 : 0);
-#define OOMATTN_RA(I, Q, K) rope_append_kernel<I, Q, K><<<grid, 256, 0, ctx->stream>>>(ap, pool, sb, T)
+  cudaError_t le = cudaSuccess;
+#define OOMATTN_RA(I, Q, K) le = launch_pdl(rope_append_kernel<I, Q, K>, dim3(grid), dim3(256), 0, ctx->stream, ap, pool, sb, T)
   switch (combo) {
     case 0: OOMATTN_RA(false, false, false); break;
     case 1: OOMATTN_RA(false, false, true); break;
@@ -504,7 +524,7 @@ int launch_rope_append(oomattn_ctx* ctx, const AppendArgs& ap, const SeqBatch& s
     default: OOMATTN_RA(true, true, true); break;
   }
 #undef OOMATTN_RA
-  CKLAUNCH();
+  if (le != cudaSuccess) return fail(ctx, OOMATTN_ERR_CUDA, "append launch: %s", cudaGetErrorString(le));
   return OOMATTN_OK;
 }
 
@@ -850,6 +870,8 @@ int oomattn_sync(oomattn_ctx* ctx) {
   CK(cudaMemcpy(&st, ctx->d_status, sizeof(int), cudaMemcpyDeviceToHost));
   if (st) {
     CK(cudaMemset(ctx->d_status, 0, sizeof(int)));
+    // a linear that gave up on a wait may have left cut-tile arrivals behind
+    if (ctx->d_q8_counters) CK(cudaMemset(ctx->d_q8_counters, 0, sizeof(unsigned) * ctx->q8_counters_n));
     if (st & kDevErrTimeout) return fail(ctx, OOMATTN_ERR_TIMEOUT, "a device-side wait timed out (status %d)", st);
     if (st & kDevErrRange)
       return fail(ctx, OOMATTN_ERR_DEVICE_CHECK,
@@ -1828,17 +1850,20 @@ cudaError_t launch_q8_linear_xs(const Q8Args& a, int groups, cudaStream_t st) {
 // dependent of the split.
 // The tensor-core form of a decode-sized pass (q8_tc_kernel) for large
 // matrices: rows in tiles of 128, all of a launch's matrices' tiles in one
-// grid; a grid of less than a wave of tiles is also split along the columns
-// into ranges of whole 256-column blocks.
+// persistent grid of at most one CTA per SM, each CTA an equal range of the
+// (row tile, 256-column block) units.  It takes passes of 9 or more tokens,
+// and passes of any size over matrices of at least a wave of row tiles (the
+// gate/up pair, the LM head); a smaller matrix with few tokens leaves each
+// CTA too little to stream and stays on the CUDA-core form.
 #ifndef OOMATTN_Q8_TC_MIN_TOKENS
 #define OOMATTN_Q8_TC_MIN_TOKENS 9
 #endif
 constexpr int kQ8TcMinTokens = OOMATTN_Q8_TC_MIN_TOKENS;
 struct Q8TcPlan {
-  int row_tiles, splits, sps;
+  int row_tiles, units, grid;
 };
 bool q8_tc_fits(const Q8Job* jobs, int n_jobs, int total_rows, int cols) {
-  if (!q8_xs_size_ok(total_rows, cols) || cols % 256) return false;
+  if (!q8_xs_size_ok(total_rows, cols) || cols % 256 || cols > 256 * kTcMaxBlocks) return false;
   for (int j = 0; j < n_jobs; ++j)
     if (jobs[j].w->rows % kTcRows) return false;
   return true;
@@ -1846,12 +1871,8 @@ bool q8_tc_fits(const Q8Job* jobs, int n_jobs, int total_rows, int cols) {
 Q8TcPlan plan_q8_tc(const oomattn_ctx* ctx, int total_rows, int cols) {
   Q8TcPlan p;
   p.row_tiles = total_rows / kTcRows;
-  const int n_st = cols / kTcCols;
-  int splits = std::max(1, std::min(ctx->num_sms / std::max(1, p.row_tiles), n_st / 8));
-  int sps = (n_st + splits - 1) / splits;
-  sps += sps & 1;  // whole 256-column blocks
-  p.sps = sps;
-  p.splits = (n_st + sps - 1) / sps;
+  p.units = p.row_tiles * (cols / 256);
+  p.grid = std::max(1, std::min(ctx->num_sms, p.units));
   return p;
 }
 
@@ -1868,13 +1889,12 @@ int launch_q8_tc(oomattn_ctx* ctx, const Q8Job* jobs, int n_jobs, int cols, int 
   a.xsum = xsum;
   a.sx = sx;
   a.n_tokens = nt;
-  a.splits = p.splits;
-  a.stages_per_split = p.sps;
+  a.units = p.units;
+  a.part = part;
   a.counters = ctx->d_q8_counters;
   a.status = ctx->d_status;
   a.timeout_ns = ctx->timeout_ns;
   int tiles = 0;
-  size_t row_prefix = 0;
   for (int j = 0; j < n_jobs; ++j) {
     const oomattn_q8_matrix* w = jobs[j].w;
     rc = encode_2d(ctx, w->q, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, cols, w->rows, kTcCols, kTcRows, &wm[j]);
@@ -1887,13 +1907,11 @@ int launch_q8_tc(oomattn_ctx* ctx, const Q8Job* jobs, int n_jobs, int cols, int 
     m.bias = jobs[j].bias;
     m.residual = jobs[j].residual ? jobs[j].residual + (size_t)t0 * w->rows : nullptr;
     m.y = jobs[j].y + (size_t)t0 * w->rows;
-    m.part = part + (size_t)p.splits * 16 * row_prefix;
     tiles += w->rows / kTcRows;
-    row_prefix += w->rows;
   }
   for (int j = n_jobs; j < kTcMaxMats; ++j) wm[j] = wm[0];
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(tiles, p.splits);
+  cfg.gridDim = dim3(p.grid);
   cfg.blockDim = dim3(kTcThreads);
   cfg.dynamicSmemBytes = kTcSmemBytes;
   cfg.stream = ctx->stream;
@@ -1995,9 +2013,11 @@ int q8_run(oomattn_ctx* ctx, const Q8Job* jobs, int n_jobs, const float* x, cons
     }
   }
   const bool tc_fits = q8_tc_fits(jobs, n_jobs, total_rows, cols);
+  bool tc_wide = false;  // a wave of row tiles or more
   if (tc_fits) {
     const Q8TcPlan tp = plan_q8_tc(ctx, total_rows, cols);
-    part_floats = std::max(part_floats, (size_t)tp.splits * 16 * total_rows);
+    tc_wide = tp.row_tiles >= ctx->num_sms;
+    part_floats = std::max(part_floats, (size_t)tp.grid * 2 * 16 * kTcRows);
     max_blocks = std::max(max_blocks, tp.row_tiles);
   }
   if (n_tokens == 0) return OOMATTN_OK;
@@ -2017,13 +2037,14 @@ int q8_run(oomattn_ctx* ctx, const Q8Job* jobs, int n_jobs, const float* x, cons
   float* part = sx + (size_t)group * (cols / 256);
   for (int t0 = 0; t0 < n_tokens; t0 += group) {
     const int nt = std::min(group, n_tokens - t0);
-    if (tc_fits && nt >= kQ8TcMinTokens) {
+    if (tc_fits && (nt >= kQ8TcMinTokens || tc_wide)) {
       // the integer tensor-core pass: x as digits (the 64 x cols bytes over the xh/xl area)
       uint8_t* digits = reinterpret_cast<uint8_t*>(xh);
       const dim3 dgrid(16, (cols / 256 + kDigitBlocksPerCta - 1) / kDigitBlocksPerCta);
-      q8_digits_kernel<<<dgrid, 256, 0, ctx->stream>>>(x + (size_t)t0 * cols, up ? up + (size_t)t0 * cols : nullptr,
-                                                      norm_w, eps, nt, cols, digits, xsum, sx, ctx->d_status);
-      CKLAUNCH();
+      const cudaError_t de =
+          launch_pdl(q8_digits_kernel, dgrid, dim3(256), 0, ctx->stream, x + (size_t)t0 * cols,
+                     up ? up + (size_t)t0 * cols : nullptr, norm_w, eps, nt, cols, digits, xsum, sx, ctx->d_status);
+      if (de != cudaSuccess) return fail(ctx, OOMATTN_ERR_CUDA, "digit split launch: %s", cudaGetErrorString(de));
       rc = launch_q8_tc(ctx, jobs, n_jobs, cols, t0, nt, digits, xsum, sx, part, total_rows);
       if (rc) return rc;
       continue;

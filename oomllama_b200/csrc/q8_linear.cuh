@@ -124,8 +124,10 @@ __device__ __forceinline__ float q8_epilogue(const Q8View& a, int tok, int row, 
 // so the down projection reads it without a separate kernel or buffer.
 __global__ void q8_prep_x_kernel(const float* __restrict__ x, const float* __restrict__ up, int n_tokens, int cols,
                                  uint32_t* xh, uint32_t* xl, float* xsum, int* status) {
-  // let the dependent linear kernel launch now: it waits for this grid's
-  // completion (griddepcontrol.wait) before it reads x
+  // the linear kernel may launch now: it waits for this grid before it reads
+  // the split.  (This kernel launches after the one before it; launched as its
+  // programmatic dependent, resident beside a tensor-core pass, it slowed a
+  // Qwen2.5-7B layer's four linears at 1 token from 68 to 101 us.)
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int lane = threadIdx.x & 31;
   const int nchunks = cols / kQ8Chunk;
@@ -598,7 +600,7 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_prep_x_kernel(const floa
                                                                       const float* __restrict__ w, float eps,
                                                                       int cols, uint32_t* xh, uint32_t* xl,
                                                                       float* xsum, int* status) {
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");  // as in q8_prep_x_kernel
   __shared__ float part[kNormThreads / 32];
   const int t = blockIdx.x;
   const float* xr = x + (size_t)t * cols;

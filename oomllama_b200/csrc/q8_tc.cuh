@@ -22,15 +22,21 @@
 //                digit box (8 KB), 128-byte swizzled, into an 8-stage ring
 //                (192 KB in flight per SM)
 //   warp 5       MMA issuer (one lane): M = 128 weight rows, N = 64, K = 32:
-//                4 MMAs per stage; the D of a 256-column block in one of two
+//                4 MMAs per stage; the D of a 256-column block in one of four
 //                TMEM buffers
-//   warps 0-3    promoters: thread r holds row r's 16 accumulators; each
-//                block's scale, min and the tokens' block sums and sx are
-//                loaded before the thread waits for the block's D
-// Matrices of a launch (q/k/v, gate/up) split the grid's row tiles; a matrix
-// with few row tiles is also split along its columns (grid.y), and the last
-// CTA of a row tile to finish adds the splits' partial sums in split order,
-// so results do not depend on CTA timing.
+//   warps 0-3    promoters: thread r holds row r's 16 accumulators; the
+//                blocks' token sums and scales sit in shared memory, and each
+//                row's block scale and min arrive by cp.async into an 8-deep
+//                shared-memory ring ahead of the block's D
+// The kernel is persistent: the work is the launch's (row tile, 256-column
+// block) units in row-tile order (the matrices of a launch -- q/k/v,
+// gate/up -- one after another), and CTA c takes the contiguous range
+// [c U / G, (c + 1) U / G) of the U units, so every SM streams the same
+// number of weight bytes and its ring runs on from one row tile into the
+// next.  A row tile that a range covers whole is written directly; one cut
+// between CTAs leaves each CTA's partial sums in its first or last slot, and
+// the last CTA to finish the tile adds them in column order, so results do
+// not depend on CTA timing.
 #pragma once
 #include "common.cuh"
 #include "prefill.cuh"
@@ -38,13 +44,18 @@
 
 namespace oomattn {
 
-constexpr int kTcRows = 128;                       // weight rows per CTA (TMEM lanes)
+constexpr int kTcRows = 128;                       // weight rows per row tile (TMEM lanes)
 constexpr int kTcCols = 128;                       // columns per stage
 constexpr int kTcStages = 8;
 constexpr int kTcWBytes = kTcRows * kTcCols;       // 16 KB of Q8 weights per stage
 constexpr int kTcXBytes = 64 * kTcCols;            // 8 KB: 64 digit rows x 128 columns
 constexpr int kTcStageBytes = kTcWBytes + kTcXBytes;
-constexpr int kTcSmemBytes = kTcStages * kTcStageBytes + 1024 + 256;
+constexpr int kTcDBufs = 4;                        // D buffers of 64 TMEM columns
+constexpr int kTcMaxBlocks = 128;                  // cols <= 32768: the blocks' token operands in shared memory
+constexpr int kTcOpBytes = kTcMaxBlocks * 16 * 8;
+constexpr int kTcSmAhead = 8;                      // blocks of row scales and minima in flight
+constexpr int kTcSmBytes = kTcSmAhead * kTcRows * 8;
+constexpr int kTcSmemBytes = kTcStages * kTcStageBytes + kTcOpBytes + kTcSmBytes + 1024 + 256;
 constexpr int kTcThreads = 192;
 constexpr int kTcMaxMats = 3;
 constexpr int kTcDigitRows = 64;                   // B rows: 3 digits x 16 tokens, the ones row, zeros
@@ -52,12 +63,11 @@ constexpr int kTcDigitRows = 64;                   // B rows: 3 digits x 16 toke
 struct Q8TcMat {
   const float* scale;
   const float* min;
-  int rows;
-  int rb_begin;           // first row tile of this matrix in the grid
+  int rows;               // a multiple of 128
+  int rb_begin;           // first row tile of this matrix in the launch's tile order
   const float* bias;      // [rows] or null
   const float* residual;  // [n_tokens][rows] or null (may alias y)
   float* y;               // [n_tokens][rows]
-  float* part;            // [splits][16][rows]: split partial sums
 };
 
 struct Q8TcArgs {
@@ -67,12 +77,45 @@ struct Q8TcArgs {
   const float* xsum;      // [16][cols / 64] sums of x per 64-column chunk
   const float* sx;        // [16][cols / 256] each token's largest |x| per 256-column block
   int n_tokens;           // <= 16
-  int splits;             // column ranges per row tile
-  int stages_per_split;   // even: a range holds whole 256-column blocks
-  unsigned* counters;     // [row tiles]: arrivals, zero between launches
+  int units;              // row tiles x 256-column blocks
+  float* part;            // [gridDim.x][2][16][128]: a CTA's partial first and last row tiles
+  unsigned* counters;     // [row tiles]: arrivals at a cut tile, zero between launches
   int* status;
   unsigned long long timeout_ns;
 };
+
+// CTA c's units start at c U / G; the CTA holding unit u is the last c whose
+// start is <= u.
+__device__ __forceinline__ int tc_unit_begin(int c, int units, int g) {
+  return (int)((long long)c * units / g);
+}
+__device__ __forceinline__ int tc_cta_of(int u, int units, int g) {
+  return (int)(((long long)(u + 1) * g - 1) / units);
+}
+__device__ __forceinline__ int tc_mat_of(const Q8TcArgs& a, int tile) {
+  int mi = 0;
+#pragma unroll
+  for (int j = 1; j < kTcMaxMats; ++j)
+    if (j < a.n_mats && tile >= a.m[j].rb_begin) mi = j;
+  return mi;
+}
+#define OOMATTN_TC_FIELD(a, mi, f) ((mi) == 0 ? (a).m[0].f : ((mi) == 1 ? (a).m[1].f : (a).m[2].f))
+
+__device__ __forceinline__ void cp_async4(void* dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+// An arrival at a cut tile: releases the writes the promoter barrier ordered
+// before it and acquires the other CTAs' released partial sums.
+__device__ __forceinline__ unsigned atom_add_acq_rel_gpu(unsigned* p, unsigned v) {
+  unsigned old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
 
 // kind::i8 instruction descriptor: s32 accumulate, A and B unsigned 8-bit,
 // both K-major, M = 128, N = 64.
@@ -98,71 +141,85 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                  const Q8TcArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kTcStages * kTcStageBytes);
+  float2* s_op = reinterpret_cast<float2*>(smem + kTcStages * kTcStageBytes);  // [kb][16]: (block sum, sx / 127)
+  float2* s_sm = reinterpret_cast<float2*>(smem + kTcStages * kTcStageBytes + kTcOpBytes);  // [kTcSmAhead][128]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kTcStages * kTcStageBytes + kTcOpBytes + kTcSmBytes);
   uint64_t* full = bars;                   // [kTcStages]: weights + digits of a stage landed
   uint64_t* empty = full + kTcStages;      // [kTcStages]: the stage's MMAs completed
-  uint64_t* d_full = empty + kTcStages;    // [2]: a block's D complete
-  uint64_t* d_empty = d_full + 2;          // [2]: the promoters have read D
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(d_empty + 2);
+  uint64_t* d_full = empty + kTcStages;    // [kTcDBufs]: a block's D complete
+  uint64_t* d_empty = d_full + kTcDBufs;   // [kTcDBufs]: the promoters have read D
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(d_empty + kTcDBufs);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int rb = blockIdx.x;
-  int mi = 0;
-#pragma unroll
-  for (int j = 1; j < kTcMaxMats; ++j)
-    if (j < a.n_mats && rb >= a.m[j].rb_begin) mi = j;
-  const CUtensorMap* wmap = mi == 0 ? &wmap0 : (mi == 1 ? &wmap1 : &wmap2);
-  const Q8TcMat& M = a.m[mi];
-  const int r0 = (rb - M.rb_begin) * kTcRows;
-  const int split = blockIdx.y;
-  const int n_stages_all = a.cols / kTcCols;
-  const int s_begin = split * a.stages_per_split;
-  const int n_st = max(0, min(n_stages_all - s_begin, a.stages_per_split));
-  const int n_blocks = n_st / 2;
-  const int kb_total = a.cols / 256;
+  const int kbt = a.cols / 256;  // 256-column blocks per row tile
+  const int u_begin = tc_unit_begin(blockIdx.x, a.units, gridDim.x);
+  const int n_blocks = tc_unit_begin(blockIdx.x + 1, a.units, gridDim.x) - u_begin;
+  const int n_st = 2 * n_blocks;
+  const int tile0 = u_begin / kbt, kb0 = u_begin - tile0 * kbt;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kTcStages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < kTcDBufs; ++b) {
       mbar_init(&d_full[b], 1);
       mbar_init(&d_empty[b], 4);
     }
     fence_mbar_init();
   }
   if (warp == 5) {
-    tmem_alloc(tmem_slot, 128);
+    tmem_alloc(tmem_slot, 64 * kTcDBufs);
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem = *tmem_slot;  // D buffers at columns 0 and 64
+  const uint32_t tmem = *tmem_slot;  // D buffer j at column 64 j
 
   if (warp == 4) {
     // ------------------------------------------------ TMA producer
     if (lane == 0) {
-      prefetch_tensormap(wmap);
+      prefetch_tensormap(&wmap0);
+      if (a.n_mats > 1) prefetch_tensormap(&wmap1);
+      if (a.n_mats > 2) prefetch_tensormap(&wmap2);
       prefetch_tensormap(&dmap);
+      // stage i: block i / 2 of the range, its (i % 2)-th 128 columns
+      int tile = tile0, kb = kb0, half = 0;
+      auto issue_w = [&](int s) {
+        const int mi = tc_mat_of(a, tile);
+        const CUtensorMap* wm = mi == 0 ? &wmap0 : (mi == 1 ? &wmap1 : &wmap2);
+        const int r0 = (tile - OOMATTN_TC_FIELD(a, mi, rb_begin)) * kTcRows;
+        tma_load_2d(smem + s * kTcStageBytes, wm, &full[s], kb * 256 + half * kTcCols, r0);
+      };
+      auto advance = [&]() {
+        half ^= 1;
+        if (!half && ++kb == kbt) {
+          kb = 0;
+          ++tile;
+        }
+      };
       // the first stages' weights go out before the digit split this kernel
       // depends on has finished (programmatic dependent launch)
       const int pre = min(n_st, kTcStages);
       for (int i = 0; i < pre; ++i) {
         mbar_arrive_expect_tx(&full[i], kTcStageBytes);
-        tma_load_2d(smem + i * kTcStageBytes, wmap, &full[i], (s_begin + i) * kTcCols, r0);
+        issue_w(i);
+        advance();
       }
       asm volatile("griddepcontrol.wait;" ::: "memory");
-      for (int i = 0; i < pre; ++i)
-        tma_load_2d(smem + i * kTcStageBytes + kTcWBytes, &dmap, &full[i], (s_begin + i) * kTcCols, 0);
+      for (int i = 0; i < pre; ++i) {
+        const int u = u_begin + (i >> 1), kbi = u % kbt;
+        tma_load_2d(smem + i * kTcStageBytes + kTcWBytes, &dmap, &full[i], kbi * 256 + (i & 1) * kTcCols, 0);
+      }
       int issued = pre;
       for (int i = pre; i < n_st; ++i) {
         const int s = i % kTcStages;
         if (!mbar_wait(&empty[s], ((i / kTcStages) - 1) & 1, a.status, a.timeout_ns)) break;
         mbar_arrive_expect_tx(&full[s], kTcStageBytes);
-        tma_load_2d(smem + s * kTcStageBytes, wmap, &full[s], (s_begin + i) * kTcCols, r0);
-        tma_load_2d(smem + s * kTcStageBytes + kTcWBytes, &dmap, &full[s], (s_begin + i) * kTcCols, 0);
+        issue_w(s);
+        tma_load_2d(smem + s * kTcStageBytes + kTcWBytes, &dmap, &full[s], kb * 256 + half * kTcCols, 0);
+        advance();
         issued = i + 1;
       }
       // drain: the last copies this lane issued land before the CTA can exit
@@ -178,118 +235,187 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       bool ok = true;
       for (int i = 0; i < n_st && ok; ++i) {
         const int s = i % kTcStages, b = i >> 1, first = (i & 1) == 0;
+        const int db = b % kTcDBufs;
         ok = mbar_wait(&full[s], (i / kTcStages) & 1, a.status, a.timeout_ns);
-        if (ok && first && b >= 2) ok = mbar_wait(&d_empty[b & 1], ((b >> 1) - 1) & 1, a.status, a.timeout_ns);
+        if (ok && first && b >= kTcDBufs)
+          ok = mbar_wait(&d_empty[db], ((b / kTcDBufs) - 1) & 1, a.status, a.timeout_ns);
         if (!ok) break;
         tc_fence_after();
-        const uint32_t d = tmem + 64 * (b & 1);
+        const uint32_t d = tmem + 64 * db;
         const uint32_t wa = dlo + (uint32_t)((s * kTcStageBytes) >> 4);
         const uint32_t xb = wa + (uint32_t)(kTcWBytes >> 4);
 #pragma unroll
         for (int kk = 0; kk < kTcCols / 32; ++kk)  // 32 columns (bytes) per k-step of the 128-byte row
           mma_i8_ss(d, wa + kk * 2, dhi, xb + kk * 2, dhi, idesc, (first && kk == 0) ? 0u : 1u);
         tc_commit(&empty[s]);
-        if (!first) tc_commit(&d_full[b & 1]);
+        if (!first) tc_commit(&d_full[db]);
       }
     }
   } else {
     // ------------------------------------------------ promoters (warps 0-3)
     const int r = warp * 32 + lane;  // weight row within the tile = TMEM lane
-    const int R = r0 + r;
     const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    asm volatile("griddepcontrol.wait;" ::: "memory");  // sx and xsum come from the digit split
+    // the next kernel may launch now; it waits for this grid before it
+    // touches anything this one reads or writes
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    // only the blocks of this CTA's range: kb0, kb0 + 1, ... (mod kbt)
+    const int n_kb = min(n_blocks, kbt);
+#pragma unroll 4
+    for (int i = threadIdx.x; i < n_kb * 16; i += 128) {
+      int kb = kb0 + (i >> 4);
+      if (kb >= kbt) kb -= kbt;
+      const int t = i & 15;
+      float2 v = make_float2(0.f, 0.f);
+      if (t < a.n_tokens) {
+        const float4 x4 = __ldg(reinterpret_cast<const float4*>(a.xsum + (size_t)t * (a.cols / 64) + 4 * kb));
+        v = make_float2((x4.x + x4.y) + (x4.z + x4.w), __ldg(a.sx + (size_t)t * kbt + kb) * (1.f / 127.f));
+      }
+      s_op[kb * 16 + t] = v;
+    }
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+    // this row's scale and min of block b go to ring slot b % kTcSmAhead, one
+    // cp.async group per block (empty past the range), kTcSmAhead - 1 blocks
+    // ahead of the block being promoted; each thread reads only what it copied
+    int p_tile = tile0, p_kb = kb0;
+    auto fetch = [&](int b) {
+      if (b < n_blocks) {
+        const int mi = tc_mat_of(a, p_tile);
+        const size_t blk = (size_t)((p_tile - OOMATTN_TC_FIELD(a, mi, rb_begin)) * kTcRows + r) * kbt + p_kb;
+        float2* dst = s_sm + (b % kTcSmAhead) * kTcRows + r;
+        cp_async4(&dst->x, OOMATTN_TC_FIELD(a, mi, scale) + blk);
+        cp_async4(&dst->y, OOMATTN_TC_FIELD(a, mi, min) + blk);
+        if (++p_kb == kbt) {
+          p_kb = 0;
+          ++p_tile;
+        }
+      }
+      cp_async_commit();
+    };
+#pragma unroll 1
+    for (int b = 0; b < kTcSmAhead - 1; ++b) fetch(b);
     float acc[16];
 #pragma unroll
     for (int t = 0; t < 16; ++t) acc[t] = 0.f;
-    asm volatile("griddepcontrol.wait;" ::: "memory");  // sx and xsum come from the digit split
+    __shared__ int s_last;
+    int tile = tile0, kb = kb0;
     bool ok = true;
-    for (int b = 0; b < n_blocks && ok; ++b) {
-      // this block's operands first: their latency overlaps the wait for D
-      const int kb = s_begin / 2 + b;
-      float sc = 0.f, mn = 0.f;
-      if (R < M.rows) {
-        const size_t blk = (size_t)R * kb_total + kb;
-        sc = __ldg(M.scale + blk);
-        mn = __ldg(M.min + blk);
-      }
-      float X[16], unit[16];  // block sums, sx / 127
-      const float* xs = a.xsum + 4 * kb;
-#pragma unroll
-      for (int t = 0; t < 16; ++t) {
-        if (t < a.n_tokens) {
-          const float4 x4 = __ldg(reinterpret_cast<const float4*>(xs + (size_t)t * (a.cols / 64)));
-          X[t] = (x4.x + x4.y) + (x4.z + x4.w);
-          unit[t] = __ldg(a.sx + (size_t)t * kb_total + kb) * (1.f / 127.f);
-        } else {
-          X[t] = 0.f;
-          unit[t] = 0.f;
-        }
-      }
-      ok = mbar_wait(&d_full[b & 1], (b >> 1) & 1, a.status, a.timeout_ns);
+    for (int b = 0; b < n_blocks; ++b) {
+      fetch(b + kTcSmAhead - 1);
+      cp_async_wait<kTcSmAhead - 1>();  // block b's group has landed
+      const float2 scmn = s_sm[(b % kTcSmAhead) * kTcRows + r];
+      const float sc = scmn.x, mn = scmn.y;
+      const int db = b % kTcDBufs;
+      ok = mbar_wait(&d_full[db], (b / kTcDBufs) & 1, a.status, a.timeout_ns);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc_fence_after();
       uint32_t dr[64];
-      OOMATTN_TMEM_LD32(tmem + lane_off + 64 * (b & 1), dr);
-      OOMATTN_TMEM_LD32(tmem + lane_off + 64 * (b & 1) + 32, (dr + 32));
+      OOMATTN_TMEM_LD32(tmem + lane_off + 64 * db, dr);
+      OOMATTN_TMEM_LD32(tmem + lane_off + 64 * db + 32, (dr + 32));
       tmem_wait_ld();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&d_empty[b & 1]);
+      if (lane == 0) mbar_arrive(&d_empty[db]);
+      const float4* op = reinterpret_cast<const float4*>(s_op + kb * 16);
       const int s128 = 128 * (int)dr[48];  // 128 x the sum of the block's q of this row
 #pragma unroll
-      for (int t = 0; t < 16; ++t) {
-        const float e0 = (float)((int)dr[t] - s128), e1 = (float)((int)dr[16 + t] - s128);
-        const float e2 = (float)((int)dr[32 + t] - s128);
-        const float dot = unit[t] * (e0 + (e1 * (1.f / 128.f) + e2 * (1.f / 16384.f)));
-        acc[t] = fmaf(sc, dot, fmaf(mn, X[t], acc[t]));
-      }
-    }
-    ok = __all_sync(0xffffffffu, ok);
-    // ------------------------------------------------ epilogue
-    if (ok && R < M.rows) {
-      if (a.splits == 1) {
+      for (int t2 = 0; t2 < 8; ++t2) {
+        const float4 xu = op[t2];  // (X, unit) of tokens 2 t2 and 2 t2 + 1
 #pragma unroll
-        for (int t = 0; t < 16; ++t) {
-          if (t < a.n_tokens) {
-            float v = acc[t];
-            if (M.bias) v += M.bias[R];
-            if (M.residual) v += M.residual[(size_t)t * M.rows + R];
-            M.y[(size_t)t * M.rows + R] = v;
+        for (int h = 0; h < 2; ++h) {
+          const int t = 2 * t2 + h;
+          const float X = h ? xu.z : xu.x, unit = h ? xu.w : xu.y;
+          const float e0 = (float)((int)dr[t] - s128), e1 = (float)((int)dr[16 + t] - s128);
+          const float e2 = (float)((int)dr[32 + t] - s128);
+          const float dot = unit * (e0 + (e1 * (1.f / 128.f) + e2 * (1.f / 16384.f)));
+          acc[t] = fmaf(sc, dot, fmaf(mn, X, acc[t]));
+        }
+      }
+      if (kb == kbt - 1 || b == n_blocks - 1) {
+        // ---------------------------------------------- the end of a row tile's segment
+        const int mi = tc_mat_of(a, tile);
+        const int rows = OOMATTN_TC_FIELD(a, mi, rows);
+        const int R = (tile - OOMATTN_TC_FIELD(a, mi, rb_begin)) * kTcRows + r;
+        const float* bias = OOMATTN_TC_FIELD(a, mi, bias);
+        const float* residual = OOMATTN_TC_FIELD(a, mi, residual);
+        float* y = OOMATTN_TC_FIELD(a, mi, y);
+        const int seg_kb0 = tile == tile0 ? kb0 : 0;
+        if (seg_kb0 == 0 && kb == kbt - 1) {
+#pragma unroll
+          for (int t = 0; t < 16; ++t) {
+            if (t < a.n_tokens) {
+              float v = acc[t];
+              if (bias) v += bias[R];
+              if (residual) v += residual[(size_t)t * rows + R];
+              y[(size_t)t * rows + R] = v;
+            }
+          }
+        } else {
+          float* pp = a.part + ((size_t)blockIdx.x * 2 + (tile == tile0 ? 0 : 1)) * 16 * kTcRows;
+#pragma unroll
+          for (int t = 0; t < 16; ++t)
+            if (t < a.n_tokens) pp[t * kTcRows + r] = acc[t];
+          const int c_lo = tc_cta_of(tile * kbt, a.units, gridDim.x);
+          const int c_hi = tc_cta_of(tile * kbt + kbt - 1, a.units, gridDim.x);
+          asm volatile("bar.sync 1, 128;" ::: "memory");
+          if (r == 0) s_last = atom_add_acq_rel_gpu(&a.counters[tile], 1u) == (unsigned)(c_hi - c_lo);
+          asm volatile("bar.sync 1, 128;" ::: "memory");
+          if (s_last) {
+            // the last CTA of the tile adds its segments in column order;
+            // two segments' 16 token sums are loaded together, this CTA's
+            // own taken from its registers
+            auto seg = [&](int c, float* p) {
+              if (c > c_hi) {
+#pragma unroll
+                for (int t = 0; t < 16; ++t) p[t] = 0.f;
+              } else if (c == (int)blockIdx.x) {
+#pragma unroll
+                for (int t = 0; t < 16; ++t) p[t] = acc[t];
+              } else {
+                const int slot = tc_unit_begin(c, a.units, gridDim.x) >= tile * kbt ? 0 : 1;
+                const float* pc = a.part + ((size_t)c * 2 + slot) * 16 * kTcRows + r;
+#pragma unroll
+                for (int t = 0; t < 16; ++t) p[t] = t < a.n_tokens ? __ldcg(pc + t * kTcRows) : 0.f;
+              }
+            };
+            float v[16];
+#pragma unroll
+            for (int t = 0; t < 16; ++t) v[t] = 0.f;
+            for (int c = c_lo; c <= c_hi; c += 2) {
+              float p0[16], p1[16];
+              seg(c, p0);
+              seg(c + 1, p1);
+#pragma unroll
+              for (int t = 0; t < 16; ++t) v[t] = (v[t] + p0[t]) + p1[t];
+            }
+#pragma unroll
+            for (int t = 0; t < 16; ++t) {
+              if (t < a.n_tokens) {
+                float o = v[t];
+                if (bias) o += bias[R];
+                if (residual) o += residual[(size_t)t * rows + R];
+                y[(size_t)t * rows + R] = o;
+              }
+            }
+            if (r == 0) a.counters[tile] = 0u;
           }
         }
-      } else {
 #pragma unroll
-        for (int t = 0; t < 16; ++t)
-          if (t < a.n_tokens) M.part[((size_t)split * 16 + t) * M.rows + R] = acc[t];
+        for (int t = 0; t < 16; ++t) acc[t] = 0.f;
+      }
+      if (++kb == kbt) {
+        kb = 0;
+        ++tile;
       }
     }
-    if (a.splits > 1) {
-      // the last CTA of this row tile adds the splits in order
-      __shared__ int s_last;
-      __threadfence();
-      asm volatile("bar.sync 1, 128;" ::: "memory");
-      if (r == 0) s_last = atomicAdd(&a.counters[rb], 1u) == (unsigned)(a.splits - 1);
-      asm volatile("bar.sync 1, 128;" ::: "memory");
-      if (s_last) {
-        __threadfence();
-        if (R < M.rows) {
-          for (int t = 0; t < a.n_tokens; ++t) {
-            float v = 0.f;
-            for (int sp = 0; sp < a.splits; ++sp) v += __ldcg(M.part + ((size_t)sp * 16 + t) * M.rows + R);
-            if (M.bias) v += M.bias[R];
-            if (M.residual) v += M.residual[(size_t)t * M.rows + R];
-            M.y[(size_t)t * M.rows + R] = v;
-          }
-        }
-        if (r == 0) a.counters[rb] = 0u;
-      }
-    }
+    cp_async_wait<0>();  // no copy into this CTA's shared memory outlives it
   }
   tc_fence_before();
   __syncthreads();
   if (warp == 5) {
     tc_fence_after();
-    tmem_dealloc(tmem, 128);
+    tmem_dealloc(tmem, 64 * kTcDBufs);
   }
 }
 
@@ -309,6 +435,10 @@ __global__ void __launch_bounds__(256) q8_digits_kernel(const float* __restrict_
                                                         int cols, uint8_t* __restrict__ digits,
                                                         float* __restrict__ xsum, float* __restrict__ sx,
                                                         int* status) {
+  // launched as a programmatic dependent of the kernel before it: x, and the
+  // digit buffers the previous pass may still read, are touched only after it
+  // ends; then the tensor-core pass may launch (one kernel of lookahead)
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   __shared__ float red[8];
   const int t = blockIdx.x;

@@ -135,7 +135,10 @@ __device__ __forceinline__ void add_bias8(float* x, const float* b) {
 template <bool IN_BF16, bool Q_BF16, bool KV_BF16>
 __global__ void __launch_bounds__(256)
     rope_append_kernel(const AppendArgs ap, const KVPool pool, const __grid_constant__ SeqBatch sb, int T) {
-  // the decode that follows may launch now: it waits for this grid before reading
+  // launched as a programmatic dependent of the kernel before it (the QKV
+  // projection): q/k/v and the cache are touched only after that kernel ends;
+  // then the decode that follows may launch (it waits for this grid before reading)
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int hq = ap.n_heads, hkv = pool.n_kv;
   const int units_tok = (hq + 2 * hkv) * 8;
