@@ -570,6 +570,7 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(const float* __re
   const int t = blockIdx.x;
   const float* xr = x + (size_t)t * hidden;
   float s = 0.f;
+#pragma unroll 4  // the loads go out together; the sum keeps its order
   for (int i = threadIdx.x * 4; i < hidden; i += kNormThreads * 4) {
     const float4 v = *reinterpret_cast<const float4*>(xr + i);
     s += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
@@ -605,6 +606,7 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_prep_x_kernel(const floa
   const int t = blockIdx.x;
   const float* xr = x + (size_t)t * cols;
   float s = 0.f;
+#pragma unroll 4  // the loads go out together; the sum keeps its order
   for (int i = threadIdx.x * 4; i < cols; i += kNormThreads * 4) {
     const float4 v = *reinterpret_cast<const float4*>(xr + i);
     s += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;

@@ -465,6 +465,7 @@ __global__ void __launch_bounds__(256) q8_digits_kernel(const float* __restrict_
   if (norm_w) {
     // the sum of squares exactly as rmsnorm_kernel forms it (every CTA of the token forms it)
     float s = 0.f;
+#pragma unroll 4  // the loads go out together; the sum keeps its order
     for (int i = tid * 4; i < cols; i += 256 * 4) {
       const float4 v = *reinterpret_cast<const float4*>(xr + i);
       s += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
