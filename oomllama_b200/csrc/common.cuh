@@ -85,6 +85,17 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* s
   }
 }
 
+// An arrival at a counter shared by CTAs that merge partial results: one
+// thread's acquire-release add after a barrier of the threads that wrote their
+// partials releases those writes (the barrier orders them before it) and
+// acquires the partials the earlier arrivals released, so neither side needs
+// a fence in every thread.
+__device__ __forceinline__ unsigned atom_add_acq_rel_gpu(unsigned* p, unsigned v) {
+  unsigned old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+
 // ---------------------------------------------------------------- TMA loads
 // 2D tiled bulk-tensor load into this CTA's shared memory, completing on `bar`.
 // x is the innermost coordinate; callers keep x * element size a multiple of

@@ -93,15 +93,13 @@ __device__ __forceinline__ void combine_and_store(const MergeSmem& ms, const Dec
     }
   }
   if (nsplit == 1) return;
-  __threadfence();
   consumer_bar();
   if (tid == 0) {
-    const unsigned prev = atomicAdd(&a.counters[(size_t)z * n_kv + g], 1u);
+    const unsigned prev = atom_add_acq_rel_gpu(&a.counters[(size_t)z * n_kv + g], 1u);
     *s_last = (prev == (unsigned)(nsplit - 1));
   }
   consumer_bar();
   if (!*s_last) return;
-  __threadfence();
   // every (q head, split) lse in one round of loads, staged over the per-warp
   // O area (its last reader passed the barriers above); then each thread's
   // partial O loads run eight splits ahead

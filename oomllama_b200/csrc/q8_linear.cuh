@@ -388,15 +388,13 @@ __global__ void __launch_bounds__(kQ8Warps * 32, 2) q8_linear_kernel(const Q8Arg
   }
   if (a.splits == 1) return;
   // split-K merge: the last CTA of this row block sums the splits in order
-  __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) {
-    const unsigned prev = atomicAdd(&args.counters[blockIdx.y], 1u);
+    const unsigned prev = atom_add_acq_rel_gpu(&args.counters[blockIdx.y], 1u);
     s_last = (prev == (unsigned)a.splits - 1);
   }
   __syncthreads();
   if (!s_last) return;
-  __threadfence();
   for (int i = threadIdx.x; i < rows_cta * a.n_tokens; i += blockDim.x) {
     const int tok = i / rows_cta, row = row0 + i % rows_cta;
     if (row >= a.rows) continue;
@@ -538,15 +536,13 @@ __global__ void __launch_bounds__(kQ8XsWarps * 32, 1) q8_linear_xs_kernel(const 
       }
   if (a.splits == 1) return;
   // the last CTA of this row group sums the ranges in order
-  __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) {
-    const unsigned prev = atomicAdd(&args.counters[blockIdx.y], 1u);
+    const unsigned prev = atom_add_acq_rel_gpu(&args.counters[blockIdx.y], 1u);
     s_last = (prev == (unsigned)a.splits - 1);
   }
   __syncthreads();
   if (!s_last) return;
-  __threadfence();
   const int rg0 = a.rb * rows_cta;
   for (int i = threadIdx.x; i < rows_cta * a.n_tokens; i += blockDim.x) {
     const int tok = i / rows_cta, row = rg0 + i % rows_cta;

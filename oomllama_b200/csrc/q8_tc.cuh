@@ -109,13 +109,6 @@ template <int N>
 __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
-// An arrival at a cut tile: releases the writes the promoter barrier ordered
-// before it and acquires the other CTAs' released partial sums.
-__device__ __forceinline__ unsigned atom_add_acq_rel_gpu(unsigned* p, unsigned v) {
-  unsigned old;
-  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
-  return old;
-}
 
 // kind::i8 instruction descriptor: s32 accumulate, A and B unsigned 8-bit,
 // both K-major, M = 128, N = 64.
