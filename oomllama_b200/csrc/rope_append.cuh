@@ -221,6 +221,14 @@ __global__ void f32_to_bf16_kernel(const float* __restrict__ x, uint16_t* __rest
     y[i] = f32_to_bf16_bits(x[i]);
 }
 
+#ifndef OOMATTN_GEMV_PRE
+#define OOMATTN_GEMV_PRE 12
+#endif
+// f32 weight chunks (of 128 columns per warp) each lane loads before the wait:
+// C1 step 26.7 us with none, 22.7 with 8, 20.9 with 10, 20.1 with 12, 27.2 with
+// 14 and 25.8 with 16 (the registers then cut the resident CTAs)
+constexpr int kGemvPre = OOMATTN_GEMV_PRE;
+
 template <int T, bool WBF16>
 __global__ void __launch_bounds__(256)
     qkv_gemv_rope_append_kernel(const GemvArgs ga, const KVPool pool, const __grid_constant__ SeqBatch sb) {
@@ -249,9 +257,24 @@ __global__ void __launch_bounds__(256)
   }
   // Launched as a programmatic dependent of the kernel before it (in a token
   // loop, the previous layer's decode), so its launch overlaps that kernel's
-  // tail; it waits for it before it reads x or writes q and the cache.
-  // Pulling the weight rows into L2 before the wait was slower (C1 step 29.9
-  // against 26.7 us for all rows, 26.8 for the first 4 KB of each row).
+  // tail; it waits for it before it reads x or writes q and the cache.  The
+  // weights do not depend on that kernel: with f32 weights each lane's first
+  // kGemvPre chunks of both rows are loaded into registers before the wait
+  // (C1 step 20.1 against 26.7 us).  Pulling the rows into L2 instead was
+  // slower (29.9 us for all rows, 26.8 for the first 4 KB of each row).
+  float4 pa[WBF16 ? 1 : kGemvPre], pb[WBF16 ? 1 : kGemvPre];
+  if (!WBF16) {
+    const float* wp0 = reinterpret_cast<const float*>(W) + wrow[0];
+    const float* wp1 = reinterpret_cast<const float*>(W) + wrow[1];
+#pragma unroll
+    for (int u = 0; u < kGemvPre; ++u) {
+      const int j = lane * 4 + u * 128;
+      if (j < H) {
+        pa[u] = __ldcs(reinterpret_cast<const float4*>(wp0 + j));
+        pb[u] = __ldcs(reinterpret_cast<const float4*>(wp1 + j));
+      }
+    }
+  }
   asm volatile("griddepcontrol.wait;" ::: "memory");
   float acc[2][T];
 #pragma unroll
@@ -282,8 +305,21 @@ __global__ void __launch_bounds__(256)
   } else {
     const float* wp0 = reinterpret_cast<const float*>(W) + wrow[0];
     const float* wp1 = reinterpret_cast<const float*>(W) + wrow[1];
+    // the preloaded chunks first, then the rest in the same column order
+#pragma unroll
+    for (int u = 0; u < kGemvPre; ++u) {
+      const int j = lane * 4 + u * 128;
+      if (j < H) {
+#pragma unroll
+        for (int t = 0; t < T; ++t) {
+          const float4 x = __ldg(reinterpret_cast<const float4*>(ga.x + (size_t)t * H + j));
+          acc[0][t] += x.x * pa[u].x + x.y * pa[u].y + x.z * pa[u].z + x.w * pa[u].w;
+          acc[1][t] += x.x * pb[u].x + x.y * pb[u].y + x.z * pb[u].z + x.w * pb[u].w;
+        }
+      }
+    }
 #pragma unroll 8
-    for (int j = lane * 4; j < H; j += 128) {  // 16 loads of 16 bytes in flight per lane
+    for (int j = lane * 4 + kGemvPre * 128; j < H; j += 128) {  // 16 loads of 16 bytes in flight per lane
       const float4 wa = __ldcs(reinterpret_cast<const float4*>(wp0 + j));
       const float4 wb = __ldcs(reinterpret_cast<const float4*>(wp1 + j));
 #pragma unroll
