@@ -1784,7 +1784,9 @@ Q8Plan plan_q8(const oomattn_ctx* ctx, int rows, int cols, int nt) {
   return p;
 }
 
-// The form with x staged in shared memory (q8_linear_xs_kernel): for matrices
+// The form with x staged in shared memory (q8_linear_xs_kernel), for passes
+// the tensor-core form below does not take (with cols % 256 and rows % 128 it
+// takes 9-16 tokens, and any count on a wave of row tiles): for matrices
 // of at least 32 M weights, one CTA per SM over a row group of 256 * MT rows
 // and a column range of 8 to 96 / NT chunks.  MT and the ranges minimise
 // waves x (MT x chunks per range + kQ8XsFixed), a fixed cost for staging x,
