@@ -54,9 +54,9 @@ def test_q8_mlp_with_residual(oracle, T, H, inter):
     eng.close()
 
 
-def _layer_case(oracle, kv_dtype, variant, theta, lens, seed):
+def _layer_case(oracle, kv_dtype, variant, theta, lens, seed, hq=2, hkv=1, inter=512):
     from oomllama_b200 import Q8DecoderLayer
-    hq, hkv, D, inter, eps = 2, 1, 128, 512, 1e-6
+    D, eps = 128, 1e-6
     H = hq * D
     B = len(lens)
     rng = np.random.default_rng(seed)
@@ -100,3 +100,14 @@ def test_decoder_layer_q8_f32_cache(oracle):
 def test_decoder_layer_q8_bf16_cache_split_half(oracle):
     out, ref, _ = _layer_case(oracle, "bf16", "split_half", 5e5, [1, 33, 200, 64], seed=4)
     assert_close(out, ref, BF16_ATOL * max(1.0, np.abs(ref).max()), BF16_RTOL, what="decoder layer bf16 KV")
+
+
+def test_decoder_layer_q8_qkv_on_tensor_cores(oracle):
+    # 40 q / 8 kv heads over hidden 5120 for 12 sequences: q, k and v (36.7 M weights) run as ONE
+    # tensor-core pass over the three matrices (their row tiles in one persistent grid, tiles cut
+    # between CTAs merged in order) with the RMSNorm folded into the digit split and the biases in
+    # the epilogue; against the composed oracle
+    lens = [3, 40, 77, 16, 100, 5, 9, 64, 31, 2, 18, 50]
+    out, ref, lens_after = _layer_case(oracle, "bf16", "interleaved", 1e6, lens, seed=6, hq=40, hkv=8, inter=512)
+    assert lens_after == [L + 1 for L in lens]
+    assert_close(out, ref, BF16_ATOL * max(1.0, np.abs(ref).max()), BF16_RTOL, what="decoder layer, q/k/v on tcgen05")

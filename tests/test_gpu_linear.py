@@ -95,9 +95,10 @@ def test_q8_mlp_tensor_core_form(oracle, eng):
 
 @pytest.mark.parametrize("T,rows,cols", [(16, 8192, 4096), (9, 8192, 4096), (12, 512, 65536)])
 def test_q8_linear_tensor_core_decode_form(oracle, eng, T, rows, cols):
-    # 9-16 tokens on a matrix of at least 32 M weights: the tcgen05 pass (weights converted into TMEM,
-    # x hi/lo as a 32-row B operand); 512 x 65536 has 4 row tiles, so its columns split into ranges
-    # whose partial sums the last CTA of a row tile adds in order; bias and residual in the epilogue
+    # 9-16 tokens on a matrix of at least 32 M weights: the integer tensor-core pass (weight bytes as
+    # stored x base-128 digits of x, tcgen05 kind::i8); the persistent grid's equal unit ranges cut
+    # row tiles between CTAs (512 x 65536: each of the 4 row tiles among ~37 CTAs), whose partial
+    # sums the last CTA to arrive adds in order; the bias in the epilogue; repeatable bit for bit
     wq, wd = _q8(oracle, rows, cols, seed=T + rows)
     rng = np.random.default_rng(T + 7)
     x = rng.standard_normal((T, cols)).astype(np.float32)
