@@ -58,7 +58,7 @@ enum { OOMATTN_DTYPE_F32 = 0, OOMATTN_DTYPE_BF16 = 1 };
  * natural-log LSE at 128, 3 floats of padding (16-byte aligned rows). */
 #define OOMATTN_PACKED_STRIDE 132
 /* Test-only flags (oomattn_set_test_flags). */
-enum { OOMATTN_TEST_DROP_DECODE_COPIES = 1 };
+enum { OOMATTN_TEST_DROP_DECODE_COPIES = 1, OOMATTN_TEST_DROP_LINEAR_COPIES = 2 };
 /* RoPE pairing: split-half pairs (x[i], x[i+64]) -- apply_rope_llama,
  * src/oomllama_turbo.rs:443-467, and TurboEngine::apply_rope :737-786;
  * interleaved pairs (x[2i], x[2i+1]) -- apply_rope, :402-438. */
@@ -107,8 +107,10 @@ int oomattn_set_wait_limit(oomattn_ctx* ctx, uint64_t timeout_ns);
 
 /* Test-only launch flags, 0 in normal use.  OOMATTN_TEST_DROP_DECODE_COPIES
  * makes the bf16 decode's copy producer issue nothing, so that its consumers'
- * bounded waits run out: a test of the timeout path that faults nothing.  No
- * counterpart in the reference. */
+ * bounded waits run out: a test of the timeout path that faults nothing.
+ * OOMATTN_TEST_DROP_LINEAR_COPIES does the same for the Q8 tensor-core pass
+ * (its MMA issuer's and promoters' waits run out).  No counterpart in the
+ * reference. */
 int oomattn_set_test_flags(oomattn_ctx* ctx, int32_t flags);
 
 /* TurboEngine::reset / ModelKVCache::clear (src/oomllama_turbo.rs:95-99,

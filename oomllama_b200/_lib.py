@@ -19,6 +19,7 @@ STATUS_NAMES = {
 DTYPE_F32, DTYPE_BF16 = 0, 1
 PACKED_STRIDE = 132                 # floats per (row, q head) of a packed decode output: O[128], lse, pad
 TEST_DROP_DECODE_COPIES = 1         # oomattn_set_test_flags: the bf16 decode's producer issues no copies
+TEST_DROP_LINEAR_COPIES = 2         # oomattn_set_test_flags: the Q8 tensor-core pass's producer issues no copies
 ROPE_SPLIT_HALF, ROPE_INTERLEAVED = 0, 1
 
 # Every exported symbol of include/oomattn.h.

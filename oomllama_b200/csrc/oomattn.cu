@@ -1232,7 +1232,7 @@ int oomattn_set_wait_limit(oomattn_ctx* ctx, uint64_t timeout_ns) {
 }
 
 int oomattn_set_test_flags(oomattn_ctx* ctx, int32_t flags) {
-  if (!ctx || (flags & ~OOMATTN_TEST_DROP_DECODE_COPIES))
+  if (!ctx || (flags & ~(OOMATTN_TEST_DROP_DECODE_COPIES | OOMATTN_TEST_DROP_LINEAR_COPIES)))
     return fail(ctx, OOMATTN_ERR_INVALID_ARG, "unknown test flags %d", flags);
   ctx->test_flags = flags;
   return OOMATTN_OK;
@@ -1896,6 +1896,7 @@ int launch_q8_tc(oomattn_ctx* ctx, const Q8Job* jobs, int n_jobs, int cols, int 
   a.counters = ctx->d_q8_counters;
   a.status = ctx->d_status;
   a.timeout_ns = ctx->timeout_ns;
+  a.test_flags = ctx->test_flags;
   int tiles = 0;
   for (int j = 0; j < n_jobs; ++j) {
     const oomattn_q8_matrix* w = jobs[j].w;

@@ -39,6 +39,7 @@ struct KVPool {
 // Test-only launch flags of the decode kernel (DecodeArgs::test_flags).
 enum : int {
   kTestDropDecodeCopies = 1,  // the bf16 producer issues no copies: every consumer wait runs out its limit
+  kTestDropLinearCopies = 2,  // the Q8 tensor-core pass's producer issues no copies: its MMA and promoter waits run out
 };
 
 struct DecodeArgs {

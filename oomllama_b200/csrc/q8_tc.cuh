@@ -82,6 +82,7 @@ struct Q8TcArgs {
   unsigned* counters;     // [row tiles]: arrivals at a cut tile, zero between launches
   int* status;
   unsigned long long timeout_ns;
+  int test_flags;         // 0 outside tests
 };
 
 // CTA c's units start at c U / G; the CTA holding unit u is the last c whose
@@ -172,7 +173,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
   if (warp == 4) {
     // ------------------------------------------------ TMA producer
-    if (lane == 0) {
+    // (kTestDropLinearCopies: a test makes the MMA issuer's and promoters'
+    // bounded waits run out by issuing nothing; they record kDevErrTimeout.)
+    if (lane == 0 && !(a.test_flags & kTestDropLinearCopies)) {
       prefetch_tensormap(&wmap0);
       if (a.n_mats > 1) prefetch_tensormap(&wmap1);
       if (a.n_mats > 2) prefetch_tensormap(&wmap2);

@@ -162,7 +162,7 @@ class TurboEngine:
         check(self._ctx, self._L.oomattn_set_wait_limit(self._ctx, int(timeout_ns)))
 
     def set_test_flags(self, flags: int):
-        """Test-only launch flags (_lib.TEST_DROP_DECODE_COPIES); 0 in normal use."""
+        """Test-only launch flags (_lib.TEST_DROP_DECODE_COPIES, _lib.TEST_DROP_LINEAR_COPIES); 0 in normal use."""
         check(self._ctx, self._L.oomattn_set_test_flags(self._ctx, int(flags)))
 
     def reset(self):

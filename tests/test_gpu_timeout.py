@@ -4,7 +4,8 @@ A test-only launch flag makes the bf16 decode's copy producer issue nothing, so 
 mbarrier wait runs out its limit (set to 1 ms here): the kernel records the timeout bit and returns,
 oomattn_sync reports OOMATTN_ERR_TIMEOUT, and the same context then decodes correctly.  Nothing
 faults or hangs: the waits are the kernel's own bounded ones.  The reference has no device waits
-(its only failure handling is a CPU fallback, src/oomllama.rs:702-719)."""
+(its only failure handling is a CPU fallback, src/oomllama.rs:702-719).  A second flag does the same
+for the Q8 tensor-core pass."""
 import numpy as np
 import pytest
 import torch
@@ -41,6 +42,40 @@ def test_decode_wait_runs_out_then_context_recovers(oracle):
         for s in range(3):
             ref = oracle.gqa_attention(as_f32_np(q[s:s + 1].cpu()), ks[s], vs[s], causal=False)[0]
             assert_close(out[s], ref, BF16_ATOL, BF16_RTOL, what=f"row {s} after the timeout")
+    eng.close()
+
+
+def test_q8_tensor_core_wait_runs_out_then_context_recovers():
+    # the same for the Q8 tensor-core pass (16 tokens over 8192 x 4096): with its producer silent,
+    # the MMA issuer's and promoters' waits run out, no cut tile is counted, and the next pass on the
+    # same context is correct (against float64) and repeatable
+    from oomllama_b200 import Q8Matrix
+    from oomllama_b200._lib import TEST_DROP_LINEAR_COPIES, OomAttnError
+    eng = make_engine(8, 1, [16])
+    g = torch.Generator(device="cuda").manual_seed(3)
+    rows, cols, T = 8192, 4096, 16
+    nb = rows * cols // 256
+    w = Q8Matrix(torch.randint(0, 256, (rows * cols,), dtype=torch.uint8, device="cuda", generator=g),
+                 torch.rand(nb, device="cuda", generator=g) * 2e-4,
+                 -torch.rand(nb, device="cuda", generator=g) * 0.02, rows, cols)
+    x = torch.randn(T, cols, device="cuda", generator=g)
+    eng.sync()
+    eng.set_wait_limit(1_000_000)  # 1 ms
+    eng.set_test_flags(TEST_DROP_LINEAR_COPIES)
+    eng.q8_linear(w, x)
+    with pytest.raises(OomAttnError) as e:
+        eng.sync()
+    assert e.value.code == 6, str(e.value)  # OOMATTN_ERR_TIMEOUT
+    eng.set_test_flags(0)
+    eng.set_wait_limit(2_000_000_000)
+    y1 = eng.q8_linear(w, x)
+    y2 = eng.q8_linear(w, x)
+    eng.sync()
+    q = w.q.view(rows, cols).double()
+    wd = w.min.double().repeat_interleave(256).view(rows, cols) + q * w.scale.double().repeat_interleave(256).view(rows, cols)
+    ref = (x.double() @ wd.T).cpu().numpy()
+    assert_close(y1.cpu().numpy(), ref, 1e-4 * max(1.0, float(np.abs(ref).max())), what="q8 pass after the timeout")
+    assert torch.equal(y1, y2)
     eng.close()
 
 
