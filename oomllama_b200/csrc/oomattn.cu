@@ -638,7 +638,7 @@ int plan_decode(const SeqBatch& sb, int n_kv, int slots, int max_splits, int fil
 int launch_decode_rows(oomattn_ctx* ctx, int layer, const SeqBatch& sb, const float* q, float* out, float* lse,
                        int o_stride, int lse_stride) {
   const int n_kv = ctx->cfg.n_kv_heads;
-  const int slots = ctx->num_sms * (ctx->cfg.kv_dtype == OOMATTN_DTYPE_BF16 ? 2 : 3);
+  const int slots = ctx->num_sms * (ctx->cfg.kv_dtype == OOMATTN_DTYPE_BF16 ? kDecCtasPerSm : 3);
   int key[kMaxBatch + 1];
   key[0] = sb.n;
   for (int z = 0; z < sb.n; ++z) key[z + 1] = sb.len[z] > 0 ? (sb.len[z] + kPageSize - 1) / kPageSize : 0;
@@ -1556,7 +1556,7 @@ extern "C" int oomattn_decode_static_scratch(int device, void* stream, int32_t k
   // partial fits the static array: nsplit <= slots / (rows * heads).
   const int cap_splits = std::max(1, std::min(split_cap(kv_dtype), kStaticPartSlots / (n_rows * n_heads)));
   DecodeSched sched;
-  const int n_items = plan_decode(sb, n_kv_heads, num_sms * (kv_dtype == OOMATTN_DTYPE_BF16 ? 2 : 3), cap_splits,
+  const int n_items = plan_decode(sb, n_kv_heads, num_sms * (kv_dtype == OOMATTN_DTYPE_BF16 ? kDecCtasPerSm : 3), cap_splits,
                                   kv_dtype == OOMATTN_DTYPE_BF16 ? kDecodeFillPages : kDecodeFillPagesF32, sched);
   if (n_items == 0) return OOMATTN_OK;
 
