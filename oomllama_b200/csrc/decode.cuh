@@ -38,7 +38,7 @@ constexpr int kDecStages = 2;
 constexpr int kDecCtasPerSm = 3;
 constexpr int kChunkBytes = kPageSize * kHeadDim * 2;           // one (page, kv head) bf16 chunk: 4 KB
 constexpr int kDecStageBytes = 2 * kDecWarps * kChunkBytes;     // K and V of 4 pages: 32 KB
-constexpr int kDecSmemBytes = kDecStages * kDecStageBytes + 1024 + 2 * kDecStages * 8 + 64;
+constexpr int kDecSmemBytes = kDecStages * kDecStageBytes + 1024 + 2 * kDecStages * 8 + 64 + kMaxGroup * 32 * 4;
 
 constexpr int kF32Tok = 4;                 // f32 path: tokens loaded and scored together
 constexpr int kMergeStride = kHeadDim + 4;  // padded row of the per-warp O staging area
@@ -50,16 +50,106 @@ struct MergeSmem {
 
 __device__ __forceinline__ void consumer_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
+// The last CTA's merge when it has a shared-memory area to stage into (the
+// bf16 kernel's page ring, free by then): every (q head, split) partial O row
+// of the (row, kv head) is copied in by cp.async (one warp per row, one lane
+// per 16 bytes, no index division; chunks of cs splits when they do not all
+// fit).  While the copies fly, the 16 threads of each q head load its split
+// lse values (two each), reduce the maximum by shuffles and write each
+// split's weight 2^(lse - M) once to shared memory; the unrolled sums then
+// read only shared memory.  A thread's dims are 4t..4t+3 and 64+4t..64+4t+3,
+// so a quarter-warp's 16-byte reads are consecutive.  Against loading the
+// partials eight splits ahead into registers with every thread computing
+// every weight, the last CTA's merge (globaltimer stamps) takes 1.8-2.4 us
+// instead of 2.2-4 us at 6-32 splits; the decode of a 16-row, 67 MB layer
+// 18.3 -> 16.6 us.  The sums still run in split order, so the result is the
+// same to the bit.
+__device__ __forceinline__ void merge_splits_staged(const DecodeArgs& a, int z, int g, int nsplit, int tid,
+                                                    float* stage, int stage_floats, float* s_w) {
+  const int j = tid >> 4, da = (tid & 15) * 4, db = da + kHeadDim / 2;
+  const int warp = tid >> 5, lane = tid & 31;
+  const bool active = j < a.group;
+  const size_t head0 = (size_t)z * a.n_heads + (size_t)g * a.group;
+  const int cs = max(1, min(nsplit, stage_floats / (a.group * kHeadDim)));
+  // the 16 threads of a q head (a half-warp) hold its split lse values, two
+  // each (splits t and t + 16)
+  static_assert(kMaxSplitsBf16 <= 32, "two split weights per thread of a half-warp");
+  const int t = tid & 15;
+  float w0 = -INFINITY, w1 = -INFINITY;
+  if (active) {
+    const float* lrow = a.part_lse + (head0 + j) * a.max_splits;
+    if (t < nsplit) w0 = __ldcg(lrow + t);
+    if (t + 16 < nsplit) w1 = __ldcg(lrow + t + 16);
+  }
+  auto issue = [&](int s0) {
+    const int n = min(cs, nsplit - s0);
+    for (int jj = 0; jj < a.group; ++jj) {
+      const float* src = a.part_o + ((head0 + jj) * a.max_splits + s0) * kHeadDim + lane * 4;
+      float* dst = stage + (size_t)jj * cs * kHeadDim + lane * 4;
+      for (int s = warp; s < n; s += kDecWarps) cp_async16_cg(dst + s * kHeadDim, src + (size_t)s * kHeadDim);
+    }
+    cp_async_commit();
+  };
+  issue(0);
+  float M = fmaxf(w0, w1);
+#pragma unroll
+  for (int off = 8; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+  // the weights go to shared memory once, for the half-warp's unrolled sums
+  float* w_j = s_w + (active ? j : 0) * 32;
+  if (active) {
+    w_j[t] = (w0 == -INFINITY) ? 0.f : exp2f(w0 - M);
+    w_j[t + 16] = (w1 == -INFINITY) ? 0.f : exp2f(w1 - M);
+  }
+  __syncwarp();
+  float wsum = 0.f, acc[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+  for (int s0 = 0; s0 < nsplit; s0 += cs) {
+    if (s0 > 0) {
+      consumer_bar();  // every thread is done with the previous chunk
+      issue(s0);
+    }
+    cp_async_wait<0>();
+    consumer_bar();
+    if (active) {
+      const int n = min(cs, nsplit - s0);
+      const float* st = stage + (size_t)j * cs * kHeadDim;
+#pragma unroll 8
+      for (int s = 0; s < n; ++s) {
+        const float wt = w_j[s0 + s];
+        wsum += wt;
+        const float4 u = *reinterpret_cast<const float4*>(st + s * kHeadDim + da);
+        const float4 v = *reinterpret_cast<const float4*>(st + s * kHeadDim + db);
+        acc[0] += wt * u.x; acc[1] += wt * u.y; acc[2] += wt * u.z; acc[3] += wt * u.w;
+        acc[4] += wt * v.x; acc[5] += wt * v.y; acc[6] += wt * v.z; acc[7] += wt * v.w;
+      }
+    }
+  }
+  if (active) {
+    const int h = g * a.group + j;
+    const float inv = 1.f / wsum;
+    float* orow = a.out + ((size_t)z * a.n_heads + h) * a.o_stride;
+    *reinterpret_cast<float4*>(orow + da) = make_float4(acc[0] * inv, acc[1] * inv, acc[2] * inv, acc[3] * inv);
+    *reinterpret_cast<float4*>(orow + db) = make_float4(acc[4] * inv, acc[5] * inv, acc[6] * inv, acc[7] * inv);
+    if (a.lse && (tid & 15) == 0)
+      a.lse[((size_t)z * a.n_heads + h) * a.lse_stride] = (M + log2f(wsum)) * 0.69314718055994531f;
+  }
+}
+
 // Combine the four warps' (m, l, O) of this CTA, then either write the final
 // row (single split) or this split's normalised partial; the last CTA of the
 // (row, kv head) to finish merges all partials:
 //   M = max lse_s ; O = sum 2^(lse_s - M) O_s / sum 2^(lse_s - M) ;
 //   lse = M + log2(sum 2^(lse_s - M))   (base 2; stored as natural log).
-// Runs on the 128 consumer threads (tid 0..127).
+// Runs on the 128 consumer threads (tid 0..127).  With a staging area
+// (`stage`, and `s_w` for the weights) the merge is merge_splits_staged;
+// without one (the f32 kernel, which holds no shared ring) the partials are
+// loaded into registers.
 __device__ __forceinline__ void combine_and_store(const MergeSmem& ms, const DecodeArgs& a, int z, int g, int split,
-                                                  int nsplit, int n_kv, int tid, int* s_last) {
-  const int j = tid >> 4;           // q head within the group
-  const int d0 = (tid & 15) * 8;    // 8 output dims per thread
+                                                  int nsplit, int n_kv, int tid, int* s_last, float* stage,
+                                                  int stage_floats, float* s_w) {
+  const int j = tid >> 4;                       // q head within the group
+  const int da = (tid & 15) * 4, db = da + 64;  // the thread's output dims: da..da+3, db..db+3
   const bool active = j < a.group;
   const int h = g * a.group + j;
   float acc[8];
@@ -77,23 +167,26 @@ __device__ __forceinline__ void combine_and_store(const MergeSmem& ms, const Dec
       const float wt = (mw == -INFINITY) ? 0.f : exp2f(mw - M);
       lsum += wt * ms.l[w][j];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) acc[i] += wt * ms.o[w][j][d0 + i];
+      for (int i = 0; i < 4; ++i) {
+        acc[i] += wt * ms.o[w][j][da + i];
+        acc[4 + i] += wt * ms.o[w][j][db + i];
+      }
     }
     const float inv = 1.f / lsum;
 #pragma unroll
     for (int i = 0; i < 8; ++i) acc[i] *= inv;
     lse2 = M + log2f(lsum);
     if (nsplit == 1) {
-      float4* op = reinterpret_cast<float4*>(a.out + ((size_t)z * a.n_heads + h) * a.o_stride + d0);
-      op[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
-      op[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+      float* orow = a.out + ((size_t)z * a.n_heads + h) * a.o_stride;
+      *reinterpret_cast<float4*>(orow + da) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+      *reinterpret_cast<float4*>(orow + db) = make_float4(acc[4], acc[5], acc[6], acc[7]);
       if (a.lse && (tid & 15) == 0)
         a.lse[((size_t)z * a.n_heads + h) * a.lse_stride] = lse2 * 0.69314718055994531f;
     } else {
       const size_t prow = ((size_t)z * a.n_heads + h) * a.max_splits + split;
-      float4* pp = reinterpret_cast<float4*>(a.part_o + prow * kHeadDim + d0);
-      pp[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
-      pp[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+      float* prow_o = a.part_o + prow * kHeadDim;
+      *reinterpret_cast<float4*>(prow_o + da) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+      *reinterpret_cast<float4*>(prow_o + db) = make_float4(acc[4], acc[5], acc[6], acc[7]);
       if ((tid & 15) == 0) a.part_lse[prow] = lse2;
     }
   }
@@ -105,6 +198,11 @@ __device__ __forceinline__ void combine_and_store(const MergeSmem& ms, const Dec
   }
   consumer_bar();
   if (!*s_last) return;
+  if (stage != nullptr) {
+    merge_splits_staged(a, z, g, nsplit, tid, stage, stage_floats, s_w);
+    if (tid == 0) a.counters[(size_t)z * n_kv + g] = 0u;
+    return;
+  }
   // every (q head, split) lse in one round of loads, staged over the per-warp
   // O area (its last reader passed the barriers above); then each thread's
   // partial O loads run eight splits ahead
@@ -127,15 +225,16 @@ __device__ __forceinline__ void combine_and_store(const MergeSmem& ms, const Dec
       const float ls = ls_j[s];
       const float wt = (ls == -INFINITY) ? 0.f : exp2f(ls - M);
       wsum += wt;
-      const float4* pp = reinterpret_cast<const float4*>(a.part_o + (prow0 + s) * kHeadDim + d0);
-      const float4 u = __ldcg(pp), v = __ldcg(pp + 1);
+      const float* pp = a.part_o + (prow0 + s) * kHeadDim;
+      const float4 u = __ldcg(reinterpret_cast<const float4*>(pp + da));
+      const float4 v = __ldcg(reinterpret_cast<const float4*>(pp + db));
       acc[0] += wt * u.x; acc[1] += wt * u.y; acc[2] += wt * u.z; acc[3] += wt * u.w;
       acc[4] += wt * v.x; acc[5] += wt * v.y; acc[6] += wt * v.z; acc[7] += wt * v.w;
     }
     const float inv = 1.f / wsum;
-    float4* op = reinterpret_cast<float4*>(a.out + ((size_t)z * a.n_heads + h) * a.o_stride + d0);
-    op[0] = make_float4(acc[0] * inv, acc[1] * inv, acc[2] * inv, acc[3] * inv);
-    op[1] = make_float4(acc[4] * inv, acc[5] * inv, acc[6] * inv, acc[7] * inv);
+    float* orow = a.out + ((size_t)z * a.n_heads + h) * a.o_stride;
+    *reinterpret_cast<float4*>(orow + da) = make_float4(acc[0] * inv, acc[1] * inv, acc[2] * inv, acc[3] * inv);
+    *reinterpret_cast<float4*>(orow + db) = make_float4(acc[4] * inv, acc[5] * inv, acc[6] * inv, acc[7] * inv);
     if (a.lse && (tid & 15) == 0)
       a.lse[((size_t)z * a.n_heads + h) * a.lse_stride] = (M + log2f(wsum)) * 0.69314718055994531f;
   }
@@ -209,6 +308,7 @@ __global__ void __launch_bounds__((kDecWarps + 1) * 32, kDecCtasPerSm)
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kDecStages * kDecStageBytes);
   uint64_t* empty = full + kDecStages;
   int* s_last = reinterpret_cast<int*>(empty + kDecStages);
+  float* s_w = reinterpret_cast<float*>(s_last + 16);  // [kMaxGroup][32] merge weights
 
   const DecodeItem item = decode_item(sched, sb, blockIdx.x);
   const int split = item.split, g = item.g, z = item.z;
@@ -368,7 +468,10 @@ __global__ void __launch_bounds__((kDecWarps + 1) * 32, kDecCtasPerSm)
     ms.o[warp][h0 + 1][d + 8] = o[mt][3];
   }
   consumer_bar();
-  combine_and_store(ms, a, z, g, split, nsplit, pool.n_kv, threadIdx.x, s_last);
+  // the merge stages partials over the page ring (MergeSmem's last reader is
+  // past the barriers before the merge)
+  combine_and_store(ms, a, z, g, split, nsplit, pool.n_kv, threadIdx.x, s_last, reinterpret_cast<float*>(smem),
+                    kDecStages * kDecStageBytes / 4, s_w);
 }
 
 __global__ void __launch_bounds__(kDecWarps * 32)
@@ -477,7 +580,7 @@ __global__ void __launch_bounds__(kDecWarps * 32)
     *reinterpret_cast<float4*>(&ms.o[warp][j][lane * 4]) = o[j];
   }
   __syncthreads();
-  combine_and_store(ms, a, z, g, split, nsplit, pool.n_kv, threadIdx.x, &s_last);
+  combine_and_store(ms, a, z, g, split, nsplit, pool.n_kv, threadIdx.x, &s_last, nullptr, 0, nullptr);
 }
 
 // K-B2 standalone: merge P split-context partials (from P GPUs or P launches)

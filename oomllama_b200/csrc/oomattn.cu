@@ -29,15 +29,9 @@ using namespace oomattn;
 
 namespace {
 
-// Split-KV partials per (row, q head).  f32 caches: up to 64, a one-page split
-// per CTA up to 1024 cached tokens (C1 f32 decode: 10.9 us at 33 splits, 12.3
-// at 17).  bf16 caches keep 32: one row of 2048 tokens ran 2.8 us slower per
-// layer step at 43 splits than at 26.
-constexpr int kMaxSplits = 64;
-constexpr int kMaxSplitsBf16 = 32;
 int split_cap(int kv_dtype) { return kv_dtype == OOMATTN_DTYPE_BF16 ? kMaxSplitsBf16 : kMaxSplits; }
 static_assert(kMaxGroup * kMaxSplits <= kDecWarps * kMaxGroup * kMergeStride,
-              "the decode merge stages [group][splits] lse values over the per-warp O area");
+              "the f32 decode merge stages [group][splits] lse values over the per-warp O area");
 constexpr unsigned long long kDefaultTimeoutNs = 2000000000ull;  // bounded device waits: 2 s
 constexpr int kPfMinKeyChunk = 4;  // key tiles per unit of a key-split prefill, at least
 

@@ -8,6 +8,12 @@ constexpr int kHeadDim = 128;   // head_dim this library is built for (Qwen2.5 /
 constexpr int kPageSize = 16;   // tokens per KV page
 constexpr int kMaxBatch = 128;  // sequence rows carried in one launch's parameters
 constexpr int kMaxGroup = 8;    // q heads per kv head handled by one decode CTA
+// Split-KV partials per (row, q head).  f32 caches: up to 64, a one-page split
+// per CTA up to 1024 cached tokens (C1 f32 decode: 10.9 us at 33 splits, 12.3
+// at 17).  bf16 caches keep 32: one row of 2048 tokens ran 2.8 us slower per
+// layer step at 43 splits than at 26.
+constexpr int kMaxSplits = 64;
+constexpr int kMaxSplitsBf16 = 32;
 
 // Per-launch sequence rows, passed by value so a launch needs no host->device
 // metadata copy (and can be captured in a CUDA graph).

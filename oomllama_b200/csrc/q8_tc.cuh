@@ -102,14 +102,6 @@ __device__ __forceinline__ int tc_mat_of(const Q8TcArgs& a, int tile) {
 }
 #define OOMATTN_TC_FIELD(a, mi, f) ((mi) == 0 ? (a).m[0].f : ((mi) == 1 ? (a).m[1].f : (a).m[2].f))
 
-__device__ __forceinline__ void cp_async4(void* dst, const void* src) {
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
 
 // kind::i8 instruction descriptor: s32 accumulate, A and B unsigned 8-bit,
 // both K-major, M = 128, N = 64.
